@@ -1,0 +1,208 @@
+// Elementwise kernels (sm_100a): SwiGLU forward/backward, interleaved-pair RoPE, token
+// embedding gather / scatter-add.  All use 16-byte vector accesses on bf16 data.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace mykb {
+
+struct alignas(16) bf16x8 {
+  __nv_bfloat162 v[4];
+};
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+
+// gu (rows, 2F): gate = gu[:, :F], up = gu[:, F:];  a = silu(gate) * up.
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int64_t rows,
+                                  int F) {
+  const int vec_per_row = F / 8;
+  const int64_t total = rows * vec_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int c = (int)(i % vec_per_row) * 8;
+    bf16x8 g = *reinterpret_cast<const bf16x8*>(gu + r * 2 * F + c);
+    bf16x8 u = *reinterpret_cast<const bf16x8*>(gu + r * 2 * F + F + c);
+    bf16x8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 gf = __bfloat1622float2(g.v[j]);
+      float2 uf = __bfloat1622float2(u.v[j]);
+      o.v[j] = __floats2bfloat162_rn(silu_f(gf.x) * uf.x, silu_f(gf.y) * uf.y);
+    }
+    *reinterpret_cast<bf16x8*>(a + r * F + c) = o;
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ gu,
+                                  __nv_bfloat16* __restrict__ dgu, int64_t rows, int F) {
+  const int vec_per_row = F / 8;
+  const int64_t total = rows * vec_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int c = (int)(i % vec_per_row) * 8;
+    bf16x8 g = *reinterpret_cast<const bf16x8*>(gu + r * 2 * F + c);
+    bf16x8 u = *reinterpret_cast<const bf16x8*>(gu + r * 2 * F + F + c);
+    bf16x8 d = *reinterpret_cast<const bf16x8*>(da + r * F + c);
+    bf16x8 dg, du;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 gf = __bfloat1622float2(g.v[j]);
+      float2 uf = __bfloat1622float2(u.v[j]);
+      float2 df = __bfloat1622float2(d.v[j]);
+      float s0 = 1.f / (1.f + __expf(-gf.x)), s1 = 1.f / (1.f + __expf(-gf.y));
+      float ds0 = s0 * (1.f + gf.x * (1.f - s0)), ds1 = s1 * (1.f + gf.y * (1.f - s1));
+      dg.v[j] = __floats2bfloat162_rn(df.x * uf.x * ds0, df.y * uf.y * ds1);
+      du.v[j] = __floats2bfloat162_rn(df.x * gf.x * s0, df.y * gf.y * s1);
+    }
+    *reinterpret_cast<bf16x8*>(dgu + r * 2 * F + c) = dg;
+    *reinterpret_cast<bf16x8*>(dgu + r * 2 * F + F + c) = du;
+  }
+}
+
+static int ew_grid(int64_t work, int threads) {
+  int dev;
+  cudaGetDevice(&dev);
+  int sms;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = (work + threads - 1) / threads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * 16));
+}
+
+torch::Tensor swiglu_fwd(torch::Tensor gu) {
+  c10::cuda::CUDAGuard guard(gu.device());
+  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.is_contiguous(), "swiglu: contiguous bf16");
+  const int F = gu.size(-1) / 2;
+  TORCH_CHECK(F % 8 == 0, "swiglu: half width must be a multiple of 8");
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto a = torch::empty(sizes, gu.options());
+  const int64_t rows = gu.numel() / (2 * F);
+  if (rows == 0) return a;
+  swiglu_fwd_kernel<<<ew_grid(rows * F / 8, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)a.data_ptr(), rows, F);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return a;
+}
+
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu) {
+  c10::cuda::CUDAGuard guard(gu.device());
+  TORCH_CHECK(da.scalar_type() == at::kBFloat16 && da.is_contiguous(), "swiglu_bwd: contiguous bf16 grad");
+  const int F = gu.size(-1) / 2;
+  auto dgu = torch::empty_like(gu);
+  const int64_t rows = gu.numel() / (2 * F);
+  if (rows == 0) return dgu;
+  swiglu_bwd_kernel<<<ew_grid(rows * F / 8, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)da.data_ptr(), (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)dgu.data_ptr(), rows,
+      F);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dgu;
+}
+
+// ------------------------------------------------------------------------------ RoPE
+// x (B, S, H, D) with arbitrary strides for B, S, H (unit stride along D); out is
+// contiguous (B, S, H, D).  Pairs (2i, 2i+1) rotate by angle table[pos][2i].
+// inverse=true applies the transpose rotation (the backward pass).
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                            const int64_t* __restrict__ pos, int B, int S, int H, int D, int64_t sb, int64_t ss,
+                            int64_t sh, int64_t table_len, bool inverse) {
+  const int pairs = D / 2;
+  const int64_t total = (int64_t)B * S * H * pairs;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int p = (int)(i % pairs);
+    int64_t t = i / pairs;
+    const int h = (int)(t % H);
+    t /= H;
+    const int s = (int)(t % S);
+    const int b = (int)(t / S);
+    int64_t ps = pos[(int64_t)b * S + s];
+    ps = ps < 0 ? 0 : (ps >= table_len ? table_len - 1 : ps);
+    const float c = cos_t[ps * D + 2 * p];
+    const float sn = sin_t[ps * D + 2 * p];
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(x + b * sb + s * ss + h * sh + 2 * p);
+    const float2 f = __bfloat1622float2(v);
+    float o0, o1;
+    if (!inverse) {
+      o0 = f.x * c - f.y * sn;
+      o1 = f.y * c + f.x * sn;
+    } else {
+      o0 = f.x * c + f.y * sn;
+      o1 = f.y * c - f.x * sn;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(y + (((int64_t)b * S + s) * H + h) * D + 2 * p) = __floats2bfloat162_rn(o0, o1);
+  }
+}
+
+torch::Tensor rope(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos, bool inverse) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.dim() == 4 && x.stride(3) == 1 && x.scalar_type() == at::kBFloat16, "rope: bf16 (B,S,H,D), unit D stride");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.is_contiguous() && sin_t.is_contiguous(), "rope: fp32 tables");
+  const int B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
+  auto y = torch::empty({B, S, H, D}, x.options());
+  const int64_t total = (int64_t)B * S * H * (D / 2);
+  if (total == 0) return y;
+  TORCH_CHECK(pos.is_contiguous() && pos.scalar_type() == at::kLong && pos.numel() == (int64_t)B * S, "rope: positions");
+  rope_kernel<<<ew_grid(total, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)y.data_ptr(), cos_t.data_ptr<float>(),
+      sin_t.data_ptr<float>(), pos.data_ptr<int64_t>(), B, S, H, D, x.stride(0), x.stride(1), x.stride(2),
+      cos_t.size(0), inverse);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
+// ------------------------------------------------------------------------ embedding
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
+                                     float* __restrict__ out, int64_t n, int dim, int64_t vocab) {
+  const int v4 = dim / 4;
+  const int64_t total = n * v4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / v4;
+    const int c = (int)(i % v4);
+    int64_t id = ids[r];
+    float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (id >= 0 && id < vocab) val = reinterpret_cast<const float4*>(w + id * dim)[c];
+    reinterpret_cast<float4*>(out + r * dim)[c] = val;
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dout_bf,
+                                     const float* __restrict__ dout_f, float* __restrict__ grad, int64_t n, int dim,
+                                     int64_t vocab) {
+  const int64_t total = n * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / dim;
+    const int c = (int)(i % dim);
+    const int64_t id = ids[r];
+    if (id < 0 || id >= vocab) continue;
+    const float g = dout_f != nullptr ? dout_f[i] : __bfloat162float(dout_bf[i]);
+    atomicAdd(grad + id * dim + c, g);
+  }
+}
+
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w) {
+  c10::cuda::CUDAGuard guard(w.device());
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.size(1) % 4 == 0, "embedding: fp32 table");
+  const int64_t n = ids.numel();
+  auto out = torch::empty({n, w.size(1)}, w.options());
+  if (n == 0) return out;
+  embedding_fwd_kernel<<<ew_grid(n * w.size(1) / 4, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(), n, w.size(1), w.size(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+void embedding_bwd(torch::Tensor ids, torch::Tensor dout, torch::Tensor grad) {
+  c10::cuda::CUDAGuard guard(grad.device());
+  TORCH_CHECK(grad.scalar_type() == at::kFloat && grad.is_contiguous(), "embedding_bwd: fp32 grad");
+  const int64_t n = ids.numel();
+  if (n == 0) return;
+  const bool f32 = dout.scalar_type() == at::kFloat;
+  embedding_bwd_kernel<<<ew_grid(n * grad.size(1), 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), f32 ? nullptr : (const __nv_bfloat16*)dout.data_ptr(),
+      f32 ? dout.data_ptr<float>() : nullptr, grad.data_ptr<float>(), n, grad.size(1), grad.size(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb

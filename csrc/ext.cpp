@@ -1,0 +1,81 @@
+// Python bindings of the sm_100a kernels (module myk_llm_b200._C).
+#include <torch/extension.h>
+
+namespace mykb {
+// gemm.cu
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
+          double alpha, double beta, bool accumulate);
+// norm.cu
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<std::vector<torch::Tensor>> add,
+                                       double eps, c10::ScalarType out_dtype);
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                                       c10::optional<torch::Tensor> dres);
+std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, c10::optional<torch::Tensor> g, torch::Tensor w,
+                                             double eps, int64_t act);
+std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, c10::optional<torch::Tensor> g,
+                                             torch::Tensor w, torch::Tensor rstd, int64_t act);
+// elementwise.cu
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
+torch::Tensor rope(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos, bool inverse);
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
+void embedding_bwd(torch::Tensor ids, torch::Tensor dout, torch::Tensor grad);
+// loss.cu
+void ce_fwd_grad(torch::Tensor logits, torch::Tensor targets, double scale, double z_coef, int64_t ignore_index,
+                 torch::Tensor ce_sum, torch::Tensor z_sum);
+// optim.cu
+void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
+                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd);
+void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> bufs, double mu, bool nesterov,
+                  torch::Tensor out);
+void muon_apply(std::vector<torch::Tensor> params, torch::Tensor orth, double decay, double step_scale);
+void frob_normalize_(torch::Tensor x, double eps);
+// attention.cu
+std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> cu_q,
+                                  c10::optional<torch::Tensor> cu_k, c10::optional<torch::Tensor> seqused_k,
+                                  int64_t max_q, int64_t max_k, double scale, int64_t left, int64_t right);
+std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                  torch::Tensor out, torch::Tensor lse, c10::optional<torch::Tensor> cu_q,
+                                  c10::optional<torch::Tensor> cu_k, int64_t max_q, int64_t max_k, double scale,
+                                  int64_t left, int64_t right);
+// gdn.cu
+std::vector<torch::Tensor> conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> cu,
+                                      c10::optional<torch::Tensor> init);
+std::vector<torch::Tensor> conv1d_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w,
+                                      c10::optional<torch::Tensor> cu, c10::optional<torch::Tensor> init);
+std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                               torch::Tensor beta, c10::optional<torch::Tensor> init,
+                                               c10::optional<torch::Tensor> cu, bool per_channel);
+std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                         torch::Tensor g, torch::Tensor beta, c10::optional<torch::Tensor> init,
+                                         c10::optional<torch::Tensor> cu, std::vector<torch::Tensor> saved,
+                                         bool per_channel);
+std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                         torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
+}  // namespace mykb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "myk_llm_b200 sm_100a kernels";
+  m.def("gemm", &mykb::gemm, "tcgen05 bf16 GEMM");
+  m.def("rmsnorm_fwd", &mykb::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &mykb::rmsnorm_bwd);
+  m.def("gated_rmsnorm_fwd", &mykb::gated_rmsnorm_fwd);
+  m.def("gated_rmsnorm_bwd", &mykb::gated_rmsnorm_bwd);
+  m.def("swiglu_fwd", &mykb::swiglu_fwd);
+  m.def("swiglu_bwd", &mykb::swiglu_bwd);
+  m.def("rope", &mykb::rope);
+  m.def("embedding_fwd", &mykb::embedding_fwd);
+  m.def("embedding_bwd", &mykb::embedding_bwd);
+  m.def("ce_fwd_grad", &mykb::ce_fwd_grad);
+  m.def("adamw_step", &mykb::adamw_step);
+  m.def("muon_prepare", &mykb::muon_prepare);
+  m.def("muon_apply", &mykb::muon_apply);
+  m.def("frob_normalize_", &mykb::frob_normalize_);
+  m.def("fa_fwd", &mykb::fa_fwd);
+  m.def("fa_bwd", &mykb::fa_bwd);
+  m.def("conv1d_fwd", &mykb::conv1d_fwd);
+  m.def("conv1d_bwd", &mykb::conv1d_bwd);
+  m.def("gdn_chunk_fwd", &mykb::gdn_chunk_fwd_entry);
+  m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
+  m.def("gdn_recurrent", &mykb::gdn_recurrent);
+}

@@ -1,0 +1,405 @@
+// Persistent, warp-specialised bf16 GEMM on tcgen05 (sm_100a).
+//
+//   D[b, m, n] = alpha * sum_k A[b, m, k] * B[b, n, k] + beta * C[b, m, n]     (store mode)
+//   D[b, m, n] += alpha * sum_k A[b, m, k] * B[b, n, k]                        (accumulate mode)
+//
+// Operands are bf16, each either K-major (reduction dim contiguous) or MN-major (output
+// dim contiguous); D is bf16 or fp32.  Layout per CTA (one CTA per SM, persistent over
+// output tiles in a grouped raster order for L2 reuse):
+//
+//   warp 0      TMA producer: streams 128x64 A and BNx64 B tiles (128-byte swizzle) into a
+//               STAGES-deep shared-memory ring, one mbarrier pair per stage.
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into
+//               one of two tensor-memory accumulators, commits each stage back to the
+//               producer and each finished tile to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns 32 TMEM lanes = 32 rows),
+//               scale / add C, convert, write a 128-byte-swizzled staging tile and issue a
+//               TMA store (or a TMA reduce-add into fp32 D in accumulate mode, which also
+//               carries split-K partial sums).
+//
+// Two accumulators let the epilogue of tile i overlap the main loop of tile i+1.  No TMA
+// multicast is used: this kernel may read operands that other ranks wrote into this GPU's
+// memory, never another GPU's memory.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace mykb {
+
+struct GemmParams {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, k_blocks, split_k, kb_per_split;
+  int total_units;
+  const void* C;  // optional epilogue input, same layout/dtype as D
+  int64_t ldc, c_batch_stride;
+  float alpha, beta;
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGroupM = 8;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagingBytes = 32 * 128;  // per epilogue warp: 32 rows x 128 B
+  static constexpr int kBarOffset = STAGES * kStageBytes + kEpiWarps * kStagingBytes;
+  static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+__device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& b, int& mt, int& nt, int& split) {
+  int tiles = p.tiles_m * p.tiles_n;
+  int tile = unit % tiles;
+  int rest = unit / tiles;
+  split = rest % p.split_k;
+  b = rest / p.split_k;
+  int group_span = kGroupM * p.tiles_n;
+  int group = tile / group_span;
+  int first_m = group * kGroupM;
+  int gsize = min(p.tiles_m - first_m, kGroupM);
+  int in_group = tile % group_span;
+  mt = first_m + in_group % gsize;
+  nt = in_group / gsize;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + STAGES * S::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* full = bars;                  // [STAGES]
+  uint64_t* empty = bars + STAGES;        // [STAGES]
+  uint64_t* acc_full = bars + 2 * STAGES; // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x) {
+        int b, mt, nt, split;
+        unit_coords(p, unit, b, mt, nt, split);
+        int kb0 = split * p.kb_per_split;
+        int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kTimeoutProducer)) { ok = false; break; }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          const int k0 = kb * kBK;
+          if (A_MN) {
+            tma_load_3d(sa, &tmA, &full[stage], mt * kBM, k0, b);
+            tma_load_3d(sa + 8192, &tmA, &full[stage], mt * kBM + 64, k0, b);
+          } else {
+            tma_load_3d(sa, &tmA, &full[stage], k0, mt * kBM, b);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * 8192, &tmB, &full[stage], nt * BN + j * 64, k0, b);
+          } else {
+            tma_load_3d(sb, &tmB, &full[stage], k0, nt * BN, b);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x, ++local) {
+        int b, mt, nt, split;
+        unit_coords(p, unit, b, mt, nt, split);
+        int kb0 = split * p.kb_per_split;
+        int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        const int buf = local & 1;
+        if (!mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, p.status, kTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t b_addr = a_addr + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            uint64_t da = A_MN ? make_sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                               : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            uint64_t db = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                               : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* stage_buf = staging + (warp - 2) * S::kStagingBytes;
+    const uint32_t stage_addr = smem_u32(stage_buf);
+    int local = 0;
+    for (int unit = blockIdx.x; unit < p.total_units; unit += gridDim.x, ++local) {
+      int b, mt, nt, split;
+      unit_coords(p, unit, b, mt, nt, split);
+      const int buf = local & 1;
+      if (!mbar_wait(&acc_full[buf], (local >> 1) & 1, p.status, kTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = mt * kBM + q * 32 + lane;
+      const int col0 = nt * BN;
+      // Each slab is 128 bytes of output columns: 64 bf16 or 32 fp32.
+      constexpr int kSlab = OUT_F32 ? 32 : 64;
+#pragma unroll 1
+      for (int s = 0; s < BN / kSlab; ++s) {
+        float v[kSlab];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + s * kSlab;
+        tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
+        if constexpr (!OUT_F32) tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+        const bool add_c = !ACCUM && p.C != nullptr && p.beta != 0.f;
+#pragma unroll
+        for (int i = 0; i < kSlab; ++i) v[i] *= p.alpha;
+        if (add_c && row < p.M) {
+          const int cbase = col0 + s * kSlab;
+          if (OUT_F32) {
+            const float* c = reinterpret_cast<const float*>(p.C) + b * p.c_batch_stride + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < kSlab; ++i)
+              if (cbase + i < p.N) v[i] += p.beta * c[cbase + i];
+          } else {
+            const __nv_bfloat16* c =
+                reinterpret_cast<const __nv_bfloat16*>(p.C) + b * p.c_batch_stride + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < kSlab; ++i)
+              if (cbase + i < p.N) v[i] += p.beta * __bfloat162float(c[cbase + i]);
+          }
+        }
+        // The previous TMA store from this staging buffer must have finished reading it.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+        // Row `lane` of the staging tile: 8 chunks of 16 bytes, chunk j stored at j ^ (lane & 7)
+        // (the 128-byte swizzle the store tensor map expects).
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t w0, w1, w2, w3;
+          if (OUT_F32) {
+            w0 = __float_as_uint(v[4 * j + 0]);
+            w1 = __float_as_uint(v[4 * j + 1]);
+            w2 = __float_as_uint(v[4 * j + 2]);
+            w3 = __float_as_uint(v[4 * j + 3]);
+          } else {
+            w0 = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            w1 = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            w2 = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            w3 = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+          }
+          const uint32_t addr = stage_addr + lane * 128 + ((j ^ (lane & 7)) * 16);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int x = col0 + s * kSlab;
+          const int y = mt * kBM + q * 32;
+          if (ACCUM) {
+            asm volatile(
+                "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];"
+                ::"l"(reinterpret_cast<uint64_t>(&tmD)), "r"(stage_addr), "r"(x), "r"(y), "r"(b)
+                : "memory");
+          } else {
+            asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                         ::"l"(reinterpret_cast<uint64_t>(&tmD)), "r"(stage_addr), "r"(x), "r"(y), "r"(b)
+                         : "memory");
+          }
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
+      // All TMEM reads of this accumulator are done: hand it back to the MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// -------------------------------------------------------------------------------------
+// host side
+// -------------------------------------------------------------------------------------
+static int num_sms(int device) {
+  static int cached[64] = {0};
+  if (cached[device] == 0) {
+    cudaDeviceGetAttribute(&cached[device], cudaDevAttrMultiProcessorCount, device);
+  }
+  return cached[device];
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const GemmParams& p,
+                        int grid, cudaStream_t stream) {
+  using S = GemmSmem<BN, STAGES>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, OUT_F32, ACCUM>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    configured = true;
+  }
+  kern<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, td, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
+static void dispatch_stages(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const GemmParams& p,
+                            int grid, cudaStream_t stream) {
+  // 4 stages for BN=256 (48 KB each), 6 for BN=128 (32 KB each).
+  if constexpr (BN == 256) {
+    launch_gemm<BN, 4, A_MN, B_MN, OUT_F32, ACCUM>(ta, tb, td, p, grid, stream);
+  } else {
+    launch_gemm<BN, 6, A_MN, B_MN, OUT_F32, ACCUM>(ta, tb, td, p, grid, stream);
+  }
+}
+
+template <int BN>
+static void dispatch_layout(bool a_mn, bool b_mn, bool out_f32, bool accum, const CUtensorMap& ta,
+                            const CUtensorMap& tb, const CUtensorMap& td, const GemmParams& p, int grid,
+                            cudaStream_t s) {
+#define MYKB_GEMM_CASE(AM, BM)                                                       \
+  if (a_mn == AM && b_mn == BM) {                                                    \
+    if (accum) return dispatch_stages<BN, AM, BM, true, true>(ta, tb, td, p, grid, s); \
+    if (out_f32) return dispatch_stages<BN, AM, BM, true, false>(ta, tb, td, p, grid, s); \
+    return dispatch_stages<BN, AM, BM, false, false>(ta, tb, td, p, grid, s);          \
+  }
+  MYKB_GEMM_CASE(false, false)
+  MYKB_GEMM_CASE(false, true)
+  MYKB_GEMM_CASE(true, false)
+  MYKB_GEMM_CASE(true, true)
+#undef MYKB_GEMM_CASE
+}
+
+// a: (batch?, M, K) or (batch?, K, M); b: (batch?, N, K) or (batch?, K, N); d: (batch?, M, N)
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
+          double alpha, double beta, bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda(), "gemm: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands required");
+  TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm: D must be bf16 or fp32");
+  TORCH_CHECK(a.dim() == b.dim() && a.dim() == d.dim() && (a.dim() == 2 || a.dim() == 3), "gemm: rank mismatch");
+  TORCH_CHECK(!accumulate || d.scalar_type() == at::kFloat, "gemm: accumulate needs fp32 D");
+  const bool batched = a.dim() == 3;
+  const int batch = batched ? a.size(0) : 1;
+  const int M = a_mn ? a.size(-1) : a.size(-2);
+  const int K = a_mn ? a.size(-2) : a.size(-1);
+  const int N = b_mn ? b.size(-1) : b.size(-2);
+  const int Kb = b_mn ? b.size(-2) : b.size(-1);
+  TORCH_CHECK(K == Kb, "gemm: reduction sizes differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(d.size(-2) == M && d.size(-1) == N, "gemm: D has the wrong shape");
+  TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && d.stride(-1) == 1, "gemm: inner dims must be contiguous");
+  c10::cuda::CUDAGuard guard(a.device());
+  const bool out_f32 = d.scalar_type() == at::kFloat;
+
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batch = batch;
+  const int BN = (N <= 128) ? 128 : 256;
+  p.tiles_m = (M + kBM - 1) / kBM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.k_blocks = (K + kBK - 1) / kBK;
+  const int sms = num_sms(a.get_device());
+  int split = 1;
+  const int tiles = batch * p.tiles_m * p.tiles_n;
+  if (accumulate && tiles < sms) {
+    split = std::max(1, std::min(sms / tiles, p.k_blocks / 4));
+  }
+  p.kb_per_split = (p.k_blocks + split - 1) / split;
+  p.split_k = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.total_units = tiles * p.split_k;
+  p.alpha = (float)alpha;
+  p.beta = (float)beta;
+  p.C = nullptr;
+  if (c.has_value() && c->defined() && beta != 0.0) {
+    TORCH_CHECK(c->scalar_type() == d.scalar_type() && c->size(-1) == N && c->size(-2) == M && c->stride(-1) == 1,
+                "gemm: C must match D");
+    p.C = c->data_ptr();
+    p.ldc = c->stride(-2);
+    p.c_batch_stride = batched ? c->stride(0) : 0;
+  }
+  p.status = nullptr;
+
+  // Tensor maps (dims innermost first): A/B tiles of 64 elements (128 B) along the
+  // contiguous dim; D boxes of 128 bytes x 32 rows.
+  const int64_t a_bs = batched ? a.stride(0) : 0, b_bs = batched ? b.stride(0) : 0, d_bs = batched ? d.stride(0) : 0;
+  CUtensorMap ta = a_mn ? make_tmap_3d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, batch, a.stride(-2),
+                                       a_bs, 64, 64)
+                        : make_tmap_3d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, batch, a.stride(-2),
+                                       a_bs, 64, kBM);
+  CUtensorMap tb = b_mn ? make_tmap_3d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, batch, b.stride(-2),
+                                       b_bs, 64, 64)
+                        : make_tmap_3d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, batch, b.stride(-2),
+                                       b_bs, 64, BN);
+  CUtensorMap td = out_f32 ? make_tmap_3d(d.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, batch,
+                                          d.stride(-2), d_bs, 32, 32)
+                           : make_tmap_3d(d.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, batch,
+                                          d.stride(-2), d_bs, 64, 32);
+  const int grid = std::min(p.total_units, sms);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (BN == 128) {
+    dispatch_layout<128>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
+  } else {
+    dispatch_layout<256>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
+  }
+}
+
+}  // namespace mykb

@@ -1,0 +1,237 @@
+// Optimizer kernels (sm_100a):
+//   adamw_step       one launch over any number of fp32 tensors (pointer table in device
+//                    memory, chunk -> tensor lookup by binary search over prefix sums)
+//   muon_prepare     momentum lerp, Nesterov blend and bf16 pack of a same-shape bucket
+//   muon_apply       decoupled weight decay + orthogonalised update of a bucket
+//   frob_normalize_  per-matrix Frobenius normalisation of a bf16 batch (Newton-Schulz input)
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace mykb {
+
+constexpr int kChunk = 4096;
+constexpr int kOptThreads = 256;
+
+struct TensorTable {
+  const int64_t* prefix;  // [n+1] chunk prefix
+  const int64_t* numel;   // [n]
+  const int64_t* ptrs;    // [n * k] pointers, k per tensor
+  int n;
+};
+
+__device__ __forceinline__ int find_tensor(const int64_t* prefix, int n, int64_t chunk) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= chunk) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <typename TG>
+__global__ void __launch_bounds__(kOptThreads)
+adamw_kernel(TensorTable tab, int64_t total_chunks, float lr, float b1, float b2, float eps, float wd, float bc1,
+             float bc2_sqrt) {
+  for (int64_t chunk = blockIdx.x; chunk < total_chunks; chunk += gridDim.x) {
+    const int t = find_tensor(tab.prefix, tab.n, chunk);
+    const int64_t start = (chunk - tab.prefix[t]) * kChunk;
+    const int64_t n = tab.numel[t];
+    float* p = reinterpret_cast<float*>(tab.ptrs[4 * t + 0]);
+    const TG* g = reinterpret_cast<const TG*>(tab.ptrs[4 * t + 1]);
+    float* m = reinterpret_cast<float*>(tab.ptrs[4 * t + 2]);
+    float* v = reinterpret_cast<float*>(tab.ptrs[4 * t + 3]);
+    const int64_t end = min(n, start + kChunk);
+    for (int64_t i = start + threadIdx.x; i < end; i += kOptThreads) {
+      float gi;
+      if constexpr (sizeof(TG) == 4) gi = g[i]; else gi = __bfloat162float(g[i]);
+      float pi = p[i] * (1.f - lr * wd);
+      float mi = m[i] + (1.f - b1) * (gi - m[i]);
+      float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+      m[i] = mi;
+      v[i] = vi;
+      const float denom = sqrtf(vi) / bc2_sqrt + eps;
+      p[i] = pi - (lr / bc1) * mi / denom;
+    }
+  }
+}
+
+static int grid_for(int64_t chunks) {
+  int dev;
+  cudaGetDevice(&dev);
+  int sms;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(chunks, (int64_t)sms * 8));
+}
+
+// Builds the device tables: prefix/numel/pointer arrays in one pinned host buffer, copied
+// asynchronously on the current stream.
+static torch::Tensor build_table(const std::vector<std::vector<torch::Tensor>>& lists, std::vector<int64_t>& numels,
+                                 int64_t& total_chunks, torch::Device dev) {
+  const int n = lists[0].size();
+  const int k = lists.size();
+  auto host = torch::empty({(int64_t)(n + 1) + n + (int64_t)n * k}, torch::dtype(torch::kLong).pinned_memory(true));
+  int64_t* h = host.data_ptr<int64_t>();
+  int64_t acc = 0;
+  for (int i = 0; i < n; ++i) {
+    h[i] = acc;
+    const int64_t ne = lists[0][i].numel();
+    numels.push_back(ne);
+    acc += (ne + kChunk - 1) / kChunk;
+    h[(n + 1) + i] = ne;
+    for (int j = 0; j < k; ++j) {
+      TORCH_CHECK(lists[j][i].is_contiguous() && lists[j][i].numel() == ne, "multi-tensor: mismatched tensor ", i);
+      h[(n + 1) + n + (int64_t)i * k + j] = reinterpret_cast<int64_t>(lists[j][i].data_ptr());
+    }
+  }
+  h[n] = acc;
+  total_chunks = acc;
+  auto d = host.to(dev, /*non_blocking=*/true);
+  // keep the pinned buffer alive until the copy has run
+  c10::cuda::CUDACachingAllocator::recordStream(d.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
+  return d;
+}
+
+void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
+                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd) {
+  if (params.empty()) return;
+  c10::cuda::CUDAGuard guard(params[0].device());
+  for (auto& p : params) TORCH_CHECK(p.scalar_type() == at::kFloat, "adamw: fp32 params");
+  const bool g_bf16 = grads[0].scalar_type() == at::kBFloat16;
+  for (auto& g : grads) TORCH_CHECK(g.scalar_type() == grads[0].scalar_type(), "adamw: one grad dtype per call");
+  std::vector<int64_t> numels;
+  int64_t chunks = 0;
+  auto table = build_table({params, grads, m, v}, numels, chunks, params[0].device());
+  const int n = params.size();
+  TensorTable tab{table.data_ptr<int64_t>(), table.data_ptr<int64_t>() + n + 1,
+                  table.data_ptr<int64_t>() + 2 * n + 1, n};
+  const float bc1 = 1.f - (float)std::pow(b1, (double)step);
+  const float bc2s = (float)std::sqrt(1.0 - std::pow(b2, (double)step));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (g_bf16)
+    adamw_kernel<__nv_bfloat16><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s);
+  else
+    adamw_kernel<float><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  // keep the table alive until the kernel ran
+  c10::cuda::CUDACachingAllocator::recordStream(table.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
+}
+
+// ------------------------------------------------------------------------------ Muon
+__global__ void muon_prepare_kernel(const int64_t* gptrs, const int64_t* mptrs, int n, int64_t numel, float mu,
+                                    bool nesterov, bool g_bf16, __nv_bfloat16* __restrict__ out) {
+  const int64_t total = (int64_t)n * numel;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / numel);
+    const int64_t j = i - (int64_t)t * numel;
+    float* m = reinterpret_cast<float*>(mptrs[t]);
+    float g = g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(gptrs[t])[j])
+                     : reinterpret_cast<const float*>(gptrs[t])[j];
+    float mv = m[j] + (1.f - mu) * (g - m[j]);
+    m[j] = mv;
+    float u = nesterov ? g + mu * (mv - g) : mv;
+    out[i] = __float2bfloat16(u);
+  }
+}
+
+__global__ void muon_apply_kernel(const int64_t* pptrs, int n, int64_t numel, float decay, float step_scale,
+                                  const __nv_bfloat16* __restrict__ orth) {
+  const int64_t total = (int64_t)n * numel;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / numel);
+    const int64_t j = i - (int64_t)t * numel;
+    float* p = reinterpret_cast<float*>(pptrs[t]);
+    p[j] = p[j] * (1.f - decay) + step_scale * __bfloat162float(orth[i]);
+  }
+}
+
+static torch::Tensor ptr_table(const std::vector<std::vector<torch::Tensor>>& lists, torch::Device dev) {
+  const int n = lists[0].size();
+  auto host = torch::empty({(int64_t)lists.size() * n}, torch::dtype(torch::kLong).pinned_memory(true));
+  int64_t* h = host.data_ptr<int64_t>();
+  for (size_t j = 0; j < lists.size(); ++j)
+    for (int i = 0; i < n; ++i) {
+      TORCH_CHECK(lists[j][i].is_contiguous(), "muon: contiguous tensors required");
+      h[j * n + i] = reinterpret_cast<int64_t>(lists[j][i].data_ptr());
+    }
+  auto d = host.to(dev, true);
+  return d;
+}
+
+void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> bufs, double mu, bool nesterov,
+                  torch::Tensor out) {
+  if (grads.empty()) return;
+  c10::cuda::CUDAGuard guard(out.device());
+  const int n = grads.size();
+  const int64_t numel = grads[0].numel();
+  TORCH_CHECK(out.numel() == n * numel && out.scalar_type() == at::kBFloat16, "muon_prepare: bad output");
+  for (auto& b : bufs) TORCH_CHECK(b.scalar_type() == at::kFloat, "muon_prepare: fp32 momentum");
+  const bool g_bf16 = grads[0].scalar_type() == at::kBFloat16;
+  auto tab = ptr_table({grads, bufs}, out.device());
+  const int64_t total = n * numel;
+  muon_prepare_kernel<<<grid_for((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      tab.data_ptr<int64_t>(), tab.data_ptr<int64_t>() + n, n, numel, (float)mu, nesterov, g_bf16,
+      (__nv_bfloat16*)out.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  c10::cuda::CUDACachingAllocator::recordStream(tab.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
+}
+
+void muon_apply(std::vector<torch::Tensor> params, torch::Tensor orth, double decay, double step_scale) {
+  if (params.empty()) return;
+  c10::cuda::CUDAGuard guard(orth.device());
+  const int n = params.size();
+  const int64_t numel = params[0].numel();
+  for (auto& p : params) TORCH_CHECK(p.scalar_type() == at::kFloat, "muon_apply: fp32 params");
+  auto tab = ptr_table({params}, orth.device());
+  const int64_t total = n * numel;
+  muon_apply_kernel<<<grid_for((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      tab.data_ptr<int64_t>(), n, numel, (float)decay, (float)step_scale, (const __nv_bfloat16*)orth.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  c10::cuda::CUDACachingAllocator::recordStream(tab.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
+}
+
+// ------------------------------------------------------------- Frobenius normalisation
+__global__ void sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t per, float* __restrict__ out) {
+  const int b = blockIdx.y;
+  const __nv_bfloat16* xb = x + (int64_t)b * per;
+  float s = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = __bfloat162float(xb[i]);
+    s += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    atomicAdd(out + b, t);
+  }
+}
+
+__global__ void scale_kernel(__nv_bfloat16* __restrict__ x, int64_t per, const float* __restrict__ ss, float eps) {
+  const int b = blockIdx.y;
+  __nv_bfloat16* xb = x + (int64_t)b * per;
+  const float inv = 1.f / fmaxf(sqrtf(ss[b]), eps);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
+    xb[i] = __float2bfloat16(__bfloat162float(xb[i]) * inv);
+}
+
+void frob_normalize_(torch::Tensor x, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3, "frob_normalize_: bf16 (B, r, c)");
+  const int B = x.size(0);
+  const int64_t per = x.size(1) * x.size(2);
+  auto ss = torch::zeros({B}, x.options().dtype(at::kFloat));
+  dim3 grid((unsigned)std::min<int64_t>(64, (per + 255) / 256), B);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  sumsq_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x.data_ptr(), per, ss.data_ptr<float>());
+  scale_kernel<<<grid, 256, 0, st>>>((__nv_bfloat16*)x.data_ptr(), per, ss.data_ptr<float>(), (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb

@@ -1,0 +1,94 @@
+"""Gated DeltaNet / Kimi Delta Attention ops: short causal convolution, decay gates,
+the gated delta rule (chunked for training, recurrent for decode) and the gated norm.
+
+Semantics are those of the flash-linear-attention calls in the reference
+(``src/myk_llm/model/mixers.py:220-314``): q and k are L2-normalised inside the op, the
+scale is ``head_k_dim ** -0.5``, the decay is ``g = -exp(A_log) * softplus(a + dt_bias)`` in
+log space (per head for GDN, per key channel for KDA), beta arrives already passed
+through a sigmoid.
+
+CUDA kernels (``csrc/gdn.cu``):
+
+* ``conv1d_fwd/bwd``: depthwise causal conv + SiLU over the packed q/k/v, resetting at
+  document boundaries;
+* ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64) with the state kept in fp32;
+  each CTA owns one (sequence, head) and walks its chunks, doing the intra-chunk WY
+  transform and the inter-chunk state products on tensor cores;
+* ``gdn_recurrent``: token-by-token decode over a state cache.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as ref
+from ._ext import ext
+
+
+def gdn_gate(a: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor) -> torch.Tensor:
+    """Log-space decay per head: -exp(A_log) * softplus(a + dt_bias), fp32."""
+    return -torch.exp(A_log.float()) * F.softplus(a.float() + dt_bias.float())
+
+
+def kda_gate(f: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor) -> torch.Tensor:
+    """Per-channel KDA decay: -exp(A_log[h]) * softplus(f + dt_bias), f (B, T, H, dk)."""
+    heads, dk = f.shape[-2], f.shape[-1]
+    return -torch.exp(A_log.float()).view(heads, 1) * F.softplus(f.float() + dt_bias.float().view(heads, dk))
+
+
+class _Conv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, cu, init):
+        y, final = ext().conv1d_fwd(x, w, cu, init)
+        ctx.save_for_backward(x, w, cu, init)
+        return y, final
+
+    @staticmethod
+    def backward(ctx, dy, _dfinal):
+        x, w, cu, init = ctx.saved_tensors
+        dx, dw = ext().conv1d_bwd(dy.contiguous(), x, w, cu, init)
+        return dx, dw.to(w.dtype), None, None
+
+
+def causal_conv1d(x, weight, cu_seqlens=None, initial_state=None, return_final_state=False):
+    """x (B, T, D), weight (D, K) -> (silu(conv(x)), final_state (B or N, D, K-1) or None)."""
+    if not x.is_cuda or (initial_state is not None and torch.is_grad_enabled()):
+        y, fin = ref.causal_conv1d_ref(x, weight, cu_seqlens=cu_seqlens, initial_state=initial_state)
+        return y, (fin.to(x.dtype) if return_final_state else None)
+    xb = x.contiguous()
+    y, fin = _Conv.apply(xb, weight.contiguous(), cu_seqlens, initial_state)
+    return y, (fin if return_final_state else None)
+
+
+class _DeltaRule(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, init, cu, per_channel):
+        o, final, saved = ext().gdn_chunk_fwd(q, k, v, g, beta, init, cu, bool(per_channel))
+        ctx.save_for_backward(q, k, v, g, beta, init, cu, *saved)
+        ctx.per_channel = per_channel
+        return o, final
+
+    @staticmethod
+    def backward(ctx, do, dfinal):
+        q, k, v, g, beta, init, cu, *saved = ctx.saved_tensors
+        dq, dk, dv, dg, db = ext().gdn_chunk_bwd(do.contiguous(), q, k, v, g, beta, init, cu, list(saved),
+                                                 bool(ctx.per_channel))
+        return dq, dk, dv, dg, db, None, None, None
+
+
+def gated_delta_rule(q, k, v, g, beta, initial_state=None, cu_seqlens=None, cu_seqlens_cpu=None,
+                     output_final_state=False, per_channel_decay=False):
+    """o_t = S_t^T (q_t / sqrt(dk)) with S_t = exp(g_t) S_{t-1} + k_t (beta_t (v_t - S^T k_t))^T,
+    q/k L2-normalised.  Returns (o (B, T, H, dv), final state or None)."""
+    if not q.is_cuda:
+        o, fin = ref.delta_rule_ref(q, k, v, g, beta, initial_state=initial_state, cu_seqlens=cu_seqlens,
+                                    per_channel_decay=per_channel_decay)
+        return o, (fin if output_final_state else None)
+    if not torch.is_grad_enabled() and q.shape[1] <= 64 and cu_seqlens is None:
+        o, fin = ext().gdn_recurrent(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(),
+                                     beta.contiguous(), initial_state, bool(per_channel_decay))
+        return o, (fin if output_final_state else None)
+    o, fin = _DeltaRule.apply(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
+                              beta.float().contiguous(), initial_state, cu_seqlens, per_channel_decay)
+    return o, (fin if output_final_state else None)

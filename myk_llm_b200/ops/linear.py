@@ -1,0 +1,119 @@
+"""Linear layers on the tcgen05 GEMM.
+
+``gemm`` computes ``D[m, n] = alpha * sum_k A[m, k] * B[n, k] + beta * C[m, n]`` with bf16
+operands and fp32 accumulation in tensor memory.  Each operand is passed either K-major
+(the reduction dimension is contiguous) or MN-major (the output dimension is
+contiguous), which covers the forward ``x W^T``, the data gradient ``dy W`` and the weight
+gradient ``dy^T x`` of a linear layer without any transposing copy.  With
+``accumulate=True`` the fp32 output is added to atomically, which also lets the kernel
+split K across CTAs when the output has too few tiles to fill the 148 SMs.
+
+The reference runs these through cuBLAS under autocast (``nn.Linear`` in
+``src/myk_llm/model/*.py``); here every block linear is this kernel.
+
+Master weights stay fp32.  The bf16 copy a GEMM reads is cached on the parameter and
+refreshed when the parameter's version counter changes (i.e. after an optimizer step), so
+gradient accumulation and the backward pass reuse one cast per step.  A parameter that
+carries a ``main_grad`` fp32 buffer receives its weight gradient accumulated in place by
+the GEMM epilogue (no separate gradient tensor, no extra add).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_major: str = "k", b_major: str = "k",
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
+         beta: float = 0.0, c: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """See module docstring.  ``a`` is (.., M, K) for K-major or (.., K, M) for M-major; ``b`` is
+    (.., N, K) for K-major or (.., K, N) for N-major.  Leading dims are a batch."""
+    a_mn, b_mn = a_major == "mn", b_major == "mn"
+    if not a.is_cuda:
+        am = a.transpose(-1, -2) if a_mn else a
+        bm = b.transpose(-1, -2) if b_mn else b
+        res = alpha * (am.float() @ bm.float().transpose(-1, -2))
+        if c is not None and beta != 0.0:
+            res = res + beta * c.float()
+        if out is None:
+            return res.to(out_dtype)
+        if accumulate:
+            out.add_(res.to(out.dtype))
+        else:
+            out.copy_(res)
+        return out
+    m = a.shape[-1] if a_mn else a.shape[-2]
+    n = b.shape[-1] if b_mn else b.shape[-2]
+    if out is None:
+        out = torch.empty(*a.shape[:-2], m, n, dtype=out_dtype, device=a.device)
+    ext().gemm(a, b, out, c, a_mn, b_mn, float(alpha), float(beta), bool(accumulate))
+    return out
+
+
+def bf16_weight(w: torch.Tensor) -> torch.Tensor:
+    """bf16 view of a (usually fp32 master) weight, cast once per parameter version."""
+    if w.dtype == torch.bfloat16:
+        return w if w.is_contiguous() else w.contiguous()
+    cache = getattr(w, "_mykb_bf16", None)
+    ver = w._version
+    if cache is not None and cache[0] == ver and cache[1].data_ptr() != 0:
+        return cache[1]
+    wb = w.detach().to(torch.bfloat16).contiguous()
+    try:
+        w._mykb_bf16 = (ver, wb)
+    except AttributeError:  # pragma: no cover - tensors that refuse attributes
+        pass
+    return wb
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, w: torch.Tensor):
+        k = x.shape[-1]
+        x2 = x.reshape(-1, k)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        wb = bf16_weight(w)
+        y = gemm(x2, wb)
+        ctx.save_for_backward(x2, wb)
+        ctx.w = w
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        x2, wb = ctx.saved_tensors
+        w = ctx.w
+        n = wb.shape[0]
+        dy2 = dy.reshape(-1, n)
+        if dy2.dtype != torch.bfloat16:
+            dy2 = dy2.to(torch.bfloat16)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dy2, wb, b_major="mn").view(ctx.x_shape)
+            if ctx.x_dtype != torch.bfloat16:
+                dx = dx.to(ctx.x_dtype)
+        if ctx.needs_input_grad[1]:
+            main = getattr(w, "main_grad", None)
+            if main is not None:
+                gemm(dy2, x2, a_major="mn", b_major="mn", out=main, accumulate=True)
+                w._mykb_grad_added = True
+            else:
+                dw = gemm(dy2, x2, a_major="mn", b_major="mn", out_dtype=torch.float32)
+                if w.dtype != torch.float32:
+                    dw = dw.to(w.dtype)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM; CPU: ``F.linear`` in x's dtype."""
+    if not x.is_cuda:
+        return F.linear(x, weight.to(x.dtype))
+    return _Linear.apply(x, weight)

@@ -1,0 +1,189 @@
+"""Memory-bound kernels (RMSNorm, add+RMSNorm, gated norm, SwiGLU, RoPE, embedding, CE,
+AdamW, Muon prep/apply) vs their fp32 PyTorch statements."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, tol):
+    err = (a.float() - b.float()).abs().max().item()
+    scale = b.float().abs().max().item() + 1e-6
+    assert err <= tol * scale, f"err {err} scale {scale}"
+
+
+@pytest.mark.parametrize("hidden", [64, 128, 1024, 2048])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_rmsnorm_fwd_bwd(hidden, xdt):
+    from myk_llm_b200 import ops
+
+    if hidden == 64 and xdt == torch.float32:
+        pytest.skip("width-64 norms run on bf16 q/k heads only")
+    torch.manual_seed(0)
+    x = torch.randn(333, hidden, device="cuda", dtype=xdt, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda")).requires_grad_(True)
+    y = ops.rms_norm(x, w, 1e-6, out_dtype=torch.bfloat16)
+    g = torch.randn_like(y)
+    (y.float() * g.float()).sum().backward()
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    (yr * g.float()).sum().backward()
+    _close(y, yr, 1e-2)
+    _close(x.grad, xr.grad, 2e-2)
+    _close(w.grad, wr.grad, 2e-2)
+
+
+def test_add_rmsnorm():
+    from myk_llm_b200 import ops
+
+    torch.manual_seed(1)
+    x = torch.randn(257, 1024, device="cuda", requires_grad=True)
+    u = torch.randn(257, 1024, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(1024, device="cuda", requires_grad=True)
+    s, y = ops.add_rms_norm(x, u, w, 1e-6, out_dtype=torch.bfloat16)
+    gs, gy = torch.randn_like(s), torch.randn_like(y)
+    ((s * gs).sum() + (y.float() * gy.float()).sum()).backward()
+    xr, ur, wr = (t.detach().float().requires_grad_(True) for t in (x, u, w))
+    sr = xr + ur
+    yr = sr * torch.rsqrt(sr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    ((sr * gs).sum() + (yr * gy.float()).sum()).backward()
+    _close(s, sr, 1e-5)
+    _close(y, yr, 1e-2)
+    _close(x.grad, xr.grad, 2e-2)
+    _close(u.grad, ur.grad, 2e-2)
+    _close(w.grad, wr.grad, 2e-2)
+
+
+@pytest.mark.parametrize("act", ["swish", "sigmoid"])
+def test_gated_rmsnorm(act):
+    from myk_llm_b200 import ops
+    from myk_llm_b200.ops import reference as ref
+
+    torch.manual_seed(2)
+    o = torch.randn(64, 3, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    g = torch.randn(64, 3, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(128, device="cuda", requires_grad=True)
+    y = ops.gated_rms_norm(o, g, w, 1e-5, act)
+    gy = torch.randn_like(y)
+    (y.float() * gy.float()).sum().backward()
+    orf, grf, wrf = (t.detach().float().requires_grad_(True) for t in (o, g, w))
+    yr = ref.gated_rms_norm_ref(orf, grf, wrf, 1e-5, act)
+    (yr * gy.float()).sum().backward()
+    _close(y, yr, 2e-2)
+    _close(o.grad, orf.grad, 3e-2)
+    _close(g.grad, grf.grad, 3e-2)
+    _close(w.grad, wrf.grad, 3e-2)
+
+
+def test_swiglu():
+    from myk_llm_b200 import ops
+
+    torch.manual_seed(3)
+    gu = torch.randn(100, 2 * 704, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    a = ops.swiglu(gu)
+    ga = torch.randn_like(a)
+    (a.float() * ga.float()).sum().backward()
+    r = gu.detach().float().requires_grad_(True)
+    g, u = r.chunk(2, -1)
+    ar = F.silu(g) * u
+    (ar * ga.float()).sum().backward()
+    _close(a, ar, 1e-2)
+    _close(gu.grad, r.grad, 2e-2)
+
+
+def test_rope_strided_and_inverse():
+    from myk_llm_b200 import ops
+    from myk_llm_b200.models.layers import RotaryEmbedding
+
+    torch.manual_seed(4)
+    rope = RotaryEmbedding(64, 512, 10000.0).cuda()
+    qkv = torch.randn(2, 77, 6 * 64, device="cuda", dtype=torch.bfloat16)
+    q = qkv[..., : 4 * 64].view(2, 77, 4, 64)  # strided view into the fused projection
+    pos = torch.arange(77, device="cuda").expand(2, -1) + 5
+    y = ops.apply_rope(q, rope.cos_cached, rope.sin_cached, pos)
+    c = rope.cos_cached[pos].unsqueeze(2)
+    s = rope.sin_cached[pos].unsqueeze(2)
+    from myk_llm_b200.ops.reference import rope_ref
+
+    _close(y, rope_ref(q.float(), c, s), 1e-2)
+    q2 = q.detach().clone().requires_grad_(True)
+    y2 = ops.apply_rope(q2, rope.cos_cached, rope.sin_cached, pos)
+    gy = torch.randn_like(y2)
+    (y2.float() * gy.float()).sum().backward()
+    qr = q.detach().float().requires_grad_(True)
+    (rope_ref(qr, c, s) * gy.float()).sum().backward()
+    _close(q2.grad, qr.grad, 2e-2)
+
+
+def test_embedding():
+    from myk_llm_b200 import ops
+
+    w = torch.randn(1000, 128, device="cuda", requires_grad=True)
+    ids = torch.randint(0, 1000, (4, 33), device="cuda")
+    out = ops.embedding(ids, w)
+    g = torch.randn_like(out)
+    (out * g).sum().backward()
+    wr = w.detach().clone().requires_grad_(True)
+    (F.embedding(ids, wr) * g).sum().backward()
+    _close(out, F.embedding(ids, w.detach()), 1e-6)
+    _close(w.grad, wr.grad, 1e-5)
+
+
+@pytest.mark.parametrize("z", [0.0, 1e-4])
+def test_fused_linear_ce(z):
+    from myk_llm_b200.ops import fused_linear_cross_entropy
+    from myk_llm_b200.ops.reference import linear_cross_entropy_ref
+
+    torch.manual_seed(5)
+    n, h, v = 1000, 256, 4096
+    hid = (0.5 * torch.randn(n, h, device="cuda")).bfloat16().requires_grad_(True)
+    w = (0.05 * torch.randn(v, h, device="cuda")).requires_grad_(True)
+    t = torch.randint(0, v, (n,), device="cuda")
+    t[::7] = -100
+    norm = float((t != -100).sum())
+    loss, ce, zs = fused_linear_cross_entropy(hid, w, t, norm, z, chunk_size=384)
+    loss.backward()
+    hr = hid.detach().float().requires_grad_(True)
+    wr = w.detach().bfloat16().float().requires_grad_(True)
+    lr_, cer, zr = linear_cross_entropy_ref(hr, wr, t, norm, z)
+    lr_.backward()
+    assert abs(loss.item() - lr_.item()) < 2e-2 * abs(lr_.item())
+    assert abs(ce.item() - cer.item()) < 2e-2 * abs(cer.item())
+    _close(hid.grad, hr.grad, 5e-2)
+    _close(w.grad, wr.grad, 5e-2)
+
+
+def test_adamw_multi_tensor():
+    from myk_llm_b200.ops import adamw_multi_tensor
+    from myk_llm_b200.ops.reference import adamw_ref
+
+    torch.manual_seed(6)
+    shapes = [(1000,), (37, 91), (4096, 8), (5,)]
+    ps = [torch.randn(s, device="cuda") for s in shapes]
+    gs = [torch.randn(s, device="cuda") for s in shapes]
+    ms = [torch.randn(s, device="cuda").abs() for s in shapes]
+    vs = [torch.randn(s, device="cuda").abs() for s in shapes]
+    ref = [[t.clone() for t in ts] for ts in (ps, gs, ms, vs)]
+    adamw_multi_tensor(ps, gs, ms, vs, 3, 1e-3, 0.9, 0.95, 1e-8, 0.1)
+    for i in range(len(shapes)):
+        adamw_ref(ref[0][i], ref[1][i], ref[2][i], ref[3][i], 3, 1e-3, 0.9, 0.95, 1e-8, 0.1)
+        _close(ps[i], ref[0][i], 1e-5)
+        _close(ms[i], ref[2][i], 1e-5)
+        _close(vs[i], ref[3][i], 1e-5)
+
+
+def test_newton_schulz_matches_reference():
+    from myk_llm_b200.ops import batched_newton_schulz_orthogonalize
+    from myk_llm_b200.ops.reference import newton_schulz_ref
+
+    torch.manual_seed(7)
+    for shape in [(4, 256, 512), (3, 512, 256), (2, 384, 384)]:
+        g = torch.randn(*shape, device="cuda")
+        out = batched_newton_schulz_orthogonalize(g, 5)
+        ref = newton_schulz_ref(g, 5)
+        _close(out, ref, 6e-2)

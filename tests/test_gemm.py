@@ -1,0 +1,87 @@
+"""tcgen05 GEMM vs an fp32 PyTorch reference, over operand layouts, ragged edges, batch,
+fp32 output, epilogue C and split-K accumulation."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, a_mn, b_mn):
+    am = a.float().transpose(-1, -2) if a_mn else a.float()
+    bm = b.float().transpose(-1, -2) if b_mn else b.float()
+    return am @ bm.transpose(-1, -2)
+
+
+def _mk(m, n, k, a_mn, b_mn, batch=None):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    lead = (batch,) if batch else ()
+    a = torch.randn(*lead, *((k, m) if a_mn else (m, k)), device="cuda", generator=g).bfloat16()
+    b = torch.randn(*lead, *((k, n) if b_mn else (n, k)), device="cuda", generator=g).bfloat16()
+    return a, b
+
+
+def _close(out, ref, rel=2e-2):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= rel * scale, f"max err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", [(128, 128, 64), (256, 384, 256), (264, 200, 136), (1024, 1536, 1024)])
+def test_gemm_layouts(a_mn, b_mn, shape):
+    from myk_llm_b200.ops import gemm
+
+    m, n, k = shape
+    a, b = _mk(m, n, k, a_mn, b_mn)
+    out = gemm(a, b, a_major="mn" if a_mn else "k", b_major="mn" if b_mn else "k")
+    torch.cuda.synchronize()
+    _close(out, _ref(a, b, a_mn, b_mn))
+
+
+def test_gemm_fp32_out_and_alpha():
+    from myk_llm_b200.ops import gemm
+
+    a, b = _mk(512, 256, 320, False, False)
+    out = gemm(a, b, out_dtype=torch.float32, alpha=0.5)
+    _close(out, 0.5 * _ref(a, b, False, False), rel=1e-2)
+
+
+def test_gemm_accumulate_split_k():
+    from myk_llm_b200.ops import gemm
+
+    # few output tiles, long K: the kernel splits K and reduces with TMA reduce-add
+    a, b = _mk(4096, 256, 384, True, True)  # a: (K=4096, M=256)... rows are the reduction
+    a = torch.randn(8192, 256, device="cuda").bfloat16()  # (K, M)
+    b = torch.randn(8192, 384, device="cuda").bfloat16()  # (K, N)
+    d = torch.randn(256, 384, device="cuda")
+    base = d.clone()
+    gemm(a, b, a_major="mn", b_major="mn", out=d, accumulate=True)
+    _close(d, base + a.float().t() @ b.float(), rel=1e-2)
+
+
+def test_gemm_batched_with_c():
+    from myk_llm_b200.ops import gemm
+
+    a, b = _mk(192, 192, 256, False, False, batch=3)
+    c = torch.randn(3, 192, 192, device="cuda").bfloat16()
+    out = gemm(a, b, alpha=2.0, beta=-0.5, c=c)
+    _close(out, 2.0 * _ref(a, b, False, False) - 0.5 * c.float())
+
+
+def test_linear_autograd_matches_reference():
+    from myk_llm_b200.ops import linear
+
+    torch.manual_seed(0)
+    x = torch.randn(4, 96, 256, device="cuda", requires_grad=True)
+    w = torch.randn(384, 256, device="cuda", requires_grad=True)
+    y = linear(x, w)
+    y.float().square().sum().backward()
+    xr = x.detach().clone().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = xr.bfloat16().float() @ wr.bfloat16().float().t()
+    yr.square().sum().backward()
+    _close(y, yr)
+    _close(x.grad, xr.grad, rel=3e-2)
+    _close(w.grad, wr.grad, rel=3e-2)
