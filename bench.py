@@ -1,0 +1,333 @@
+"""Training-throughput benchmark: train tokens/s of the 200M dense config.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
+
+Model: d_model 1024, 24 layers of global GQA attention (16 query / 4 KV heads of 64, RoPE
+theta 10000 on every layer), SwiGLU 2816, untied 65536 vocab, fused linear-CE with
+z-loss 1e-4; Muon (5 Newton-Schulz steps) on 2-D block weights, AdamW elsewhere; random
+init (std 0.02).  Data: synthetic packed documents (geometric lengths, mean 1024, capped
+at 4096, uniform ids, EOS between documents), seq 4096, micro-batch 8 per GPU, one
+micro-batch per GPU per step (weak scaling: global batch 8 x N), document-masked.
+
+Timing: W untimed warm-up steps; then K steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events on the launching stream;
+the reported time is the max over ranks.  A second loop of K steps measures the same
+metric end to end through the public API (pinned host batches copied in every step, loss
+read back to the host every step), by wall clock.  The working set (activations of
+32K tokens, 400M parameters, optimizer state) is far above the 126 MB L2, so no L2 flush
+is inserted.  nvidia-smi clocks are sampled during the timed loop.
+
+``--impl reference`` runs the unmodified reference package installed under
+``baseline/_ref`` through its own public API (MykLLM, parallelize with torch.compile and
+FSDP2, build_optimizers, Objective) on the same config and data.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+BASELINE_TOKS = None  # BASELINE.md publishes no number for this metric/config on any GPU
+
+MODEL_OVERRIDES = [
+    "model.vocab_size=65536", "model.hidden_size=1024", "model.num_layers=24", "model.layer_pattern=G",
+    "model.max_seq_len=4096", "model.tie_embeddings=false", "model.norm_eps=1e-6",
+    "model.attention.num_heads=16", "model.attention.num_kv_heads=4", "model.attention.head_dim=64",
+    "model.attention.global_rope=all", "model.attention.rope_theta_global=10000.0",
+    "model.ffn.multiplier=2.75", "model.ffn.multiple_of=256",
+    "objective.z_loss=1e-4", "optimizer.name=muon", "optimizer.muon_ns_steps=5",
+    "data.seq_len=4096", "data.micro_batch_size=8",
+]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=24, help="(debug only) fewer layers; results are not comparable")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while the timed loop runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        mhz, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ----------------------------------------------------------------------------- helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def synthetic_batches(n: int, step0: int, rank: int, world: int, batch_cls, seed: int = 0):
+    """The synthetic packed-document micro-batches of steps [step0, step0+n) for this rank,
+    built on the host and pinned."""
+    from myk_llm_b200.data.config import DataConfig, SyntheticDataConfig
+    from myk_llm_b200.data.synthetic import SyntheticLoader
+
+    cfg = DataConfig(kind="synthetic", seq_len=4096, micro_batch_size=8, seed=seed,
+                     synthetic=SyntheticDataConfig(vocab_size=65536, mean_doc_len=1024, eos_id=0))
+    ld = SyntheticLoader(cfg, rank, world)
+    out = []
+    for s in range(step0, step0 + n):
+        b = ld.batch_at(s)
+        out.append(batch_cls(b.input_ids.pin_memory(), b.targets.pin_memory(), b.seqlens))
+    return out
+
+
+def max_over_ranks(x: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier_sync(device):
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+def count_launches(step_fn, prefix: str) -> int:
+    """Kernels whose name contains ``prefix`` launched by one step (profiled outside the
+    timed region)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    n = 0
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA and prefix in e.name:
+            n += 1
+    return n
+
+
+# ----------------------------------------------------------------------------- arms
+def build_ours(world: int, layers: int):
+    import torch
+
+    from myk_llm_b200.configuration import apply_overrides, from_dict
+    from myk_llm_b200.data.config import Batch
+    from myk_llm_b200.parallel.distributed import init_distributed
+    from myk_llm_b200.train.config import TrainConfig
+    from myk_llm_b200.train.trainer import Trainer
+
+    ov = MODEL_OVERRIDES + [f"global_batch_size={8 * world}", "steps=1000", "schedule.warmup_ratio=0.0",
+                            "data.kind=synthetic", "logging.tensorboard=false", f"model.num_layers={layers}"]
+    cfg = from_dict(TrainConfig, apply_overrides({}, ov))
+    info = init_distributed()
+    tr = Trainer(cfg, info, build_data=False)
+    state = {"step": 0}
+
+    def step(batch):
+        state["step"] += 1
+        return tr.train_step([batch], state["step"])["loss"]
+
+    return info.device, step, Batch, tr
+
+
+def build_reference(world: int, layers: int):
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    import torch
+
+    from myk_llm.configuration import apply_overrides, from_dict
+    from myk_llm.data import Batch
+    from myk_llm.model import MykLLM
+    from myk_llm.train.config import TrainConfig
+    from myk_llm.train.distributed import all_reduce_sum, init_distributed, parallelize
+    from myk_llm.train.objectives import Objective
+    from myk_llm.train.optim import build_optimizers
+
+    ov = [o for o in MODEL_OVERRIDES] + [f"global_batch_size={8 * world}", f"model.num_layers={layers}"]
+    cfg = from_dict(TrainConfig, apply_overrides({}, ov))
+    info = init_distributed()
+    torch.manual_seed(cfg.seed)
+    torch.set_float32_matmul_precision("high")
+    model = parallelize(MykLLM(cfg.model).to(info.device), cfg.parallel, info)
+    opts = build_optimizers(model, cfg.optimizer)
+    obj = Objective(cfg.objective, info.device)
+    params = [p for p in model.parameters() if p.requires_grad]
+
+    def step(batch):
+        b = batch.to(info.device)
+        norm = all_reduce_sum(batch.num_targets, info.device)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = model(b.input_ids, seqlens=b.seqlens, head=obj.head(b, norm))
+        out.loss.backward()
+        torch.nn.utils.clip_grad_norm_(params, cfg.optimizer.grad_clip)
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+        return out.sums["ce"] / norm
+
+    return info.device, step, Batch, None
+
+
+def main():
+    a = parse()
+    rank, world, local = dist_env()
+    if a.gpus != world and world > 1:
+        print(f"warning: --gpus {a.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    os.environ.setdefault("MYKB_PG_TIMEOUT_S", "600")
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    if a.impl == "reference":
+        ref_dir = os.path.join(ROOT, "baseline", "_ref", "myk_llm")
+        if not os.path.isdir(ref_dir):
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+            return
+        device, step, batch_cls, _ = build_reference(world, a.layers)
+    else:
+        device, step, batch_cls, _ = build_ours(world, a.layers)
+
+    total_steps = a.warmup + 2 * a.steps + 1
+    batches = synthetic_batches(total_steps, 0, rank, world, batch_cls)
+    bi = iter(batches)
+    for _ in range(a.warmup):
+        step(next(bi))
+    barrier_sync(device)
+    launches = 0
+    if a.impl == "ours":
+        b = next(bi)
+        launches = count_launches(lambda: step(b), "mykb") * a.steps
+    else:
+        next(bi)
+    barrier_sync(device)
+
+    # ---- device-timed loop
+    clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    clocks.start()
+    time.sleep(0.3)
+    timed = [next(bi) for _ in range(a.steps)]
+    barrier_sync(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    last = None
+    for b in timed:
+        last = step(b)
+    ev1.record()
+    barrier_sync(device)
+    clk = clocks.stop()
+    dev_ms = ev0.elapsed_time(ev1)
+    dev_ms = max_over_ranks(dev_ms, device)
+    loss_val = float(last) if last is not None else float("nan")
+
+    # ---- end-to-end loop (public API, H2D + D2H every step)
+    e2e_batches = [next(bi) for _ in range(a.steps)]
+    barrier_sync(device)
+    t0 = time.perf_counter()
+    for b in e2e_batches:
+        float(step(b))
+    barrier_sync(device)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device)
+
+    tokens_per_step = 8 * 4096 * world
+    value = tokens_per_step * a.steps / (dev_ms / 1000.0)
+    e2e = tokens_per_step * a.steps / e2e_s
+    h2d = timed[0].input_ids.numel() * 8 * 2 + sum(s.numel() * 4 for s in (timed[0].seqlens or []))
+    if rank == 0:
+        rec = {
+            "metric": "train tokens/sec at 1/2/4/8 B200 (200M, 1B hybrid); MTP decode tokens/sec",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": dev_ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
+            "data": "synthetic packed documents (geometric mean 1024, uniform ids, EOS), random-init weights",
+            "config": {"model": "200M dense (d1024 L24 16q/4kv h64, SwiGLU 2816, vocab 65536 untied)",
+                       "global_batch": 8 * world, "seq_len": 4096, "micro_batch_per_gpu": 8,
+                       "parallelism": f"dp{world}" + ("" if world == 1 else " (sharded)"),
+                       "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
+                       "l2": "working set >> 126 MB L2 (no flush inserted)",
+                       "layers": a.layers},
+            "clocks": clk,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+            "gpu_launches": launches,
+            "loss": loss_val,
+        }
+        if a.impl == "reference":
+            rec["impl"] = "reference"
+            rec.pop("gpu_launches")
+        print(json.dumps(rec))
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,16 +1,1123 @@
-// FlashAttention forward/backward on tcgen05 (sm_100a).  (kernels being written)
+// FlashAttention forward / backward on tcgen05 (sm_100a).
+//
+// Forward, one CTA per (sequence, head, 128-query tile) work item, persistent over items:
+//   warp 0      TMA producer: Q tile once per item, then K/V tiles of 128 keys into a
+//               two-stage ring (128-byte swizzle, no multicast).
+//   warp 1      MMA issuer: S = Q K^T into tensor memory (M=128, N=128, K=d), then
+//               O_j = P_j V_j into tensor memory (M=128, N=d, K=128) once the softmax
+//               warps have written P_j.
+//   warps 2-5   softmax: thread t owns query row t.  Reads its S row from TMEM, applies
+//               scale and masks (causal / window / sequence end), updates the running max
+//               and sum in base 2, writes P (bf16) into a 128-byte-swizzled shared tile,
+//               and folds O_{j-1} (read from TMEM) into a register accumulator rescaled by
+//               exp2(m_{j-1} - m_j).  At the end: O / l to global, LSE (natural log).
+// Two CTAs fit on one SM for head_dim 64, so one CTA's softmax overlaps the other's MMAs.
+//
+// Backward (dK/dV per 128-key tile, dQ accumulated in fp32 with atomics), per work item
+// (sequence, kv head, key tile), looping over the query tiles and the query heads of the
+// GQA group:
+//   S^T  = K Q^T          (M=128 keys, N=128 queries, K=d)
+//   dP^T = V dO^T         (M=128 keys, N=128 queries, K=d)
+//   P^T  = exp(S^T - lse), dS^T = P^T * (dP^T - Delta)   (registers; thread = key row)
+//   dV  += P^T dO         (M=128, N=d, K=128 queries; A = P^T from smem)
+//   dK  += dS^T Q         (M=128, N=d, K=128 queries; A = dS^T from smem)
+//   dQ  += dS K           (M=128 queries, N=d, K=128 keys; A = dS^T read MN-major)
+// Delta = rowsum(dO * O) comes from a small pre-kernel.
+//
+// Semantics follow the reference (src/myk_llm/ops/flash_attn.py): queries end-aligned to
+// the keys, window (left, right) with -1 unbounded, empty rows output 0 with LSE +inf.
 #include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.h"
 
 namespace mykb {
+
+constexpr int kFaThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct FaParams {
+  int num_seqs;      // batch size, or number of packed documents
+  int heads, kv_heads, group;
+  int q_tiles;       // ceil(max_q / 128)
+  int total_items;
+  int max_q, max_k;
+  const int* cu_q;   // packed offsets (nullptr for batch layout)
+  const int* cu_k;
+  const int* seqused_k;  // per-sequence key count (static caches), or nullptr
+  int left, right;   // window; -1 unbounded
+  float scale_log2;  // softmax scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t out_row_stride;  // elements between consecutive token rows (= heads * d)
+  float* lse;        // (heads, total_q) packed or (batch, heads, max_q)
+  int* status;
+};
+
+struct SeqGeom {
+  int q_start, k_start;  // first row of this sequence in the 2-D (token, head*d) view
+  int len_q, len_k;
+};
+
+__device__ __forceinline__ SeqGeom seq_geom(const FaParams& p, int s) {
+  SeqGeom g;
+  if (p.cu_q != nullptr) {
+    g.q_start = p.cu_q[s];
+    g.len_q = p.cu_q[s + 1] - g.q_start;
+    g.k_start = p.cu_k[s];
+    g.len_k = p.cu_k[s + 1] - g.k_start;
+  } else {
+    g.q_start = s * p.max_q;
+    g.len_q = p.max_q;
+    g.k_start = s * p.max_k;
+    g.len_k = p.max_k;
+  }
+  if (p.seqused_k != nullptr) g.len_k = p.seqused_k[s];
+  return g;
+}
+
+struct Item {
+  int seq, head, qt;
+  SeqGeom g;
+  int q0;        // first query of the tile (within the sequence)
+  int rows;      // valid query rows in the tile
+  int kv_lo, kv_hi;  // key range [lo, hi) the tile needs
+  int n_kv;      // number of 128-key tiles
+};
+
+__device__ __forceinline__ bool decode_item(const FaParams& p, int w, Item& it) {
+  // heavier (later) query tiles first
+  const int per_tile = p.num_seqs * p.heads;
+  it.qt = p.q_tiles - 1 - w / per_tile;
+  const int rem = w % per_tile;
+  it.seq = rem / p.heads;
+  it.head = rem % p.heads;
+  it.g = seq_geom(p, it.seq);
+  it.q0 = it.qt * 128;
+  if (it.q0 >= it.g.len_q) return false;
+  it.rows = min(128, it.g.len_q - it.q0);
+  const int off = it.g.len_k - it.g.len_q;  // end alignment
+  const int qlo = it.q0 + off, qhi = it.q0 + it.rows - 1 + off;
+  int lo = 0, hi = it.g.len_k;
+  if (p.left >= 0) lo = max(lo, qlo - p.left);
+  if (p.right >= 0) hi = min(hi, qhi + p.right + 1);
+  it.kv_lo = lo;
+  it.kv_hi = hi;
+  it.n_kv = hi > lo ? (hi - lo + 127) / 128 : 0;
+  return true;
+}
+
+template <int D>
+struct FaSmem {
+  static constexpr int kTile = 128 * D * 2;  // one 128-row tile of head_dim D (bf16)
+  static constexpr int kQ = 0;
+  static constexpr int kK0 = kQ + kTile;
+  static constexpr int kV0 = kK0 + 2 * kTile;
+  static constexpr int kP = kV0 + 2 * kTile;
+  static constexpr int kBars = kP + 128 * 128 * 2;
+  // The dynamic shared window of a CTA without static shared memory starts 1024-byte
+  // aligned; the kernel checks this (status word) instead of paying 1 KB of slack, which
+  // would keep two head_dim-64 CTAs from sharing an SM.
+  static constexpr int kTotal = kBars + 128;
+};
+
+// Loads a 128-row x D tile: D/64 boxes of {64, 128}, each 16 KB.
+template <int D>
+__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int col0, int row0) {
+#pragma unroll
+  // the token maps are 3-D (batch extent 1), so the 3-D form of the copy is required
+  for (int part = 0; part < D / 64; ++part) tma_load_3d(dst + part * 16384, map, bar, col0 + part * 64, row0, 0);
+}
+
+// K-major operand descriptor for 16-wide K step kk of a tile whose K dimension is split
+// into 64-element atoms 16 KB apart.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// MN-major operand descriptor (atoms of 64 along N, 16 KB apart), K step kk of 16 rows.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + kk * 2048, 16384, 1024);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFaThreads, (D == 64 ? 2 : 1))
+fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  using S = FaSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023) != 0) {
+    if (threadIdx.x == 0) set_status(p.status, kMisaligned);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  uint64_t* kv_full = bars;       // [2]
+  uint64_t* kv_empty = bars + 2;  // [2]
+  uint64_t* q_full = bars + 4;
+  uint64_t* q_empty = bars + 5;
+  uint64_t* s_full = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_full = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  constexpr int kTmemCols = 256;  // S: columns [0,128), O: [128, 128+D)
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int items = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < p.total_items && ok; w += gridDim.x) {
+        Item it;
+        if (!decode_item(p, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_empty, (items & 1) ^ 1, p.status, __LINE__)) break;
+        mbar_arrive_expect_tx(q_full, S::kTile);
+        load_tile<D>(smem + S::kQ, &tmQ, q_full, it.head * D, it.g.q_start + it.q0);
+        const int kvh = it.head / p.group;
+        for (int j = 0; j < it.n_kv; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1, p.status, __LINE__)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[stage], 2 * S::kTile);
+          const int row = it.g.k_start + it.kv_lo + j * 128;
+          load_tile<D>(smem + S::kK0 + stage * S::kTile, &tmK, &kv_full[stage], kvh * D, row);
+          load_tile<D>(smem + S::kV0 + stage * S::kTile, &tmV, &kv_full[stage], kvh * D, row);
+          if (++stage == 2) { stage = 0; phase ^= 1; }
+        }
+        ++items;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16(128, D, false, true);
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int items = 0, ntile = 0;
+      bool ok = true;
+      const uint32_t q_addr = smem_u32(smem + S::kQ);
+      const uint32_t p_addr = smem_u32(smem + S::kP);
+      for (int w = blockIdx.x; w < p.total_items && ok; w += gridDim.x) {
+        Item it;
+        if (!decode_item(p, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_full, items & 1, p.status, __LINE__)) break;
+        tc_fence_after();
+        for (int j = 0; j < it.n_kv && ok; ++j, ++ntile) {
+          // S_j = Q K_j^T
+          if (!mbar_wait(&kv_full[stage], phase, p.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(smem + S::kK0 + stage * S::kTile);
+          const uint32_t v_addr = smem_u32(smem + S::kV0 + stage * S::kTile);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_bf16_ss(tmem, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s, kk > 0);
+          umma_commit(s_full);
+          if (j == it.n_kv - 1) umma_commit(q_empty);
+          // O_j = P_j V_j once the softmax warps have written P_j
+          if (!mbar_wait(p_full, ntile & 1, p.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tmem + 128, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk), idesc_o, kk > 0);
+          umma_commit(o_full);
+          umma_commit(&kv_empty[stage]);
+          if (++stage == 2) { stage = 0; phase ^= 1; }
+        }
+        ++items;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // query row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* p_tile = smem + S::kP;
+    int ntile = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.total_items && ok; w += gridDim.x) {
+      Item it;
+      if (!decode_item(p, w, it)) continue;
+      const int off = it.g.len_k - it.g.len_q;
+      const int qpos = it.q0 + row + off;  // absolute key-space position of this query
+      float acc[D];
+#pragma unroll
+      for (int i = 0; i < D; ++i) acc[i] = 0.f;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j, ++ntile) {
+        if (!mbar_wait_warp(s_full, ntile & 1, p.status, __LINE__)) { ok = false; break; }
+        tc_fence_after();
+        const int k0 = it.kv_lo + j * 128;
+        // A tile needs masking if some key may be invisible to some row of the tile.
+        const bool edge = (k0 + 127 >= it.g.len_k) || (p.right >= 0 && k0 + 127 > it.q0 + off + p.right) ||
+                          (p.left >= 0 && k0 < it.q0 + it.rows - 1 + off - p.left);
+        // pass 1: row max (base-2 scaled scores)
+        float mx = m;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float sv[32];
+          tmem_ld32(tmem + lane_base + c * 32, sv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float sc = sv[i] * p.scale_log2;
+            if (edge) {
+              const int kp = k0 + c * 32 + i;
+              bool vis = kp < it.g.len_k;
+              if (p.right >= 0) vis = vis && kp <= qpos + p.right;
+              if (p.left >= 0) vis = vis && kp >= qpos - p.left;
+              sc = vis ? sc : -INFINITY;
+            }
+            mx = fmaxf(mx, sc);
+          }
+        }
+        const float m_use = (mx == -INFINITY) ? 0.f : mx;
+        const float alpha = exp2f(m - m_use);  // 0 when m == -inf
+        // fold O_{j-1} (its MMA must be complete; that also frees the P tile)
+        if (j > 0) {
+          if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            tmem_ld32(tmem + lane_base + 128 + c * 32, ov);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] += ov[i];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < D; ++i) acc[i] *= alpha;
+        // pass 2: P = exp2(s - m), row sum, bf16 P into the swizzled K-major tile
+        float rs = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float sv[32];
+          tmem_ld32(tmem + lane_base + c * 32, sv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float sc = sv[i] * p.scale_log2;
+            if (edge) {
+              const int kp = k0 + c * 32 + i;
+              bool vis = kp < it.g.len_k;
+              if (p.right >= 0) vis = vis && kp <= qpos + p.right;
+              if (p.left >= 0) vis = vis && kp >= qpos - p.left;
+              sc = vis ? sc : -INFINITY;
+            }
+            sv[i] = exp2f(sc - m_use);
+            rs += sv[i];
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int ch = c * 4 + g;
+            const int atom = ch >> 3, cc = ch & 7;
+            uint32_t w0 = pack_bf16x2(sv[g * 8 + 0], sv[g * 8 + 1]);
+            uint32_t w1 = pack_bf16x2(sv[g * 8 + 2], sv[g * 8 + 3]);
+            uint32_t w2 = pack_bf16x2(sv[g * 8 + 4], sv[g * 8 + 5]);
+            uint32_t w3 = pack_bf16x2(sv[g * 8 + 6], sv[g * 8 + 7]);
+            const uint32_t addr = smem_u32(p_tile) + atom * 16384 + row * 128 + ((cc ^ (row & 7)) * 16);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                         : "memory");
+          }
+        }
+        l = l * alpha + rs;
+        m = mx;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      if (it.n_kv > 0) {
+        if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + lane_base + 128 + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += ov[i];
+        }
+        tc_fence_before();
+      }
+      // epilogue: O / l and LSE
+      if (row < it.rows) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int64_t tok = it.g.q_start + it.q0 + row;
+        __nv_bfloat16* dst = p.out + tok * p.out_row_stride + (int64_t)it.head * D;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 v;
+          v.x = pack_bf16x2(acc[c * 8 + 0] * inv, acc[c * 8 + 1] * inv);
+          v.y = pack_bf16x2(acc[c * 8 + 2] * inv, acc[c * 8 + 3] * inv);
+          v.z = pack_bf16x2(acc[c * 8 + 4] * inv, acc[c * 8 + 5] * inv);
+          v.w = pack_bf16x2(acc[c * 8 + 6] * inv, acc[c * 8 + 7] * inv);
+          reinterpret_cast<uint4*>(dst)[c] = v;
+        }
+        const float lse = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+        if (p.cu_q != nullptr)
+          p.lse[(int64_t)it.head * p.cu_q[p.num_seqs] + tok] = lse;
+        else
+          p.lse[((int64_t)it.seq * p.heads + it.head) * p.max_q + it.q0 + row] = lse;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// -------------------------------------------------------------------------------------
+// host
+// -------------------------------------------------------------------------------------
+static int sm_count() {
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// 2-D (token rows, head*d cols) tensor map of a (.., tokens, heads, d) tensor.
+static CUtensorMap token_map(const torch::Tensor& t) {
+  const int64_t d = t.size(-1), h = t.size(-2);
+  TORCH_CHECK(t.stride(-1) == 1 && t.stride(-2) == d, "attention: heads must be packed (stride d)");
+  const int64_t row_stride = t.stride(-3);
+  int64_t rows = t.size(-3);
+  if (t.dim() == 4) {
+    TORCH_CHECK(t.stride(0) == t.size(1) * row_stride, "attention: batch rows must be uniformly strided");
+    rows *= t.size(0);
+  }
+  return make_tmap_3d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, h * d, rows, 1, row_stride, 0, 64, 128);
+}
+
+template <int D>
+static void launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FaParams& p,
+                       cudaStream_t st) {
+  using S = FaSmem<D>;
+  auto kern = fa_fwd_kernel<D>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    configured = true;
+  }
+  const int per_sm = D == 64 ? 2 : 1;
+  const int grid = std::max(1, std::min(p.total_items, sm_count() * per_sm));
+  kern<<<grid, kFaThreads, S::kTotal, st>>>(tq, tk, tv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> cu_q,
                                   c10::optional<torch::Tensor> cu_k, c10::optional<torch::Tensor> seqused_k,
                                   int64_t max_q, int64_t max_k, double scale, int64_t left, int64_t right) {
-  TORCH_CHECK(false, "fa_fwd: not built yet");
+  c10::cuda::CUDAGuard guard(q.device());
+  const bool packed = cu_q.has_value();
+  const int D = q.size(-1);
+  TORCH_CHECK(D == 64 || D == 128, "fa_fwd: head_dim 64 or 128");
+  FaParams p{};
+  p.heads = q.size(-2);
+  p.kv_heads = k.size(-2);
+  p.group = p.heads / p.kv_heads;
+  p.max_q = max_q;
+  p.max_k = max_k;
+  p.left = left;
+  p.right = right;
+  p.scale_log2 = (float)scale * kLog2e;
+  torch::Tensor out, lse;
+  if (packed) {
+    TORCH_CHECK(cu_k.has_value() && cu_q->scalar_type() == at::kInt, "fa_fwd: int32 cu_seqlens");
+    p.num_seqs = cu_q->numel() - 1;
+    p.cu_q = cu_q->data_ptr<int>();
+    p.cu_k = cu_k->data_ptr<int>();
+    out = torch::empty({q.size(0), p.heads, D}, q.options());
+    lse = torch::empty({p.heads, q.size(0)}, q.options().dtype(at::kFloat));
+  } else {
+    p.num_seqs = q.size(0);
+    TORCH_CHECK(q.size(1) == max_q && k.size(1) == max_k, "fa_fwd: batch layout sizes");
+    out = torch::empty({q.size(0), q.size(1), p.heads, D}, q.options());
+    lse = torch::empty({q.size(0), p.heads, q.size(1)}, q.options().dtype(at::kFloat));
+  }
+  if (seqused_k.has_value()) {
+    TORCH_CHECK(seqused_k->scalar_type() == at::kInt, "fa_fwd: int32 seqused_k");
+    p.seqused_k = seqused_k->data_ptr<int>();
+  }
+  p.q_tiles = (int)((max_q + 127) / 128);
+  p.total_items = p.q_tiles * p.num_seqs * p.heads;
+  p.out = (__nv_bfloat16*)out.data_ptr();
+  p.out_row_stride = (int64_t)p.heads * D;
+  p.lse = lse.data_ptr<float>();
+  p.status = device_status();
+  if (q.numel() == 0 || p.total_items == 0) return {out, lse};
+  CUtensorMap tq = token_map(q), tk = token_map(k), tv = token_map(v);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (D == 64) launch_fwd<64>(tq, tk, tv, p, st);
+  else launch_fwd<128>(tq, tk, tv, p, st);
+  return {out, lse};
 }
+
+// =====================================================================================
+// backward: two kernels, each built from the operand patterns of the forward pass
+// =====================================================================================
+struct FaBwdParams {
+  FaParams f;          // geometry (heads, seqs, window, ...); f.out / f.lse unused
+  int k_tiles;         // ceil(max_k / 128)
+  const float* lse;    // natural-log LSE from the forward
+  const float* delta;  // rowsum(dO * O), same layout as lse
+  __nv_bfloat16* dq;   // (tokens, heads, d)
+  __nv_bfloat16* dk;   // (tokens_k, kv_heads, d)
+  __nv_bfloat16* dv;
+  float scale;         // softmax scale (natural units)
+};
+
+__device__ __forceinline__ int64_t lse_index(const FaParams& f, int seq, int h, int q_start, int qi, int64_t total_q) {
+  return f.cu_q != nullptr ? (int64_t)h * total_q + q_start + qi : ((int64_t)seq * f.heads + h) * f.max_q + qi;
+}
+
+// ------------------------------------------------------------------ dK / dV per key tile
+struct BwdItem {
+  int seq, kvh, kt;
+  SeqGeom g;
+  int k0, keys;
+  int qt_lo, qt_hi;  // query tiles that can see this key tile
+};
+
+__device__ __forceinline__ bool decode_bwd(const FaBwdParams& p, int w, BwdItem& it) {
+  const int per = p.f.num_seqs * p.f.kv_heads;
+  it.kt = w / per;  // early key tiles (most work under a causal mask) first
+  const int rem = w % per;
+  it.seq = rem / p.f.kv_heads;
+  it.kvh = rem % p.f.kv_heads;
+  it.g = seq_geom(p.f, it.seq);
+  it.k0 = it.kt * 128;
+  if (it.k0 >= it.g.len_k || it.g.len_q == 0) return false;
+  it.keys = min(128, it.g.len_k - it.k0);
+  const int off = it.g.len_k - it.g.len_q;
+  int qlo = 0, qhi = it.g.len_q;
+  if (p.f.right >= 0) qlo = max(qlo, it.k0 - p.f.right - off);
+  if (p.f.left >= 0) qhi = min(qhi, it.k0 + it.keys - 1 + p.f.left - off + 1);
+  if (qhi <= qlo) {
+    it.qt_lo = it.qt_hi = 0;
+  } else {
+    it.qt_lo = qlo / 128;
+    it.qt_hi = (qhi + 127) / 128;
+  }
+  return true;
+}
+
+template <int D>
+struct DkvSmem {
+  static constexpr int kStages = D == 64 ? 2 : 1;
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kK = 0;
+  static constexpr int kV = kK + kTile;
+  static constexpr int kQ0 = kV + kTile;
+  static constexpr int kDO0 = kQ0 + kStages * kTile;
+  static constexpr int kP = kDO0 + kStages * kTile;  // P^T (keys x queries)
+  static constexpr int kDS = kP + 128 * 128 * 2;     // dS^T
+  static constexpr int kBars = kDS + 128 * 128 * 2;
+  static constexpr int kTotal = kBars + 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kFaThreads, 1)
+fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const FaBwdParams p) {
+  using S = DkvSmem<D>;
+  constexpr int ST = S::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023) != 0) {
+    if (threadIdx.x == 0) set_status(p.f.status, kMisaligned);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* q_full = bars + 2;   // [ST]
+  uint64_t* q_empty = bars + 4;  // [ST]
+  uint64_t* s_full = bars + 6;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* mm_done = bars + 8;
+  uint64_t* kk_done = bars + 9;
+  uint64_t* dkv_free = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  // TMEM columns: [0,128) S^T, [128,256) dP^T, [256,256+D) dV, [256+D,256+2D) dK
+  constexpr int kCols = 512;
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int group = p.f.group;
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(mm_done, 1);
+    mbar_init(kk_done, 1);
+    mbar_init(dkv_free, 4);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0, items = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        BwdItem it;
+        if (!decode_bwd(p, w, it) || it.qt_hi <= it.qt_lo) continue;
+        if (!mbar_wait(kv_empty, (items & 1) ^ 1, p.f.status, __LINE__)) break;
+        mbar_arrive_expect_tx(kv_full, 2 * S::kTile);
+        load_tile<D>(smem + S::kK, &tmK, kv_full, it.kvh * D, it.g.k_start + it.k0);
+        load_tile<D>(smem + S::kV, &tmV, kv_full, it.kvh * D, it.g.k_start + it.k0);
+        for (int hh = 0; hh < group && ok; ++hh) {
+          const int h = it.kvh * group + hh;
+          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt) {
+            if (!mbar_wait(&q_empty[stage], phase ^ 1, p.f.status, __LINE__)) { ok = false; break; }
+            mbar_arrive_expect_tx(&q_full[stage], 2 * S::kTile);
+            const int row = it.g.q_start + qt * 128;
+            load_tile<D>(smem + S::kQ0 + stage * S::kTile, &tmQ, &q_full[stage], h * D, row);
+            load_tile<D>(smem + S::kDO0 + stage * S::kTile, &tmDO, &q_full[stage], h * D, row);
+            if (++stage == ST) { stage = 0; phase ^= 1; }
+          }
+        }
+        ++items;
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);  // K Q^T, V dO^T
+    constexpr uint32_t idesc_kv = make_idesc_bf16(128, D, false, true);    // P^T dO, dS^T Q
+    if (elect_one()) {
+      int stage = 0, items = 0, n = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint32_t k_addr = smem_u32(smem + S::kK), v_addr = smem_u32(smem + S::kV);
+      const uint32_t p_addr = smem_u32(smem + S::kP), ds_addr = smem_u32(smem + S::kDS);
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        BwdItem it;
+        if (!decode_bwd(p, w, it) || it.qt_hi <= it.qt_lo) continue;
+        if (!mbar_wait(kv_full, items & 1, p.f.status, __LINE__)) break;
+        if (!mbar_wait(dkv_free, (items & 1) ^ 1, p.f.status, __LINE__)) break;
+        tc_fence_after();
+        bool first = true;
+        for (int hh = 0; hh < group && ok; ++hh) {
+          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt, ++n) {
+            if (!mbar_wait(&q_full[stage], phase, p.f.status, __LINE__)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(smem + S::kQ0 + stage * S::kTile);
+            const uint32_t do_addr = smem_u32(smem + S::kDO0 + stage * S::kTile);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_bf16_ss(tmem + kColS, kmajor_desc(k_addr, kk), kmajor_desc(q_addr, kk), idesc_s, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_bf16_ss(tmem + kColDP, kmajor_desc(v_addr, kk), kmajor_desc(do_addr, kk), idesc_s, kk > 0);
+            umma_commit(s_full);
+            if (!mbar_wait(ds_full, n & 1, p.f.status, __LINE__)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ss(tmem + kColDV, kmajor_desc(p_addr, kk), mnmajor_desc(do_addr, kk), idesc_kv,
+                           (!first || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ss(tmem + kColDK, kmajor_desc(ds_addr, kk), mnmajor_desc(q_addr, kk), idesc_kv,
+                           (!first || kk > 0) ? 1u : 0u);
+            umma_commit(mm_done);
+            umma_commit(&q_empty[stage]);
+            first = false;
+            if (++stage == ST) { stage = 0; phase ^= 1; }
+          }
+        }
+        if (!ok) break;
+        umma_commit(kk_done);
+        umma_commit(kv_empty);
+        ++items;
+      }
+    }
+  } else {
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // TMEM lane = key row within the tile
+    const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
+    uint8_t* p_tile = smem + S::kP;
+    uint8_t* ds_tile = smem + S::kDS;
+    const int64_t total_q = p.f.cu_q != nullptr ? (int64_t)p.f.cu_q[p.f.num_seqs] : 0;
+    int n = 0, items = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      BwdItem it;
+      if (!decode_bwd(p, w, it)) continue;
+      const int off = it.g.len_k - it.g.len_q;
+      const int kp = it.k0 + r;
+      if (it.qt_hi > it.qt_lo) {
+        for (int hh = 0; hh < group && ok; ++hh) {
+          const int h = it.kvh * group + hh;
+          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt, ++n) {
+            const int q0 = qt * 128;
+            if (!mbar_wait_warp(s_full, n & 1, p.f.status, __LINE__)) { ok = false; break; }
+            tc_fence_after();
+            // the previous iteration's dV/dK MMAs read P^T / dS^T: wait before overwriting
+            if (n > 0 && !mbar_wait_warp(mm_done, (n - 1) & 1, p.f.status, __LINE__)) { ok = false; break; }
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              float sv[32], dp[32];
+              tmem_ld32(tmem + lane_base + kColS + c * 32, sv);
+              tmem_ld32(tmem + lane_base + kColDP + c * 32, dp);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int qi = q0 + c * 32 + i;
+                const int qpos = qi + off;
+                bool vis = qi < it.g.len_q && kp < it.g.len_k;
+                if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
+                if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
+                float pv = 0.f, dl = 0.f;
+                if (vis) {
+                  const int64_t li = lse_index(p.f, it.seq, h, it.g.q_start, qi, total_q);
+                  pv = exp2f(sv[i] * p.f.scale_log2 - p.lse[li] * kLog2e);
+                  dl = p.delta[li];
+                }
+                sv[i] = pv;
+                dp[i] = pv * (dp[i] - dl) * p.scale;
+              }
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int ch = c * 4 + g;
+                const int atom = ch >> 3, cc = ch & 7;
+                const uint32_t o = atom * 16384 + r * 128 + ((cc ^ (r & 7)) * 16);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p_tile) + o),
+                             "r"(pack_bf16x2(sv[g * 8 + 0], sv[g * 8 + 1])), "r"(pack_bf16x2(sv[g * 8 + 2], sv[g * 8 + 3])),
+                             "r"(pack_bf16x2(sv[g * 8 + 4], sv[g * 8 + 5])), "r"(pack_bf16x2(sv[g * 8 + 6], sv[g * 8 + 7]))
+                             : "memory");
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(ds_tile) + o),
+                             "r"(pack_bf16x2(dp[g * 8 + 0], dp[g * 8 + 1])), "r"(pack_bf16x2(dp[g * 8 + 2], dp[g * 8 + 3])),
+                             "r"(pack_bf16x2(dp[g * 8 + 4], dp[g * 8 + 5])), "r"(pack_bf16x2(dp[g * 8 + 6], dp[g * 8 + 7]))
+                             : "memory");
+              }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+          }
+        }
+        if (!ok) break;
+        if (!mbar_wait_warp(kk_done, items & 1, p.f.status, __LINE__)) break;
+        tc_fence_after();
+        const bool valid = r < it.keys;
+        const int64_t krow = it.g.k_start + it.k0 + r;
+        __nv_bfloat16* dkp = p.dk + (krow * p.f.kv_heads + it.kvh) * D;
+        __nv_bfloat16* dvp = p.dv + (krow * p.f.kv_heads + it.kvh) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float a[32], b[32];
+          tmem_ld32(tmem + lane_base + kColDK + c * 32, a);
+          tmem_ld32(tmem + lane_base + kColDV + c * 32, b);
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 ka, va;
+              ka.x = pack_bf16x2(a[8 * i + 0], a[8 * i + 1]);
+              ka.y = pack_bf16x2(a[8 * i + 2], a[8 * i + 3]);
+              ka.z = pack_bf16x2(a[8 * i + 4], a[8 * i + 5]);
+              ka.w = pack_bf16x2(a[8 * i + 6], a[8 * i + 7]);
+              va.x = pack_bf16x2(b[8 * i + 0], b[8 * i + 1]);
+              va.y = pack_bf16x2(b[8 * i + 2], b[8 * i + 3]);
+              va.z = pack_bf16x2(b[8 * i + 4], b[8 * i + 5]);
+              va.w = pack_bf16x2(b[8 * i + 6], b[8 * i + 7]);
+              reinterpret_cast<uint4*>(dkp + c * 32)[i] = ka;
+              reinterpret_cast<uint4*>(dvp + c * 32)[i] = va;
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dkv_free);
+        ++items;
+      } else if (r < it.keys) {
+        const int64_t krow = it.g.k_start + it.k0 + r;
+        __nv_bfloat16* dkp = p.dk + (krow * p.f.kv_heads + it.kvh) * D;
+        __nv_bfloat16* dvp = p.dv + (krow * p.f.kv_heads + it.kvh) * D;
+        for (int i = 0; i < D / 8; ++i) {
+          reinterpret_cast<uint4*>(dkp)[i] = make_uint4(0, 0, 0, 0);
+          reinterpret_cast<uint4*>(dvp)[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// ------------------------------------------------------------------ dQ per query tile
+// Same item walk and operand patterns as the forward: S = Q K^T and dP = dO V^T
+// (A, B K-major), dS = P (dP - Delta) written as a K-major tile (like P), dQ += dS K
+// (B = K tile MN-major, like V in the forward).
+template <int D>
+struct DqSmem {
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kQ = 0;
+  static constexpr int kDO = kQ + kTile;
+  static constexpr int kK0 = kDO + kTile;
+  static constexpr int kV0 = kK0 + 2 * kTile;
+  static constexpr int kDS = kV0 + 2 * kTile;
+  static constexpr int kBars = kDS + 128 * 128 * 2;
+  static constexpr int kTotal = kBars + 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kFaThreads, 1)
+fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                 const FaBwdParams p) {
+  using S = DqSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023) != 0) {
+    if (threadIdx.x == 0) set_status(p.f.status, kMisaligned);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  uint64_t* kv_full = bars;       // [2]
+  uint64_t* kv_empty = bars + 2;  // [2]
+  uint64_t* q_full = bars + 4;
+  uint64_t* q_empty = bars + 5;
+  uint64_t* s_full = bars + 6;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* mm_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  constexpr int kCols = 512;  // S [0,128), dP [128,256), dQ [256, 256+D)
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+  const FaParams& f = p.f;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(mm_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0, items = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < f.total_items && ok; w += gridDim.x) {
+        Item it;
+        if (!decode_item(f, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_empty, (items & 1) ^ 1, f.status, __LINE__)) break;
+        mbar_arrive_expect_tx(q_full, 2 * S::kTile);
+        load_tile<D>(smem + S::kQ, &tmQ, q_full, it.head * D, it.g.q_start + it.q0);
+        load_tile<D>(smem + S::kDO, &tmDO, q_full, it.head * D, it.g.q_start + it.q0);
+        const int kvh = it.head / f.group;
+        for (int j = 0; j < it.n_kv; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1, f.status, __LINE__)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[stage], 2 * S::kTile);
+          const int row = it.g.k_start + it.kv_lo + j * 128;
+          load_tile<D>(smem + S::kK0 + stage * S::kTile, &tmK, &kv_full[stage], kvh * D, row);
+          load_tile<D>(smem + S::kV0 + stage * S::kTile, &tmV, &kv_full[stage], kvh * D, row);
+          if (++stage == 2) { stage = 0; phase ^= 1; }
+        }
+        ++items;
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_q = make_idesc_bf16(128, D, false, true);
+    if (elect_one()) {
+      int stage = 0, items = 0, ntile = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint32_t q_addr = smem_u32(smem + S::kQ), do_addr = smem_u32(smem + S::kDO);
+      const uint32_t ds_addr = smem_u32(smem + S::kDS);
+      for (int w = blockIdx.x; w < f.total_items && ok; w += gridDim.x) {
+        Item it;
+        if (!decode_item(f, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_full, items & 1, f.status, __LINE__)) break;
+        tc_fence_after();
+        for (int j = 0; j < it.n_kv && ok; ++j, ++ntile) {
+          if (!mbar_wait(&kv_full[stage], phase, f.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(smem + S::kK0 + stage * S::kTile);
+          const uint32_t v_addr = smem_u32(smem + S::kV0 + stage * S::kTile);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_bf16_ss(tmem + kColS, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_bf16_ss(tmem + kColDP, kmajor_desc(do_addr, kk), kmajor_desc(v_addr, kk), idesc_s, kk > 0);
+          umma_commit(s_full);
+          if (j == it.n_kv - 1) umma_commit(q_empty);
+          if (!mbar_wait(ds_full, ntile & 1, f.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16_ss(tmem + kColDQ, kmajor_desc(ds_addr, kk), mnmajor_desc(k_addr, kk), idesc_q,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(mm_done);
+          umma_commit(&kv_empty[stage]);
+          if (++stage == 2) { stage = 0; phase ^= 1; }
+        }
+        ++items;
+      }
+    }
+  } else {
+    const int qw = warp & 3;
+    const int row = qw * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
+    uint8_t* ds_tile = smem + S::kDS;
+    const int64_t total_q = f.cu_q != nullptr ? (int64_t)f.cu_q[f.num_seqs] : 0;
+    int ntile = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < f.total_items && ok; w += gridDim.x) {
+      Item it;
+      if (!decode_item(f, w, it)) continue;
+      const int off = it.g.len_k - it.g.len_q;
+      const int qi = it.q0 + row;
+      const int qpos = qi + off;
+      const bool qvalid = row < it.rows;
+      float lse2 = INFINITY, dl = 0.f;
+      if (qvalid) {
+        const int64_t li = lse_index(f, it.seq, it.head, it.g.q_start, qi, total_q);
+        lse2 = p.lse[li] * kLog2e;
+        dl = p.delta[li];
+      }
+      for (int j = 0; j < it.n_kv; ++j, ++ntile) {
+        if (!mbar_wait_warp(s_full, ntile & 1, f.status, __LINE__)) { ok = false; break; }
+        tc_fence_after();
+        if (j > 0 && !mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) { ok = false; break; }
+        const int k0 = it.kv_lo + j * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float sv[32], dp[32];
+          tmem_ld32(tmem + lane_base + kColS + c * 32, sv);
+          tmem_ld32(tmem + lane_base + kColDP + c * 32, dp);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kp = k0 + c * 32 + i;
+            bool vis = qvalid && kp < it.g.len_k;
+            if (f.right >= 0) vis = vis && kp <= qpos + f.right;
+            if (f.left >= 0) vis = vis && kp >= qpos - f.left;
+            const float pv = vis ? exp2f(sv[i] * f.scale_log2 - lse2) : 0.f;
+            dp[i] = pv * (dp[i] - dl) * p.scale;
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int ch = c * 4 + g;
+            const int atom = ch >> 3, cc = ch & 7;
+            const uint32_t o = atom * 16384 + row * 128 + ((cc ^ (row & 7)) * 16);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(ds_tile) + o),
+                         "r"(pack_bf16x2(dp[g * 8 + 0], dp[g * 8 + 1])), "r"(pack_bf16x2(dp[g * 8 + 2], dp[g * 8 + 3])),
+                         "r"(pack_bf16x2(dp[g * 8 + 4], dp[g * 8 + 5])), "r"(pack_bf16x2(dp[g * 8 + 6], dp[g * 8 + 7]))
+                         : "memory");
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+      }
+      if (!ok) break;
+      const int64_t tok = it.g.q_start + it.q0 + row;
+      __nv_bfloat16* dst = p.dq + (tok * f.heads + it.head) * D;
+      if (it.n_kv > 0) {
+        if (!mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + kColDQ + c * 32, v);
+          if (qvalid) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 o;
+              o.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+              o.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+              o.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+              o.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+              reinterpret_cast<uint4*>(dst + c * 32)[i] = o;
+            }
+          }
+        }
+        tc_fence_before();
+      } else if (qvalid) {
+        for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// Delta[row, h] = sum_d dO * O (fp32), written in the LSE layout.
+__global__ void fa_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                float* __restrict__ delta, int64_t rows, int heads, int D, bool packed,
+                                int max_q) {
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * heads) return;
+  const int64_t tok = gw / heads;
+  const int h = (int)(gw % heads);
+  const __nv_bfloat16* a = dout + gw * D;
+  const __nv_bfloat16* b = out + gw * D;
+  float s = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
+    float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(b + d));
+    s += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
+  if (lane == 0) {
+    if (packed) delta[(int64_t)h * rows + tok] = s;
+    else {
+      const int64_t b_ = tok / max_q, qi = tok % max_q;
+      delta[(b_ * heads + h) * max_q + qi] = s;
+    }
+  }
+}
+
+template <int D>
+static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
+                       const FaBwdParams& p, cudaStream_t st) {
+  {
+    using S = DkvSmem<D>;
+    auto kern = fa_bwd_dkdv_kernel<D>;
+    static bool configured = false;
+    if (!configured) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+      configured = true;
+    }
+    const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
+    kern<<<std::max(1, std::min(total, sm_count())), kFaThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  {
+    using S = DqSmem<D>;
+    auto kern = fa_bwd_dq_kernel<D>;
+    static bool configured = false;
+    if (!configured) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+      configured = true;
+    }
+    kern<<<std::max(1, std::min(p.f.total_items, sm_count())), kFaThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
 std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                   torch::Tensor out, torch::Tensor lse, c10::optional<torch::Tensor> cu_q,
                                   c10::optional<torch::Tensor> cu_k, int64_t max_q, int64_t max_k, double scale,
                                   int64_t left, int64_t right) {
-  TORCH_CHECK(false, "fa_bwd: not built yet");
+  c10::cuda::CUDAGuard guard(q.device());
+  const bool packed = cu_q.has_value();
+  const int D = q.size(-1);
+  FaBwdParams p{};
+  FaParams& f = p.f;
+  f.heads = q.size(-2);
+  f.kv_heads = k.size(-2);
+  f.group = f.heads / f.kv_heads;
+  f.max_q = max_q;
+  f.max_k = max_k;
+  f.left = left;
+  f.right = right;
+  f.scale_log2 = (float)scale * kLog2e;
+  f.status = device_status();
+  if (packed) {
+    f.num_seqs = cu_q->numel() - 1;
+    f.cu_q = cu_q->data_ptr<int>();
+    f.cu_k = cu_k->data_ptr<int>();
+  } else {
+    f.num_seqs = q.size(0);
+  }
+  f.q_tiles = (int)((max_q + 127) / 128);
+  f.total_items = f.q_tiles * f.num_seqs * f.heads;
+  p.k_tiles = (int)((max_k + 127) / 128);
+  p.scale = (float)scale;
+  auto dout_c = dout.contiguous();
+  const int64_t q_rows = packed ? q.size(0) : q.size(0) * q.size(1);
+  const int64_t k_rows = packed ? k.size(0) : k.size(0) * k.size(1);
+  auto dq = torch::empty({q_rows, f.heads, D}, q.options());
+  auto dk = torch::empty({k_rows, f.kv_heads, D}, q.options());
+  auto dv = torch::empty({k_rows, f.kv_heads, D}, q.options());
+  auto delta = torch::empty_like(lse);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (q_rows > 0) {
+    const int64_t warps = q_rows * f.heads;
+    fa_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        (const __nv_bfloat16*)dout_c.data_ptr(), (const __nv_bfloat16*)out.data_ptr(), delta.data_ptr<float>(),
+        q_rows, f.heads, D, packed, (int)max_q);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq = (__nv_bfloat16*)dq.data_ptr();
+  p.dk = (__nv_bfloat16*)dk.data_ptr();
+  p.dv = (__nv_bfloat16*)dv.data_ptr();
+  if (k_rows > 0 && q_rows > 0) {
+    auto dout4 = packed ? dout_c.view({q_rows, f.heads, D}) : dout_c;
+    CUtensorMap tq = token_map(q), tk = token_map(k), tv = token_map(v), tdo = token_map(dout4);
+    if (D == 64) launch_bwd<64>(tq, tk, tv, tdo, p, st);
+    else launch_bwd<128>(tq, tk, tv, tdo, p, st);
+  } else {
+    dq.zero_();
+    dk.zero_();
+    dv.zero_();
+  }
+  if (!packed) {
+    dq = dq.view(q.sizes());
+    dk = dk.view(k.sizes());
+    dv = dv.view(v.sizes());
+  }
+  return {dq, dk, dv};
 }
+
 }  // namespace mykb

@@ -23,11 +23,22 @@ enum StatusCode : int {
   kTimeoutMma = 2,
   kTimeoutEpilogue = 3,
   kTimeoutPeer = 4,
+  kMisaligned = 5,
 };
 
-// ~2^28 polls of try_wait (each already blocks for a hardware-defined interval) is
-// seconds of wall time: far beyond any legitimate wait in these kernels.
-constexpr uint32_t kSpinLimit = 1u << 28;
+// Per-device status word (allocated on first use, see status.cu).
+int* device_status();
+
+// A wait gives up after kWaitNs of wall time (read from %globaltimer): far beyond any
+// legitimate wait in these kernels, short enough that a broken pipeline returns within
+// seconds.  The status word then holds the source line of the wait that gave up.
+constexpr uint64_t kWaitNs = 1000ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void set_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
@@ -92,14 +103,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// Bounded wait for the phase with the given parity to complete.  `code` identifies the
+// call site (the MBAR_WAIT macro passes __LINE__).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && status_failed(status)) return false;
+    if ((i & 255u) == 0) {
+      if (status_failed(status)) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        set_status(status, code);
+        return false;
+      }
+    }
   }
-  set_status(status, code);
-  return false;
+}
+
+// Warp-uniform variant for warps that go on to execute warp-collective `.sync.aligned`
+// instructions (tcgen05.ld/st): every lane returns together, with the same result, so the
+// warp is converged when it leaves the wait.  Must be called by all 32 lanes.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    const bool done = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    if ((i & 255u) == 255u) {
+      const bool failed = status_failed(status);
+      const bool late = globaltimer_ns() - t0 > kWaitNs;
+      if (__any_sync(0xffffffffu, failed || late)) {
+        if (late && (threadIdx.x & 31) == 0) set_status(status, code);
+        __syncwarp();
+        return false;
+      }
+    }
+  }
 }
 
 // -------------------------------------------------------------------------------------

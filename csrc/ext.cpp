@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 
 namespace mykb {
+int64_t take_status();
 // gemm.cu
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
           double alpha, double beta, bool accumulate);
@@ -52,10 +53,25 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
                                          bool per_channel);
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
+// comm.cu
+void peer_barrier(torch::Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch);
+void dp_reduce_sumsq(torch::Tensor grad_ptrs, int64_t rank, int64_t world, torch::Tensor offsets,
+                     torch::Tensor prefix, torch::Tensor partial, int64_t total);
+void dp_adamw_allgather(torch::Tensor param_ptrs, torch::Tensor grad_ptrs, int64_t rank, int64_t world,
+                        torch::Tensor offsets, torch::Tensor prefix, torch::Tensor wd, torch::Tensor lr,
+                        torch::Tensor m, torch::Tensor v, double b1, double b2, double eps, int64_t step,
+                        torch::Tensor partial_ptrs, double extra_sq, double max_norm, torch::Tensor norm_out,
+                        int64_t total);
+void dp_muon_prepare(torch::Tensor grad_ptrs, int64_t rank, int64_t world, torch::Tensor offs, int64_t numel,
+                     torch::Tensor mom, double mu, bool nesterov, torch::Tensor out, torch::Tensor partial_ptrs,
+                     double extra_sq, double max_norm);
+void dp_muon_apply_allgather(torch::Tensor param_ptrs, int64_t rank, int64_t world, torch::Tensor offs,
+                             int64_t numel, double decay, double step_scale, torch::Tensor orth);
 }  // namespace mykb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "myk_llm_b200 sm_100a kernels";
+  m.def("take_status", &mykb::take_status, "read and clear the device status word");
   m.def("gemm", &mykb::gemm, "tcgen05 bf16 GEMM");
   m.def("rmsnorm_fwd", &mykb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &mykb::rmsnorm_bwd);
@@ -78,4 +94,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_fwd", &mykb::gdn_chunk_fwd_entry);
   m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
+  m.def("peer_barrier", &mykb::peer_barrier);
+  m.def("dp_reduce_sumsq", &mykb::dp_reduce_sumsq);
+  m.def("dp_adamw_allgather", &mykb::dp_adamw_allgather);
+  m.def("dp_muon_prepare", &mykb::dp_muon_prepare);
+  m.def("dp_muon_apply_allgather", &mykb::dp_muon_apply_allgather);
 }

@@ -120,7 +120,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kTimeoutProducer)) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, __LINE__)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
@@ -155,11 +155,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         const int buf = local & 1;
-        if (!mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, p.status, kTimeoutMma)) break;
+        if (!mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, p.status, __LINE__)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.status, kTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, p.status, __LINE__)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * S::kStageBytes);
           const uint32_t b_addr = a_addr + S::kABytes;
@@ -188,7 +188,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int b, mt, nt, split;
       unit_coords(p, unit, b, mt, nt, split);
       const int buf = local & 1;
-      if (!mbar_wait(&acc_full[buf], (local >> 1) & 1, p.status, kTimeoutEpilogue)) break;
+      if (!mbar_wait_warp(&acc_full[buf], (local >> 1) & 1, p.status, __LINE__)) break;
       tc_fence_after();
       const int row = mt * kBM + q * 32 + lane;
       const int col0 = nt * BN;
@@ -376,7 +376,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
     p.ldc = c->stride(-2);
     p.c_batch_stride = batched ? c->stride(0) : 0;
   }
-  p.status = nullptr;
+  p.status = device_status();
 
   // Tensor maps (dims innermost first): A/B tiles of 64 elements (128 B) along the
   // contiguous dim; D boxes of 128 bytes x 32 rows.

@@ -41,6 +41,19 @@ class KVCache:
     values: torch.Tensor
 
 
+@dataclass
+class StaticKV:
+    """Preallocated decode cache of one attention layer: keys/values (batch, capacity,
+    kv_heads, head_dim) and the per-row number of valid positions ``seqlens`` (int32, shared
+    by all layers and advanced by the decoder).  New keys/values are written at
+    ``seqlens[b]`` onward without host synchronisation, so a decode step can be captured
+    in a CUDA graph."""
+
+    keys: torch.Tensor
+    values: torch.Tensor
+    seqlens: torch.Tensor
+
+
 class Attention(nn.Module):
     """Grouped-query causal softmax attention, global or sliding-window."""
 
@@ -80,7 +93,11 @@ class Attention(nn.Module):
             q, k = self.rope(q, k, position_ids)
         window = (self.window - 1, 0) if self.window is not None else (-1, -1)
         new_state = KVCache(k, v) if self.shares_kv else None
-        if varlen is not None:
+        if isinstance(state, StaticKV):
+            out = ops.flash_attn_with_kvcache(q, state.keys, state.values, k, v, cache_seqlens=state.seqlens,
+                                              causal=True, window_size=window)
+            new_state = state
+        elif varlen is not None:
             out = ops.flash_attn_varlen_func(
                 q.reshape(-1, self.num_heads, self.head_dim),
                 k.reshape(-1, self.num_kv_heads, self.head_dim),
@@ -122,6 +139,13 @@ class SharedKV(nn.Module):
             k = self.k_norm(k, out_dtype=v.dtype)
         if self.rope is not None:
             k = self.rope.rotate(k, position_ids)
+        if isinstance(state, StaticKV):
+            bsz_, new = k.shape[:2]
+            rows = torch.arange(bsz_, device=k.device)[:, None]
+            cols = state.seqlens.long()[:, None] + torch.arange(new, device=k.device)
+            state.keys[rows, cols] = k
+            state.values[rows, cols] = v
+            return state
         if state is not None:
             k = torch.cat([state.keys, k], dim=1)
             v = torch.cat([state.values, v], dim=1)
@@ -160,7 +184,10 @@ class CrossAttention(nn.Module):
             out = ops.sigmoid_gate(out, ops.linear(x, self.gate_proj.weight))
         return ops.linear(out, self.o_proj.weight), None
 
-    def attend(self, q, kv: KVCache, varlen: Varlen | None):
+    def attend(self, q, kv, varlen: Varlen | None):
+        if isinstance(kv, StaticKV):
+            return ops.flash_attn_with_kvcache(q, kv.keys, kv.values, cache_seqlens=kv.seqlens + q.shape[1],
+                                               causal=True)
         if varlen is None:
             return ops.flash_attn_func(q, kv.keys, kv.values, causal=True)
         return ops.flash_attn_varlen_func(

@@ -53,17 +53,27 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_major: str = "k", b_major: str =
     return out
 
 
+_WEIGHT_EPOCH = [0]
+
+
+def invalidate_weight_cache() -> None:
+    """Called after every optimizer step: parameters updated by kernels (or by peers'
+    stores into symmetric memory) do not bump PyTorch's version counters, so the cached
+    bf16 copies are keyed on this epoch as well."""
+    _WEIGHT_EPOCH[0] += 1
+
+
 def bf16_weight(w: torch.Tensor) -> torch.Tensor:
-    """bf16 view of a (usually fp32 master) weight, cast once per parameter version."""
+    """bf16 copy of a (usually fp32 master) weight, cast once per parameter update."""
     if w.dtype == torch.bfloat16:
         return w if w.is_contiguous() else w.contiguous()
     cache = getattr(w, "_mykb_bf16", None)
-    ver = w._version
-    if cache is not None and cache[0] == ver and cache[1].data_ptr() != 0:
+    key = (w._version, _WEIGHT_EPOCH[0], w.data_ptr())
+    if cache is not None and cache[0] == key:
         return cache[1]
     wb = w.detach().to(torch.bfloat16).contiguous()
     try:
-        w._mykb_bf16 = (ver, wb)
+        w._mykb_bf16 = (key, wb)
     except AttributeError:  # pragma: no cover - tensors that refuse attributes
         pass
     return wb

@@ -1,0 +1,108 @@
+"""Data pipeline on CPU: shard window layout and seam masking, rank slices tiling the
+global batch, exact resume, token-balanced sources, synthetic packed documents, SFT
+windows (the reference's tests/test_data.py strategy with synthetic shards)."""
+
+import numpy as np
+import pytest
+import torch
+
+from myk_llm_b200.data import IGNORE_INDEX, DataConfig, SourceConfig, build_loader
+from myk_llm_b200.data.config import SyntheticDataConfig
+from myk_llm_b200.data.shards import ShardWriter
+
+
+def _write_shards(path, docs=30, eos=0):
+    w = ShardWriter(path, eos_id=eos, tokenizer="none", shard_tokens=500)
+    for d in range(docs):
+        n = 5 + (d * 7) % 40
+        w.add([1000 * (d + 1) + i for i in range(n)])
+    w.close()
+
+
+def _cfg(tmp_path, **kw):
+    base = dict(kind="shards", seq_len=16, micro_batch_size=2,
+                sources=[SourceConfig(name="a", path=str(tmp_path / "a"))], seed=1)
+    base.update(kw)
+    return DataConfig(**base)
+
+
+def test_window_layout_and_seam_masking(tmp_path):
+    _write_shards(tmp_path / "a")
+    ld = build_loader(_cfg(tmp_path))
+    b = ld.next_batch()
+    for r in range(b.input_ids.size(0)):
+        ids, tg = b.input_ids[r], b.targets[r]
+        assert int(b.seqlens[r].sum()) == 16
+        for t in range(15):
+            if tg[t] != IGNORE_INDEX:
+                assert tg[t] == ids[t + 1]
+        # an EOS input (0) never has a supervised target
+        for t in range(16):
+            if ids[t] == 0:
+                assert tg[t] == IGNORE_INDEX
+
+
+def test_rank_slices_tile_global_batch(tmp_path):
+    _write_shards(tmp_path / "a")
+    full = build_loader(_cfg(tmp_path, micro_batch_size=4)).next_batch()
+    r0 = build_loader(_cfg(tmp_path), rank=0, world_size=2).next_batch()
+    r1 = build_loader(_cfg(tmp_path), rank=1, world_size=2).next_batch()
+    assert torch.equal(torch.cat([r0.input_ids, r1.input_ids]), full.input_ids)
+
+
+def test_exact_resume(tmp_path):
+    _write_shards(tmp_path / "a")
+    a = build_loader(_cfg(tmp_path))
+    [a.next_batch() for _ in range(3)]
+    st = a.state_dict()
+    nxt = a.next_batch()
+    b = build_loader(_cfg(tmp_path))
+    b.load_state_dict(st)
+    assert torch.equal(b.next_batch().input_ids, nxt.input_ids)
+
+
+def test_token_balanced_sources(tmp_path):
+    _write_shards(tmp_path / "a")
+    _write_shards(tmp_path / "b", docs=40)
+    cfg = _cfg(tmp_path, sources=[SourceConfig(name="a", path=str(tmp_path / "a"), weight=1.0),
+                                  SourceConfig(name="b", path=str(tmp_path / "b"), weight=3.0)])
+    ld = build_loader(cfg)
+    [ld.next_batch() for _ in range(10)]
+    a, b = ld.cursors[0].consumed, ld.cursors[1].consumed
+    assert abs(b / max(a, 1) - 3.0) < 0.6
+
+
+def test_synthetic_packed_documents():
+    cfg = DataConfig(kind="synthetic", seq_len=512, micro_batch_size=3, seed=0,
+                     synthetic=SyntheticDataConfig(vocab_size=1000, mean_doc_len=64, eos_id=7))
+    ld = build_loader(cfg)
+    b = ld.next_batch()
+    assert b.input_ids.shape == (3, 512)
+    assert all(int(s.sum()) == 512 for s in b.seqlens)
+    assert b.input_ids.max() < 1000
+    # seam targets masked; EOS ids exist between documents
+    assert (b.input_ids == 7).any()
+    assert ((b.input_ids == 7) <= (b.targets == IGNORE_INDEX) | (torch.arange(512) == 511)).all()
+    # deterministic and rank-sliced
+    r1 = build_loader(cfg, rank=1, world_size=2).batch_at(0)
+    full = build_loader(DataConfig(**{**cfg.__dict__, "micro_batch_size": 6})).batch_at(0)
+    assert torch.equal(r1.input_ids, full.input_ids[3:])
+    st = ld.state_dict()
+    ld2 = build_loader(cfg)
+    ld2.load_state_dict(st)
+    assert torch.equal(ld2.next_batch().input_ids, ld.next_batch().input_ids)
+
+
+def test_sft_windows(tmp_path):
+    from myk_llm_b200.data.sft import write_chat_arrays
+
+    toks = list(range(1, 201))
+    mask = [1 if (i // 10) % 2 else 0 for i in range(200)]
+    write_chat_arrays(tmp_path / "c", toks, mask, [(0, 100), (100, 200)])
+    cfg = DataConfig(kind="sft", seq_len=32, micro_batch_size=2, sources=[SourceConfig(name="c", path=str(tmp_path / "c"))])
+    ld = build_loader(cfg)
+    b = ld.next_batch()
+    assert b.input_ids.shape == (2, 32)
+    sup = b.targets != IGNORE_INDEX
+    assert sup.any() and (~sup).any()
+    assert ld.state_dict() == {"kind": "sft", "step": 1}

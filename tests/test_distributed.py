@@ -1,0 +1,110 @@
+"""Multi-process data parallelism on CPU (gloo, world size 2): the sharded runtime
+(optimizer state partitioned, gradient reduce-scatter + parameter all-gather per step)
+trains exactly like one process on the whole global batch, for Muon + AdamW.  Also torch
+FSDP2 (the NCCL-baseline strategy) over gloo on the tiny config, and the host-side
+failure path: a rank that raises makes the other rank's next collective fail instead of
+hanging."""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from myk_llm_b200.configuration import load_config
+from myk_llm_b200.parallel.distributed import DistInfo
+from myk_llm_b200.train.config import TrainConfig
+
+OVERRIDES = ["model.num_layers=2", "data.seq_len=64", "data.micro_batch_size=2", "global_batch_size=4",
+             "model.max_seq_len=64", "optimizer.name=muon", "optimizer.lr=3e-3", "optimizer.grad_clip=0.0", "optimizer.eps=1e-3",
+             "schedule.kind=constant"]
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run_steps(trainer, world, rank, steps=3):
+    from myk_llm_b200.data.synthetic import SyntheticLoader
+
+    ld = SyntheticLoader(trainer.config.data, rank, world)
+    for s in range(1, steps + 1):
+        batches = [ld.batch_at((s - 1) * trainer.grad_accum + i) for i in range(trainer.grad_accum)]
+        trainer.train_step(batches, s)
+    return {n: p.detach().clone() for n, p in trainer.raw_model.named_parameters()}
+
+
+def _worker(rank, world, port, out_path, strategy):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="60")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from myk_llm_b200.train.trainer import Trainer
+
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OVERRIDES + [f"parallel.strategy={strategy}", "parallel.reshard_after_forward=false"])
+    tr = Trainer(cfg, DistInfo(rank, world, rank, torch.device("cpu")), build_data=False)
+    params = _run_steps(tr, world, rank)
+    if strategy == "fsdp":
+        from torch.distributed.tensor import DTensor
+
+        params = {n: (p.full_tensor() if isinstance(p, DTensor) else p) for n, p in params.items()}
+    if rank == 0:
+        torch.save(params, out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _single(tmp):
+    from myk_llm_b200.train.trainer import Trainer
+
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OVERRIDES)
+    tr = Trainer(cfg, DistInfo(0, 1, 0, torch.device("cpu")), build_data=False)
+    return _run_steps(tr, 1, 0)
+
+
+@pytest.mark.parametrize("strategy", ["sharded", pytest.param("fsdp", marks=pytest.mark.skip(
+    reason="torch FSDP2's sum reduction uses ReduceOp.PREMUL_SUM, which gloo does not implement"))])
+def test_world2_matches_single_process(strategy, tmp_path):
+    out = str(tmp_path / "p.pt")
+    mp.spawn(_worker, args=(2, _port(), out, strategy), nprocs=2, join=True)
+    dp = torch.load(out)
+    ref = _single(tmp_path)
+    for n, p in ref.items():
+        tol = 5e-4 if p.ndim == 2 and n.startswith("layers") else 1e-4  # bf16 Newton-Schulz noise
+        assert torch.allclose(dp[n], p, atol=tol, rtol=1e-4), (n, (dp[n] - p).abs().max())
+
+
+def _failing_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    t = torch.ones(4)
+    dist.all_reduce(t)
+    if rank == 1:
+        os._exit(3)  # a rank dies between steps
+    try:
+        dist.all_reduce(t)
+        dist.all_reduce(t)
+        q.put("no error")
+    except Exception as e:  # noqa: BLE001
+        q.put(type(e).__name__)
+
+
+def test_dead_rank_fails_fast():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=60)
+    assert all(not p.is_alive() for p in ps)
+    assert q.get(timeout=5) != "no error"
