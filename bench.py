@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=24, help="(debug only) fewer layers; results are not comparable")
+    ap.add_argument("--ref-compile", default="auto", choices=["auto", "on", "off"],
+                    help="reference arm: its parallel.compile switch (auto: on, falling back to off if Inductor fails)")
     return ap.parse_args()
 
 
@@ -200,7 +202,7 @@ def build_ours(world: int, layers: int):
     return info.device, step, Batch, tr
 
 
-def build_reference(world: int, layers: int):
+def build_reference(world: int, layers: int, compile_blocks: bool = True):
     sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
     import torch
 
@@ -212,7 +214,8 @@ def build_reference(world: int, layers: int):
     from myk_llm.train.objectives import Objective
     from myk_llm.train.optim import build_optimizers
 
-    ov = [o for o in MODEL_OVERRIDES] + [f"global_batch_size={8 * world}", f"model.num_layers={layers}"]
+    ov = [o for o in MODEL_OVERRIDES] + [f"global_batch_size={8 * world}", f"model.num_layers={layers}",
+                                         f"parallel.compile={'true' if compile_blocks else 'false'}"]
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
     torch.manual_seed(cfg.seed)
@@ -247,13 +250,36 @@ def main():
     import torch
     import torch.distributed as dist
 
+    compile_on = None
     if a.impl == "reference":
         ref_dir = os.path.join(ROOT, "baseline", "_ref", "myk_llm")
         if not os.path.isdir(ref_dir):
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
             return
-        device, step, batch_cls, _ = build_reference(world, a.layers)
+        compile_on = a.ref_compile in ("auto", "on")
+        device, step, batch_cls, _ = build_reference(world, a.layers, compile_on)
+        if a.ref_compile == "auto":
+            # try one step with torch.compile; if Inductor cannot build the reference's
+            # kernels on this GPU, rebuild the reference with its compile switch off
+            probe = synthetic_batches(1, 10_000, rank, world, batch_cls)[0]
+            ok = True
+            try:
+                step(probe)
+            except Exception as err:  # noqa: BLE001
+                ok = False
+                print(f"reference with torch.compile failed ({type(err).__name__}); using parallel.compile=false",
+                      file=sys.stderr)
+            if dist.is_initialized():
+                t = torch.tensor([1.0 if ok else 0.0], device=device)
+                dist.all_reduce(t, op=dist.ReduceOp.MIN)
+                ok = bool(t.item() > 0)
+            if not ok:
+                import torch._dynamo
+
+                torch._dynamo.reset()
+                compile_on = False
+                device, step, batch_cls, _ = build_reference(world, a.layers, False)
     else:
         device, step, batch_cls, _ = build_ours(world, a.layers)
 
@@ -263,12 +289,7 @@ def main():
     for _ in range(a.warmup):
         step(next(bi))
     barrier_sync(device)
-    launches = 0
-    if a.impl == "ours":
-        b = next(bi)
-        launches = count_launches(lambda: step(b), "mykb") * a.steps
-    else:
-        next(bi)
+    launch_batch = next(bi)
     barrier_sync(device)
 
     # ---- device-timed loop
@@ -298,6 +319,12 @@ def main():
     barrier_sync(device)
     e2e_s = max_over_ranks(time.perf_counter() - t0, device)
 
+    # kernel launches of this framework in one step (profiled after the timed loops)
+    launches = 0
+    if a.impl == "ours":
+        launches = count_launches(lambda: step(launch_batch), "mykb") * a.steps
+    barrier_sync(device)
+
     tokens_per_step = 8 * 4096 * world
     value = tokens_per_step * a.steps / (dev_ms / 1000.0)
     e2e = tokens_per_step * a.steps / e2e_s
@@ -322,6 +349,7 @@ def main():
         }
         if a.impl == "reference":
             rec["impl"] = "reference"
+            rec["config"]["reference_compile"] = compile_on
             rec.pop("gpu_launches")
         print(json.dumps(rec))
     if dist.is_initialized():

@@ -239,7 +239,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tmem + 128, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk), idesc_o, kk > 0);
+            umma_bf16_ss(tmem + 128, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk), idesc_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);  // O accumulates in TMEM over the KV tiles
           umma_commit(o_full);
           umma_commit(&kv_empty[stage]);
           if (++stage == 2) { stage = 0; phase ^= 1; }
@@ -249,10 +250,17 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     }
   } else {
     // ------------------------------------------------------------------ softmax
+    // One pass per KV tile: the 128 scores of this thread's row are loaded into registers,
+    // the row max taken on the raw scores, and p = exp2(s * scale_log2 - m_ref) computed
+    // with one FFMA + one EX2.  O accumulates in TMEM (PV MMAs with accumulate); the
+    // reference max m_ref only moves when the row max grows by more than 2^8 (lazy
+    // rescale), and then this warp rescales its 32 rows of O in TMEM before the next PV.
     const int q = warp & 3;
     const int row = q * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    uint8_t* p_tile = smem + S::kP;
+    const uint32_t p_base = smem_u32(smem + S::kP) + row * 128;
+    const uint32_t swz = row & 7;
+    constexpr float kRescaleThreshold = 8.f;  // log2 units
     int ntile = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.total_items && ok; w += gridDim.x) {
@@ -260,119 +268,125 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       if (!decode_item(p, w, it)) continue;
       const int off = it.g.len_k - it.g.len_q;
       const int qpos = it.q0 + row + off;  // absolute key-space position of this query
-      float acc[D];
-#pragma unroll
-      for (int i = 0; i < D; ++i) acc[i] = 0.f;
-      float m = -INFINITY, l = 0.f;
+      float m_ref = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j, ++ntile) {
         if (!mbar_wait_warp(s_full, ntile & 1, p.status, __LINE__)) { ok = false; break; }
         tc_fence_after();
         const int k0 = it.kv_lo + j * 128;
-        // A tile needs masking if some key may be invisible to some row of the tile.
         const bool edge = (k0 + 127 >= it.g.len_k) || (p.right >= 0 && k0 + 127 > it.q0 + off + p.right) ||
                           (p.left >= 0 && k0 < it.q0 + it.rows - 1 + off - p.left);
-        // pass 1: row max (base-2 scaled scores)
-        float mx = m;
+        // keys visible to this row form one range [kmin, kmax); as offsets into this tile:
+        const int kmin = (p.left >= 0 ? max(0, qpos - p.left) : 0) - k0;
+        const int kspan = max(0, min(it.g.len_k, p.right >= 0 ? qpos + p.right + 1 : it.g.len_k) - k0 - kmin);
+        // pass 1 over TMEM: row max of the raw scores (masked on edge tiles)
+        float mx = -INFINITY;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          float sv[32];
-          tmem_ld32(tmem + lane_base + c * 32, sv);
+          uint32_t cr[32];
+          tmem_ld32_raw(tmem + lane_base + c * 32, cr);
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            float sc = sv[i] * p.scale_log2;
-            if (edge) {
-              const int kp = k0 + c * 32 + i;
-              bool vis = kp < it.g.len_k;
-              if (p.right >= 0) vis = vis && kp <= qpos + p.right;
-              if (p.left >= 0) vis = vis && kp >= qpos - p.left;
-              sc = vis ? sc : -INFINITY;
-            }
+            float sc = __uint_as_float(cr[i]);
+            if (edge && (unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
             mx = fmaxf(mx, sc);
           }
         }
-        const float m_use = (mx == -INFINITY) ? 0.f : mx;
-        const float alpha = exp2f(m - m_use);  // 0 when m == -inf
-        // fold O_{j-1} (its MMA must be complete; that also frees the P tile)
-        if (j > 0) {
-          if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) { ok = false; break; }
-          tc_fence_after();
+        const float m_tile = mx * p.scale_log2;  // scale > 0: max commutes with it
+        const bool grow = m_tile > m_ref + kRescaleThreshold;
+        bool o_ready = false;
+        if (__any_sync(0xffffffffu, grow)) {
+          // rescale: every lane adopts its current max (a no-op factor for lanes that
+          // did not grow beyond it)
+          const float m_new = fmaxf(m_ref, m_tile);
+          const float alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - m_new);
+          l *= alpha;
+          m_ref = m_new;
+          if (j > 0) {
+            if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) { ok = false; break; }
+            tc_fence_after();
+            o_ready = true;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float ov[32];
-            tmem_ld32(tmem + lane_base + 128 + c * 32, ov);
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tmem_ld32_raw(tmem + lane_base + 128 + c * 32, ov);
+              tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c * 32 + i] += ov[i];
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < D; ++i) acc[i] *= alpha;
-        // pass 2: P = exp2(s - m), row sum, bf16 P into the swizzled K-major tile
-        float rs = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float sv[32];
-          tmem_ld32(tmem + lane_base + c * 32, sv);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float sc = sv[i] * p.scale_log2;
-            if (edge) {
-              const int kp = k0 + c * 32 + i;
-              bool vis = kp < it.g.len_k;
-              if (p.right >= 0) vis = vis && kp <= qpos + p.right;
-              if (p.left >= 0) vis = vis && kp >= qpos - p.left;
-              sc = vis ? sc : -INFINITY;
+              for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+              tmem_st32(tmem + lane_base + 128 + c * 32, ov);
             }
-            sv[i] = exp2f(sc - m_use);
-            rs += sv[i];
-          }
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int ch = c * 4 + g;
-            const int atom = ch >> 3, cc = ch & 7;
-            uint32_t w0 = pack_bf16x2(sv[g * 8 + 0], sv[g * 8 + 1]);
-            uint32_t w1 = pack_bf16x2(sv[g * 8 + 2], sv[g * 8 + 3]);
-            uint32_t w2 = pack_bf16x2(sv[g * 8 + 4], sv[g * 8 + 5]);
-            uint32_t w3 = pack_bf16x2(sv[g * 8 + 6], sv[g * 8 + 7]);
-            const uint32_t addr = smem_u32(p_tile) + atom * 16384 + row * 128 + ((cc ^ (row & 7)) * 16);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
-                         : "memory");
           }
         }
-        l = l * alpha + rs;
-        m = mx;
+        // pass 2 over TMEM: exponentials (overlapping the previous PV MMA), bf16 pairs
+        const float neg = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        float rs = 0.f;
+        uint32_t sr[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t cr[32];
+          tmem_ld32_raw(tmem + lane_base + c * 32, cr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float s0 = __uint_as_float(cr[i]), s1 = __uint_as_float(cr[i + 1]);
+            if (edge) {
+              if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) s0 = -INFINITY;
+              if ((unsigned)(c * 32 + i + 1 - kmin) >= (unsigned)kspan) s1 = -INFINITY;
+            }
+            const float p0 = exp2f(fmaf(s0, p.scale_log2, neg));
+            const float p1 = exp2f(fmaf(s1, p.scale_log2, neg));
+            rs += p0 + p1;
+            sr[(c * 32 + i) >> 1] = pack_bf16x2(p0, p1);
+          }
+        }
+        l += rs;
+        if (j > 0 && !o_ready) {
+          // PV_{j-1} must be done before P is overwritten
+          if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) { ok = false; break; }
+        }
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const uint32_t addr = p_base + (ch >> 3) * 16384 + (((ch & 7) ^ swz) * 16);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(sr[ch * 4 + 0]),
+                       "r"(sr[ch * 4 + 1]), "r"(sr[ch * 4 + 2]), "r"(sr[ch * 4 + 3])
+                       : "memory");
+        }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
       }
       if (!ok) break;
+      // epilogue: O / l and LSE
+      float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t tok = it.g.q_start + it.q0 + row;
+      __nv_bfloat16* dst = p.out + tok * p.out_row_stride + (int64_t)it.head * D;
       if (it.n_kv > 0) {
         if (!mbar_wait_warp(o_full, (ntile - 1) & 1, p.status, __LINE__)) break;
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          float ov[32];
-          tmem_ld32(tmem + lane_base + 128 + c * 32, ov);
+          uint32_t ov[32];
+          tmem_ld32_raw(tmem + lane_base + 128 + c * 32, ov);
+          tmem_wait_ld();
+          if (row < it.rows) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += ov[i];
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(ov[8 * i + 0]) * inv, __uint_as_float(ov[8 * i + 1]) * inv);
+              v.y = pack_bf16x2(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv);
+              v.z = pack_bf16x2(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv);
+              v.w = pack_bf16x2(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv);
+              reinterpret_cast<uint4*>(dst + c * 32)[i] = v;
+            }
+          }
         }
         tc_fence_before();
+      } else if (row < it.rows) {
+        for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
       }
-      // epilogue: O / l and LSE
       if (row < it.rows) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        const int64_t tok = it.g.q_start + it.q0 + row;
-        __nv_bfloat16* dst = p.out + tok * p.out_row_stride + (int64_t)it.head * D;
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          uint4 v;
-          v.x = pack_bf16x2(acc[c * 8 + 0] * inv, acc[c * 8 + 1] * inv);
-          v.y = pack_bf16x2(acc[c * 8 + 2] * inv, acc[c * 8 + 3] * inv);
-          v.z = pack_bf16x2(acc[c * 8 + 4] * inv, acc[c * 8 + 5] * inv);
-          v.w = pack_bf16x2(acc[c * 8 + 6] * inv, acc[c * 8 + 7] * inv);
-          reinterpret_cast<uint4*>(dst)[c] = v;
-        }
-        const float lse = l > 0.f ? (m + log2f(l)) * kLn2 : INFINITY;
+        const float lse = l > 0.f ? (m_ref + log2f(l)) * kLn2 : INFINITY;
         if (p.cu_q != nullptr)
           p.lse[(int64_t)it.head * p.cu_q[p.num_seqs] + tok] = lse;
         else
@@ -534,7 +548,9 @@ struct DkvSmem {
   static constexpr int kDO0 = kQ0 + kStages * kTile;
   static constexpr int kP = kDO0 + kStages * kTile;  // P^T (keys x queries)
   static constexpr int kDS = kP + 128 * 128 * 2;     // dS^T
-  static constexpr int kBars = kDS + 128 * 128 * 2;
+  static constexpr int kLse = kDS + 128 * 128 * 2;   // [stages][128] base-2 LSE of the query tile
+  static constexpr int kDelta = kLse + kStages * 512;  // [stages][128] Delta of the query tile
+  static constexpr int kBars = kDelta + kStages * 512;
   static constexpr int kTotal = kBars + 256;
 };
 
@@ -589,30 +605,54 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
 
   if (warp == 0) {
-    if (elect_one()) {
-      int stage = 0, items = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        BwdItem it;
-        if (!decode_bwd(p, w, it) || it.qt_hi <= it.qt_lo) continue;
-        if (!mbar_wait(kv_empty, (items & 1) ^ 1, p.f.status, __LINE__)) break;
+    // Producer warp: lane 0 issues the TMA copies; all lanes stage the query tile's LSE
+    // (pre-scaled to base 2) and Delta into shared memory before lane 0 arrives.
+    float* s_lse = reinterpret_cast<float*>(smem + S::kLse);
+    float* s_delta = reinterpret_cast<float*>(smem + S::kDelta);
+    const int64_t total_q = p.f.cu_q != nullptr ? (int64_t)p.f.cu_q[p.f.num_seqs] : 0;
+    int stage = 0, items = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      BwdItem it;
+      if (!decode_bwd(p, w, it) || it.qt_hi <= it.qt_lo) continue;
+      bool good = true;
+      if (lane == 0) good = mbar_wait(kv_empty, (items & 1) ^ 1, p.f.status, __LINE__);
+      if (!__shfl_sync(0xffffffffu, good, 0)) break;
+      if (lane == 0) {
         mbar_arrive_expect_tx(kv_full, 2 * S::kTile);
         load_tile<D>(smem + S::kK, &tmK, kv_full, it.kvh * D, it.g.k_start + it.k0);
         load_tile<D>(smem + S::kV, &tmV, kv_full, it.kvh * D, it.g.k_start + it.k0);
-        for (int hh = 0; hh < group && ok; ++hh) {
-          const int h = it.kvh * group + hh;
-          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt) {
-            if (!mbar_wait(&q_empty[stage], phase ^ 1, p.f.status, __LINE__)) { ok = false; break; }
+      }
+      for (int hh = 0; hh < group && ok; ++hh) {
+        const int h = it.kvh * group + hh;
+        for (int qt = it.qt_lo; qt < it.qt_hi; ++qt) {
+          if (lane == 0) good = mbar_wait(&q_empty[stage], phase ^ 1, p.f.status, __LINE__);
+          if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = lane * 4 + i;
+            const int qi = qt * 128 + c;
+            float l2 = INFINITY, dl = 0.f;
+            if (qi < it.g.len_q) {
+              const int64_t li = lse_index(p.f, it.seq, h, it.g.q_start, qi, total_q);
+              l2 = p.lse[li] * kLog2e;
+              dl = p.delta[li];
+            }
+            s_lse[stage * 128 + c] = l2;
+            s_delta[stage * 128 + c] = dl;
+          }
+          __syncwarp();
+          if (lane == 0) {
             mbar_arrive_expect_tx(&q_full[stage], 2 * S::kTile);
             const int row = it.g.q_start + qt * 128;
             load_tile<D>(smem + S::kQ0 + stage * S::kTile, &tmQ, &q_full[stage], h * D, row);
             load_tile<D>(smem + S::kDO0 + stage * S::kTile, &tmDO, &q_full[stage], h * D, row);
-            if (++stage == ST) { stage = 0; phase ^= 1; }
           }
+          if (++stage == ST) { stage = 0; phase ^= 1; }
         }
-        ++items;
       }
+      ++items;
     }
   } else if (warp == 1) {
     constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);  // K Q^T, V dO^T
@@ -688,26 +728,40 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tc_fence_after();
             // the previous iteration's dV/dK MMAs read P^T / dS^T: wait before overwriting
             if (n > 0 && !mbar_wait_warp(mm_done, (n - 1) & 1, p.f.status, __LINE__)) { ok = false; break; }
+            const int st_idx = n % ST;
+            const float* c_lse = reinterpret_cast<const float*>(smem + S::kLse) + st_idx * 128;
+            const float* c_delta = reinterpret_cast<const float*>(smem + S::kDelta) + st_idx * 128;
+            // every (key, query) pair of the tile visible: no per-element masks
+            const bool edge = (it.k0 + 127 >= it.g.len_k) || (q0 + 127 >= it.g.len_q) ||
+                              (p.f.right >= 0 && it.k0 + 127 > q0 + off + p.f.right) ||
+                              (p.f.left >= 0 && it.k0 < q0 + 127 + off - p.f.left);
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
               float sv[32], dp[32];
-              tmem_ld32(tmem + lane_base + kColS + c * 32, sv);
-              tmem_ld32(tmem + lane_base + kColDP + c * 32, dp);
+              tmem_ld32_raw(tmem + lane_base + kColS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv));
+              tmem_ld32_raw(tmem + lane_base + kColDP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(dp));
+              tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int qi = q0 + c * 32 + i;
-                const int qpos = qi + off;
-                bool vis = qi < it.g.len_q && kp < it.g.len_k;
-                if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
-                if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
-                float pv = 0.f, dl = 0.f;
-                if (vis) {
-                  const int64_t li = lse_index(p.f, it.seq, h, it.g.q_start, qi, total_q);
-                  pv = exp2f(sv[i] * p.f.scale_log2 - p.lse[li] * kLog2e);
-                  dl = p.delta[li];
+              for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 l4 = reinterpret_cast<const float4*>(c_lse + c * 32)[i4];
+                const float4 d4 = reinterpret_cast<const float4*>(c_delta + c * 32)[i4];
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+                const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int i = i4 * 4 + e;
+                  float pv = exp2f(fmaf(sv[i], p.f.scale_log2, -lv[e]));
+                  if (edge) {
+                    const int qi = q0 + c * 32 + i;
+                    const int qpos = qi + off;
+                    bool vis = qi < it.g.len_q && kp < it.g.len_k;
+                    if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
+                    if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
+                    pv = vis ? pv : 0.f;
+                  }
+                  sv[i] = pv;
+                  dp[i] = (pv * p.scale) * (dp[i] - dv[e]);
                 }
-                sv[i] = pv;
-                dp[i] = pv * (dp[i] - dl) * p.scale;
               }
 #pragma unroll
               for (int g = 0; g < 4; ++g) {
@@ -920,6 +974,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       const int qi = it.q0 + row;
       const int qpos = qi + off;
       const bool qvalid = row < it.rows;
+      const bool qvalid_tile = it.rows == 128;
       float lse2 = INFINITY, dl = 0.f;
       if (qvalid) {
         const int64_t li = lse_index(f, it.seq, it.head, it.g.q_start, qi, total_q);
@@ -931,19 +986,24 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         tc_fence_after();
         if (j > 0 && !mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) { ok = false; break; }
         const int k0 = it.kv_lo + j * 128;
+        const bool edge = !qvalid_tile || (k0 + 127 >= it.g.len_k) ||
+                          (f.right >= 0 && k0 + 127 > it.q0 + off + f.right) ||
+                          (f.left >= 0 && k0 < it.q0 + it.rows - 1 + off - f.left);
+        const int kmin = (f.left >= 0 ? max(0, qpos - f.left) : 0) - k0;
+        const int kspan = qvalid ? max(0, min(it.g.len_k, f.right >= 0 ? qpos + f.right + 1 : it.g.len_k) - k0 - kmin)
+                                 : 0;
+        const float ps = p.scale;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float sv[32], dp[32];
-          tmem_ld32(tmem + lane_base + kColS + c * 32, sv);
-          tmem_ld32(tmem + lane_base + kColDP + c * 32, dp);
+          tmem_ld32_raw(tmem + lane_base + kColS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_ld32_raw(tmem + lane_base + kColDP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(dp));
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int kp = k0 + c * 32 + i;
-            bool vis = qvalid && kp < it.g.len_k;
-            if (f.right >= 0) vis = vis && kp <= qpos + f.right;
-            if (f.left >= 0) vis = vis && kp >= qpos - f.left;
-            const float pv = vis ? exp2f(sv[i] * f.scale_log2 - lse2) : 0.f;
-            dp[i] = pv * (dp[i] - dl) * p.scale;
+            float pv = exp2f(fmaf(sv[i], f.scale_log2, -lse2));
+            if (edge && (unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) pv = 0.f;
+            dp[i] = (pv * ps) * (dp[i] - dl);
           }
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
