@@ -1181,3 +1181,119 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
 }
 
 }  // namespace mykb
+
+// =====================================================================================
+// C entry point without device allocation (declared in noalloc.h).  No counterpart in
+// the reference project: see noalloc.h for who needs it and the contract.
+// =====================================================================================
+#include "noalloc.h"
+
+namespace mykb {
+namespace {
+// Working memory of mykb_flash_attn_bwd_noalloc: Delta (one float per query row and head)
+// and the status word its bounded waits write.  Every GPU that loads this library holds
+// these (4 MB + 4 B) until the process exits.
+static __device__ __align__(256) float g_noalloc_delta[MYKB_NOALLOC_MAX_ROWS_X_HEADS];
+static __device__ __align__(256) int g_noalloc_status[64];
+
+thread_local char g_noalloc_err[256] = {0};
+
+struct NoallocScratch {
+  float* delta = nullptr;
+  int* status = nullptr;
+};
+
+// Host-side stand-ins of the arrays are not device addresses: look the addresses up once
+// per device (with that device current) and pass them to the kernels.
+NoallocScratch noalloc_scratch(int dev, cudaError_t* err) {
+  static NoallocScratch cache[64];
+  static bool ready[64] = {false};
+  *err = cudaSuccess;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return {};
+  }
+  if (!ready[dev]) {
+    NoallocScratch s;
+    *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.delta), g_noalloc_delta);
+    if (*err != cudaSuccess) return {};
+    *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_noalloc_status);
+    if (*err != cudaSuccess) return {};
+    cache[dev] = s;
+    ready[dev] = true;
+  }
+  return cache[dev];
+}
+
+int noalloc_fail(int code, const char* msg) {
+  snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s", msg);
+  return code;
+}
+
+CUtensorMap raw_token_map(const void* base, int64_t rows, int heads, int d) {
+  return make_tmap_3d(const_cast<void*>(base), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (int64_t)heads * d, rows, 1,
+                      (int64_t)heads * d, 0, 64, 128);
+}
+}  // namespace
+}  // namespace mykb
+
+extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, const void* k, const void* v,
+                                           const void* out, const float* lse, void* dq, void* dk, void* dv,
+                                           const int* cu_seqlens, int num_seqs, int rows_q, int rows_k, int max_q,
+                                           int max_k, int heads, int kv_heads, int head_dim, float softmax_scale,
+                                           int window_left, int window_right, cudaStream_t stream) {
+  using namespace mykb;
+  g_noalloc_err[0] = 0;
+  if (head_dim != 64 && head_dim != 128) return noalloc_fail(1, "head_dim must be 64 or 128");
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads) return noalloc_fail(2, "heads must be a multiple of kv_heads");
+  if ((int64_t)rows_q * heads > MYKB_NOALLOC_MAX_ROWS_X_HEADS)
+    return noalloc_fail(3, "rows_q * heads exceeds MYKB_NOALLOC_MAX_ROWS_X_HEADS (the built-in scratch size)");
+  if (rows_q <= 0 || rows_k <= 0 || num_seqs <= 0) return noalloc_fail(4, "empty problem");
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return noalloc_fail(5, cudaGetErrorString(err));
+  NoallocScratch sc = noalloc_scratch(dev, &err);
+  if (err != cudaSuccess) return noalloc_fail(6, cudaGetErrorString(err));
+  try {
+    FaBwdParams p{};
+    FaParams& f = p.f;
+    f.heads = heads;
+    f.kv_heads = kv_heads;
+    f.group = heads / kv_heads;
+    f.max_q = max_q;
+    f.max_k = max_k;
+    f.left = window_left;
+    f.right = window_right;
+    f.scale_log2 = softmax_scale * kLog2e;
+    f.status = sc.status;
+    f.num_seqs = num_seqs;
+    f.cu_q = cu_seqlens;
+    f.cu_k = cu_seqlens;
+    f.q_tiles = (max_q + 127) / 128;
+    f.total_items = f.q_tiles * f.num_seqs * f.heads;
+    p.k_tiles = (max_k + 127) / 128;
+    p.scale = softmax_scale;
+    p.lse = lse;
+    p.delta = sc.delta;
+    p.dq = static_cast<__nv_bfloat16*>(dq);
+    p.dk = static_cast<__nv_bfloat16*>(dk);
+    p.dv = static_cast<__nv_bfloat16*>(dv);
+    const int64_t warps = (int64_t)rows_q * heads;
+    fa_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), sc.delta, rows_q, heads,
+        head_dim, cu_seqlens != nullptr, max_q);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return noalloc_fail(7, cudaGetErrorString(err));
+    CUtensorMap tq = raw_token_map(q, rows_q, heads, head_dim), tk = raw_token_map(k, rows_k, kv_heads, head_dim),
+                tv = raw_token_map(v, rows_k, kv_heads, head_dim), tdo = raw_token_map(dout, rows_q, heads, head_dim);
+    if (head_dim == 64) launch_bwd<64>(tq, tk, tv, tdo, p, stream);
+    else launch_bwd<128>(tq, tk, tv, tdo, p, stream);
+  } catch (const std::exception& e) {
+    return noalloc_fail(8, e.what());
+  }
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return noalloc_fail(7, cudaGetErrorString(err));
+  return 0;
+}
+
+extern "C" const char* mykb_noalloc_last_error(void) { return mykb::g_noalloc_err; }
