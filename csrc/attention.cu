@@ -2,7 +2,7 @@
 //
 // Forward, one CTA per (sequence, head, 128-query tile) work item, persistent over items:
 //   warp 0      TMA producer: Q tile once per item, then K/V tiles of 128 keys into a
-//               two-stage ring (128-byte swizzle, no multicast).
+//               two-stage ring (128-byte swizzle, plain per-CTA copies).
 //   warp 1      MMA issuer: S = Q K^T into tensor memory (M=128, N=128, K=d), then
 //               O_j = P_j V_j into tensor memory (M=128, N=d, K=128) once the softmax
 //               warps have written P_j.

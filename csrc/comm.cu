@@ -20,7 +20,7 @@
 // so the reduce-scatter is fused with the norm, and the all-gather with the optimizer
 // update; no NCCL call is on this path.  Cross-GPU waits spin on flags with an acquire
 // load and give up after kWaitNs, recording the call site in the status word.  Plain
-// peer loads/stores only: no TMA, no multicast.
+// peer loads/stores only, no TMA.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>

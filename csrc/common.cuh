@@ -141,7 +141,7 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
 }
 
 // -------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this code base)
+// TMA: plain per-CTA tile copies of this GPU's memory
 // -------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

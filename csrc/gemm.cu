@@ -17,8 +17,8 @@
 //               TMA store (or a TMA reduce-add into fp32 D in accumulate mode, which also
 //               carries split-K partial sums).
 //
-// Two accumulators let the epilogue of tile i overlap the main loop of tile i+1.  No TMA
-// multicast is used: this kernel may read operands that other ranks wrote into this GPU's
+// Two accumulators let the epilogue of tile i overlap the main loop of tile i+1.  Every TMA
+// load is a plain per-CTA copy: this kernel may read operands that other ranks wrote into this GPU's
 // memory, never another GPU's memory.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>

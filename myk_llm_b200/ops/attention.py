@@ -9,7 +9,7 @@ static cache at ``cache_seqlens[b]`` before attending (no host sync, so it can b
 in a CUDA graph).
 
 The kernels (``csrc/attention.cu``) keep S and the P·V product in tensor memory, stage
-K/V tiles with TMA (no multicast) and write the output plus a natural-log LSE.  The
+K/V tiles with TMA (plain loads of local memory) and write the output plus a natural-log LSE.  The
 backward pass computes dK/dV per key tile and accumulates dQ in fp32.
 """
 

@@ -1,0 +1,74 @@
+"""The sharded data-parallel runtime on 2 GPUs (peer-memory reduce-scatter fused with the
+norm, AdamW / Muon fused with the parameter all-gather) trains like one GPU on the whole
+global batch.  Skipped with fewer than 2 GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+OV = ["model.num_layers=2", "data.seq_len=256", "data.micro_batch_size=2", "global_batch_size=4",
+      "model.max_seq_len=256", "optimizer.name=muon", "optimizer.lr=3e-3", "optimizer.grad_clip=0.0",
+      "optimizer.eps=1e-3", "schedule.kind=constant"]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _steps(tr, world, rank, n=3):
+    from myk_llm_b200.data.synthetic import SyntheticLoader
+
+    ld = SyntheticLoader(tr.config.data, rank, world)
+    for s in range(1, n + 1):
+        tr.train_step([ld.batch_at((s - 1) * tr.grad_accum + i) for i in range(tr.grad_accum)], s)
+    torch.cuda.synchronize()
+    return {k: v.detach().float().cpu().clone() for k, v in tr.raw_model.named_parameters()}
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
+    from myk_llm_b200.configuration import load_config
+    from myk_llm_b200.ops import ext
+    from myk_llm_b200.parallel.distributed import init_distributed
+    from myk_llm_b200.train.config import TrainConfig
+    from myk_llm_b200.train.trainer import Trainer
+
+    info = init_distributed()
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OV + ["parallel.strategy=sharded"])
+    tr = Trainer(cfg, info, build_data=False)
+    params = _steps(tr, world, rank)
+    status = ext().take_status()
+    if rank == 0:
+        torch.save({"params": params, "status": status}, out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_two_gpus_matches_one(tmp_path):
+    out = str(tmp_path / "p.pt")
+    mp.spawn(_worker, args=(2, _port(), out), nprocs=2, join=True)
+    got = torch.load(out)
+    assert got["status"] == 0
+    from myk_llm_b200.configuration import load_config
+    from myk_llm_b200.parallel.distributed import DistInfo
+    from myk_llm_b200.train.config import TrainConfig
+    from myk_llm_b200.train.trainer import Trainer
+
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OV)
+    tr = Trainer(cfg, DistInfo(0, 1, 0, torch.device("cuda", 0)), build_data=False)
+    ref = _steps(tr, 1, 0)
+    for n, p in ref.items():
+        d = (got["params"][n] - p).abs().max().item()
+        assert d < 3e-3, (n, d)
