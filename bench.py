@@ -37,15 +37,32 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 BASELINE_TOKS = None  # BASELINE.md publishes no number for this metric/config on any GPU
 
-MODEL_OVERRIDES = [
-    "model.vocab_size=65536", "model.hidden_size=1024", "model.num_layers=24", "model.layer_pattern=G",
-    "model.max_seq_len=4096", "model.tie_embeddings=false", "model.norm_eps=1e-6",
-    "model.attention.num_heads=16", "model.attention.num_kv_heads=4", "model.attention.head_dim=64",
-    "model.attention.global_rope=all", "model.attention.rope_theta_global=10000.0",
-    "model.ffn.multiplier=2.75", "model.ffn.multiple_of=256",
-    "objective.z_loss=1e-4", "optimizer.name=muon", "optimizer.muon_ns_steps=5",
-    "data.seq_len=4096", "data.micro_batch_size=8",
-]
+_COMMON = ["objective.z_loss=1e-4", "optimizer.name=muon", "optimizer.muon_ns_steps=5"]
+
+# name -> (config overrides, seq_len, micro-batch per GPU, description for the JSON line)
+MODELS = {
+    "200m": ([
+        "model.vocab_size=65536", "model.hidden_size=1024", "model.num_layers=24", "model.layer_pattern=G",
+        "model.max_seq_len=4096", "model.tie_embeddings=false", "model.norm_eps=1e-6",
+        "model.attention.num_heads=16", "model.attention.num_kv_heads=4", "model.attention.head_dim=64",
+        "model.attention.global_rope=all", "model.attention.rope_theta_global=10000.0",
+        "model.ffn.multiplier=2.75", "model.ffn.multiple_of=256",
+        "data.seq_len=4096", "data.micro_batch_size=8"] + _COMMON, 4096, 8,
+        "200M dense (d1024 L24 16q/4kv h64, SwiGLU 2816, vocab 65536 untied)"),
+    "1b-hybrid": ([
+        "model.vocab_size=65536", "model.hidden_size=2048", "model.num_layers=24", "model.layer_pattern=DDDG",
+        "model.max_seq_len=8192", "model.tie_embeddings=false", "model.norm_eps=1e-6",
+        "model.attention.num_heads=16", "model.attention.num_kv_heads=4", "model.attention.head_dim=128",
+        "model.attention.global_rope=all", "model.attention.rope_theta_global=10000.0",
+        "model.deltanet.kind=gdn", "model.deltanet.num_heads=16", "model.deltanet.head_dim=128",
+        "model.deltanet.expand_v=1.0", "model.deltanet.conv_size=4", "model.deltanet.use_short_conv=true",
+        "model.deltanet.use_gate=true",
+        "model.ngram.orders=[2,3]", "model.ngram.num_buckets=1048576", "model.ngram.dim=2048",
+        "model.ffn.multiplier=2.75", "model.ffn.multiple_of=256",
+        "data.seq_len=8192", "data.micro_batch_size=2"] + _COMMON, 8192, 2,
+        "1B hybrid (d2048 L24 DDDG: 18 GDN 16x128 + 6 GQA 16q/4kv h128, SwiGLU 5632, 2/3-gram 2^20 x 2048, "
+        "vocab 65536 untied)"),
+}
 
 
 def parse():
@@ -54,6 +71,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="200m", choices=sorted(MODELS), help="benchmark config (default: 200m)")
     ap.add_argument("--layers", type=int, default=24, help="(debug only) fewer layers; results are not comparable")
     ap.add_argument("--ref-compile", default="auto", choices=["auto", "on", "off"],
                     help="reference arm: its parallel.compile switch (auto: on, falling back to off if Inductor fails)")
@@ -126,13 +144,14 @@ def dist_env():
     return rank, world, local
 
 
-def synthetic_batches(n: int, step0: int, rank: int, world: int, batch_cls, seed: int = 0):
+def synthetic_batches(n: int, step0: int, rank: int, world: int, batch_cls, seq_len: int, micro: int,
+                      seed: int = 0):
     """The synthetic packed-document micro-batches of steps [step0, step0+n) for this rank,
     built on the host and pinned."""
     from myk_llm_b200.data.config import DataConfig, SyntheticDataConfig
     from myk_llm_b200.data.synthetic import SyntheticLoader
 
-    cfg = DataConfig(kind="synthetic", seq_len=4096, micro_batch_size=8, seed=seed,
+    cfg = DataConfig(kind="synthetic", seq_len=seq_len, micro_batch_size=micro, seed=seed,
                      synthetic=SyntheticDataConfig(vocab_size=65536, mean_doc_len=1024, eos_id=0))
     ld = SyntheticLoader(cfg, rank, world)
     out = []
@@ -179,7 +198,7 @@ def count_launches(step_fn, prefix: str) -> int:
 
 
 # ----------------------------------------------------------------------------- arms
-def build_ours(world: int, layers: int):
+def build_ours(world: int, layers: int, model: str):
     import torch
 
     from myk_llm_b200.configuration import apply_overrides, from_dict
@@ -188,7 +207,8 @@ def build_ours(world: int, layers: int):
     from myk_llm_b200.train.config import TrainConfig
     from myk_llm_b200.train.trainer import Trainer
 
-    ov = MODEL_OVERRIDES + [f"global_batch_size={8 * world}", "steps=1000", "schedule.warmup_ratio=0.0",
+    ov, _, micro, _ = MODELS[model]
+    ov = ov + [f"global_batch_size={micro * world}", "steps=1000", "schedule.warmup_ratio=0.0",
                             "data.kind=synthetic", "logging.tensorboard=false", f"model.num_layers={layers}"]
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
@@ -202,7 +222,7 @@ def build_ours(world: int, layers: int):
     return info.device, step, Batch, tr
 
 
-def build_reference(world: int, layers: int, compile_blocks: bool = True):
+def build_reference(world: int, layers: int, model: str, compile_blocks: bool = True):
     sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
     import torch
 
@@ -214,7 +234,8 @@ def build_reference(world: int, layers: int, compile_blocks: bool = True):
     from myk_llm.train.objectives import Objective
     from myk_llm.train.optim import build_optimizers
 
-    ov = [o for o in MODEL_OVERRIDES] + [f"global_batch_size={8 * world}", f"model.num_layers={layers}",
+    ov, _, micro, _ = MODELS[model]
+    ov = list(ov) + [f"global_batch_size={micro * world}", f"model.num_layers={layers}",
                                          f"parallel.compile={'true' if compile_blocks else 'false'}"]
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
@@ -250,6 +271,7 @@ def main():
     import torch
     import torch.distributed as dist
 
+    _, seq_len, micro, model_desc = MODELS[a.model]
     compile_on = None
     if a.impl == "reference":
         ref_dir = os.path.join(ROOT, "baseline", "_ref", "myk_llm")
@@ -258,11 +280,11 @@ def main():
                 print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
             return
         compile_on = a.ref_compile in ("auto", "on")
-        device, step, batch_cls, _ = build_reference(world, a.layers, compile_on)
+        device, step, batch_cls, _ = build_reference(world, a.layers, a.model, compile_on)
         if a.ref_compile == "auto":
             # try one step with torch.compile; if Inductor cannot build the reference's
             # kernels on this GPU, rebuild the reference with its compile switch off
-            probe = synthetic_batches(1, 10_000, rank, world, batch_cls)[0]
+            probe = synthetic_batches(1, 10_000, rank, world, batch_cls, seq_len, micro)[0]
             ok = True
             try:
                 step(probe)
@@ -279,12 +301,12 @@ def main():
 
                 torch._dynamo.reset()
                 compile_on = False
-                device, step, batch_cls, _ = build_reference(world, a.layers, False)
+                device, step, batch_cls, _ = build_reference(world, a.layers, a.model, False)
     else:
-        device, step, batch_cls, _ = build_ours(world, a.layers)
+        device, step, batch_cls, _ = build_ours(world, a.layers, a.model)
 
     total_steps = a.warmup + 2 * a.steps + 1
-    batches = synthetic_batches(total_steps, 0, rank, world, batch_cls)
+    batches = synthetic_batches(total_steps, 0, rank, world, batch_cls, seq_len, micro)
     bi = iter(batches)
     for _ in range(a.warmup):
         step(next(bi))
@@ -325,10 +347,10 @@ def main():
         launches = count_launches(lambda: step(launch_batch), "mykb") * a.steps
     barrier_sync(device)
 
-    tokens_per_step = 8 * 4096 * world
+    tokens_per_step = micro * seq_len * world
     value = tokens_per_step * a.steps / (dev_ms / 1000.0)
     e2e = tokens_per_step * a.steps / e2e_s
-    h2d = timed[0].input_ids.numel() * 8 * 2 + sum(s.numel() * 4 for s in (timed[0].seqlens or []))
+    h2d = timed[0].input_ids.numel() * 8 * 2 + sum(x.numel() * 4 for x in (timed[0].seqlens or []))
     if rank == 0:
         rec = {
             "metric": "train tokens/sec at 1/2/4/8 B200 (200M, 1B hybrid); MTP decode tokens/sec",
@@ -336,8 +358,8 @@ def main():
             "ms_per_step": dev_ms / a.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
             "data": "synthetic packed documents (geometric mean 1024, uniform ids, EOS), random-init weights",
-            "config": {"model": "200M dense (d1024 L24 16q/4kv h64, SwiGLU 2816, vocab 65536 untied)",
-                       "global_batch": 8 * world, "seq_len": 4096, "micro_batch_per_gpu": 8,
+            "config": {"model": model_desc,
+                       "global_batch": micro * world, "seq_len": seq_len, "micro_batch_per_gpu": micro,
                        "parallelism": f"dp{world}" + ("" if world == 1 else " (sharded)"),
                        "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
                        "l2": "working set >> 126 MB L2 (no flush inserted)",

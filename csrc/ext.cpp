@@ -50,7 +50,7 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
 std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                          torch::Tensor g, torch::Tensor beta, c10::optional<torch::Tensor> init,
                                          c10::optional<torch::Tensor> cu, std::vector<torch::Tensor> saved,
-                                         bool per_channel);
+                                         c10::optional<torch::Tensor> dfinal, bool per_channel);
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
 // comm.cu

@@ -11,9 +11,9 @@ CUDA kernels (``csrc/gdn.cu``):
 
 * ``conv1d_fwd/bwd``: depthwise causal conv + SiLU over the packed q/k/v, resetting at
   document boundaries;
-* ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64) with the state kept in fp32;
-  each CTA owns one (sequence, head) and walks its chunks, doing the intra-chunk WY
-  transform and the inter-chunk state products on tensor cores;
+* ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64, head dims 128) with the state
+  kept in fp32; each CTA owns one (sequence, head, half of the value columns) and walks
+  its chunks; the algorithm is stated in :mod:`myk_llm_b200.ops.gdn_chunk`;
 * ``gdn_recurrent``: token-by-token decode over a state cache.
 """
 
@@ -63,24 +63,51 @@ def causal_conv1d(x, weight, cu_seqlens=None, initial_state=None, return_final_s
 
 class _DeltaRule(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, init, cu, per_channel):
-        o, final, saved = ext().gdn_chunk_fwd(q, k, v, g, beta, init, cu, bool(per_channel))
-        ctx.save_for_backward(q, k, v, g, beta, init, cu, *saved)
-        ctx.per_channel = per_channel
+    def forward(ctx, q, k, v, g, beta, init, cu):
+        o, final, states = ext().gdn_chunk_fwd(q, k, v, g, beta, init, cu, False)
+        ctx.save_for_backward(q, k, v, g, beta, init, cu, states)
         return o, final
 
     @staticmethod
     def backward(ctx, do, dfinal):
-        q, k, v, g, beta, init, cu, *saved = ctx.saved_tensors
-        dq, dk, dv, dg, db = ext().gdn_chunk_bwd(do.contiguous(), q, k, v, g, beta, init, cu, list(saved),
-                                                 bool(ctx.per_channel))
-        return dq, dk, dv, dg, db, None, None, None
+        q, k, v, g, beta, init, cu, states = ctx.saved_tensors
+        dq, dk, dv, dg, db, dinit = ext().gdn_chunk_bwd(do.contiguous(), q, k, v, g, beta, init, cu, [states],
+                                                        dfinal, False)
+        return dq, dk, dv, dg, db, (dinit if ctx.needs_input_grad[5] else None), None
+
+
+def _chunked_torch(q, k, v, g, beta, initial_state, cu_seqlens, per_channel):
+    """Differentiable chunked statement (``gdn_chunk.chunk_fwd``) per sequence and head;
+    the path for per-channel (KDA) decay on the GPU."""
+    from .gdn_chunk import chunk_fwd
+
+    bsz, t_len, heads, dk = q.shape
+    qf = F.normalize(q.float(), dim=-1, eps=1e-6) * dk ** -0.5
+    kf = F.normalize(k.float(), dim=-1, eps=1e-6)
+    spans = ([(0, a, b) for a, b in zip(cu_seqlens.tolist()[:-1], cu_seqlens.tolist()[1:])] if cu_seqlens is not None
+             else [(b, 0, t_len) for b in range(bsz)])
+    rows, finals = [], []
+    for i, (b, a, e) in enumerate(spans):
+        outs, fins = [], []
+        for h in range(heads):
+            s0 = initial_state[i, h] if initial_state is not None else None
+            o, s, _ = chunk_fwd(qf[b, a:e, h], kf[b, a:e, h], v[b, a:e, h], g[b, a:e, h], beta[b, a:e, h], s0,
+                                per_channel=per_channel)
+            outs.append(o)
+            fins.append(s)
+        rows.append(torch.stack(outs, 1))
+        finals.append(torch.stack(fins))
+    if cu_seqlens is not None:
+        o = torch.cat(rows, 0)[None]
+    else:
+        o = torch.stack(rows)
+    return o.to(v.dtype), torch.stack(finals)
 
 
 def gated_delta_rule(q, k, v, g, beta, initial_state=None, cu_seqlens=None, cu_seqlens_cpu=None,
                      output_final_state=False, per_channel_decay=False):
     """o_t = S_t^T (q_t / sqrt(dk)) with S_t = exp(g_t) S_{t-1} + k_t (beta_t (v_t - S^T k_t))^T,
-    q/k L2-normalised.  Returns (o (B, T, H, dv), final state or None)."""
+    q/k L2-normalised.  Returns (o (B, T, H, dv), final state (N, H, dk, dv) fp32 or None)."""
     if not q.is_cuda:
         o, fin = ref.delta_rule_ref(q, k, v, g, beta, initial_state=initial_state, cu_seqlens=cu_seqlens,
                                     per_channel_decay=per_channel_decay)
@@ -89,6 +116,10 @@ def gated_delta_rule(q, k, v, g, beta, initial_state=None, cu_seqlens=None, cu_s
         o, fin = ext().gdn_recurrent(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(),
                                      beta.contiguous(), initial_state, bool(per_channel_decay))
         return o, (fin if output_final_state else None)
+    if per_channel_decay or q.shape[-1] != 128 or v.shape[-1] != 128 or v.shape[-2] != q.shape[-2]:
+        o, fin = _chunked_torch(q, k, v, g, beta, initial_state, cu_seqlens, per_channel_decay)
+        return o, (fin if output_final_state else None)
+    cu = cu_seqlens.int() if cu_seqlens is not None else None
     o, fin = _DeltaRule.apply(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
-                              beta.float().contiguous(), initial_state, cu_seqlens, per_channel_decay)
+                              beta.float().contiguous(), initial_state, cu)
     return o, (fin if output_final_state else None)
