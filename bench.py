@@ -279,6 +279,15 @@ def main():
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
             return
+        if a.model == "1b-hybrid":
+            try:
+                import fla.modules.causal_conv1d  # noqa: F401  (the reference's Gated DeltaNet imports it)
+            except ImportError as err:
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      f"the reference's Gated DeltaNet needs fla.modules.causal_conv1d; the installed "
+                                      f"flash-linear-attention has none ({err})"}))
+                return
         compile_on = a.ref_compile in ("auto", "on")
         device, step, batch_cls, _ = build_reference(world, a.layers, a.model, compile_on)
         if a.ref_compile == "auto":

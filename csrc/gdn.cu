@@ -1,20 +1,32 @@
-// Gated DeltaNet kernels (sm_100a): short causal convolution + SiLU, the chunked gated
-// delta rule forward / backward (chunk 64), the token recurrence for decoding, and the
-// q/k L2-norm backward.
+// Gated DeltaNet kernels (sm_100a): the chunked gated delta rule forward / backward
+// (chunk 64, head dims 128), the token recurrence for decoding, and the short causal
+// convolution + SiLU with its backward.
 //
-// The chunk algorithm is the one stated in myk_llm_b200/ops/gdn_chunk.py:
-//   E_ts = exp(gamma_t - gamma_s), A = strictly_lower(diag(beta) (E * K K^T)),
-//   U = (I + A)^{-1} diag(beta) (V - Gamma K S0)   (forward substitution),
-//   O = Gamma Q S0 + lower_incl(E * Q K^T) U,
-//   S_C = exp(gamma_C) S0 + K^T diag(exp(gamma_C - gamma)) U,
-// and its hand-derived reverse (backward substitution for dY = (I + A)^{-T} dU).
+// Per chunk of 64 tokens (myk_llm_b200/ops/gdn_chunk.py states the same algebra and is
+// the oracle), with k^ / q^ the L2-normalised key / query (q^ also scaled by dk^-1/2),
+// gamma the cumulative log decay inside the chunk, E_ts = exp(gamma_t - gamma_s):
 //
-// One CTA owns one (sequence, head, half of the value dimension) and walks the sequence's
-// chunks in order (forward) or in reverse (backward), keeping its half of the state in
-// shared memory.  Splitting the value dimension in halves is exact: U, O, S, dV and dS
-// are column-separable, and every quantity that mixes value columns (dq, dk, dbeta,
-// dgamma, dA, dP) is a sum of per-half parts, accumulated with fp32 atomics.  The chunk
-// products run on fp32 CUDA cores with 4x4 / 8x4 register tiles from shared memory.
+//   A  = strictly_lower(diag(beta) (E * K^ K^T)),   T = (I + A)^-1
+//   W  = T diag(beta e^gamma) K^,                   U~ = T diag(beta) V
+//   U  = U~ - W S0                                  (S0: state entering the chunk)
+//   O  = diag(e^gamma) Q^ S0 + lower_incl(E * Q^ K^T) U
+//   S1 = e^{gamma_C} S0 + (F * K^)^T U,             F_s = exp(gamma_C - gamma_s)
+//
+// Everything except the S0 -> S1 recurrence is independent per chunk, so the work is
+// split into chunk-parallel kernels (one CTA per (chunk, head)) around a thin sequential
+// kernel (one CTA per (sequence, head, 32 value columns)) that carries the state:
+//
+//   forward:  gdn_prep   (K^K^T, blocked triangular inverse, W, U~)
+//             gdn_state  (U = U~ - W S0, S1 = ...; saves S0 per chunk, U)
+//             gdn_out    (P = lower(E * Q^K^T), O)
+//   backward: gdn_dstate (dS at every chunk end, reverse recurrence)
+//             gdn_grad   (dq, dk, dv, dg, dbeta of every chunk, l2-norm backward)
+//
+// All chunk products run on the tensor cores through warp-level bf16 MMAs (fp32
+// accumulate) fed by ldmatrix from padded shared-memory tiles; the state and every
+// reduction stay in fp32.  A 64-row chunk maps onto 16-row MMA fragments without the
+// 128-row minimum of a TMEM accumulator tile, and the sequential kernel keeps its state
+// slice in registers between chunks.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -22,22 +34,30 @@
 #include "common.cuh"
 
 namespace mykb {
+namespace gdnk {
 
-constexpr int kC = 64;        // chunk length
-constexpr int kDK = 128;      // head_k_dim supported by the chunk kernels
-constexpr int kDVH = 64;      // value columns per CTA (half of head_v_dim 128)
-constexpr int kGdnThreads = 256;
+typedef __nv_bfloat16 bf16;
+constexpr int C = 64;      // chunk length
+constexpr int DK = 128;    // head_k_dim
+constexpr int DV = 128;    // head_v_dim
+constexpr int LD = 136;    // padded row stride (elements) of 128-wide bf16 tiles
+constexpr int LDS = 72;    // padded row stride of 64-wide bf16 tiles
+constexpr int LDP = 40;    // padded row stride of 32-wide bf16 tiles
+constexpr int LDF = 65;    // row stride of 64-wide fp32 tiles
+constexpr int PARTS = 4;   // value-column slices of the sequential kernels
+constexpr int PW = DV / PARTS;  // 32 columns per slice
+constexpr int NT = 256;    // threads of every chunk kernel (8 warps)
 
-struct GdnGeom {
-  const int* cu;          // packed document offsets or nullptr (batch layout)
-  const int* chunk_off;   // first global chunk index of every sequence
-  int num_seqs, heads, seq_len;  // seq_len: batch layout length
-  int64_t row_q;          // elements between token rows of q/k (heads * dk)
-  int64_t row_v;          // heads * dv
-  int dv;                 // full head_v_dim
+struct Geo {
+  const int* cu;         // packed document offsets or nullptr (batch layout)
+  const int* chunk_off;  // first global chunk of every sequence; [num_seqs] = total
+  const int* order;      // sequences by decreasing length (sequential kernels start long ones first)
+  int num_seqs, heads, seq_len;
+  int64_t rows;          // token rows (batch x time); per-token scalars are head-major [heads][rows]
+  int64_t row_q, row_v;  // elements between consecutive token rows of q/k and of v
 };
 
-__device__ __forceinline__ void seq_span(const GdnGeom& g, int s, int& t0, int& len) {
+__device__ __forceinline__ void seq_span(const Geo& g, int s, int& t0, int& len) {
   if (g.cu != nullptr) {
     t0 = g.cu[s];
     len = g.cu[s + 1] - t0;
@@ -47,611 +67,9 @@ __device__ __forceinline__ void seq_span(const GdnGeom& g, int s, int& t0, int& 
   }
 }
 
-// out[4][4] += A(rows r0..r0+3, k) * B(k, cols c0..c0+3) over k in [0, K)
-// A element (r, k) at A[r * sar + k * sak]; B element (k, c) at B[k * sbk + c * sbc].
-template <int R, int CC>
-__device__ __forceinline__ void mm_acc(float (&out)[R][CC], const float* A, int sar, int sak, const float* B, int sbk,
-                                       int sbc, int r0, int c0, int K) {
-#pragma unroll 4
-  for (int k = 0; k < K; ++k) {
-    float a[R], b[CC];
-#pragma unroll
-    for (int i = 0; i < R; ++i) a[i] = A[(r0 + i) * sar + k * sak];
-#pragma unroll
-    for (int j = 0; j < CC; ++j) b[j] = B[k * sbk + (c0 + j) * sbc];
-#pragma unroll
-    for (int i = 0; i < R; ++i)
-#pragma unroll
-      for (int j = 0; j < CC; ++j) out[i][j] = fmaf(a[i], b[j], out[i][j]);
-  }
-}
-
-template <int R, int CC>
-__device__ __forceinline__ void zero(float (&o)[R][CC]) {
-#pragma unroll
-  for (int i = 0; i < R; ++i)
-#pragma unroll
-    for (int j = 0; j < CC; ++j) o[i][j] = 0.f;
-}
-
-// Shared-memory plan of the forward (floats)
-struct FwdSm {
-  static constexpr int S = 0;                        // [dk][64]
-  static constexpr int K = S + kDK * kDVH;           // [C][dk]
-  static constexpr int Q = K + kC * kDK;             // [C][dk]
-  static constexpr int V = Q + kC * kDK;             // [C][64]  V -> W -> U
-  static constexpr int A = V + kC * kDVH;            // [C][C]   A, then P
-  static constexpr int KS = A + kC * kC;             // [C][64]  K S0, then Q S0
-  static constexpr int GAM = KS + kC * kDVH;         // [C] gamma, [C] beta, [C] exp(gamma)
-  static constexpr int TOTAL = GAM + 3 * kC;
-};
-
-// Loads a chunk: L2-normalised k and q (q also scaled), this half of v, gamma (cumulative
-// log decay), beta.  One warp normalises 8 rows.
-__device__ __forceinline__ void load_chunk(const GdnGeom& g, float* sm_k, float* sm_q, float* sm_v, float* gam,
-                                           float* bet, float* eg, const __nv_bfloat16* q, const __nv_bfloat16* k,
-                                           const __nv_bfloat16* v, const float* gg, const float* bb, int t0, int a,
-                                           int n, int h, int half, float qscale) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int r = warp; r < kC; r += kGdnThreads / 32) {
-    float kv[4], qv[4];
-    if (r < n) {
-      const int64_t row = (int64_t)(t0 + a + r);
-      const __nv_bfloat16* kp = k + row * g.row_q + (int64_t)h * kDK + lane * 4;
-      const __nv_bfloat16* qp = q + row * g.row_q + (int64_t)h * kDK + lane * 4;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kv[i] = __bfloat162float(kp[i]);
-        qv[i] = __bfloat162float(qp[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) kv[i] = qv[i] = 0.f;
-    }
-    float sk = kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3];
-    float sq = qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      sk += __shfl_xor_sync(0xffffffff, sk, o);
-      sq += __shfl_xor_sync(0xffffffff, sq, o);
-    }
-    const float ik = 1.f / fmaxf(sqrtf(sk), 1e-6f), iq = qscale / fmaxf(sqrtf(sq), 1e-6f);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sm_k[r * kDK + lane * 4 + i] = kv[i] * ik;
-      sm_q[r * kDK + lane * 4 + i] = qv[i] * iq;
-    }
-    // v half: 64 columns, 2 per lane
-    for (int c = lane; c < kDVH; c += 32) {
-      float val = 0.f;
-      if (r < n) val = __bfloat162float(v[(int64_t)(t0 + a + r) * g.row_v + (int64_t)h * g.dv + half * kDVH + c]);
-      sm_v[r * kDVH + c] = val;
-    }
-  }
-  if (warp == 0) {
-    // gamma = inclusive cumsum of g over the chunk (2 elements per lane), padded with 0
-    float x0 = (2 * lane < n) ? gg[(int64_t)(t0 + a + 2 * lane) * g.heads + h] : 0.f;
-    float x1 = (2 * lane + 1 < n) ? gg[(int64_t)(t0 + a + 2 * lane + 1) * g.heads + h] : 0.f;
-    float s = x0 + x1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      float y = __shfl_up_sync(0xffffffff, s, o);
-      if (lane >= o) s += y;
-    }
-    const float c1 = s, c0 = s - x1;
-    gam[2 * lane] = c0;
-    gam[2 * lane + 1] = c1;
-    eg[2 * lane] = __expf(c0);
-    eg[2 * lane + 1] = __expf(c1);
-    bet[2 * lane] = (2 * lane < n) ? bb[(int64_t)(t0 + a + 2 * lane) * g.heads + h] : 0.f;
-    bet[2 * lane + 1] = (2 * lane + 1 < n) ? bb[(int64_t)(t0 + a + 2 * lane + 1) * g.heads + h] : 0.f;
-  }
-}
-
-__global__ void __launch_bounds__(kGdnThreads, 1)
-gdn_chunk_fwd_kernel(GdnGeom g, const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                     const __nv_bfloat16* __restrict__ v, const float* __restrict__ gg, const float* __restrict__ bb,
-                     const float* __restrict__ init, __nv_bfloat16* __restrict__ out, float* __restrict__ states,
-                     float* __restrict__ final_state, float qscale) {
-  extern __shared__ float sm[];
-  float* S = sm + FwdSm::S;
-  float* Ks = sm + FwdSm::K;
-  float* Qs = sm + FwdSm::Q;
-  float* Vs = sm + FwdSm::V;
-  float* As = sm + FwdSm::A;
-  float* KS = sm + FwdSm::KS;
-  float* gam = sm + FwdSm::GAM;
-  float* bet = gam + kC;
-  float* eg = bet + kC;
-  const int seq = blockIdx.x / (g.heads * 2);
-  const int h = (blockIdx.x / 2) % g.heads;
-  const int half = blockIdx.x % 2;
-  const int tid = threadIdx.x;
-  int t0, len;
-  seq_span(g, seq, t0, len);
-  // initial state (this half)
-  for (int i = tid; i < kDK * kDVH; i += kGdnThreads) {
-    const int r = i / kDVH, c = i % kDVH;
-    S[i] = init != nullptr ? init[(((int64_t)seq * g.heads + h) * kDK + r) * g.dv + half * kDVH + c] : 0.f;
-  }
-  __syncthreads();
-  const int ty = tid / 16, tx = tid % 16;
-  int chunk = g.chunk_off[seq];
-  for (int a = 0; a < len; a += kC, ++chunk) {
-    const int n = min(kC, len - a);
-    // save the chunk's starting state for the backward
-    float* st = states + (((int64_t)chunk * g.heads + h) * kDK) * g.dv + half * kDVH;
-    for (int i = tid; i < kDK * kDVH; i += kGdnThreads) st[(int64_t)(i / kDVH) * g.dv + i % kDVH] = S[i];
-    load_chunk(g, Ks, Qs, Vs, gam, bet, eg, q, k, v, gg, bb, t0, a, n, h, half, qscale);
-    __syncthreads();
-    // KS = K S0  (C x 64), W = V - e^gamma * KS  (in place in Vs)
-    {
-      float o[4][4];
-      zero(o);
-      mm_acc<4, 4>(o, Ks, kDK, 1, S, kDVH, 1, ty * 4, tx * 4, kDK);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = ty * 4 + i, c = tx * 4 + j;
-          Vs[r * kDVH + c] = Vs[r * kDVH + c] - eg[r] * o[i][j];
-        }
-      // A = strictly_lower(beta_t * E_ts * k_t . k_s)
-      float kk[4][4];
-      zero(kk);
-      mm_acc<4, 4>(kk, Ks, kDK, 1, Ks, 1, kDK, ty * 4, tx * 4, kDK);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = ty * 4 + i, s = tx * 4 + j;
-          As[t * kC + s] = (s < t) ? bet[t] * __expf(gam[t] - gam[s]) * kk[i][j] : 0.f;
-        }
-    }
-    __syncthreads();
-    // U = (I + A)^{-1} diag(beta) W: forward substitution, row by row; thread c of 64
-    // owns value column c (4 threads per column split the inner sum).
-    {
-      const int c = tid % kDVH, part = tid / kDVH;  // 4 parts
-      for (int t = 0; t < kC; ++t) {
-        float acc = 0.f;
-        for (int s = part; s < t; s += 4) acc = fmaf(As[t * kC + s], Vs[s * kDVH + c], acc);
-        // combine the 4 parts through shared scratch (KS area row t)
-        KS[part * kDVH + c] = acc;
-        __syncthreads();
-        if (part == 0) {
-          const float tot = KS[c] + KS[kDVH + c] + KS[2 * kDVH + c] + KS[3 * kDVH + c];
-          Vs[t * kDVH + c] = bet[t] * Vs[t * kDVH + c] - tot;
-        }
-        __syncthreads();
-      }
-    }
-    // P = lower_incl(E * Q K^T) into As (A is no longer needed)
-    {
-      float qk[4][4];
-      zero(qk);
-      mm_acc<4, 4>(qk, Qs, kDK, 1, Ks, 1, kDK, ty * 4, tx * 4, kDK);
-      __syncthreads();
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = ty * 4 + i, s = tx * 4 + j;
-          As[t * kC + s] = (s <= t) ? __expf(gam[t] - gam[s]) * qk[i][j] : 0.f;
-        }
-    }
-    __syncthreads();
-    // O = e^gamma * (Q S0) + P U
-    {
-      float o[4][4], pu[4][4];
-      zero(o);
-      zero(pu);
-      mm_acc<4, 4>(o, Qs, kDK, 1, S, kDVH, 1, ty * 4, tx * 4, kDK);
-      mm_acc<4, 4>(pu, As, kC, 1, Vs, kDVH, 1, ty * 4, tx * 4, kC);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = ty * 4 + i;
-        if (r < n) {
-          __nv_bfloat16* op = out + (int64_t)(t0 + a + r) * g.row_v + (int64_t)h * g.dv + half * kDVH + tx * 4;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) op[j] = __float2bfloat16(eg[r] * o[i][j] + pu[i][j]);
-        }
-      }
-    }
-    __syncthreads();
-    // S <- e^{gamma_C} S + K^T (F * U),  F_s = exp(gamma_C - gamma_s)  (dk x 64; 8x4 tiles)
-    {
-      const float gl = gam[n - 1];
-      // scale U rows by F in place (U in Vs is no longer needed unscaled)
-      for (int i = tid; i < kC * kDVH; i += kGdnThreads) {
-        const int s = i / kDVH;
-        Vs[i] = (s < n) ? Vs[i] * __expf(gl - gam[s]) : 0.f;
-      }
-      __syncthreads();
-      float o[8][4];
-      zero(o);
-      mm_acc<8, 4>(o, Ks, 1, kDK, Vs, kDVH, 1, ty * 8, tx * 4, n);
-      const float egl = __expf(gl);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = ty * 8 + i, c = tx * 4 + j;
-          S[r * kDVH + c] = egl * S[r * kDVH + c] + o[i][j];
-        }
-    }
-    __syncthreads();
-  }
-  if (final_state != nullptr) {
-    for (int i = tid; i < kDK * kDVH; i += kGdnThreads) {
-      const int r = i / kDVH, c = i % kDVH;
-      final_state[(((int64_t)seq * g.heads + h) * kDK + r) * g.dv + half * kDVH + c] = S[i];
-    }
-  }
-}
-
-// ------------------------------------------------------------------------------ backward
-struct BwdSm {
-  static constexpr int S0 = 0;                      // [dk][64] chunk start state
-  static constexpr int DS = S0 + kDK * kDVH;        // [dk][64] carried dS
-  static constexpr int K = DS + kDK * kDVH;         // [C][dk]
-  static constexpr int Q = K + kC * kDK;            // [C][dk]
-  static constexpr int R = Q + kC * kDK;            // [C][64]  V - Gamma K S0
-  static constexpr int U = R + kC * kDVH;           // [C][64]
-  static constexpr int DU = U + kC * kDVH;          // [C][64]  dU -> dY
-  static constexpr int DO = DU + kC * kDVH;         // [C][64]
-  static constexpr int A = DO + kC * kDVH;          // [C][C]
-  static constexpr int P = A + kC * kC;             // [C][C]   P, then dP-derived
-  static constexpr int GAM = P + kC * kC;           // gamma, beta, e^gamma, dgam, dbeta
-  static constexpr int TOTAL = GAM + 5 * kC;
-};
-
-__global__ void __launch_bounds__(kGdnThreads, 1)
-gdn_chunk_bwd_kernel(GdnGeom g, const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                     const __nv_bfloat16* __restrict__ v, const float* __restrict__ gg, const float* __restrict__ bb,
-                     const float* __restrict__ states, const __nv_bfloat16* __restrict__ dout,
-                     const float* __restrict__ dfinal, float* __restrict__ dq_acc, float* __restrict__ dk_acc,
-                     __nv_bfloat16* __restrict__ dv, float* __restrict__ dgam_acc, float* __restrict__ db_acc,
-                     float* __restrict__ dinit, float qscale) {
-  extern __shared__ float sm[];
-  float* S0 = sm + BwdSm::S0;
-  float* dS = sm + BwdSm::DS;
-  float* Ks = sm + BwdSm::K;
-  float* Qs = sm + BwdSm::Q;
-  float* Rs = sm + BwdSm::R;
-  float* Us = sm + BwdSm::U;
-  float* dUs = sm + BwdSm::DU;
-  float* dOs = sm + BwdSm::DO;
-  float* As = sm + BwdSm::A;
-  float* Ps = sm + BwdSm::P;
-  float* gam = sm + BwdSm::GAM;
-  float* bet = gam + kC;
-  float* eg = bet + kC;
-  float* dgam = eg + kC;
-  float* dbet = dgam + kC;
-  const int seq = blockIdx.x / (g.heads * 2);
-  const int h = (blockIdx.x / 2) % g.heads;
-  const int half = blockIdx.x % 2;
-  const int tid = threadIdx.x;
-  const int ty = tid / 16, tx = tid % 16;
-  int t0, len;
-  seq_span(g, seq, t0, len);
-  for (int i = tid; i < kDK * kDVH; i += kGdnThreads) {
-    const int r = i / kDVH, c = i % kDVH;
-    dS[i] = dfinal != nullptr ? dfinal[(((int64_t)seq * g.heads + h) * kDK + r) * g.dv + half * kDVH + c] : 0.f;
-  }
-  const int nchunks = (len + kC - 1) / kC;
-  for (int ci = nchunks - 1; ci >= 0; --ci) {
-    const int a = ci * kC;
-    const int n = min(kC, len - a);
-    const int chunk = g.chunk_off[seq] + ci;
-    __syncthreads();
-    const float* st = states + (((int64_t)chunk * g.heads + h) * kDK) * g.dv + half * kDVH;
-    for (int i = tid; i < kDK * kDVH; i += kGdnThreads) S0[i] = st[(int64_t)(i / kDVH) * g.dv + i % kDVH];
-    load_chunk(g, Ks, Qs, Rs, gam, bet, eg, q, k, v, gg, bb, t0, a, n, h, half, qscale);
-    for (int i = tid; i < kC * kDVH; i += kGdnThreads) {
-      const int r = i / kDVH, c = i % kDVH;
-      dOs[i] = r < n ? __bfloat162float(dout[(int64_t)(t0 + a + r) * g.row_v + (int64_t)h * g.dv + half * kDVH + c])
-                     : 0.f;
-    }
-    if (tid < kC) {
-      dgam[tid] = 0.f;
-      dbet[tid] = 0.f;
-    }
-    __syncthreads();
-    const float gl = gam[n - 1];
-    const float egl = __expf(gl);
-    // KS = K S0 -> R = V - e^gamma KS; dgamma partial needs KS too (kept in registers).
-    float ks[4][4];
-    zero(ks);
-    mm_acc<4, 4>(ks, Ks, kDK, 1, S0, kDVH, 1, ty * 4, tx * 4, kDK);
-    // A (strictly lower), and keep KK in registers
-    float kk[4][4];
-    zero(kk);
-    mm_acc<4, 4>(kk, Ks, kDK, 1, Ks, 1, kDK, ty * 4, tx * 4, kDK);
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = ty * 4 + i, c = tx * 4 + j;
-        Rs[r * kDVH + c] = Rs[r * kDVH + c] - eg[r] * ks[i][j];
-        As[r * kC + c] = (c < r) ? bet[r] * __expf(gam[r] - gam[c]) * kk[i][j] : 0.f;
-      }
-    __syncthreads();
-    // U = (I + A)^{-1} diag(beta) R  (forward substitution)
-    {
-      const int c = tid % kDVH, part = tid / kDVH;
-      for (int t = 0; t < kC; ++t) {
-        float acc = 0.f;
-        for (int s = part; s < t; s += 4) acc = fmaf(As[t * kC + s], Us[s * kDVH + c], acc);
-        dUs[part * kDVH + c] = acc;
-        __syncthreads();
-        if (part == 0)
-          Us[t * kDVH + c] = bet[t] * Rs[t * kDVH + c] - (dUs[c] + dUs[kDVH + c] + dUs[2 * kDVH + c] + dUs[3 * kDVH + c]);
-        __syncthreads();
-      }
-    }
-    // P = lower_incl(E * QK)
-    float qk[4][4];
-    zero(qk);
-    mm_acc<4, 4>(qk, Qs, kDK, 1, Ks, 1, kDK, ty * 4, tx * 4, kDK);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int t = ty * 4 + i, s = tx * 4 + j;
-        Ps[t * kC + s] = (s <= t) ? __expf(gam[t] - gam[s]) * qk[i][j] : 0.f;
-      }
-    __syncthreads();
-    // dU = P^T dO + F * (K dS); also dFw_s = sum_c (K dS)_{s,c} U_{s,c}
-    float kds[4][4];
-    zero(kds);
-    mm_acc<4, 4>(kds, Ks, kDK, 1, dS, kDVH, 1, ty * 4, tx * 4, kDK);
-    float ptdo[4][4];
-    zero(ptdo);
-    mm_acc<4, 4>(ptdo, Ps, 1, kC, dOs, kDVH, 1, ty * 4, tx * 4, kC);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = ty * 4 + i;
-      const float fw = (r < n) ? __expf(gl - gam[r]) : 0.f;
-      float dfw = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = tx * 4 + j;
-        dUs[r * kDVH + c] = ptdo[i][j] + fw * kds[i][j];
-        dfw += kds[i][j] * Us[r * kDVH + c];
-      }
-      // dgamma_s -= dFw_s F_s ; dgamma_C += sum_s dFw_s F_s
-      atomicAdd(&dgam[r], -dfw * fw);
-      atomicAdd(&dgam[n - 1], dfw * fw);
-    }
-    __syncthreads();
-    // dY = (I + A)^{-T} dU: backward substitution, in place in dUs
-    {
-      const int c = tid % kDVH, part = tid / kDVH;
-      float* scratch = Ps;  // 4 x 64 floats; P is rebuilt from the registers below
-      for (int t = kC - 1; t >= 0; --t) {
-        __syncthreads();  // row t + 1 of dY is written
-        float acc = 0.f;
-        for (int s = t + 1 + part; s < kC; s += 4) acc = fmaf(As[s * kC + t], dUs[s * kDVH + c], acc);
-        scratch[part * kDVH + c] = acc;
-        __syncthreads();
-        if (part == 0)
-          dUs[t * kDVH + c] = dUs[t * kDVH + c] - (scratch[c] + scratch[kDVH + c] + scratch[2 * kDVH + c] +
-                                                   scratch[3 * kDVH + c]);
-      }
-      __syncthreads();
-    }
-    // rebuild P (its storage served as scratch)
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int t = ty * 4 + i, s = tx * 4 + j;
-        Ps[t * kC + s] = (s <= t) ? __expf(gam[t] - gam[s]) * qk[i][j] : 0.f;
-      }
-    // dR = beta dY -> dV; dbeta += sum_c dY R; dKS = -e^gamma dR; dgamma -= e^gamma KS . dR
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = ty * 4 + i;
-      float db = 0.f, dgk = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = tx * 4 + j;
-        const float dy = dUs[r * kDVH + c];
-        const float dr = bet[r] * dy;
-        db += dy * Rs[r * kDVH + c];
-        dgk += ks[i][j] * dr;
-        if (r < n) dv[(int64_t)(t0 + a + r) * g.row_v + (int64_t)h * g.dv + half * kDVH + c] = __float2bfloat16(dr);
-      }
-      atomicAdd(&dbet[r], db);
-      atomicAdd(&dgam[r], -eg[r] * dgk);
-    }
-    __syncthreads();
-    // dA = -dY U^T (strictly lower) and dP = dO U^T (lower incl.), each over this half.
-    // Derived C x C terms: dKK = dA * E * beta; dPE = dP * E; contributions to dbeta, dgamma.
-    float da[4][4], dp[4][4];
-    zero(da);
-    zero(dp);
-    mm_acc<4, 4>(da, dUs, kDVH, 1, Us, 1, kDVH, ty * 4, tx * 4, kDVH);
-    mm_acc<4, 4>(dp, dOs, kDVH, 1, Us, 1, kDVH, ty * 4, tx * 4, kDVH);
-    __syncthreads();
-    // store dKK in As and dPE in Ps (both C x C), accumulate dbeta / dgamma parts
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = ty * 4 + i;
-      float dbt = 0.f, dgt = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int s = tx * 4 + j;
-        const float e = __expf(gam[t] - gam[s]);
-        float dkk = 0.f, dpe = 0.f;
-        if (s < t) {
-          const float dA = -da[i][j];
-          const float dAE = dA * e;
-          dbt += dAE * kk[i][j];
-          dkk = dAE * bet[t];
-          const float dEA = dAE * bet[t] * kk[i][j];
-          dgt += dEA;
-          atomicAdd(&dgam[s], -dEA);
-        }
-        if (s <= t) {
-          const float P = e * qk[i][j];
-          dpe = dp[i][j] * e;
-          const float dEP = dp[i][j] * P;
-          dgt += dEP;
-          atomicAdd(&dgam[s], -dEP);
-        }
-        As[t * kC + s] = dkk;
-        Ps[t * kC + s] = dpe;
-      }
-      atomicAdd(&dbet[t], dbt);
-      atomicAdd(&dgam[t], dgt);
-    }
-    __syncthreads();
-    // dQ (C x dk; 4 x 8 tiles: ty -> 4 rows, tx -> 8 cols) = dPE K + e^gamma dO S0^T
-    // dK = dKS S0^T + dKK K + dKK^T K + dPE^T Q + F (U dS^T), with dKS = -e^gamma dR
-    {
-      float dqt[4][8], dkt[4][8];
-      zero(dqt);
-      zero(dkt);
-      mm_acc<4, 8>(dqt, Ps, kC, 1, Ks, kDK, 1, ty * 4, tx * 8, kC);
-      float tmp[4][8];
-      zero(tmp);
-      mm_acc<4, 8>(tmp, dOs, kDVH, 1, S0, 1, kDVH, ty * 4, tx * 8, kDVH);  // dO S0^T
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dqt[i][j] += eg[ty * 4 + i] * tmp[i][j];
-      mm_acc<4, 8>(dkt, As, kC, 1, Ks, kDK, 1, ty * 4, tx * 8, kC);   // dKK K
-      mm_acc<4, 8>(dkt, As, 1, kC, Ks, kDK, 1, ty * 4, tx * 8, kC);   // dKK^T K
-      mm_acc<4, 8>(dkt, Ps, 1, kC, Qs, kDK, 1, ty * 4, tx * 8, kC);   // dPE^T Q
-      zero(tmp);
-      mm_acc<4, 8>(tmp, dUs, kDVH, 1, S0, 1, kDVH, ty * 4, tx * 8, kDVH);  // dY S0^T
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dkt[i][j] += -eg[ty * 4 + i] * bet[ty * 4 + i] * tmp[i][j];
-      zero(tmp);
-      mm_acc<4, 8>(tmp, Us, kDVH, 1, dS, 1, kDVH, ty * 4, tx * 8, kDVH);  // U dS^T
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = ty * 4 + i;
-        const float fw = (r < n) ? __expf(gl - gam[r]) : 0.f;
-        if (r < n) {
-          float* dqp = dq_acc + ((int64_t)(t0 + a + r) * g.heads + h) * kDK + tx * 8;
-          float* dkp = dk_acc + ((int64_t)(t0 + a + r) * g.heads + h) * kDK + tx * 8;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            atomicAdd(dqp + j, dqt[i][j]);
-            atomicAdd(dkp + j, dkt[i][j] + fw * tmp[i][j]);
-          }
-        }
-      }
-    }
-    // dgamma from Gamma Q S0 (Q S0 . dO) and from e^{gamma_C} S0 (<S0, dS>)
-    {
-      float qs[4][4];
-      zero(qs);
-      mm_acc<4, 4>(qs, Qs, kDK, 1, S0, kDVH, 1, ty * 4, tx * 4, kDK);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = ty * 4 + i;
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) s += qs[i][j] * dOs[r * kDVH + tx * 4 + j];
-        atomicAdd(&dgam[r], eg[r] * s);
-      }
-      float part = 0.f;
-      for (int i = tid; i < kDK * kDVH; i += kGdnThreads) part += S0[i] * dS[i];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffff, part, o);
-      if ((tid & 31) == 0) atomicAdd(&dgam[n - 1], egl * part);
-    }
-    __syncthreads();
-    // dS <- e^{gamma_C} dS + K^T dKS + Q^T (e^gamma dO),  dKS = -e^gamma beta dY  (dk x 64)
-    for (int i = tid; i < kC * kDVH; i += kGdnThreads) {
-      const int r = i / kDVH;
-      Rs[i] = -eg[r] * bet[r] * dUs[i];  // dKS (R no longer needed)
-      dOs[i] = eg[r] * dOs[i];
-    }
-    __syncthreads();
-    {
-      float o[8][4];
-      zero(o);
-      mm_acc<8, 4>(o, Ks, 1, kDK, Rs, kDVH, 1, ty * 8, tx * 4, kC);
-      mm_acc<8, 4>(o, Qs, 1, kDK, dOs, kDVH, 1, ty * 8, tx * 4, kC);
-      __syncthreads();
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = ty * 8 + i, c = tx * 4 + j;
-          dS[r * kDVH + c] = egl * dS[r * kDVH + c] + o[i][j];
-        }
-    }
-    __syncthreads();
-    // flush dbeta / dgamma (per chunk, before the reverse cumsum done on the host side)
-    if (tid < n) {
-      atomicAdd(&db_acc[(int64_t)(t0 + a + tid) * g.heads + h], dbet[tid]);
-      atomicAdd(&dgam_acc[(int64_t)(t0 + a + tid) * g.heads + h], dgam[tid]);
-    }
-  }
-  __syncthreads();
-  if (dinit != nullptr) {
-    for (int i = tid; i < kDK * kDVH; i += kGdnThreads) {
-      const int r = i / kDVH, c = i % kDVH;
-      dinit[(((int64_t)seq * g.heads + h) * kDK + r) * g.dv + half * kDVH + c] = dS[i];
-    }
-  }
-}
-
-// dg from dgamma: reverse cumulative sum inside every chunk of every sequence; and the
-// L2-norm backward of q (with its scale) and k: dx = (dy - y (y . dy)) / ||x||.
-__global__ void gdn_post_bwd_kernel(GdnGeom g, const __nv_bfloat16* __restrict__ q,
-                                    const __nv_bfloat16* __restrict__ k, const float* __restrict__ dq_acc,
-                                    const float* __restrict__ dk_acc, __nv_bfloat16* __restrict__ dq,
-                                    __nv_bfloat16* __restrict__ dk, int64_t rows, float qscale) {
-  // one warp per (token, head) row of 128
-  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= rows * g.heads) return;
-  const int64_t tok = w / g.heads;
-  const int h = (int)(w % g.heads);
-  const int64_t base = tok * g.row_q + (int64_t)h * kDK + lane * 4;
-  const int64_t abase = w * kDK + lane * 4;
-#pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    const __nv_bfloat16* x = which ? k : q;
-    const float* dy = which ? dk_acc : dq_acc;
-    float xv[4], dv_[4];
-    float ss = 0.f, dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      xv[i] = __bfloat162float(x[base + i]);
-      dv_[i] = dy[abase + i] * (which ? 1.f : qscale);
-      ss += xv[i] * xv[i];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
-    const float nrm = fmaxf(sqrtf(ss), 1e-6f);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dot += (xv[i] / nrm) * dv_[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffff, dot, o);
-    __nv_bfloat16* out = which ? dk : dq;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) out[base + i] = __float2bfloat16((dv_[i] - (xv[i] / nrm) * dot) / nrm);
-  }
-}
-
-__global__ void gdn_dg_kernel(GdnGeom g, const float* __restrict__ dgam, float* __restrict__ dg) {
-  // one thread per (sequence, head, chunk): reverse cumsum over the chunk
-  const int64_t id = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int total_chunks = g.chunk_off[g.num_seqs];
-  if (id >= (int64_t)total_chunks * g.heads) return;
-  const int chunk = (int)(id / g.heads), h = (int)(id % g.heads);
+// Global chunk -> (first token row, valid rows).  False for chunk indices past the end.
+__device__ __forceinline__ bool locate(const Geo& g, int chunk, int& row0, int& n) {
+  if (chunk >= g.chunk_off[g.num_seqs]) return false;
   int lo = 0, hi = g.num_seqs - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -659,30 +77,1020 @@ __global__ void gdn_dg_kernel(GdnGeom g, const float* __restrict__ dgam, float* 
   }
   int t0, len;
   seq_span(g, lo, t0, len);
-  const int a = (chunk - g.chunk_off[lo]) * kC;
-  const int n = min(kC, len - a);
-  float acc = 0.f;
-  for (int i = n - 1; i >= 0; --i) {
-    const int64_t idx = (int64_t)(t0 + a + i) * g.heads + h;
-    acc += dgam[idx];
-    dg[idx] = acc;
+  const int a = (chunk - g.chunk_off[lo]) * C;
+  row0 = t0 + a;
+  n = min(C, len - a);
+  return n > 0;
+}
+
+// ---------------------------------------------------------------- warp MMA helpers
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const bf16* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], const bf16* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// acc[j] (16 x 8 tile j) += A(m0.., 0..K) * B(0..K, n0 + 8j ..)
+//   A_T == false: A(m, k) at A[m * lda + k];  true: at A[k * lda + m]
+//   B_T == false: B(k, n) at B[n * ldb + k];  true: at B[k * ldb + n]
+// Fragment element e of acc[j] sits at row m0 + lane/4 + 8 (e >= 2), column
+// n0 + 8j + 2 (lane % 4) + (e & 1).
+template <int NT8, bool A_T, bool B_T>
+__device__ __forceinline__ void warp_mma(float (&acc)[NT8][4], const bf16* A, int lda, int m0, const bf16* B, int ldb,
+                                         int n0, int K) {
+  static_assert(NT8 % 2 == 0, "pairs of n8 tiles");
+  const int lane = threadIdx.x & 31;
+  const int r = lane & 7, mat = lane >> 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    uint32_t a[4];
+    if (!A_T) ldsm4(a, A + (m0 + (lane & 15)) * lda + k0 + (lane >> 4) * 8);
+    else ldsm4t(a, A + (k0 + r + (mat >> 1) * 8) * lda + m0 + (mat & 1) * 8);
+#pragma unroll
+    for (int j = 0; j < NT8; j += 2) {
+      uint32_t b[4];
+      if (!B_T) ldsm4(b, B + (n0 + j * 8 + r + (mat >> 1) * 8) * ldb + k0 + (mat & 1) * 8);
+      else ldsm4t(b, B + (k0 + (mat & 1) * 8 + r) * ldb + n0 + j * 8 + (mat >> 1) * 8);
+      mma(acc[j], a, b[0], b[1]);
+      mma(acc[j + 1], a, b[2], b[3]);
+    }
   }
 }
 
-// ------------------------------------------------------------------------- recurrent
+template <int NT8>
+__device__ __forceinline__ void zero(float (&acc)[NT8][4]) {
+#pragma unroll
+  for (int j = 0; j < NT8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void st2(bf16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack2(a, b); }
+__device__ __forceinline__ float2 ld2(const bf16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
+// T = (I + A)^-1 for the strictly lower A(i, k) = beta_i exp(gamma_i - gamma_k) KK[i][k],
+// by 16 x 16 blocks: diagonal blocks by forward substitution (one thread per column),
+// then T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj level by level.  Tf: fp32 [64][LDF];
+// X: fp32 scratch of 768 floats.  Ends synchronised.
+__device__ void invert_unit_lower(const float* KK, const float* gam, const float* bet, float* Tf, float* X) {
+  auto Aik = [&](int i, int k) -> float { return k < i ? bet[i] * __expf(gam[i] - gam[k]) * KK[i * LDF + k] : 0.f; };
+  const int tid = threadIdx.x;
+  for (int i = tid; i < C * LDF; i += NT) Tf[i] = 0.f;
+  __syncthreads();
+  if (tid < C) {
+    const int b = tid >> 4, j = tid & 15, base = b * 16;
+    Tf[(base + j) * LDF + base + j] = 1.f;
+    for (int i = j + 1; i < 16; ++i) {
+      float s = 0.f;
+      for (int k = j; k < i; ++k) s = fmaf(Aik(base + i, base + k), Tf[(base + k) * LDF + base + j], s);
+      Tf[(base + i) * LDF + base + j] = -s;
+    }
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    for (int e = tid; e < nb * 256; e += NT) {
+      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
+      float s = 0.f;
+      for (int kb = bj; kb < bi; ++kb)
+        for (int kk = 0; kk < 16; ++kk)
+          s = fmaf(Aik(bi * 16 + i, kb * 16 + kk), Tf[(kb * 16 + kk) * LDF + bj * 16 + j], s);
+      X[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 256; e += NT) {
+      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
+      float s = 0.f;
+      for (int kk = 0; kk < 16; ++kk) s = fmaf(Tf[(bi * 16 + i) * LDF + bi * 16 + kk], X[(bj << 8) + kk * 16 + j], s);
+      Tf[(bi * 16 + i) * LDF + bj * 16 + j] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+// Sum over the 4 lanes of a quad (the lanes sharing a fragment row).
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffff, v, 1);
+  v += __shfl_xor_sync(0xffffffff, v, 2);
+  return v;
+}
+// Sum over the 8 lanes sharing lane % 4 (a fragment column).
+__device__ __forceinline__ float col_sum(float v) {
+  v += __shfl_xor_sync(0xffffffff, v, 4);
+  v += __shfl_xor_sync(0xffffffff, v, 8);
+  v += __shfl_xor_sync(0xffffffff, v, 16);
+  return v;
+}
+
+// ---------------------------------------------------------------- async copies
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
+  // zero-fills the 16 bytes when !valid (no bytes are read)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 64 token rows (stride `stride` elements) x 128 columns -> padded tile; rows >= n zero.
+__device__ __forceinline__ void rows128_async(bf16* dst, const bf16* src, int64_t stride, int n) {
+  for (int i = threadIdx.x; i < C * 16; i += NT) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    cp16(dst + r * LD + c, src + (r < n ? r : 0) * stride + c, r < n);
+  }
+}
+// 64 token rows x 32 columns (a value slice) -> padded tile; rows >= n zero.
+__device__ __forceinline__ void rows32_async(bf16* dst, const bf16* src, int64_t stride, int n) {
+  if (threadIdx.x < C * 4) {
+    const int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 8;
+    cp16(dst + r * LDP + c, src + (r < n ? r : 0) * stride + c, r < n);
+  }
+}
+// contiguous (rows x 128) bf16 block -> padded tile
+__device__ __forceinline__ void tile128_async(bf16* dst, const bf16* src, int rows) {
+  for (int i = threadIdx.x; i < rows * 16; i += NT) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    cp16(dst + r * LD + c, src + r * 128 + c, true);
+  }
+}
+// contiguous (64 x 64) bf16 block -> padded tile
+__device__ __forceinline__ void tile64_async(bf16* dst, const bf16* src) {
+  for (int i = threadIdx.x; i < C * 8; i += NT) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    cp16(dst + r * LDS + c, src + r * C + c, true);
+  }
+}
+// 64 per-token floats of head-major scalars (rows >= n zero) -> shared
+__device__ __forceinline__ void scal_async(float* dst, const float* src, int n) {
+  if (threadIdx.x < C) cp4(dst + threadIdx.x, src + (threadIdx.x < n ? threadIdx.x : 0), threadIdx.x < n);
+}
+// rows of a padded 128-wide tile times scale[r], in place
+__device__ __forceinline__ void scale_rows128(bf16* t, const float* scale) {
+  for (int i = threadIdx.x; i < C * 16; i += NT) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    uint4 v = *reinterpret_cast<uint4*>(t + r * LD + c);
+    const float s = scale[r];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
+      w[e] = pack2(f.x * s, f.y * s);
+    }
+    *reinterpret_cast<uint4*>(t + r * LD + c) = v;
+  }
+}
+
+// gamma of a chunk (its cumulative log decay) from the head-major scalars: entries past
+// n repeat gamma_{n-1}; e^gamma.
+__device__ __forceinline__ void pad_gamma(float* gam, float* eg, int n) {
+  if (threadIdx.x < C) {
+    const float gv = gam[min((int)threadIdx.x, n - 1)];
+    eg[threadIdx.x] = __expf(gv);
+  }
+}
+
+// ------------------------------------------------------------------------ forward
+// gdn_prep: norms, gamma, W = T diag(beta e^gamma) K^, U~ = T diag(beta) V.
+struct PrepSm {
+  bf16 kh[C * LD];    // K raw -> K^
+  bf16 kb[C * LD];    // beta e^gamma K^
+  bf16 vb[C * LD];    // V raw -> beta V
+  bf16 tb[C * LDS];   // T
+  float kk[C * LDF];  // K^ K^T
+  float tf[C * LDF];  // T (fp32)
+  float x[768];
+  float gam[C], eg[C], bet[C];
+};
+
+__global__ void __launch_bounds__(NT) gdn_prep_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                      const bf16* __restrict__ v, const float* __restrict__ gg,
+                                                      const float* __restrict__ bb, float* __restrict__ gcum,
+                                                      float* __restrict__ kinv, float* __restrict__ qinv,
+                                                      bf16* __restrict__ w_out, bf16* __restrict__ u_out,
+                                                      float qscale) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  PrepSm& s = *reinterpret_cast<PrepSm*>(smraw);
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+  rows128_async(s.vb, v + (int64_t)row0 * g.row_v + (int64_t)h * DV, g.row_v, n);
+  cp_commit();
+  const int64_t hb = (int64_t)h * g.rows + row0;  // head-major scalar index of row0
+  if (warp == 0) {  // gamma = inclusive cumsum of g over the chunk; beta
+    const int i0 = 2 * lane, i1 = 2 * lane + 1;
+    const float x0 = i0 < n ? gg[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
+    const float x1 = i1 < n ? gg[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
+    float c = x0 + x1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffff, c, o);
+      if (lane >= o) c += y;
+    }
+    const float c0 = c - x1;
+    s.gam[i0] = c0;
+    s.gam[i1] = c;
+    s.eg[i0] = __expf(c0);
+    s.eg[i1] = __expf(c);
+    s.bet[i0] = i0 < n ? bb[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
+    s.bet[i1] = i1 < n ? bb[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
+    if (i0 < n) gcum[hb + i0] = c0;
+    if (i1 < n) gcum[hb + i1] = c;
+  } else {  // q norms (rows 0..63 over warps 1..7), straight from global memory
+    for (int r = warp - 1; r < n; r += NT / 32 - 1) {
+      const float2 a = ld2(q + (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK + lane * 4);
+      const float2 b = ld2(q + (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK + lane * 4 + 2);
+      float sq = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffff, sq, o);
+      if (lane == 0) qinv[hb + r] = qscale / fmaxf(sqrtf(sq), 1e-6f);
+    }
+  }
+  cp_wait<0>();
+  __syncthreads();
+  for (int r = warp; r < C; r += NT / 32) {  // k^, beta e^gamma k^, beta v (in place)
+    bf16* kh = s.kh + r * LD + lane * 4;
+    bf16* vb = s.vb + r * LD + lane * 4;
+    const float2 a = ld2(kh), b = ld2(kh + 2), va = ld2(vb), vc = ld2(vb + 2);
+    float sk = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sk += __shfl_xor_sync(0xffffffff, sk, o);
+    const float ik = r < n ? 1.f / fmaxf(sqrtf(sk), 1e-6f) : 0.f;
+    if (lane == 0 && r < n) kinv[hb + r] = ik;
+    const float kbs = s.bet[r] * s.eg[r] * ik, bv = s.bet[r];
+    st2(kh, a.x * ik, a.y * ik);
+    st2(kh + 2, b.x * ik, b.y * ik);
+    st2(s.kb + r * LD + lane * 4, a.x * kbs, a.y * kbs);
+    st2(s.kb + r * LD + lane * 4 + 2, b.x * kbs, b.y * kbs);
+    st2(vb, va.x * bv, va.y * bv);
+    st2(vb + 2, vc.x * bv, vc.y * bv);
+  }
+  __syncthreads();
+  const int mt = warp & 3, gq = lane >> 2, cq = (lane & 3) * 2;
+  {  // KK = K^ K^T
+    float acc[4][4];
+    zero(acc);
+    const int nb = (warp >> 2) * 32;
+    warp_mma<4, false, false>(acc, s.kh, LD, mt * 16, s.kh, LD, nb, DK);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
+      s.kk[r * LDF + c] = acc[j][0];
+      s.kk[r * LDF + c + 1] = acc[j][1];
+      s.kk[(r + 8) * LDF + c] = acc[j][2];
+      s.kk[(r + 8) * LDF + c + 1] = acc[j][3];
+    }
+  }
+  __syncthreads();
+  invert_unit_lower(s.kk, s.gam, s.bet, s.tf, s.x);
+  for (int i = tid; i < C * C / 2; i += NT) {
+    const int r = i >> 5, c = (i & 31) * 2;
+    st2(s.tb + r * LDS + c, s.tf[r * LDF + c], s.tf[r * LDF + c + 1]);
+  }
+  __syncthreads();
+  const int64_t cbase = ((int64_t)chunk * g.heads + h) * C * DK;
+  const int nb = (warp >> 2) * 64;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    float acc[8][4];
+    zero(acc);
+    warp_mma<8, false, true>(acc, s.tb, LDS, mt * 16, which ? s.vb : s.kb, LD, nb, C);
+    bf16* out = (which ? u_out : w_out) + cbase;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
+      st2(out + r * DK + c, acc[j][0], acc[j][1]);
+      st2(out + (r + 8) * DK + c, acc[j][2], acc[j][3]);
+    }
+  }
+}
+
+// gdn_state: one CTA per (sequence, head, 32 value columns); the state slice (128 x 32,
+// fp32) lives in the MMA accumulators of the 8 warps (warp w: key rows 16w..16w+15).
+// The next chunk's operands stream in (cp.async, double buffered) while this one runs;
+// S += K^T diag(F kinv) U uses the raw keys with the scaling folded into U's rows.
+struct StateBuf {
+  bf16 w[C * LD];   // W
+  bf16 k[C * LD];   // raw keys
+  bf16 u[C * LDP];  // U~ slice
+  float gam[C], ki[C];
+};
+struct StateSm {
+  StateBuf buf[2];
+  bf16 uf[C * LDP];   // diag(F kinv) U (operand)
+  bf16 sb[DK * LDP];  // S0 slice (operand)
+};
+
+__global__ void __launch_bounds__(NT) gdn_state_kernel(Geo g, const bf16* __restrict__ k, const float* __restrict__ gcum,
+                                                       const float* __restrict__ kinv, const bf16* __restrict__ w_in,
+                                                       bf16* __restrict__ u_io, const float* __restrict__ init,
+                                                       bf16* __restrict__ states, float* __restrict__ fin) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  StateSm& s = *reinterpret_cast<StateSm*>(smraw);
+  const int part = blockIdx.x % PARTS;
+  const int h = (blockIdx.x / PARTS) % g.heads;
+  const int seq = g.order[blockIdx.x / (PARTS * g.heads)];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = (lane & 3) * 2;
+  const int col0 = part * PW;
+  int t0, len;
+  seq_span(g, seq, t0, len);
+  float S[4][4];
+  {
+    const float* src = init != nullptr ? init + ((int64_t)seq * g.heads + h) * DK * DV : nullptr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
+      S[j][0] = src ? src[r * DV + c] : 0.f;
+      S[j][1] = src ? src[r * DV + c + 1] : 0.f;
+      S[j][2] = src ? src[(r + 8) * DV + c] : 0.f;
+      S[j][3] = src ? src[(r + 8) * DV + c + 1] : 0.f;
+    }
+  }
+  const int nch = (len + C - 1) / C;
+  auto prefetch = [&](int ci) {
+    StateBuf& b = s.buf[ci & 1];
+    const int chunk = g.chunk_off[seq] + ci;
+    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    tile128_async(b.w, w_in + cbase * C * DK, C);
+    rows128_async(b.k, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+    rows32_async(b.u, u_io + cbase * C * DV + col0, DV, C);
+    scal_async(b.gam, gcum + (int64_t)h * g.rows + row0, n);
+    scal_async(b.ki, kinv + (int64_t)h * g.rows + row0, n);
+    cp_commit();
+  };
+  if (nch > 0) prefetch(0);
+  for (int ci = 0; ci < nch; ++ci) {
+    if (ci + 1 < nch) {
+      prefetch(ci + 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    StateBuf& b = s.buf[ci & 1];
+    const int chunk = g.chunk_off[seq] + ci;
+    const int n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    bf16* st = states + cbase * DK * DV + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // S0 of this chunk: to global and to the operand tile
+      const int r = warp * 16 + gq, c = j * 8 + cq;
+      st2(st + r * DV + c, S[j][0], S[j][1]);
+      st2(st + (r + 8) * DV + c, S[j][2], S[j][3]);
+      st2(s.sb + r * LDP + c, S[j][0], S[j][1]);
+      st2(s.sb + (r + 8) * LDP + c, S[j][2], S[j][3]);
+    }
+    __syncthreads();
+    const float gl = b.gam[n - 1];
+    {  // U = U~ - W S0  (64 x 32): warp -> rows 16 (w % 4), columns 16 (w / 4)
+      float acc[2][4];
+      zero(acc);
+      const int mt = warp & 3, nb = (warp >> 2) * 16;
+      warp_mma<2, false, true>(acc, b.w, LD, mt * 16, s.sb, LDP, nb, DK);
+      bf16* ug = u_io + cbase * C * DV + col0;
+      const int r = mt * 16 + gq;
+      const float f0 = r < n ? __expf(gl - b.gam[r]) * b.ki[r] : 0.f;
+      const float f1 = r + 8 < n ? __expf(gl - b.gam[r + 8]) * b.ki[r + 8] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = nb + j * 8 + cq;
+        const float2 u0 = ld2(b.u + r * LDP + c), u1 = ld2(b.u + (r + 8) * LDP + c);
+        const float a0 = u0.x - acc[j][0], a1 = u0.y - acc[j][1], a2 = u1.x - acc[j][2], a3 = u1.y - acc[j][3];
+        st2(ug + r * DV + c, a0, a1);
+        st2(ug + (r + 8) * DV + c, a2, a3);
+        st2(s.uf + r * LDP + c, f0 * a0, f0 * a1);
+        st2(s.uf + (r + 8) * LDP + c, f1 * a2, f1 * a3);
+      }
+    }
+    __syncthreads();
+    {  // S <- e^{gamma_C} S + K_raw^T (diag(F kinv) U)
+      const float egl = __expf(gl);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[j][e] *= egl;
+      warp_mma<4, true, true>(S, b.k, LD, warp * 16, s.uf, LDP, 0, C);
+    }
+    __syncthreads();
+  }
+  if (fin != nullptr) {
+    float* dst = fin + ((int64_t)seq * g.heads + h) * DK * DV;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
+      *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(S[j][0], S[j][1]);
+      *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(S[j][2], S[j][3]);
+    }
+  }
+}
+
+// gdn_out: P = lower_incl(E * Q^ K^T) (saved for the backward), O = e^gamma Q^ S0 + P U.
+struct OutSm {
+  bf16 qh[C * LD];
+  bf16 kh[C * LD];
+  bf16 u[C * LD];
+  bf16 sb[DK * LD];
+  bf16 p[C * LDS];
+  float gam[C], eg[C], ki[C], qi[C];
+};
+
+__global__ void __launch_bounds__(NT) gdn_out_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                     const float* __restrict__ gcum, const float* __restrict__ kinv,
+                                                     const float* __restrict__ qinv, const bf16* __restrict__ u_in,
+                                                     const bf16* __restrict__ states, bf16* __restrict__ p_out,
+                                                     bf16* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  OutSm& s = *reinterpret_cast<OutSm*>(smraw);
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = (lane & 3) * 2, mt = warp & 3;
+  const int64_t cbase = (int64_t)chunk * g.heads + h;
+  const int64_t hb = (int64_t)h * g.rows + row0;
+  rows128_async(s.qh, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+  tile128_async(s.u, u_in + cbase * C * DV, C);
+  tile128_async(s.sb, states + cbase * DK * DV, DK);
+  scal_async(s.gam, gcum + hb, n);
+  scal_async(s.ki, kinv + hb, n);
+  scal_async(s.qi, qinv + hb, n);
+  cp_commit();
+  cp_wait<0>();
+  __syncthreads();
+  pad_gamma(s.gam, s.eg, n);
+  scale_rows128(s.qh, s.qi);
+  scale_rows128(s.kh, s.ki);
+  __syncthreads();
+  if (tid < C && tid >= n) s.gam[tid] = s.gam[n - 1];
+  __syncthreads();
+  {
+    float acc[4][4];
+    zero(acc);
+    const int nb = (warp >> 2) * 32;
+    warp_mma<4, false, false>(acc, s.qh, LD, mt * 16, s.kh, LD, nb, DK);
+    bf16* pg = p_out + cbase * C * C;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = mt * 16 + gq + hf * 8, c = nb + j * 8 + cq;
+        const float p0 = c <= t ? __expf(s.gam[t] - s.gam[c]) * acc[j][2 * hf] : 0.f;
+        const float p1 = c + 1 <= t ? __expf(s.gam[t] - s.gam[c + 1]) * acc[j][2 * hf + 1] : 0.f;
+        st2(s.p + t * LDS + c, p0, p1);
+        st2(pg + t * C + c, p0, p1);
+      }
+    }
+  }
+  __syncthreads();
+  {
+    float acc[8][4];
+    zero(acc);
+    const int nb = (warp >> 2) * 64;
+    warp_mma<8, false, true>(acc, s.qh, LD, mt * 16, s.sb, LD, nb, DK);
+    const float e0 = s.eg[mt * 16 + gq], e1 = s.eg[mt * 16 + gq + 8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[j][0] *= e0, acc[j][1] *= e0, acc[j][2] *= e1, acc[j][3] *= e1;
+    }
+    warp_mma<8, false, true>(acc, s.p, LDS, mt * 16, s.u, LD, nb, C);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
+      if (r < n) st2(out + (int64_t)(row0 + r) * g.row_v + (int64_t)h * DV + c, acc[j][0], acc[j][1]);
+      if (r + 8 < n) st2(out + (int64_t)(row0 + r + 8) * g.row_v + (int64_t)h * DV + c, acc[j][2], acc[j][3]);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------- backward
+// gdn_dstate: dS at every chunk end (dS_C), in reverse:
+//   dU  = P^T dO + diag(F kinv) (K_raw dS_C)
+//   dS0 = e^{gamma_C} dS_C + Q_raw^T diag(e^gamma qinv) dO - W^T dU
+// with the next (earlier) chunk's operands streaming in while this one runs.
+struct DStateBuf {
+  bf16 q[C * LD];     // raw queries
+  bf16 w[C * LD];
+  bf16 k[C * LD];     // raw keys
+  bf16 p[C * LDS];
+  bf16 dob[C * LDP];  // dO slice
+  float gam[C], ki[C], qi[C];
+};
+struct DStateSm {
+  DStateBuf buf[2];
+  bf16 doq[C * LDP];  // diag(e^gamma qinv) dO slice
+  bf16 du[C * LDP];   // -dU slice
+  bf16 dsb[DK * LDP];
+};
+
+__global__ void __launch_bounds__(NT) gdn_dstate_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                        const float* __restrict__ gcum, const float* __restrict__ kinv,
+                                                        const float* __restrict__ qinv, const bf16* __restrict__ w_in,
+                                                        const bf16* __restrict__ p_in, const bf16* __restrict__ dout,
+                                                        const float* __restrict__ dfinal, bf16* __restrict__ dstates,
+                                                        float* __restrict__ dinit) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  DStateSm& s = *reinterpret_cast<DStateSm*>(smraw);
+  const int part = blockIdx.x % PARTS;
+  const int h = (blockIdx.x / PARTS) % g.heads;
+  const int seq = g.order[blockIdx.x / (PARTS * g.heads)];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = (lane & 3) * 2;
+  const int col0 = part * PW;
+  int t0, len;
+  seq_span(g, seq, t0, len);
+  float dS[4][4];
+  {
+    const float* src = dfinal != nullptr ? dfinal + ((int64_t)seq * g.heads + h) * DK * DV : nullptr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
+      dS[j][0] = src ? src[r * DV + c] : 0.f;
+      dS[j][1] = src ? src[r * DV + c + 1] : 0.f;
+      dS[j][2] = src ? src[(r + 8) * DV + c] : 0.f;
+      dS[j][3] = src ? src[(r + 8) * DV + c + 1] : 0.f;
+    }
+  }
+  const int nch = (len + C - 1) / C;
+  auto prefetch = [&](int ci) {
+    DStateBuf& b = s.buf[ci & 1];
+    const int chunk = g.chunk_off[seq] + ci;
+    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    const int64_t hb = (int64_t)h * g.rows + row0;
+    rows128_async(b.q, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+    tile128_async(b.w, w_in + cbase * C * DK, C);
+    rows128_async(b.k, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+    tile64_async(b.p, p_in + cbase * C * C);
+    rows32_async(b.dob, dout + (int64_t)row0 * g.row_v + (int64_t)h * DV + col0, g.row_v, n);
+    scal_async(b.gam, gcum + hb, n);
+    scal_async(b.ki, kinv + hb, n);
+    scal_async(b.qi, qinv + hb, n);
+    cp_commit();
+  };
+  if (nch > 0) prefetch(nch - 1);
+  for (int ci = nch - 1; ci >= 0; --ci) {
+    if (ci > 0) {
+      prefetch(ci - 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    DStateBuf& b = s.buf[ci & 1];
+    const int chunk = g.chunk_off[seq] + ci;
+    const int n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    bf16* dst = dstates + cbase * DK * DV + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = warp * 16 + gq, c = j * 8 + cq;
+      st2(dst + r * DV + c, dS[j][0], dS[j][1]);
+      st2(dst + (r + 8) * DV + c, dS[j][2], dS[j][3]);
+      st2(s.dsb + r * LDP + c, dS[j][0], dS[j][1]);
+      st2(s.dsb + (r + 8) * LDP + c, dS[j][2], dS[j][3]);
+    }
+    __syncthreads();  // this chunk's buffer and dsb are visible
+    const float gl = b.gam[n - 1];
+    if (tid < C * 4) {  // diag(e^gamma qinv) dO
+      const int r = tid >> 2, c = (tid & 3) * 8;
+      const float sc = r < n ? __expf(b.gam[r]) * b.qi[r] : 0.f;
+      uint4 v = *reinterpret_cast<const uint4*>(b.dob + r * LDP + c);
+      uint32_t* wv = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wv[e]));
+        wv[e] = pack2(f.x * sc, f.y * sc);
+      }
+      *reinterpret_cast<uint4*>(s.doq + r * LDP + c) = v;
+    }
+    {  // -dU = -(P^T dO + diag(F kinv) (K_raw dS_C))
+      float acc[2][4], kd[2][4];
+      zero(acc);
+      zero(kd);
+      const int mt = warp & 3, nb = (warp >> 2) * 16;
+      warp_mma<2, true, true>(acc, b.p, LDS, mt * 16, b.dob, LDP, nb, C);
+      warp_mma<2, false, true>(kd, b.k, LD, mt * 16, s.dsb, LDP, nb, DK);
+      const int r = mt * 16 + gq;
+      const float f0 = r < n ? __expf(gl - b.gam[r]) * b.ki[r] : 0.f;
+      const float f1 = r + 8 < n ? __expf(gl - b.gam[r + 8]) * b.ki[r + 8] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = nb + j * 8 + cq;
+        st2(s.du + r * LDP + c, -(acc[j][0] + f0 * kd[j][0]), -(acc[j][1] + f0 * kd[j][1]));
+        st2(s.du + (r + 8) * LDP + c, -(acc[j][2] + f1 * kd[j][2]), -(acc[j][3] + f1 * kd[j][3]));
+      }
+    }
+    __syncthreads();
+    {
+      const float egl = __expf(gl);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dS[j][e] *= egl;
+      warp_mma<4, true, true>(dS, b.q, LD, warp * 16, s.doq, LDP, 0, C);
+      warp_mma<4, true, true>(dS, b.w, LD, warp * 16, s.du, LDP, 0, C);
+    }
+    __syncthreads();
+  }
+  if (dinit != nullptr) {
+    float* dst = dinit + ((int64_t)seq * g.heads + h) * DK * DV;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
+      *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(dS[j][0], dS[j][1]);
+      *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(dS[j][2], dS[j][3]);
+    }
+  }
+}
+
+// gdn_grad: every gradient of one chunk from S0, dS_C and U (one CTA per (chunk, head)).
+struct GradSm {
+  bf16 kh[C * LD];
+  bf16 qh[C * LD];
+  bf16 dob[C * LD];
+  bf16 u[C * LD];
+  bf16 dy[C * LD];    // the inversion scratch, then dU, then dY
+  bf16 sb[DK * LD];   // S0
+  bf16 dsb[DK * LD];  // dS_C
+  bf16 pb[C * LDS];   // P, then dPE
+  bf16 tb[C * LDS];   // T, then dKK
+  float kk[C * LDF];  // K^ K^T
+  float qk[C * LDF];  // T (fp32) during the inversion, then Q^ K^T
+  float gam[C], eg[C], bet[C], ki[C], qi[C], f[C];
+  float dgam[C], dbet[C], dotq[C], dotk[C];
+};
+
+__global__ void __launch_bounds__(NT) gdn_grad_kernel(
+    Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+    const float* __restrict__ bb, const float* __restrict__ gcum, const float* __restrict__ kinv,
+    const float* __restrict__ qinv, const bf16* __restrict__ u_in, const bf16* __restrict__ states,
+    const bf16* __restrict__ dstates, const bf16* __restrict__ dout, bf16* __restrict__ dq, bf16* __restrict__ dk,
+    bf16* __restrict__ dv, float* __restrict__ dg, float* __restrict__ db, float qscale) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  GradSm& s = *reinterpret_cast<GradSm*>(smraw);
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = (lane & 3) * 2, mt = warp & 3;
+  const int64_t cbase = (int64_t)chunk * g.heads + h;
+  const int64_t hb = (int64_t)h * g.rows + row0;
+  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+  rows128_async(s.qh, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
+  rows128_async(s.dob, dout + (int64_t)row0 * g.row_v + (int64_t)h * DV, g.row_v, n);
+  tile128_async(s.u, u_in + cbase * C * DV, C);
+  tile128_async(s.sb, states + cbase * DK * DV, DK);
+  tile128_async(s.dsb, dstates + cbase * DK * DV, DK);
+  scal_async(s.gam, gcum + hb, n);
+  scal_async(s.ki, kinv + hb, n);
+  scal_async(s.qi, qinv + hb, n);
+  cp_commit();
+  if (tid < C) {
+    s.bet[tid] = tid < n ? bb[(int64_t)(row0 + tid) * g.heads + h] : 0.f;
+    s.dgam[tid] = 0.f;
+    s.dbet[tid] = 0.f;
+    s.dotq[tid] = 0.f;
+    s.dotk[tid] = 0.f;
+  }
+  cp_wait<0>();
+  __syncthreads();
+  pad_gamma(s.gam, s.eg, n);
+  if (tid < C) s.f[tid] = tid < n ? __expf(s.gam[n - 1] - s.gam[tid]) : 0.f;
+  scale_rows128(s.kh, s.ki);
+  scale_rows128(s.qh, s.qi);
+  {  // dgamma_C += e^{gamma_C} <S0, dS_C>
+    float dot = 0.f;
+    for (int i = tid; i < DK * DV / 8; i += NT) {
+      const int r = i >> 4, c = (i & 15) * 8;
+      const uint4 a = *reinterpret_cast<const uint4*>(s.sb + r * LD + c);
+      const uint4 b = *reinterpret_cast<const uint4*>(s.dsb + r * LD + c);
+      const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* bw = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[e]));
+        const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[e]));
+        dot += x.x * y.x + x.y * y.y;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffff, dot, o);
+    if (lane == 0) atomicAdd(&s.dgam[C - 1], __expf(s.gam[n - 1]) * dot);
+  }
+  __syncthreads();
+  if (tid < C && tid >= n) s.gam[tid] = s.gam[n - 1];
+  __syncthreads();
+  {  // KK
+    float acc[4][4];
+    zero(acc);
+    const int nb = (warp >> 2) * 32;
+    warp_mma<4, false, false>(acc, s.kh, LD, mt * 16, s.kh, LD, nb, DK);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
+      s.kk[r * LDF + c] = acc[j][0];
+      s.kk[r * LDF + c + 1] = acc[j][1];
+      s.kk[(r + 8) * LDF + c] = acc[j][2];
+      s.kk[(r + 8) * LDF + c + 1] = acc[j][3];
+    }
+  }
+  __syncthreads();
+  invert_unit_lower(s.kk, s.gam, s.bet, s.qk, reinterpret_cast<float*>(s.dy));
+  for (int i = tid; i < C * C / 2; i += NT) {
+    const int r = i >> 5, c = (i & 31) * 2;
+    st2(s.tb + r * LDS + c, s.qk[r * LDF + c], s.qk[r * LDF + c + 1]);
+  }
+  __syncthreads();
+  {  // QK (fp32) and P (bf16)
+    float acc[4][4];
+    zero(acc);
+    const int nb = (warp >> 2) * 32;
+    warp_mma<4, false, false>(acc, s.qh, LD, mt * 16, s.kh, LD, nb, DK);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = mt * 16 + gq + hf * 8, c = nb + j * 8 + cq;
+        s.qk[t * LDF + c] = acc[j][2 * hf];
+        s.qk[t * LDF + c + 1] = acc[j][2 * hf + 1];
+        const float p0 = c <= t ? __expf(s.gam[t] - s.gam[c]) * acc[j][2 * hf] : 0.f;
+        const float p1 = c + 1 <= t ? __expf(s.gam[t] - s.gam[c + 1]) * acc[j][2 * hf + 1] : 0.f;
+        st2(s.pb + t * LDS + c, p0, p1);
+      }
+  }
+  __syncthreads();
+  const int nb = (warp >> 2) * 64;
+  const int r0 = mt * 16 + gq, r1 = r0 + 8;
+  {  // dU = P^T dO + F (K^ dS_C); dF_s = sum_v (K^ dS_C)_sv U_sv
+    float acc[8][4], kd[8][4];
+    zero(acc);
+    zero(kd);
+    warp_mma<8, true, true>(acc, s.pb, LDS, mt * 16, s.dob, LD, nb, C);
+    warp_mma<8, false, true>(kd, s.kh, LD, mt * 16, s.dsb, LD, nb, DK);
+    const float f0 = s.f[r0], f1 = s.f[r1];
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = nb + j * 8 + cq;
+      const float2 u0 = ld2(s.u + r0 * LD + c), u1 = ld2(s.u + r1 * LD + c);
+      d0 += kd[j][0] * u0.x + kd[j][1] * u0.y;
+      d1 += kd[j][2] * u1.x + kd[j][3] * u1.y;
+      acc[j][0] += f0 * kd[j][0];
+      acc[j][1] += f0 * kd[j][1];
+      acc[j][2] += f1 * kd[j][2];
+      acc[j][3] += f1 * kd[j][3];
+    }
+    d0 = quad_sum(d0) * f0;
+    d1 = quad_sum(d1) * f1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = nb + j * 8 + cq;
+      st2(s.dy + r0 * LD + c, acc[j][0], acc[j][1]);
+      st2(s.dy + r1 * LD + c, acc[j][2], acc[j][3]);
+    }
+    if ((lane & 3) == 0) {
+      atomicAdd(&s.dgam[r0], -d0);
+      atomicAdd(&s.dgam[r1], -d1);
+      atomicAdd(&s.dgam[C - 1], d0 + d1);
+    }
+  }
+  __syncthreads();
+  {  // dY = T^T dU; dV = beta dY; R = V - e^gamma K^ S0; dbeta += dY . R; dgamma -= e^gamma beta KS . dY
+    float acc[8][4], ks[8][4];
+    zero(acc);
+    zero(ks);
+    warp_mma<8, true, true>(acc, s.tb, LDS, mt * 16, s.dy, LD, nb, C);
+    warp_mma<8, false, true>(ks, s.kh, LD, mt * 16, s.sb, LD, nb, DK);
+    __syncthreads();  // every warp has read dU
+    const float b0 = s.bet[r0], b1 = s.bet[r1], e0 = s.eg[r0], e1 = s.eg[r1];
+    float db0 = 0.f, db1 = 0.f, dk0 = 0.f, dk1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = nb + j * 8 + cq;
+      st2(s.dy + r0 * LD + c, acc[j][0], acc[j][1]);
+      st2(s.dy + r1 * LD + c, acc[j][2], acc[j][3]);
+      float2 v0 = make_float2(0.f, 0.f), v1 = v0;
+      if (r0 < n) {
+        v0 = ld2(v + (int64_t)(row0 + r0) * g.row_v + (int64_t)h * DV + c);
+        st2(dv + (int64_t)(row0 + r0) * g.row_v + (int64_t)h * DV + c, b0 * acc[j][0], b0 * acc[j][1]);
+      }
+      if (r1 < n) {
+        v1 = ld2(v + (int64_t)(row0 + r1) * g.row_v + (int64_t)h * DV + c);
+        st2(dv + (int64_t)(row0 + r1) * g.row_v + (int64_t)h * DV + c, b1 * acc[j][2], b1 * acc[j][3]);
+      }
+      db0 += acc[j][0] * (v0.x - e0 * ks[j][0]) + acc[j][1] * (v0.y - e0 * ks[j][1]);
+      db1 += acc[j][2] * (v1.x - e1 * ks[j][2]) + acc[j][3] * (v1.y - e1 * ks[j][3]);
+      dk0 += ks[j][0] * acc[j][0] + ks[j][1] * acc[j][1];
+      dk1 += ks[j][2] * acc[j][2] + ks[j][3] * acc[j][3];
+    }
+    db0 = quad_sum(db0), db1 = quad_sum(db1), dk0 = quad_sum(dk0), dk1 = quad_sum(dk1);
+    if ((lane & 3) == 0) {
+      atomicAdd(&s.dbet[r0], db0);
+      atomicAdd(&s.dbet[r1], db1);
+      atomicAdd(&s.dgam[r0], -e0 * b0 * dk0);
+      atomicAdd(&s.dgam[r1], -e1 * b1 * dk1);
+    }
+  }
+  __syncthreads();
+  {  // dA = -dY U^T (s < t), dP = dO U^T (s <= t) -> dKK (into tb), dPE (into pb), dbeta, dgamma
+    float da[4][4], dp[4][4];
+    zero(da);
+    zero(dp);
+    const int nc = (warp >> 2) * 32;
+    warp_mma<4, false, false>(da, s.dy, LD, mt * 16, s.u, LD, nc, DV);
+    warp_mma<4, false, false>(dp, s.dob, LD, mt * 16, s.u, LD, nc, DV);
+    __syncthreads();  // T and P are no longer read
+    float rowb[2] = {0.f, 0.f}, rowg[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float colg[2] = {0.f, 0.f};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = r0 + hf * 8;
+        float dkk[2], dpe[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = nc + j * 8 + cq + e;
+          const float ex = c <= t ? __expf(s.gam[t] - s.gam[c]) : 0.f;
+          float gsum = 0.f;
+          dkk[e] = 0.f;
+          if (c < t) {
+            const float dae = -da[j][2 * hf + e] * ex;
+            const float kkv = s.kk[t * LDF + c];
+            rowb[hf] += dae * kkv;
+            dkk[e] = dae * s.bet[t];
+            gsum += dkk[e] * kkv;
+          }
+          dpe[e] = dp[j][2 * hf + e] * ex;
+          gsum += dpe[e] * s.qk[t * LDF + c];  // dP * P, P = E * QK
+          rowg[hf] += gsum;
+          colg[e] -= gsum;
+        }
+        st2(s.tb + t * LDS + nc + j * 8 + cq, dkk[0], dkk[1]);
+        st2(s.pb + t * LDS + nc + j * 8 + cq, dpe[0], dpe[1]);
+      }
+      colg[0] = col_sum(colg[0]);
+      colg[1] = col_sum(colg[1]);
+      if (gq == 0) {
+        atomicAdd(&s.dgam[nc + j * 8 + cq], colg[0]);
+        atomicAdd(&s.dgam[nc + j * 8 + cq + 1], colg[1]);
+      }
+    }
+    rowb[0] = quad_sum(rowb[0]), rowb[1] = quad_sum(rowb[1]);
+    rowg[0] = quad_sum(rowg[0]), rowg[1] = quad_sum(rowg[1]);
+    if ((lane & 3) == 0) {
+      atomicAdd(&s.dbet[r0], rowb[0]);
+      atomicAdd(&s.dbet[r1], rowb[1]);
+      atomicAdd(&s.dgam[r0], rowg[0]);
+      atomicAdd(&s.dgam[r1], rowg[1]);
+    }
+  }
+  __syncthreads();
+  float dqa[8][4];
+  {  // dQ^ = dPE K^ + e^gamma dO S0^T ; dgamma += e^gamma (Q^ S0) . dO
+    float t2[8][4];
+    zero(dqa);
+    zero(t2);
+    warp_mma<8, false, true>(dqa, s.pb, LDS, mt * 16, s.kh, LD, nb, C);
+    warp_mma<8, false, false>(t2, s.dob, LD, mt * 16, s.sb, LD, nb, DV);
+    const float e0 = s.eg[r0], e1 = s.eg[r1];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      dqa[j][0] += e0 * t2[j][0], dqa[j][1] += e0 * t2[j][1];
+      dqa[j][2] += e1 * t2[j][2], dqa[j][3] += e1 * t2[j][3];
+    }
+    zero(t2);
+    warp_mma<8, false, true>(t2, s.qh, LD, mt * 16, s.sb, LD, nb, DK);
+    float g0 = 0.f, g1 = 0.f, q0 = 0.f, q1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = nb + j * 8 + cq;
+      const float2 o0 = ld2(s.dob + r0 * LD + c), o1 = ld2(s.dob + r1 * LD + c);
+      g0 += t2[j][0] * o0.x + t2[j][1] * o0.y;
+      g1 += t2[j][2] * o1.x + t2[j][3] * o1.y;
+      const float2 x0 = ld2(s.qh + r0 * LD + c), x1 = ld2(s.qh + r1 * LD + c);
+      q0 += x0.x * dqa[j][0] + x0.y * dqa[j][1];
+      q1 += x1.x * dqa[j][2] + x1.y * dqa[j][3];
+    }
+    g0 = quad_sum(g0), g1 = quad_sum(g1), q0 = quad_sum(q0), q1 = quad_sum(q1);
+    if ((lane & 3) == 0) {
+      atomicAdd(&s.dgam[r0], e0 * g0);
+      atomicAdd(&s.dgam[r1], e1 * g1);
+      atomicAdd(&s.dotq[r0], q0);
+      atomicAdd(&s.dotq[r1], q1);
+    }
+  }
+  float dka[8][4];
+  {  // dK^ = -e^gamma beta (dY S0^T) + dKK K^ + dKK^T K^ + dPE^T Q^ + F (U dS_C^T)
+    float t2[8][4];
+    zero(dka);
+    warp_mma<8, false, false>(dka, s.dy, LD, mt * 16, s.sb, LD, nb, DV);
+    const float a0 = -s.eg[r0] * s.bet[r0], a1 = -s.eg[r1] * s.bet[r1];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      dka[j][0] *= a0, dka[j][1] *= a0, dka[j][2] *= a1, dka[j][3] *= a1;
+    }
+    warp_mma<8, false, true>(dka, s.tb, LDS, mt * 16, s.kh, LD, nb, C);
+    warp_mma<8, true, true>(dka, s.tb, LDS, mt * 16, s.kh, LD, nb, C);
+    warp_mma<8, true, true>(dka, s.pb, LDS, mt * 16, s.qh, LD, nb, C);
+    zero(t2);
+    warp_mma<8, false, false>(t2, s.u, LD, mt * 16, s.dsb, LD, nb, DV);
+    const float f0 = s.f[r0], f1 = s.f[r1];
+    float k0 = 0.f, k1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = nb + j * 8 + cq;
+      dka[j][0] += f0 * t2[j][0], dka[j][1] += f0 * t2[j][1];
+      dka[j][2] += f1 * t2[j][2], dka[j][3] += f1 * t2[j][3];
+      const float2 x0 = ld2(s.kh + r0 * LD + c), x1 = ld2(s.kh + r1 * LD + c);
+      k0 += x0.x * dka[j][0] + x0.y * dka[j][1];
+      k1 += x1.x * dka[j][2] + x1.y * dka[j][3];
+    }
+    k0 = quad_sum(k0), k1 = quad_sum(k1);
+    if ((lane & 3) == 0) {
+      atomicAdd(&s.dotk[r0], k0);
+      atomicAdd(&s.dotk[r1], k1);
+    }
+  }
+  __syncthreads();
+  // l2-norm backward: q^ = c q / |q| (c = qscale): dq = (c/|q|) (dq^ - q^ (q^.dq^) / c^2);
+  // k^ = k / |k|: dk = (1/|k|) (dk^ - k^ (k^.dk^)).  qi = c/|q|, ki = 1/|k|.
+  {
+    const float ic2 = 1.f / (qscale * qscale);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = hf ? r1 : r0;
+      if (r >= n) continue;
+      const float qi = s.qi[r], ki = s.ki[r], tq = s.dotq[r] * ic2, tk = s.dotk[r];
+      const int64_t ob = (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = nb + j * 8 + cq;
+        const float2 qr = ld2(q + ob + c), kr = ld2(k + ob + c);
+        const float qh0 = qr.x * qi, qh1 = qr.y * qi, kh0 = kr.x * ki, kh1 = kr.y * ki;
+        st2(dq + ob + c, qi * (dqa[j][2 * hf] - qh0 * tq), qi * (dqa[j][2 * hf + 1] - qh1 * tq));
+        st2(dk + ob + c, ki * (dka[j][2 * hf] - kh0 * tk), ki * (dka[j][2 * hf + 1] - kh1 * tk));
+      }
+    }
+  }
+  if (warp == 0) {  // dg = reverse cumulative sum of dgamma over the chunk; dbeta
+    const int i0 = 2 * lane, i1 = 2 * lane + 1;
+    const float x0 = s.dgam[i0], x1 = s.dgam[i1];
+    float c = x0 + x1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_down_sync(0xffffffff, c, o);
+      if (lane + o < 32) c += y;
+    }
+    if (i0 < n) {
+      dg[(int64_t)(row0 + i0) * g.heads + h] = c;
+      db[(int64_t)(row0 + i0) * g.heads + h] = s.dbet[i0];
+    }
+    if (i1 < n) {
+      dg[(int64_t)(row0 + i1) * g.heads + h] = c - x0;
+      db[(int64_t)(row0 + i1) * g.heads + h] = s.dbet[i1];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------- recurrence
 // Token-by-token decoding: one CTA per (batch row, head); state (dk x dv) fp32 in shared
 // memory; q/k normalised in-kernel.  Returns the outputs and the final state.
-__global__ void __launch_bounds__(kGdnThreads)
-gdn_recurrent_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                     const __nv_bfloat16* __restrict__ v, const float* __restrict__ gg, const float* __restrict__ bb,
-                     const float* __restrict__ init, __nv_bfloat16* __restrict__ out, float* __restrict__ fin, int T,
-                     int H, int dk, int dv, float qscale, bool per_channel) {
+__global__ void __launch_bounds__(NT)
+gdn_recurrent_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+                     const float* __restrict__ gg, const float* __restrict__ bb, const float* __restrict__ init,
+                     bf16* __restrict__ out, float* __restrict__ fin, int T, int H, int dk, int dv, float qscale,
+                     bool per_channel) {
   extern __shared__ float sm[];
-  float* S = sm;                  // [dk][dv]
-  float* kv = S + dk * dv;        // [dk] normalised k
-  float* qv = kv + dk;            // [dk]
-  float* red = qv + dk;           // [2]
-  float* u = red + 32;            // [dv]
+  float* S = sm;            // [dk][dv]
+  float* kv = S + dk * dv;  // [dk] normalised k
+  float* qv = kv + dk;      // [dk]
+  float* red = qv + dk;     // [32]
+  float* u = red + 32;      // [dv]
   const int b = blockIdx.x / H, h = blockIdx.x % H;
   const int tid = threadIdx.x;
   for (int i = tid; i < dk * dv; i += blockDim.x) S[i] = init != nullptr ? init[((int64_t)b * H + h) * dk * dv + i] : 0.f;
@@ -716,7 +1124,6 @@ gdn_recurrent_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     }
     __syncthreads();
     const float beta = bb[row * H + h];
-    // decay, then u = beta (v - S^T k)
     for (int i = tid; i < dk * dv; i += blockDim.x) {
       const int r = i / dv;
       const float dec = per_channel ? __expf(gg[(row * H + h) * dk + r]) : __expf(gg[row * H + h]);
@@ -742,135 +1149,231 @@ gdn_recurrent_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
 }
 
 // ---------------------------------------------------------------------- short conv
-// y[t, c] = silu(sum_i w[c, i] x[t - K + 1 + i, c]) with zero padding before each
-// sequence start (or the initial state for the batch layout).
-__global__ void conv1d_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
-                                  const int* __restrict__ cu, const float* __restrict__ init,
-                                  __nv_bfloat16* __restrict__ y, float* __restrict__ fin, int B, int T, int D, int K,
-                                  int nseq) {
-  const int64_t total = (int64_t)B * T * D;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % D);
-    const int64_t bt = i / D;
-    const int b = (int)(bt / T), t = (int)(bt % T);
-    int start = 0;
-    if (cu != nullptr) {  // packed: B == 1, find the document of t
-      int lo = 0, hi = nseq - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (cu[mid] <= t) lo = mid; else hi = mid - 1;
-      }
-      start = cu[lo];
+// y[t, c] = silu(sum_i w[c, i] x[t - K + 1 + i, c]), inputs before a document start read
+// as 0 (batch layout: the initial state).  One thread owns 2 channels of a 64-token tile
+// and slides a register window over time.
+constexpr int kConvTile = 64;
+
+struct ConvDocs {
+  const int* cu;
+  int nseq;
+  __device__ __forceinline__ void find(int t, int T, int& start, int& end, int& d) const {
+    if (cu == nullptr) {
+      start = 0, end = T, d = 0;
+      return;
     }
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int tt = t - K + 1 + j;
-      float xv = 0.f;
-      if (tt >= start) xv = __bfloat162float(x[((int64_t)b * T + tt) * D + c]);
-      else if (init != nullptr && cu == nullptr) xv = init[((int64_t)b * D + c) * (K - 1) + (tt + K - 1)];
-      acc = fmaf(w[c * K + j], xv, acc);
+    int lo = 0, hi = nseq - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cu[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    y[i] = __float2bfloat16(acc / (1.f + __expf(-acc)));
+    d = lo, start = cu[lo], end = cu[lo + 1];
+  }
+};
+
+template <int K>
+__device__ __forceinline__ void conv_prime(float2 (&win)[K], const bf16* xb, const float* init, int b, int c, int D,
+                                           int t0, int start, bool batch) {
+#pragma unroll
+  for (int i = 0; i < K - 1; ++i) {
+    const int p = t0 - (K - 1) + i;
+    if (p >= start) win[i] = ld2(xb + (int64_t)p * D);
+    else if (init != nullptr && batch)
+      win[i] = make_float2(init[((int64_t)b * D + c) * (K - 1) + (p + K - 1)],
+                           init[((int64_t)b * D + c + 1) * (K - 1) + (p + K - 1)]);
+    else win[i] = make_float2(0.f, 0.f);
   }
 }
 
-__global__ void conv1d_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                  const float* __restrict__ w, const int* __restrict__ cu, const float* __restrict__ init,
-                                  __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int B, int T, int D, int K,
-                                  int nseq) {
-  // thread per (b, t, c): recompute z at t (for dz), and accumulate dx from the K outputs
-  // t' = t .. t+K-1 of the same sequence; dw via atomics.
-  const int64_t total = (int64_t)B * T * D;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % D);
-    const int64_t bt = i / D;
-    const int b = (int)(bt / T), t = (int)(bt % T);
-    int start = 0, end = T;
-    if (cu != nullptr) {
-      int lo = 0, hi = nseq - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (cu[mid] <= t) lo = mid; else hi = mid - 1;
-      }
-      start = cu[lo];
-      end = cu[lo + 1];
+template <int K>
+__global__ void conv1d_fwd_kernel(const bf16* __restrict__ x, const float* __restrict__ w, ConvDocs docs,
+                                  const float* __restrict__ init, bf16* __restrict__ y, int T, int D) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (c >= D) return;
+  const int b = blockIdx.z, t0 = blockIdx.y * kConvTile;
+  if (t0 >= T) return;
+  float w0[K], w1[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    w0[i] = w[c * K + i];
+    w1[i] = w[(c + 1) * K + i];
+  }
+  const bf16* xb = x + (int64_t)b * T * D + c;
+  int start, end, d;
+  docs.find(t0, T, start, end, d);
+  float2 win[K];
+  conv_prime<K>(win, xb, init, b, c, D, t0, start, docs.cu == nullptr);
+  const int t1 = min(T, t0 + kConvTile);
+  for (int t = t0; t < t1; ++t) {
+    if (t >= end) {
+      docs.find(t, T, start, end, d);
+#pragma unroll
+      for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
     }
-    // dz at t
-    float z = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int tt = t - K + 1 + j;
-      float xv = 0.f;
-      if (tt >= start) xv = __bfloat162float(x[((int64_t)b * T + tt) * D + c]);
-      else if (init != nullptr && cu == nullptr) xv = init[((int64_t)b * D + c) * (K - 1) + (tt + K - 1)];
-      z = fmaf(w[c * K + j], xv, z);
+    win[K - 1] = ld2(xb + (int64_t)t * D);
+    float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      z0 = fmaf(w0[i], win[i].x, z0);
+      z1 = fmaf(w1[i], win[i].y, z1);
     }
-    const float s = 1.f / (1.f + __expf(-z));
-    const float dz = __bfloat162float(dy[i]) * s * (1.f + z * (1.f - s));
-    for (int j = 0; j < K; ++j) {
-      const int tt = t - K + 1 + j;
-      float xv = 0.f;
-      if (tt >= start) xv = __bfloat162float(x[((int64_t)b * T + tt) * D + c]);
-      else if (init != nullptr && cu == nullptr) xv = init[((int64_t)b * D + c) * (K - 1) + (tt + K - 1)];
-      atomicAdd(&dw[c * K + j], dz * xv);
-    }
-    // dx[t] = sum_j w[c, j] dz[t + K - 1 - j]  (same sequence): recompute dz there
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int to = t + K - 1 - j;
-      if (to >= end) continue;
-      float zo = 0.f;
-      for (int jj = 0; jj < K; ++jj) {
-        const int tt = to - K + 1 + jj;
-        float xv = 0.f;
-        if (tt >= start) xv = __bfloat162float(x[((int64_t)b * T + tt) * D + c]);
-        else if (init != nullptr && cu == nullptr) xv = init[((int64_t)b * D + c) * (K - 1) + (tt + K - 1)];
-        zo = fmaf(w[c * K + jj], xv, zo);
-      }
-      const float so = 1.f / (1.f + __expf(-zo));
-      const float dzo = __bfloat162float(dy[((int64_t)b * T + to) * D + c]) * so * (1.f + zo * (1.f - so));
-      acc = fmaf(w[c * K + j], dzo, acc);
-    }
-    dx[i] = __float2bfloat16(acc);
+    st2(y + ((int64_t)b * T + t) * D + c, z0 / (1.f + __expf(-z0)), z1 / (1.f + __expf(-z1)));
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
   }
 }
 
-// -------------------------------------------------------------------------------- host
-static int gdn_grid(int64_t work) {
-  int dev, sms;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sms * 16));
+// Backward in one pass over t in [t0, t0 + 64 + K - 1): recompute z, dz = dy silu'(z);
+// dw[c][i] += dz_t x_{t-K+1+i} for the tile's own t; dx_{t'} = sum_i w_i dz_{t'+K-1-i}
+// over t' + K - 1 - i inside the document of t'.  One atomic per (channel, tap) per tile.
+template <int K>
+__global__ void conv1d_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
+                                  ConvDocs docs, const float* __restrict__ init, bf16* __restrict__ dx,
+                                  float* __restrict__ dw, int T, int D) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (c >= D) return;
+  const int b = blockIdx.z, t0 = blockIdx.y * kConvTile;
+  if (t0 >= T) return;
+  float w0[K], w1[K], g0[K], g1[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    w0[i] = w[c * K + i];
+    w1[i] = w[(c + 1) * K + i];
+    g0[i] = g1[i] = 0.f;
+  }
+  const bf16* xb = x + (int64_t)b * T * D + c;
+  const bf16* dyb = dy + (int64_t)b * T * D + c;
+  int start, end, d;
+  docs.find(t0, T, start, end, d);
+  float2 win[K];
+  conv_prime<K>(win, xb, init, b, c, D, t0, start, docs.cu == nullptr);
+  float2 dz[K];  // dz of positions t-K+1 .. t
+  int dd[K];     // their document (-1: none)
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    dz[i] = make_float2(0.f, 0.f);
+    dd[i] = -1;
+  }
+  const int tend = t0 + kConvTile + K - 1;
+  for (int t = t0; t < tend; ++t) {
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+      dz[i] = dz[i + 1];
+      dd[i] = dd[i + 1];
+    }
+    if (t < T) {
+      if (t >= end) {
+        docs.find(t, T, start, end, d);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
+      }
+      win[K - 1] = ld2(xb + (int64_t)t * D);
+      float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        z0 = fmaf(w0[i], win[i].x, z0);
+        z1 = fmaf(w1[i], win[i].y, z1);
+      }
+      const float2 gy = ld2(dyb + (int64_t)t * D);
+      const float s0 = 1.f / (1.f + __expf(-z0)), s1 = 1.f / (1.f + __expf(-z1));
+      dz[K - 1] = make_float2(gy.x * s0 * (1.f + z0 * (1.f - s0)), gy.y * s1 * (1.f + z1 * (1.f - s1)));
+      dd[K - 1] = d;
+      if (t < t0 + kConvTile) {
+#pragma unroll
+        for (int i = 0; i < K; ++i) {
+          g0[i] = fmaf(dz[K - 1].x, win[i].x, g0[i]);
+          g1[i] = fmaf(dz[K - 1].y, win[i].y, g1[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
+    } else {
+      dz[K - 1] = make_float2(0.f, 0.f);
+      dd[K - 1] = -1;
+    }
+    const int tp = t - (K - 1);  // the dx position completed at this step: dz[m] is tp + m
+    if (tp >= t0 && tp < T && tp < t0 + kConvTile) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < K; ++m) {
+        if (dd[m] == dd[0]) {
+          a0 = fmaf(w0[K - 1 - m], dz[m].x, a0);
+          a1 = fmaf(w1[K - 1 - m], dz[m].y, a1);
+        }
+      }
+      st2(dx + ((int64_t)b * T + tp) * D + c, a0, a1);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    atomicAdd(&dw[c * K + i], g0[i]);
+    atomicAdd(&dw[(c + 1) * K + i], g1[i]);
+  }
+}
+
+}  // namespace gdnk
+
+// ------------------------------------------------------------------------------ host
+using gdnk::bf16;
+
+template <int K>
+static void conv_launch(bool fwd, const torch::Tensor& x, const float* w, gdnk::ConvDocs docs, const float* init,
+                        const torch::Tensor& y_or_dy, torch::Tensor* dx, float* dw) {
+  const int B = x.size(0), T = x.size(1), D = x.size(2);
+  dim3 grid((D / 2 + 127) / 128, (T + gdnk::kConvTile - 1) / gdnk::kConvTile, B);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (fwd)
+    gdnk::conv1d_fwd_kernel<K><<<grid, 128, 0, st>>>((const bf16*)x.data_ptr(), w, docs, init,
+                                                     (bf16*)y_or_dy.data_ptr(), T, D);
+  else
+    gdnk::conv1d_bwd_kernel<K><<<grid, 128, 0, st>>>((const bf16*)y_or_dy.data_ptr(), (const bf16*)x.data_ptr(), w,
+                                                     docs, init, (bf16*)dx->data_ptr(), dw, T, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static void conv_dispatch(int K, bool fwd, const torch::Tensor& x, const float* w, gdnk::ConvDocs docs,
+                          const float* init, const torch::Tensor& y_or_dy, torch::Tensor* dx, float* dw) {
+  switch (K) {
+    case 2: conv_launch<2>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    case 3: conv_launch<3>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    case 4: conv_launch<4>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    case 5: conv_launch<5>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    case 6: conv_launch<6>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    case 8: conv_launch<8>(fwd, x, w, docs, init, y_or_dy, dx, dw); break;
+    default: TORCH_CHECK(false, "causal_conv1d: kernel width ", K, " not instantiated (2-6, 8)");
+  }
+}
+
+static void conv_check(const torch::Tensor& x, const c10::optional<torch::Tensor>& cu) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3, "causal_conv1d: bf16 (B, T, D)");
+  TORCH_CHECK(x.size(2) % 2 == 0, "causal_conv1d: even channel count");
+  TORCH_CHECK(!cu.has_value() || (x.size(0) == 1 && cu->scalar_type() == at::kInt),
+              "causal_conv1d: packed layout needs batch 1 and int32 cu_seqlens");
 }
 
 std::vector<torch::Tensor> conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> cu,
                                       c10::optional<torch::Tensor> init) {
   c10::cuda::CUDAGuard guard(x.device());
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3, "conv1d: bf16 (B, T, D)");
+  conv_check(x, cu);
   const int B = x.size(0), T = x.size(1), D = x.size(2), K = w.size(-1);
   auto wf = w.reshape({D, K}).to(at::kFloat).contiguous();
   auto y = torch::empty_like(x);
   const int nseq = cu.has_value() ? cu->numel() - 1 : B;
-  auto fin = torch::zeros({nseq, D, K - 1}, x.options().dtype(at::kFloat));
-  const float* ip = nullptr;
   torch::Tensor init_f;
-  if (init.has_value()) {
-    init_f = init->to(at::kFloat).contiguous();
-    ip = init_f.data_ptr<float>();
-  }
-  if (x.numel() > 0) {
-    conv1d_fwd_kernel<<<gdn_grid(x.numel()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        (const __nv_bfloat16*)x.data_ptr(), wf.data_ptr<float>(), cu.has_value() ? cu->data_ptr<int>() : nullptr, ip,
-        (__nv_bfloat16*)y.data_ptr(), nullptr, B, T, D, K, nseq);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
+  if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
+  if (x.numel() > 0)
+    conv_dispatch(K, true, x, wf.data_ptr<float>(),
+                  gdnk::ConvDocs{cu.has_value() ? cu->data_ptr<int>() : nullptr, nseq},
+                  init.has_value() ? init_f.data_ptr<float>() : nullptr, y, nullptr, nullptr);
   // final states (the last K-1 inputs of every sequence), assembled on the device
+  auto fin = torch::zeros({nseq, D, K - 1}, x.options().dtype(at::kFloat));
   if (K > 1) {
     if (cu.has_value()) {
       auto cuc = cu->to(at::kLong);
       auto ends = cuc.slice(0, 1);
+      auto starts = cuc.slice(0, 0, nseq);
       for (int j = 0; j < K - 1; ++j) {
         auto idx = ends - (K - 1) + j;
-        auto starts = cuc.slice(0, 0, nseq);
         auto valid = idx.ge(starts);
         auto rows = x[0].index_select(0, idx.clamp_min(0)).to(at::kFloat) * valid.unsqueeze(1).to(at::kFloat);
         fin.select(2, j).copy_(rows);
@@ -889,153 +1392,187 @@ std::vector<torch::Tensor> conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::opt
 std::vector<torch::Tensor> conv1d_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w,
                                       c10::optional<torch::Tensor> cu, c10::optional<torch::Tensor> init) {
   c10::cuda::CUDAGuard guard(x.device());
-  const int B = x.size(0), T = x.size(1), D = x.size(2), K = w.size(-1);
+  conv_check(x, cu);
+  const int B = x.size(0), D = x.size(2), K = w.size(-1);
   auto wf = w.reshape({D, K}).to(at::kFloat).contiguous();
   auto dx = torch::empty_like(x);
   auto dw = torch::zeros({D, K}, x.options().dtype(at::kFloat));
   const int nseq = cu.has_value() ? cu->numel() - 1 : B;
   torch::Tensor init_f;
-  const float* ip = nullptr;
-  if (init.has_value()) {
-    init_f = init->to(at::kFloat).contiguous();
-    ip = init_f.data_ptr<float>();
-  }
+  if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
   auto dyc = dy.to(at::kBFloat16).contiguous();
-  if (x.numel() > 0) {
-    conv1d_bwd_kernel<<<gdn_grid(x.numel()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        (const __nv_bfloat16*)dyc.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), wf.data_ptr<float>(),
-        cu.has_value() ? cu->data_ptr<int>() : nullptr, ip, (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), B, T,
-        D, K, nseq);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
+  if (x.numel() > 0)
+    conv_dispatch(K, false, x, wf.data_ptr<float>(),
+                  gdnk::ConvDocs{cu.has_value() ? cu->data_ptr<int>() : nullptr, nseq},
+                  init.has_value() ? init_f.data_ptr<float>() : nullptr, dyc, &dx, dw.data_ptr<float>());
   return {dx, dw.reshape(w.sizes())};
 }
 
-// Chunk offsets are computed on the device (no host synchronisation); total_chunks is the
-// host-side upper bound T_total / C + num_seqs used to size the saved-state buffer.
-static GdnGeom make_geom(const torch::Tensor& q, const torch::Tensor& v, const c10::optional<torch::Tensor>& cu,
-                         torch::Tensor& chunk_off_dev, int& total_chunks) {
-  GdnGeom g{};
+// Chunk offsets are computed on the device (no host synchronisation); `bound` is the
+// host-side upper bound T_total / 64 + num_seqs on the number of chunks, which sizes the
+// per-chunk buffers and the chunk-parallel grids (CTAs past the real count exit).
+static gdnk::Geo make_geo(const torch::Tensor& q, const torch::Tensor& v, const c10::optional<torch::Tensor>& cu,
+                          torch::Tensor& chunk_off, torch::Tensor& order, int& bound) {
+  gdnk::Geo g{};
   const int B = q.size(0), T = q.size(1), H = q.size(2);
   g.heads = H;
+  g.rows = (int64_t)B * T;
   g.row_q = (int64_t)H * q.size(3);
   g.row_v = (int64_t)H * v.size(3);
-  g.dv = v.size(3);
   if (cu.has_value()) {
     TORCH_CHECK(B == 1 && cu->scalar_type() == at::kInt, "gdn: packed layout needs batch 1 and int32 cu_seqlens");
     const int n = cu->numel() - 1;
     g.num_seqs = n;
     g.cu = cu->data_ptr<int>();
     auto lens = cu->slice(0, 1) - cu->slice(0, 0, n);
-    auto nch = torch::floor_divide(lens + (kC - 1), kC);
-    chunk_off_dev = torch::cat({torch::zeros({1}, cu->options()), torch::cumsum(nch, 0, at::kInt)}).contiguous();
-    total_chunks = (int)(((int64_t)T + kC - 1) / kC + n);
+    auto nch = torch::floor_divide(lens + (gdnk::C - 1), gdnk::C);
+    chunk_off = torch::cat({torch::zeros({1}, cu->options()), torch::cumsum(nch, 0, at::kInt)}).contiguous();
+    order = torch::argsort(lens, /*stable=*/true, /*dim=*/0, /*descending=*/true).to(at::kInt).contiguous();
+    bound = (int)(((int64_t)T + gdnk::C - 1) / gdnk::C + n);
   } else {
     g.num_seqs = B;
     g.seq_len = T;
-    const int per = (T + kC - 1) / kC;
-    chunk_off_dev = (torch::arange(B + 1, q.options().dtype(at::kInt)) * per).contiguous();
-    total_chunks = B * per;
+    const int per = (T + gdnk::C - 1) / gdnk::C;
+    chunk_off = (torch::arange(B + 1, q.options().dtype(at::kInt)) * per).contiguous();
+    order = torch::arange(B, q.options().dtype(at::kInt));
+    bound = B * per;
   }
-  g.chunk_off = chunk_off_dev.data_ptr<int>();
+  g.chunk_off = chunk_off.data_ptr<int>();
+  g.order = order.data_ptr<int>();
   return g;
 }
 
+template <typename Kern>
+static void set_smem(Kern kern, size_t bytes) {
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+static void gdn_check(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const char* who) {
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == gdnk::DK && k.sizes() == q.sizes() && v.size(3) == gdnk::DV &&
+                  v.size(2) == q.size(2) && v.size(1) == q.size(1),
+              who, ": head_k_dim 128, head_v_dim 128, as many value heads as key heads");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+              who, ": bf16 q/k/v");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), who, ": contiguous q/k/v");
+}
+
+// Returns (o, final state, saved...) with saved = [states, u, p, w, gcum, kinv, qinv].
 std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor gg,
                                                torch::Tensor beta, c10::optional<torch::Tensor> init,
                                                c10::optional<torch::Tensor> cu, bool per_channel) {
   c10::cuda::CUDAGuard guard(q.device());
-  TORCH_CHECK(!per_channel, "gdn_chunk_fwd: per-channel (KDA) decay runs on the chunked PyTorch statement");
-  TORCH_CHECK(q.size(3) == kDK && v.size(3) == 2 * kDVH && v.size(2) == q.size(2),
-              "gdn_chunk_fwd: head_k_dim 128, head_v_dim 128, as many value heads as key heads");
-  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "gdn_chunk_fwd: contiguous q/k/v");
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
-              "gdn_chunk_fwd: bf16 q/k/v");
-  torch::Tensor chunk_off;
-  int total_chunks = 0;
-  GdnGeom g = make_geom(q, v, cu, chunk_off, total_chunks);
+  TORCH_CHECK(!per_channel, "gdn_chunk_fwd: per-channel (KDA) decay is not handled by the chunk kernels");
+  gdn_check(q, k, v, "gdn_chunk_fwd");
+  torch::Tensor chunk_off, order;
+  int bound = 0;
+  gdnk::Geo g = make_geo(q, v, cu, chunk_off, order, bound);
   const int H = g.heads;
+  const int64_t rows = (int64_t)q.size(0) * q.size(1);
+  auto f32 = q.options().dtype(at::kFloat);
   auto out = torch::empty_like(v);
-  auto states = torch::empty({std::max(total_chunks, 1), H, kDK, g.dv}, q.options().dtype(at::kFloat));
-  auto fin = torch::empty({g.num_seqs, H, kDK, g.dv}, q.options().dtype(at::kFloat));
+  const int nb = std::max(bound, 1);
+  auto states = torch::empty({nb, H, gdnk::DK, gdnk::DV}, q.options());
+  auto w = torch::empty({nb, H, gdnk::C, gdnk::DK}, q.options());
+  auto u = torch::empty({nb, H, gdnk::C, gdnk::DV}, q.options());
+  auto p = torch::empty({nb, H, gdnk::C, gdnk::C}, q.options());
+  auto gcum = torch::empty({H, rows}, f32);  // head-major per-token scalars
+  auto kinv = torch::empty({H, rows}, f32);
+  auto qinv = torch::empty({H, rows}, f32);
+  auto fin = torch::empty({g.num_seqs, H, gdnk::DK, gdnk::DV}, f32);
   auto gf = gg.to(at::kFloat).contiguous();
   auto bf = beta.to(at::kFloat).contiguous();
   torch::Tensor init_f;
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
-  const int smem = FwdSm::TOTAL * 4;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set_smem(gdnk::gdn_prep_kernel, sizeof(gdnk::PrepSm));
+    set_smem(gdnk::gdn_state_kernel, sizeof(gdnk::StateSm));
+    set_smem(gdnk::gdn_out_kernel, sizeof(gdnk::OutSm));
     configured = true;
   }
-  const float qscale = 1.f / std::sqrt((float)kDK);
-  if (g.num_seqs > 0 && q.numel() > 0) {
-    gdn_chunk_fwd_kernel<<<g.num_seqs * H * 2, kGdnThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
-        g, (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(),
-        gf.data_ptr<float>(), bf.data_ptr<float>(), init.has_value() ? init_f.data_ptr<float>() : nullptr,
-        (__nv_bfloat16*)out.data_ptr(), states.data_ptr<float>(), fin.data_ptr<float>(), qscale);
+  const float qscale = 1.f / std::sqrt((float)gdnk::DK);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (rows > 0 && g.num_seqs > 0) {
+    gdnk::gdn_prep_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::PrepSm), st>>>(
+        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), gf.data_ptr<float>(),
+        bf.data_ptr<float>(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(),
+        (bf16*)w.data_ptr(), (bf16*)u.data_ptr(), qscale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdnk::gdn_state_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::StateSm), st>>>(
+        g, (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), (const bf16*)w.data_ptr(),
+        (bf16*)u.data_ptr(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)states.data_ptr(),
+        fin.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdnk::gdn_out_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::OutSm), st>>>(
+        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(),
+        qinv.data_ptr<float>(), (const bf16*)u.data_ptr(), (const bf16*)states.data_ptr(), (bf16*)p.data_ptr(),
+        (bf16*)out.data_ptr());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    fin.zero_();
   }
-  return {out, fin, states};
+  return {out, fin, states, u, p, w, gcum, kinv, qinv};
 }
 
+// Returns (dq, dk, dv, dg, dbeta, dinit).
 std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                          torch::Tensor gg, torch::Tensor beta, c10::optional<torch::Tensor> init,
                                          c10::optional<torch::Tensor> cu, std::vector<torch::Tensor> saved,
                                          c10::optional<torch::Tensor> dfinal, bool per_channel) {
   c10::cuda::CUDAGuard guard(q.device());
-  TORCH_CHECK(!per_channel, "gdn_chunk_bwd: per-channel decay unsupported");
-  torch::Tensor chunk_off;
-  int total_chunks = 0;
-  GdnGeom g = make_geom(q, v, cu, chunk_off, total_chunks);
+  TORCH_CHECK(!per_channel, "gdn_chunk_bwd: per-channel decay is not handled by the chunk kernels");
+  TORCH_CHECK(saved.size() == 7, "gdn_chunk_bwd: expects the 7 saved tensors of gdn_chunk_fwd");
+  gdn_check(q, k, v, "gdn_chunk_bwd");
+  torch::Tensor chunk_off, order;
+  int bound = 0;
+  gdnk::Geo g = make_geo(q, v, cu, chunk_off, order, bound);
   const int H = g.heads;
-  auto states = saved[0];
-  auto gf = gg.to(at::kFloat).contiguous();
+  auto &states = saved[0], &u = saved[1], &p = saved[2], &w = saved[3], &gcum = saved[4], &kinv = saved[5],
+       &qinv = saved[6];
   auto bf = beta.to(at::kFloat).contiguous();
   auto doc = dout.to(at::kBFloat16).contiguous();
-  const int64_t rows = (int64_t)q.size(0) * q.size(1);
-  auto dq_acc = torch::zeros({rows, H, kDK}, q.options().dtype(at::kFloat));
-  auto dk_acc = torch::zeros({rows, H, kDK}, q.options().dtype(at::kFloat));
-  auto dv = torch::empty_like(v);
-  auto dgam = torch::zeros({rows, H}, q.options().dtype(at::kFloat));
-  auto db = torch::zeros({rows, H}, q.options().dtype(at::kFloat));
-  auto dinit = torch::empty({g.num_seqs, H, kDK, g.dv}, q.options().dtype(at::kFloat));
+  auto f32 = q.options().dtype(at::kFloat);
+  auto dstates = torch::empty_like(states);
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  auto dg = torch::empty(gg.sizes(), f32);
+  auto db = torch::empty(beta.sizes(), f32);
+  auto dinit = torch::empty({g.num_seqs, H, gdnk::DK, gdnk::DV}, f32);
   torch::Tensor dfin_f;
   if (dfinal.has_value()) dfin_f = dfinal->to(at::kFloat).contiguous();
-  const int smem = BwdSm::TOTAL * 4;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set_smem(gdnk::gdn_dstate_kernel, sizeof(gdnk::DStateSm));
+    set_smem(gdnk::gdn_grad_kernel, sizeof(gdnk::GradSm));
     configured = true;
   }
-  const float qscale = 1.f / std::sqrt((float)kDK);
+  const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (g.num_seqs > 0 && rows > 0) {
-    gdn_chunk_bwd_kernel<<<g.num_seqs * H * 2, kGdnThreads, smem, st>>>(
-        g, (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(),
-        gf.data_ptr<float>(), bf.data_ptr<float>(), states.data_ptr<float>(), (const __nv_bfloat16*)doc.data_ptr(),
-        dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, dq_acc.data_ptr<float>(), dk_acc.data_ptr<float>(), (__nv_bfloat16*)dv.data_ptr(),
-        dgam.data_ptr<float>(), db.data_ptr<float>(), dinit.data_ptr<float>(), qscale);
+  const int64_t rows = (int64_t)q.size(0) * q.size(1);
+  if (rows > 0 && g.num_seqs > 0) {
+    gdnk::gdn_dstate_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::DStateSm), st>>>(
+        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(),
+        qinv.data_ptr<float>(), (const bf16*)w.data_ptr(), (const bf16*)p.data_ptr(), (const bf16*)doc.data_ptr(),
+        dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, (bf16*)dstates.data_ptr(), dinit.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
-  auto dq = torch::empty_like(q), dk = torch::empty_like(k);
-  auto dg = torch::empty_like(dgam);
-  if (rows > 0) {
-    gdn_post_bwd_kernel<<<(unsigned)((rows * H * 32 + 255) / 256), 256, 0, st>>>(
-        g, (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), dq_acc.data_ptr<float>(),
-        dk_acc.data_ptr<float>(), (__nv_bfloat16*)dq.data_ptr(), (__nv_bfloat16*)dk.data_ptr(), rows, qscale);
-    gdn_dg_kernel<<<(unsigned)(((int64_t)total_chunks * H + 255) / 256), 256, 0, st>>>(g, dgam.data_ptr<float>(),
-                                                                                    dg.data_ptr<float>());
+    gdnk::gdn_grad_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::GradSm), st>>>(
+        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), bf.data_ptr<float>(),
+        gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(), (const bf16*)u.data_ptr(),
+        (const bf16*)states.data_ptr(), (const bf16*)dstates.data_ptr(), (const bf16*)doc.data_ptr(), (bf16*)dq.data_ptr(),
+        (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(), dg.data_ptr<float>(), db.data_ptr<float>(), qscale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    dinit.zero_();
   }
-  return {dq, dk, dv, dg.view(gg.sizes()), db.view(beta.sizes()), dinit};
+  return {dq, dk, dv, dg, db, dinit};
 }
 
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor gg,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel) {
   c10::cuda::CUDAGuard guard(q.device());
   const int B = q.size(0), T = q.size(1), H = q.size(2), dk = q.size(3), dv = v.size(3);
-  auto out = torch::empty_like(v);
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && v.size(2) == H, "gdn_recurrent: bf16, as many value heads as key heads");
+  auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+  auto out = torch::empty_like(vc);
   auto fin = torch::empty({B, H, dk, dv}, q.options().dtype(at::kFloat));
   auto gf = gg.to(at::kFloat).contiguous();
   auto bf = beta.to(at::kFloat).contiguous();
@@ -1045,13 +1582,13 @@ std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch
   TORCH_CHECK(smem <= 227 * 1024, "gdn_recurrent: state too large");
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_recurrent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    set_smem(gdnk::gdn_recurrent_kernel, 227 * 1024);
     configured = true;
   }
-  gdn_recurrent_kernel<<<B * H, kGdnThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)k.data_ptr(), (const __nv_bfloat16*)v.data_ptr(),
-      gf.data_ptr<float>(), bf.data_ptr<float>(), init.has_value() ? init_f.data_ptr<float>() : nullptr,
-      (__nv_bfloat16*)out.data_ptr(), fin.data_ptr<float>(), T, H, dk, dv, 1.f / std::sqrt((float)dk), per_channel);
+  gdnk::gdn_recurrent_kernel<<<B * H, gdnk::NT, smem, at::cuda::getCurrentCUDAStream()>>>(
+      (const bf16*)qc.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), gf.data_ptr<float>(),
+      bf.data_ptr<float>(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)out.data_ptr(),
+      fin.data_ptr<float>(), T, H, dk, dv, 1.f / std::sqrt((float)dk), per_channel);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {out, fin};
 }

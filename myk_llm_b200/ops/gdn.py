@@ -64,14 +64,14 @@ def causal_conv1d(x, weight, cu_seqlens=None, initial_state=None, return_final_s
 class _DeltaRule(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, g, beta, init, cu):
-        o, final, states = ext().gdn_chunk_fwd(q, k, v, g, beta, init, cu, False)
-        ctx.save_for_backward(q, k, v, g, beta, init, cu, states)
+        o, final, *saved = ext().gdn_chunk_fwd(q, k, v, g, beta, init, cu, False)
+        ctx.save_for_backward(q, k, v, g, beta, init, cu, *saved)
         return o, final
 
     @staticmethod
     def backward(ctx, do, dfinal):
-        q, k, v, g, beta, init, cu, states = ctx.saved_tensors
-        dq, dk, dv, dg, db, dinit = ext().gdn_chunk_bwd(do.contiguous(), q, k, v, g, beta, init, cu, [states],
+        q, k, v, g, beta, init, cu, *saved = ctx.saved_tensors
+        dq, dk, dv, dg, db, dinit = ext().gdn_chunk_bwd(do.contiguous(), q, k, v, g, beta, init, cu, list(saved),
                                                         dfinal, False)
         return dq, dk, dv, dg, db, (dinit if ctx.needs_input_grad[5] else None), None
 
