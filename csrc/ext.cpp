@@ -53,6 +53,12 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
                                          c10::optional<torch::Tensor> dfinal, bool per_channel);
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
+// ngram.cu
+torch::Tensor ngram_stage(torch::Tensor ids, torch::Tensor W, torch::Tensor M, torch::Tensor V, torch::Tensor last,
+                          int64_t step, double lr, double wd, double b1, double b2, double eps, bool rowwise,
+                          bool catch_up, bool write_back);
+void ngram_adam(torch::Tensor ids, torch::Tensor grad, torch::Tensor W, torch::Tensor M, torch::Tensor V,
+                torch::Tensor last, int64_t step, double lr, double wd, double b1, double b2, double eps, bool rowwise);
 // comm.cu
 void peer_barrier(torch::Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch);
 void dp_reduce_sumsq(torch::Tensor grad_ptrs, int64_t rank, int64_t world, torch::Tensor offsets,
@@ -94,6 +100,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_fwd", &mykb::gdn_chunk_fwd_entry);
   m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
+  m.def("ngram_stage", &mykb::ngram_stage);
+  m.def("ngram_adam", &mykb::ngram_adam);
   m.def("peer_barrier", &mykb::peer_barrier);
   m.def("dp_reduce_sumsq", &mykb::dp_reduce_sumsq);
   m.def("dp_adamw_allgather", &mykb::dp_adamw_allgather);
