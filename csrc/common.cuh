@@ -28,6 +28,8 @@ enum StatusCode : int {
 
 // Per-device status word (allocated on first use, see status.cu).
 int* device_status();
+// zeroed per-device tickets for last-CTA reductions (status.cu)
+int* ticket_region(int count);
 
 // A wait gives up after kWaitNs of wall time (read from %globaltimer): far beyond any
 // legitimate wait in these kernels, short enough that a broken pipeline returns within

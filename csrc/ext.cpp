@@ -53,6 +53,13 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
                                          c10::optional<torch::Tensor> dfinal, bool per_channel);
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
+// attention_decode.cu
+torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor seqused,
+                        double scale, int64_t left, int64_t right);
+void kv_append(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor k, torch::Tensor v,
+               torch::Tensor seqlens);
+// gemm_skinny.cu
+void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d);
 // ngram.cu
 torch::Tensor ngram_stage(torch::Tensor ids, torch::Tensor W, torch::Tensor M, torch::Tensor V, torch::Tensor last,
                           int64_t step, double lr, double wd, double b1, double b2, double eps, bool rowwise,
@@ -101,6 +108,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
   m.def("ngram_stage", &mykb::ngram_stage);
+  m.def("gemm_skinny", &mykb::gemm_skinny);
+  m.def("fa_decode", &mykb::fa_decode);
+  m.def("kv_append", &mykb::kv_append);
   m.def("ngram_adam", &mykb::ngram_adam);
   m.def("peer_barrier", &mykb::peer_barrier);
   m.def("dp_reduce_sumsq", &mykb::dp_reduce_sumsq);

@@ -27,4 +27,25 @@ int64_t take_status() {
   return h;
 }
 
+// Split-K / split-KV kernels count arriving CTAs on "tickets" that the last CTA resets to
+// zero, so one zeroed pool per device serves every launch.  Each launch takes the next
+// `count` tickets of a ring of kTicketPool; a region comes round again only after
+// kTicketPool tickets of later launches, long after its own launch has finished.
+int* ticket_region(int count) {
+  constexpr int kTicketPool = 1 << 20;
+  static int* pools[64] = {nullptr};
+  static int next[64] = {0};
+  TORCH_CHECK(count > 0 && count <= kTicketPool / 4, "ticket_region: too many tickets (", count, ")");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (pools[dev] == nullptr) {
+    C10_CUDA_CHECK(cudaMalloc(&pools[dev], sizeof(int) * kTicketPool));
+    C10_CUDA_CHECK(cudaMemset(pools[dev], 0, sizeof(int) * kTicketPool));
+  }
+  if (next[dev] + count > kTicketPool) next[dev] = 0;
+  int* r = pools[dev] + next[dev];
+  next[dev] += count;
+  return r;
+}
+
 }  // namespace mykb

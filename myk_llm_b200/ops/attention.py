@@ -23,6 +23,9 @@ from . import reference as ref
 from ._ext import ext
 
 SUPPORTED_HEAD_DIMS = (64, 128)
+# KV-cache steps whose (query heads per KV head) x new tokens fit one 16-row MMA tile take
+# the split-KV decode kernel (keys spread over CTAs, partials merged by the last one).
+DECODE_MAX_ROWS = 16
 
 
 def _window(causal: bool, window_size: tuple[int, int]) -> tuple[int, int]:
@@ -97,19 +100,26 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, *, cache_seqlen
     caller advances ``cache_seqlens``.  Forward only."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     left, right = _window(causal, window_size)
-    seqused = cache_seqlens.to(torch.int32)
+    seqused = cache_seqlens if cache_seqlens.dtype == torch.int32 else cache_seqlens.to(torch.int32)
     if k is not None and v is not None:
         bsz, new = k.shape[:2]
-        rows = torch.arange(bsz, device=k.device)[:, None]
-        cols = cache_seqlens.long()[:, None] + torch.arange(new, device=k.device)
-        k_cache[rows, cols] = k
-        v_cache[rows, cols] = v
+        if k.is_cuda and k_cache.is_contiguous() and v_cache.is_contiguous():
+            ext().kv_append(k_cache, v_cache, k, v, seqused)
+        else:
+            rows = torch.arange(bsz, device=k.device)[:, None]
+            cols = cache_seqlens.long()[:, None] + torch.arange(new, device=k.device)
+            k_cache[rows, cols] = k
+            v_cache[rows, cols] = v
         seqused = seqused + new
     if not q.is_cuda:
         out, _ = ref.attention_ref(q, k_cache, v_cache, causal=causal, window=(left, right), softmax_scale=scale,
                                    seqused_k=seqused)
         return out
     _check(q, k_cache, v_cache)
-    o, _ = ext().fa_fwd(_inner(q), k_cache, v_cache, None, None, seqused, q.shape[1], k_cache.shape[1], float(scale),
+    q = _inner(q)
+    if (q.shape[2] // k_cache.shape[2]) * q.shape[1] <= DECODE_MAX_ROWS and k_cache.is_contiguous() \
+            and v_cache.is_contiguous() and q.stride(2) % 8 == 0 and q.stride(1) % 8 == 0:
+        return ext().fa_decode(q, k_cache, v_cache, seqused, float(scale), left, right)
+    o, _ = ext().fa_fwd(q, k_cache, v_cache, None, None, seqused, q.shape[1], k_cache.shape[1], float(scale),
                         left, right)
     return o

@@ -54,6 +54,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_major: str = "k", b_major: str =
 
 
 _WEIGHT_EPOCH = [0]
+# Forward linears with at most this many token rows (decode steps, small batches) use the
+# split-K skinny GEMM, which streams the weight with every SM instead of a few output tiles.
+SKINNY_MAX_ROWS = 64
 
 
 def invalidate_weight_cache() -> None:
@@ -89,7 +92,11 @@ class _Linear(torch.autograd.Function):
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         wb = bf16_weight(w)
-        y = gemm(x2, wb)
+        if x2.shape[0] <= SKINNY_MAX_ROWS and k % 8 == 0:
+            y = torch.empty(x2.shape[0], wb.shape[0], dtype=torch.bfloat16, device=x2.device)
+            ext().gemm_skinny(x2, wb, y)
+        else:
+            y = gemm(x2, wb)
         ctx.save_for_backward(x2, wb)
         ctx.w = w
         ctx.x_shape, ctx.x_dtype = x.shape, x.dtype

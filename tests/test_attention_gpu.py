@@ -125,3 +125,31 @@ def test_flash_attn_with_kvcache():
         vv = vc[i:i + 1, : n + 3].float()
         ref, _ = attention_ref(q[i:i + 1].float(), kk, vv, causal=True, window=(-1, 0))
         _close(out[i:i + 1], ref)
+
+
+@pytest.mark.parametrize("d,h,kvh,new", [(64, 16, 4, 3), (128, 16, 4, 1), (128, 8, 8, 3), (64, 4, 1, 4)])
+@pytest.mark.parametrize("left", [-1, 100])
+def test_split_kv_decode_matches_reference(d, h, kvh, new, left):
+    """The split-KV decode kernel (taken by flash_attn_with_kvcache for decode-sized
+    steps) against the fp32 reference, including ragged lengths and a sliding window."""
+    from myk_llm_b200.ops import ext, flash_attn_with_kvcache
+    from myk_llm_b200.ops.reference import attention_ref
+
+    torch.manual_seed(5)
+    b, cap = 4, 2400
+    kc = torch.randn(b, cap, kvh, d, device="cuda").bfloat16()
+    vc = torch.randn(b, cap, kvh, d, device="cuda").bfloat16()
+    lens = torch.tensor([0, 70, 1000, 2300], device="cuda", dtype=torch.int32)
+    q = torch.randn(b, new, h, d, device="cuda", dtype=torch.bfloat16)
+    kn = torch.randn(b, new, kvh, d, device="cuda", dtype=torch.bfloat16)
+    vn = torch.randn(b, new, kvh, d, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):  # twice: the merge tickets must be left at zero
+        kc2, vc2 = kc.clone(), vc.clone()
+        out = flash_attn_with_kvcache(q, kc2, vc2, kn, vn, cache_seqlens=lens, causal=True, window_size=(left, 0))
+        torch.cuda.synchronize()
+        for i, n in enumerate(lens.tolist()):
+            assert torch.equal(kc2[i, n:n + new], kn[i]) and torch.equal(vc2[i, n:n + new], vn[i])
+            ref, _ = attention_ref(q[i:i + 1].float(), kc2[i:i + 1, :n + new].float(), vc2[i:i + 1, :n + new].float(),
+                                   causal=True, window=(left, 0))
+            _close(out[i:i + 1], ref)
+    assert ext().take_status() == 0

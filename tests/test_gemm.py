@@ -85,3 +85,30 @@ def test_linear_autograd_matches_reference():
     _close(y, yr)
     _close(x.grad, xr.grad, rel=3e-2)
     _close(w.grad, wr.grad, rel=3e-2)
+
+
+@pytest.mark.parametrize("m", [1, 3, 17, 64])
+@pytest.mark.parametrize("nk", [(64, 64), (1000, 1000), (1536, 1024), (1024, 2816), (65536, 256)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_skinny_gemm(m, nk, out_dtype):
+    """Split-K skinny GEMM (decode rows) against fp32, twice in a row (the split-K tickets
+    must be left at zero)."""
+    from myk_llm_b200.ops import ext
+
+    n, k = nk
+    a, b = _mk(m, n, k, False, False)
+    ref = _ref(a, b, False, False)
+    for _ in range(2):
+        out = torch.empty(m, n, dtype=out_dtype, device="cuda")
+        ext().gemm_skinny(a, b, out)
+        torch.cuda.synchronize()
+        _close(out, ref)
+
+
+def test_linear_uses_skinny_rows():
+    from myk_llm_b200.ops import linear
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(2, 3, 512, device="cuda", generator=g).bfloat16()
+    w = torch.randn(768, 512, device="cuda", generator=g)
+    _close(linear(x, w), x.float() @ w.bfloat16().float().t())
