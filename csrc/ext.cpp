@@ -58,6 +58,10 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
                         double scale, int64_t left, int64_t right);
 void kv_append(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor k, torch::Tensor v,
                torch::Tensor seqlens);
+// mxfp8.cu
+std::vector<torch::Tensor> mx_quantize(torch::Tensor x, bool e5m2, bool dim0, bool dim1);
+void mx_gemm(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, torch::Tensor sb, bool b_e5m2,
+             torch::Tensor d, bool accumulate);
 // gemm_skinny.cu
 void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d);
 // ngram.cu
@@ -109,6 +113,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
   m.def("ngram_stage", &mykb::ngram_stage);
   m.def("gemm_skinny", &mykb::gemm_skinny);
+  m.def("mx_quantize", &mykb::mx_quantize);
+  m.def("mx_gemm", &mykb::mx_gemm);
   m.def("fa_decode", &mykb::fa_decode);
   m.def("kv_append", &mykb::kv_append);
   m.def("ngram_adam", &mykb::ngram_adam);

@@ -130,7 +130,14 @@ class _Linear(torch.autograd.Function):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM; CPU: ``F.linear`` in x's dtype."""
+    """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM, or the block-scaled MXFP8 GEMMs for
+    weights converted by ``convert_to_mxfp8_training``; CPU: ``F.linear`` in x's dtype."""
     if not x.is_cuda:
         return F.linear(x, weight.to(x.dtype))
+    fmt = getattr(weight, "_mykb_mxfp8", None)
+    if fmt is not None:
+        from .mxfp8 import eligible_shapes, mx_linear
+
+        if eligible_shapes(x, weight) and x.numel() // x.shape[-1] > SKINNY_MAX_ROWS:
+            return mx_linear(x, weight, fmt)
     return _Linear.apply(x, weight)
