@@ -3,12 +3,14 @@
 // A decode step has a handful of queries per sequence (the verify window of speculative
 // decoding: 1 + drafts) against thousands of cached keys.  The prefill kernel gives one
 // CTA per (128-query tile, head), so a decode step would run on batch x heads CTAs, each
-// walking the whole cache.  Here the keys are split instead: a warp owns 64 keys of one
-// (sequence, KV head) and all the query rows of that KV head's group (GQA heads x
-// queries, at most 16 rows = one MMA row tile), computes S = Q K^T and P V on the tensor
-// cores (bf16 MMA, fp32 accumulate) with an online-softmax partial (m, l, O); a CTA holds
-// 4 warps = 256 keys.  The last CTA of a (sequence, KV head) to finish (atomic ticket,
-// nothing waits) merges all partials in a fixed order, so results are deterministic.
+// walking the whole cache.  Here the keys are split instead: a warp owns a run of 32-key
+// tiles of one (sequence, KV head) and all the query rows of that KV head's group (GQA
+// heads x queries, at most 16 rows = one MMA row tile); it streams the tiles through a
+// double-buffered cp.async pipeline and computes S = Q K^T and P V on the tensor cores
+// (bf16 MMA, fp32 accumulate) with an online softmax.  The 4 warps of a CTA merge their
+// (m, l, O) in shared memory; the last CTA of a (sequence, KV head) to finish (atomic
+// ticket, nothing waits) merges the CTAs in a fixed order, so results are deterministic.
+// The number of tiles per warp is chosen so that the grid is about four CTAs per SM.
 //
 // Semantics match the prefill kernel's KV-cache path: queries are aligned to the end of
 // the visible keys (query i of L sits at position seqused - L + i), window (left, right)
@@ -24,9 +26,8 @@ namespace fadec {
 
 typedef __nv_bfloat16 bf16;
 constexpr int ROWS = 16;        // query rows per KV head (GQA group x queries)
-constexpr int KEYS = 64;        // keys per warp
+constexpr int KEYS = 32;        // keys per tile; a warp walks `tiles` consecutive tiles
 constexpr int WARPS = 4;
-constexpr int CTA_KEYS = KEYS * WARPS;
 
 struct Params {
   const bf16* q;       // (B, L, H, D) with strides
@@ -34,11 +35,12 @@ struct Params {
   const bf16* v;
   const int* seqused;  // (B) visible keys per sequence
   bf16* o;             // (B, L, H, D) contiguous
-  float* work;         // [B][Hkv][splits][ROWS][D] partial O, then [.][.][splits][ROWS] m, l
+  float* work;         // [B][Hkv][splits][ROWS][D] per-CTA partial O, then [.][.][splits][ROWS] m, l
   float* ml;
   int* tickets;        // [B * Hkv]
   int64_t q_sb, q_st, q_sh;
-  int B, L, H, Hkv, cap, splits;  // splits = warps per (b, hkv) = CTAs per (b, hkv) x WARPS
+  int B, L, H, Hkv, cap, splits;  // splits = CTAs per (b, hkv)
+  int tiles;                      // key tiles per warp
   float scale_log2;
   int left, right;
 };
@@ -83,119 +85,165 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
   constexpr int LDK = D + 8;
   extern __shared__ __align__(16) unsigned char smraw[];
   bf16* Qs = reinterpret_cast<bf16*>(smraw);  // [ROWS][LDK]
-  bf16* Ks = Qs + ROWS * LDK;                  // [WARPS][KEYS][LDK]
-  bf16* Vs = Ks + WARPS * KEYS * LDK;          // [WARPS][KEYS][LDK]
+  bf16* KV = Qs + ROWS * LDK;                  // [WARPS][2 buffers][K, V][KEYS][LDK]
   __shared__ int last;
   __shared__ float rowM[ROWS], rowL[ROWS];
-  const int ctas = p.splits / WARPS;
+  __shared__ float wM[WARPS][ROWS], wL[WARPS][ROWS];
+  const int ctas = p.splits;
   const int bh = blockIdx.x / ctas, cta = blockIdx.x % ctas;
   const int b = bh / p.Hkv, hk = bh % p.Hkv;
   const int G = p.H / p.Hkv, rows = G * p.L;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kv_len = min(p.seqused[b], p.cap);
-  const int key0 = cta * CTA_KEYS + warp * KEYS;
-  const int64_t kv_row = (int64_t)p.Hkv * D;  // elements between consecutive cache positions
+  const int T = p.tiles;
+  const int key0 = (cta * WARPS + warp) * KEYS * T;  // this warp's contiguous key range
+  const int64_t kv_row = (int64_t)p.Hkv * D;
   const bf16* kb = p.k + ((int64_t)b * p.cap) * kv_row + (int64_t)hk * D;
   const bf16* vb = p.v + ((int64_t)b * p.cap) * kv_row + (int64_t)hk * D;
-  // Q rows of this KV head's group (row r = g * L + i -> head hk * G + g, query i)
   for (int e = tid; e < ROWS * (D / 8); e += WARPS * 32) {
     const int r = e / (D / 8), c = (e % (D / 8)) * 8;
     const bool ok = r < rows;
     const int g = ok ? r / p.L : 0, i = ok ? r % p.L : 0;
     cp16(Qs + r * LDK + c, p.q + b * p.q_sb + i * p.q_st + (int64_t)(hk * G + g) * p.q_sh + c, ok);
   }
-  bf16* ks = Ks + warp * KEYS * LDK;
-  bf16* vs = Vs + warp * KEYS * LDK;
-  for (int e = lane; e < KEYS * (D / 8); e += 32) {
-    const int r = e / (D / 8), c = (e % (D / 8)) * 8;
-    const bool ok = key0 + r < kv_len;
-    const int64_t off = (int64_t)(ok ? key0 + r : 0) * kv_row + c;
-    cp16(ks + r * LDK + c, kb + off, ok);
-    cp16(vs + r * LDK + c, vb + off, ok);
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-
+  bf16* wbuf = KV + warp * 2 * 2 * KEYS * LDK;
+  auto load_tile = [&](int t, int buf) {
+    bf16* ks = wbuf + buf * 2 * KEYS * LDK;
+    bf16* vs = ks + KEYS * LDK;
+    const int base = key0 + t * KEYS;
+    for (int e = lane; e < KEYS * (D / 8); e += 32) {
+      const int r = e / (D / 8), c = (e % (D / 8)) * 8;
+      const bool ok = base + r < kv_len;
+      const int64_t off = (int64_t)(ok ? base + r : 0) * kv_row + c;
+      cp16(ks + r * LDK + c, kb + off, ok);
+      cp16(vs + r * LDK + c, vb + off, ok);
+    }
+  };
+  asm volatile("cp.async.commit_group;" ::: "memory");  // group: Q
+  // tiles past the visible keys are skipped (they would only be masked)
+  const int nt = max(0, min(T, (kv_len - key0 + KEYS - 1) / KEYS));
+  if (nt > 0) load_tile(0, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");  // group: tile 0
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();  // Q is visible to every warp
   const int rr = lane & 7, mat = lane >> 3, gq = lane >> 2, cq = (lane & 3) * 2;
-  // S = Q K^T (16 x 64)
-  float s[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-  for (int k0 = 0; k0 < D; k0 += 16) {
-    uint32_t a[4];
-    ldsm4(a, Qs + (lane & 15) * LDK + k0 + (lane >> 4) * 8);
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      uint32_t bq[4];
-      ldsm4(bq, ks + (j * 8 + rr + (mat >> 1) * 8) * LDK + k0 + (mat & 1) * 8);
-      mma(s[j], a, bq[0], bq[1]);
-      mma(s[j + 1], a, bq[2], bq[3]);
-    }
-  }
-  // masked online-softmax partial of this warp's keys (rows gq and gq + 8 of this lane)
-  float m[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = gq + (e >> 1) * 8, col = key0 + j * 8 + cq + (e & 1);
-      s[j][e] = visible(p, r, col, rows, kv_len) ? s[j][e] * p.scale_log2 : -INFINITY;
-      m[e >> 1] = fmaxf(m[e >> 1], s[j][e]);
-    }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    m[h] = fmaxf(m[h], __shfl_xor_sync(0xffffffff, m[h], 1));
-    m[h] = fmaxf(m[h], __shfl_xor_sync(0xffffffff, m[h], 2));
-  }
-  float l[2] = {0.f, 0.f};
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float mm = m[e >> 1];
-      s[j][e] = mm == -INFINITY ? 0.f : exp2f(s[j][e] - mm);
-      l[e >> 1] += s[j][e];
-    }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    l[h] += __shfl_xor_sync(0xffffffff, l[h], 1);
-    l[h] += __shfl_xor_sync(0xffffffff, l[h], 2);
-  }
-  // O = P V (16 x D): P from the S accumulators re-packed as A fragments
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float o[D / 8][4];
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int t = 0; t < nt; ++t) {
+    if (t + 1 < nt) load_tile(t + 1, (t + 1) & 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncwarp();
+    const bf16* ks = wbuf + (t & 1) * 2 * KEYS * LDK;
+    const bf16* vs = ks + KEYS * LDK;
+    float s[KEYS / 8][4];
 #pragma unroll
-  for (int t = 0; t < KEYS / 16; ++t) {
-    uint32_t a[4];
-    a[0] = pack2(s[2 * t][0], s[2 * t][1]);
-    a[1] = pack2(s[2 * t][2], s[2 * t][3]);
-    a[2] = pack2(s[2 * t + 1][0], s[2 * t + 1][1]);
-    a[3] = pack2(s[2 * t + 1][2], s[2 * t + 1][3]);
+    for (int j = 0; j < KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
-    for (int n = 0; n < D / 8; n += 2) {
-      uint32_t bv[4];
-      ldsm4t(bv, vs + (t * 16 + (mat & 1) * 8 + rr) * LDK + n * 8 + (mat >> 1) * 8);
-      mma(o[n], a, bv[0], bv[1]);
-      mma(o[n + 1], a, bv[2], bv[3]);
+    for (int k0 = 0; k0 < D; k0 += 16) {
+      uint32_t a[4];
+      ldsm4(a, Qs + (lane & 15) * LDK + k0 + (lane >> 4) * 8);
+#pragma unroll
+      for (int j = 0; j < KEYS / 8; j += 2) {
+        uint32_t bq[4];
+        ldsm4(bq, ks + (j * 8 + rr + (mat >> 1) * 8) * LDK + k0 + (mat & 1) * 8);
+        mma(s[j], a, bq[0], bq[1]);
+        mma(s[j + 1], a, bq[2], bq[3]);
+      }
     }
+    const int base = key0 + t * KEYS;
+    float mt[2] = {m[0], m[1]};
+#pragma unroll
+    for (int j = 0; j < KEYS / 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = gq + (e >> 1) * 8, col = base + j * 8 + cq + (e & 1);
+        s[j][e] = visible(p, r, col, rows, kv_len) ? s[j][e] * p.scale_log2 : -INFINITY;
+        mt[e >> 1] = fmaxf(mt[e >> 1], s[j][e]);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffff, mt[h], 1));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffff, mt[h], 2));
+    }
+    float corr[2], ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) corr[h] = (mt[h] == -INFINITY || m[h] == -INFINITY) ? (m[h] == -INFINITY ? 0.f : 1.f)
+                                                                                      : exp2f(m[h] - mt[h]);
+#pragma unroll
+    for (int j = 0; j < KEYS / 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mm = mt[e >> 1];
+        s[j][e] = mm == -INFINITY ? 0.f : exp2f(s[j][e] - mm);
+        ls[e >> 1] += s[j][e];
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ls[h] += __shfl_xor_sync(0xffffffff, ls[h], 1);
+      ls[h] += __shfl_xor_sync(0xffffffff, ls[h], 2);
+      l[h] = l[h] * corr[h] + ls[h];
+      m[h] = mt[h];
+    }
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= corr[0], o[n][1] *= corr[0], o[n][2] *= corr[1], o[n][3] *= corr[1];
+    }
+#pragma unroll
+    for (int kt = 0; kt < KEYS / 16; ++kt) {
+      uint32_t a[4];
+      a[0] = pack2(s[2 * kt][0], s[2 * kt][1]);
+      a[1] = pack2(s[2 * kt][2], s[2 * kt][3]);
+      a[2] = pack2(s[2 * kt + 1][0], s[2 * kt + 1][1]);
+      a[3] = pack2(s[2 * kt + 1][2], s[2 * kt + 1][3]);
+#pragma unroll
+      for (int n = 0; n < D / 8; n += 2) {
+        uint32_t bv[4];
+        ldsm4t(bv, vs + (kt * 16 + (mat & 1) * 8 + rr) * LDK + n * 8 + (mat >> 1) * 8);
+        mma(o[n], a, bv[0], bv[1]);
+        mma(o[n + 1], a, bv[2], bv[3]);
+      }
+    }
+    __syncwarp();  // this buffer is refilled by the load two tiles ahead
   }
-  // this warp's partial -> workspace slot (bh, split)
-  const int split = cta * WARPS + warp;
-  float* wo = p.work + ((int64_t)bh * p.splits + split) * ROWS * D;
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  // merge the warps of this CTA through shared memory (reusing the K/V buffers)
+  __syncthreads();
+  float* Ow = reinterpret_cast<float*>(KV);  // [WARPS][ROWS][D]
+  if ((lane & 3) == 0) {
+    wM[warp][gq] = m[0], wL[warp][gq] = l[0];
+    wM[warp][gq + 8] = m[1], wL[warp][gq + 8] = l[1];
+  }
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) {
-    *reinterpret_cast<float2*>(wo + gq * D + n * 8 + cq) = make_float2(o[n][0], o[n][1]);
-    *reinterpret_cast<float2*>(wo + (gq + 8) * D + n * 8 + cq) = make_float2(o[n][2], o[n][3]);
+    *reinterpret_cast<float2*>(Ow + (warp * ROWS + gq) * D + n * 8 + cq) = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(Ow + (warp * ROWS + gq + 8) * D + n * 8 + cq) = make_float2(o[n][2], o[n][3]);
   }
-  if ((lane & 3) == 0) {
-    float* wml = p.ml + ((int64_t)bh * p.splits + split) * ROWS * 2;
-    wml[gq * 2] = m[0];
-    wml[gq * 2 + 1] = l[0];
-    wml[(gq + 8) * 2] = m[1];
-    wml[(gq + 8) * 2 + 1] = l[1];
+  __syncthreads();
+  if (tid < ROWS) {
+    float M = -INFINITY;
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, wM[w][tid]);
+    float L = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < WARPS; ++w)
+        if (wM[w][tid] != -INFINITY) L += exp2f(wM[w][tid] - M) * wL[w][tid];
+    rowM[tid] = M, rowL[tid] = L;
+    float* wml = p.ml + ((int64_t)bh * ctas + cta) * ROWS * 2;
+    wml[tid * 2] = M;
+    wml[tid * 2 + 1] = L;
+  }
+  __syncthreads();
+  float* wo = p.work + ((int64_t)bh * ctas + cta) * ROWS * D;
+  for (int e = tid; e < ROWS * D; e += WARPS * 32) {
+    const int r = e / D;
+    const float M = rowM[r];
+    float acc = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < WARPS; ++w)
+        if (wM[w][r] != -INFINITY) acc += exp2f(wM[w][r] - M) * Ow[(w * ROWS) * D + e];
+    wo[e] = acc;
   }
   __threadfence();
   __syncthreads();
@@ -203,30 +251,30 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // merge every split of (b, hk): O = sum_s e^{m_s - M} O_s / sum_s e^{m_s - M} l_s
-  const float* ml = p.ml + (int64_t)bh * p.splits * ROWS * 2;
+  // merge the CTAs of (b, hk): O = sum_c e^{m_c - M} O_c / sum_c e^{m_c - M} l_c
+  const float* ml = p.ml + (int64_t)bh * ctas * ROWS * 2;
   if (tid < ROWS) {
     float M = -INFINITY;
-    for (int k = 0; k < p.splits; ++k) M = fmaxf(M, __ldcg(ml + (k * ROWS + tid) * 2));
+    for (int c = 0; c < ctas; ++c) M = fmaxf(M, __ldcg(ml + (c * ROWS + tid) * 2));
     float L = 0.f;
     if (M != -INFINITY)
-      for (int k = 0; k < p.splits; ++k) {
-        const float mk = __ldcg(ml + (k * ROWS + tid) * 2);
-        if (mk != -INFINITY) L += exp2f(mk - M) * __ldcg(ml + (k * ROWS + tid) * 2 + 1);
+      for (int c = 0; c < ctas; ++c) {
+        const float mc = __ldcg(ml + (c * ROWS + tid) * 2);
+        if (mc != -INFINITY) L += exp2f(mc - M) * __ldcg(ml + (c * ROWS + tid) * 2 + 1);
       }
     rowM[tid] = M;
     rowL[tid] = L;
   }
   __syncthreads();
-  const float* wb = p.work + (int64_t)bh * p.splits * ROWS * D;
+  const float* wb = p.work + (int64_t)bh * ctas * ROWS * D;
   for (int e = tid; e < rows * D; e += WARPS * 32) {
     const int r = e / D, d = e % D;
     const float M = rowM[r], L = rowL[r];
     float acc = 0.f;
     if (L > 0.f)
-      for (int k = 0; k < p.splits; ++k) {
-        const float mk = __ldcg(ml + (k * ROWS + r) * 2);
-        if (mk != -INFINITY) acc += exp2f(mk - M) * __ldcg(wb + (k * ROWS + r) * D + d);
+      for (int c = 0; c < ctas; ++c) {
+        const float mc = __ldcg(ml + (c * ROWS + r) * 2);
+        if (mc != -INFINITY) acc += exp2f(mc - M) * __ldcg(wb + (c * ROWS + r) * D + d);
       }
     const int g = r / p.L, i = r % p.L;
     p.o[(((int64_t)b * p.L + i) * p.H + hk * G + g) * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
@@ -258,7 +306,13 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
               "fa_decode: 16-byte aligned query rows");
   c10::cuda::CUDAGuard guard(q.device());
   auto o = torch::empty({B, L, H, D}, q.options());
-  const int ctas = std::max(1, (cap + CTA_KEYS - 1) / CTA_KEYS);
+  const int max_tiles = std::max(1, (cap + KEYS * WARPS - 1) / (KEYS * WARPS));  // tiles per warp at one CTA
+  static int sms[64] = {0};
+  if (!sms[q.get_device()]) cudaDeviceGetAttribute(&sms[q.get_device()], cudaDevAttrMultiProcessorCount, q.get_device());
+  const int64_t target = 4LL * sms[q.get_device()];
+  const int64_t want = ((int64_t)cap * B * Hkv + (int64_t)KEYS * WARPS * target - 1) / ((int64_t)KEYS * WARPS * target);
+  const int tiles = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, want));
+  const int ctas = std::max(1, (cap + KEYS * WARPS * tiles - 1) / (KEYS * WARPS * tiles));
   Params p{};
   p.q = (const bf16*)q.data_ptr();
   p.k = (const bf16*)k_cache.data_ptr();
@@ -267,7 +321,8 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   p.o = (bf16*)o.data_ptr();
   p.q_sb = q.stride(0), p.q_st = q.stride(1), p.q_sh = q.stride(2);
   p.B = B, p.L = L, p.H = H, p.Hkv = Hkv, p.cap = cap;
-  p.splits = ctas * WARPS;
+  p.splits = ctas;
+  p.tiles = tiles;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.left = (int)left, p.right = (int)right;
   const int64_t slots = (int64_t)B * Hkv * p.splits;
@@ -278,7 +333,7 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   const int grid = B * Hkv * ctas;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   static bool attr[2] = {false, false};
-  const size_t smem = (size_t)(ROWS + 2 * WARPS * KEYS) * (D + 8) * sizeof(bf16);
+  const size_t smem = (size_t)(ROWS + 4 * WARPS * KEYS) * (D + 8) * sizeof(bf16);
   if (D == 64) {
     if (!attr[0]) {
       C10_CUDA_CHECK(cudaFuncSetAttribute(fa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -1,4 +1,4 @@
-// Skinny GEMM for decode / small batches: D (M x N) = A (M x K) . W (N x K)^T with M <= 64.
+// Skinny GEMM for decode / small batches: D (M x N) = A (M x K) . W (N x K)^T with M <= 256.
 //
 // Decode-time linears multiply a handful of token rows by a large weight: the time is the
 // weight read, and a 128 x 256 output tile leaves most SMs idle (N = 1024 gives four
@@ -54,29 +54,32 @@ struct Params {
   bool out_f32;
 };
 
-template <int MT>  // 16-row tiles of M
-__global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
+template <int MT, int WM>  // 16-row tiles per warp, warps along M (rows of the tile = WM * MT * 16)
+__global__ void __launch_bounds__(THREADS * WM) skinny_gemm_kernel(Params p) {
+  constexpr int RT = WM * MT * 16;
   extern __shared__ __align__(16) unsigned char smraw[];
-  bf16* As = reinterpret_cast<bf16*>(smraw);  // [STAGES][MT*16][LDS]
-  bf16* Ws = As + STAGES * MT * 16 * LDS;      // [STAGES][64][LDS]
+  bf16* As = reinterpret_cast<bf16*>(smraw);  // [STAGES][RT][LDS]
+  bf16* Ws = As + STAGES * RT * LDS;           // [STAGES][64][LDS]
   __shared__ int last;
   const int tile = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const int n0 = tile * BN;
   const int nchunks = (p.K + BK - 1) / BK;
   const int c0 = split * p.chunks_per_split;
   const int c1 = min(nchunks, c0 + p.chunks_per_split);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = (tid >> 5) & 3, wrow = tid >> 7;  // column group, row group
+  const int m_base = wrow * MT * 16;
 
   auto load = [&](int chunk, int stage) {
     const int k0 = chunk * BK;
-    bf16* a = As + stage * MT * 16 * LDS;
+    bf16* a = As + stage * RT * LDS;
     bf16* w = Ws + stage * BN * LDS;
-    for (int i = tid; i < MT * 16 * 8; i += THREADS) {
+    for (int i = tid; i < RT * 8; i += THREADS * WM) {
       const int r = i >> 3, c = (i & 7) * 8;
       const bool ok = r < p.M && k0 + c < p.K;
       cp16(a + r * LDS + c, p.A + (ok ? (int64_t)r * p.lda + k0 + c : 0), ok);
     }
-    for (int i = tid; i < BN * 8; i += THREADS) {
+    for (int i = tid; i < BN * 8; i += THREADS * WM) {
       const int r = i >> 3, c = (i & 7) * 8;
       const bool ok = n0 + r < p.N && k0 + c < p.K;
       cp16(w + r * LDS + c, p.W + (ok ? (int64_t)(n0 + r) * p.ldw + k0 + c : 0), ok);
@@ -101,7 +104,7 @@ __global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 1) : "memory");
     __syncthreads();
-    const bf16* a = As + (i % STAGES) * MT * 16 * LDS;
+    const bf16* a = As + (i % STAGES) * RT * LDS;
     const bf16* w = Ws + (i % STAGES) * BN * LDS;
 #pragma unroll
     for (int k = 0; k < BK; k += 16) {
@@ -110,7 +113,7 @@ __global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         uint32_t af[4];
-        ldsm4(af, a + (m * 16 + (lane & 15)) * LDS + k + (lane >> 4) * 8);
+        ldsm4(af, a + (m_base + m * 16 + (lane & 15)) * LDS + k + (lane >> 4) * 8);
         mma(acc[m][0], af, b[0], b[1]);
         mma(acc[m][1], af, b[2], b[3]);
       }
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
       for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const int row = m * 16 + gq + hf * 8, col = n0 + warp * 16 + j * 8 + cq;
+          const int row = m_base + m * 16 + gq + hf * 8, col = n0 + warp * 16 + j * 8 + cq;
           if (row >= p.M || col >= p.N) continue;
           const float x = acc[m][j][2 * hf], y = acc[m][j][2 * hf + 1];
           if (p.out_f32) {
@@ -143,14 +146,14 @@ __global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
     return;
   }
   // split-K: partial tile to the workspace, then the last CTA of the tile reduces
-  float* part = p.work + ((int64_t)tile * p.splits + split) * (64 * BN);
+  float* part = p.work + ((int64_t)tile * p.splits + split) * (RT * BN);
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int row = m * 16 + gq + hf * 8, col = warp * 16 + j * 8 + cq;
+        const int row = m_base + m * 16 + gq + hf * 8, col = warp * 16 + j * 8 + cq;
         *reinterpret_cast<float2*>(part + row * BN + col) = make_float2(acc[m][j][2 * hf], acc[m][j][2 * hf + 1]);
       }
   __threadfence();
@@ -159,12 +162,12 @@ __global__ void __launch_bounds__(THREADS) skinny_gemm_kernel(Params p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  const float* base = p.work + (int64_t)tile * p.splits * (64 * BN);
-  for (int e = tid; e < p.M * BN; e += THREADS) {
+  const float* base = p.work + (int64_t)tile * p.splits * (RT * BN);
+  for (int e = tid; e < p.M * BN; e += THREADS * WM) {
     const int row = e / BN, col = e % BN;
     if (n0 + col >= p.N) continue;
     float s = 0.f;
-    for (int k = 0; k < p.splits; ++k) s += __ldcg(base + k * (64 * BN) + row * BN + col);
+    for (int k = 0; k < p.splits; ++k) s += __ldcg(base + k * (RT * BN) + row * BN + col);
     if (p.out_f32) reinterpret_cast<float*>(p.D)[(int64_t)row * p.ldd + n0 + col] = s;
     else reinterpret_cast<bf16*>(p.D)[(int64_t)row * p.ldd + n0 + col] = __float2bfloat16(s);
   }
@@ -179,20 +182,20 @@ static int skinny_sms(int dev) {
   return cached[dev];
 }
 
-template <int MT>
+template <int MT, int WM>
 static void skinny_launch(const skinny::Params& p, int grid, cudaStream_t st) {
   using namespace skinny;
-  const size_t smem = (size_t)STAGES * (MT * 16 + BN) * LDS * sizeof(bf16);
+  const size_t smem = (size_t)STAGES * (WM * MT * 16 + BN) * LDS * sizeof(bf16);
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(skinny_gemm_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(skinny_gemm_kernel<MT, WM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem));
     attr = true;
   }
-  skinny_gemm_kernel<MT><<<grid, THREADS, smem, st>>>(p);
+  skinny_gemm_kernel<MT, WM><<<grid, THREADS * WM, smem, st>>>(p);
 }
 
-// a (M, K) with M <= 64, w (N, K), both bf16 with contiguous K; d (M, N) bf16 or fp32.
+// a (M, K) with M <= 256, w (N, K), both bf16 with contiguous K; d (M, N) bf16 or fp32.
 void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d) {
   using namespace skinny;
   TORCH_CHECK(a.is_cuda() && w.is_cuda() && d.is_cuda() && a.dim() == 2 && w.dim() == 2 && d.dim() == 2,
@@ -200,14 +203,16 @@ void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d) {
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_skinny: bf16 operands");
   TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm_skinny: bf16 or fp32 output");
   const int M = a.size(0), K = a.size(1), N = w.size(0);
-  TORCH_CHECK(M >= 1 && M <= 64 && w.size(1) == K && d.size(0) == M && d.size(1) == N, "gemm_skinny: shapes");
+  TORCH_CHECK(M >= 1 && M <= 256 && w.size(1) == K && d.size(0) == M && d.size(1) == N, "gemm_skinny: shapes");
   TORCH_CHECK(a.stride(1) == 1 && w.stride(1) == 1 && d.stride(1) == 1 && K % 8 == 0 && a.stride(0) % 8 == 0 &&
                   w.stride(0) % 8 == 0,
               "gemm_skinny: contiguous K, K and row strides multiples of 8");
   TORCH_CHECK(((uintptr_t)a.data_ptr() % 16) == 0 && ((uintptr_t)w.data_ptr() % 16) == 0,
               "gemm_skinny: 16-byte aligned operands");
   c10::cuda::CUDAGuard guard(a.device());
-  const int MT = (M + 15) / 16;
+  const int MT = M <= 64 ? (M + 15) / 16 : 8;
+  const int WM = M <= 128 ? 1 : 2;
+  const int RT = WM * MT * 16;
   const int tiles = (N + BN - 1) / BN;
   const int nchunks = (K + BK - 1) / BK;
   const int target = 2 * skinny_sms(a.get_device());
@@ -227,18 +232,18 @@ void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d) {
   p.out_f32 = d.scalar_type() == at::kFloat;
   torch::Tensor work;
   if (splits > 1) {
-    work = torch::empty({(int64_t)tiles * splits * 64 * BN}, a.options().dtype(at::kFloat));
+    work = torch::empty({(int64_t)tiles * splits * RT * BN}, a.options().dtype(at::kFloat));
     p.work = work.data_ptr<float>();
     p.tickets = ticket_region(tiles);
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int grid = tiles * splits;
-  switch (MT) {
-    case 1: skinny_launch<1>(p, grid, st); break;
-    case 2: skinny_launch<2>(p, grid, st); break;
-    case 3: skinny_launch<3>(p, grid, st); break;
-    default: skinny_launch<4>(p, grid, st); break;
-  }
+  if (WM == 2) skinny_launch<8, 2>(p, grid, st);
+  else if (MT == 8) skinny_launch<8, 1>(p, grid, st);
+  else if (MT == 1) skinny_launch<1, 1>(p, grid, st);
+  else if (MT == 2) skinny_launch<2, 1>(p, grid, st);
+  else if (MT == 3) skinny_launch<3, 1>(p, grid, st);
+  else skinny_launch<4, 1>(p, grid, st);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -87,7 +87,7 @@ def test_linear_autograd_matches_reference():
     _close(w.grad, wr.grad, rel=3e-2)
 
 
-@pytest.mark.parametrize("m", [1, 3, 17, 64])
+@pytest.mark.parametrize("m", [1, 3, 17, 64, 100, 192, 256])
 @pytest.mark.parametrize("nk", [(64, 64), (1000, 1000), (1536, 1024), (1024, 2816), (65536, 256)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_skinny_gemm(m, nk, out_dtype):
