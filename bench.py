@@ -62,6 +62,15 @@ MODELS = {
         "data.seq_len=8192", "data.micro_batch_size=2"] + _COMMON, 8192, 2,
         "1B hybrid (d2048 L24 DDDG: 18 GDN 16x128 + 6 GQA 16q/4kv h128, SwiGLU 5632, 2/3-gram 2^20 x 2048, "
         "vocab 65536 untied)"),
+    "1b-mxfp8": ([
+        "model.vocab_size=65536", "model.hidden_size=2048", "model.num_layers=20", "model.layer_pattern=GL",
+        "model.max_seq_len=4096", "model.tie_embeddings=false", "model.norm_eps=1e-6",
+        "model.attention.num_heads=16", "model.attention.num_kv_heads=4", "model.attention.head_dim=128",
+        "model.attention.sliding_window=1024", "model.attention.global_rope=all",
+        "model.attention.rope_theta_global=10000.0", "model.ffn.multiplier=2.75", "model.ffn.multiple_of=256",
+        "parallel.float8=mxfp8", "data.seq_len=4096", "data.micro_batch_size=4"] + _COMMON, 4096, 4,
+        "1B dense MXFP8 (d2048 L20 GL, window 1024 on odd layers, 16q/4kv h128, SwiGLU 5632, vocab 65536 untied; "
+        "all block linears MXFP8, E4M3 forward)"),
 }
 
 
@@ -72,6 +81,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="200m", choices=sorted(MODELS), help="benchmark config (default: 200m)")
+    ap.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
+                    help="(experiments only) extra config overrides for our arm, e.g. parallel.float8=none")
     ap.add_argument("--layers", type=int, default=24, help="(debug only) fewer layers; results are not comparable")
     ap.add_argument("--ref-compile", default="auto", choices=["auto", "on", "off"],
                     help="reference arm: its parallel.compile switch (auto: on, falling back to off if Inductor fails)")
@@ -198,7 +209,7 @@ def count_launches(step_fn, prefix: str) -> int:
 
 
 # ----------------------------------------------------------------------------- arms
-def build_ours(world: int, layers: int, model: str):
+def build_ours(world: int, layers: int, model: str, extra: list[str] | None = None):
     import torch
 
     from myk_llm_b200.configuration import apply_overrides, from_dict
@@ -208,7 +219,7 @@ def build_ours(world: int, layers: int, model: str):
     from myk_llm_b200.train.trainer import Trainer
 
     ov, _, micro, _ = MODELS[model]
-    ov = ov + [f"global_batch_size={micro * world}", "steps=1000", "schedule.warmup_ratio=0.0",
+    ov = ov + list(extra or []) + [f"global_batch_size={micro * world}", "steps=1000", "schedule.warmup_ratio=0.0",
                             "data.kind=synthetic", "logging.tensorboard=false", f"model.num_layers={layers}"]
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
@@ -279,6 +290,14 @@ def main():
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
             return
+        if a.model == "1b-mxfp8":
+            try:
+                import torchao  # noqa: F401  (the reference's MXFP8 path wraps torchao)
+            except ImportError as err:
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable":
+                                      f"the reference's MXFP8 linears need torchao, which is not installed ({err})"}))
+                return
         if a.model == "1b-hybrid":
             try:
                 import fla.modules.causal_conv1d  # noqa: F401  (the reference's Gated DeltaNet imports it)
@@ -312,7 +331,7 @@ def main():
                 compile_on = False
                 device, step, batch_cls, _ = build_reference(world, a.layers, a.model, False)
     else:
-        device, step, batch_cls, _ = build_ours(world, a.layers, a.model)
+        device, step, batch_cls, _ = build_ours(world, a.layers, a.model, a.set)
 
     total_steps = a.warmup + 2 * a.steps + 1
     batches = synthetic_batches(total_steps, 0, rank, world, batch_cls, seq_len, micro)
@@ -365,14 +384,16 @@ def main():
             "metric": "train tokens/sec at 1/2/4/8 B200 (200M, 1B hybrid); MTP decode tokens/sec",
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": dev_ms / a.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
+            "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None,
+            "dtype": "mxfp8 (E4M3 operands, E8M0 1x32 scales; bf16 elsewhere)"
+            if a.model == "1b-mxfp8" and "parallel.float8=none" not in a.set else "bf16",
             "data": "synthetic packed documents (geometric mean 1024, uniform ids, EOS), random-init weights",
             "config": {"model": model_desc,
                        "global_batch": micro * world, "seq_len": seq_len, "micro_batch_per_gpu": micro,
                        "parallelism": f"dp{world}" + ("" if world == 1 else " (sharded)"),
                        "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
                        "l2": "working set >> 126 MB L2 (no flush inserted)",
-                       "layers": a.layers},
+                       "layers": a.layers, **({"overrides": a.set} if a.set else {})},
             "clocks": clk,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
