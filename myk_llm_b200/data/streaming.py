@@ -20,6 +20,7 @@ tokenizer at load time and resume by cursor.
 
 from __future__ import annotations
 
+import glob
 from pathlib import Path
 from typing import Any, Iterator
 
@@ -37,7 +38,7 @@ def open_stream(source: SourceConfig, seed: int, shuffle_buffer: int, rank: int 
     from datasets import load_dataset
 
     if source.path:
-        files = sorted(str(p) for p in Path().glob(source.path)) if any(c in source.path for c in "*?[") \
+        files = sorted(glob.glob(source.path)) if any(c in source.path for c in "*?[") \
             else [source.path]
         if not files:
             raise FileNotFoundError(f"source {source.name!r}: no files match {source.path!r}")

@@ -345,6 +345,9 @@ class Trainer:
             from .metrics import MetricsLogger
 
             metrics = MetricsLogger(run_dir / "metrics.jsonl", run_dir / "tb" if config.logging.tensorboard else None)
+            if ck is None:
+                metrics.log(0, {"params/total": self.raw_model.num_parameters(),
+                                "params/non_embedding": self.raw_model.num_parameters(exclude_embeddings=True)})
         log0(info, f"run {run_dir}: {info.world_size} rank(s), micro batch {config.data.micro_batch_size} x accum "
                    f"{self.grad_accum} = {config.global_batch_size} seqs = {self.tokens_per_step:,} tokens/step")
         it = iter(loader)

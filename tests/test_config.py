@@ -48,7 +48,16 @@ def test_every_config_parses():
         if "sweeps" in f.parts:
             continue
         tree = load_yaml_tree(f)
-        if "model" in tree or "steps" in tree:
+        rel = f.relative_to(ROOT / "configs").parts
+        if rel[0] == "lc":
+            from myk_llm_b200.lc.train import LcConfig
+
+            from_dict(LcConfig, tree)
+        elif rel[0] == "arith":
+            from myk_llm_b200.arith.train import ArithConfig
+
+            from_dict(ArithConfig, tree)
+        elif "model" in tree or "steps" in tree:
             from_dict(TrainConfig, tree)
 
 
