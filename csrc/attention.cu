@@ -13,16 +13,18 @@
 //               exp2(m_{j-1} - m_j).  At the end: O / l to global, LSE (natural log).
 // Two CTAs fit on one SM for head_dim 64, so one CTA's softmax overlaps the other's MMAs.
 //
-// Backward (dK/dV per 128-key tile, dQ accumulated in fp32 with atomics), per work item
-// (sequence, kv head, key tile), looping over the query tiles and the query heads of the
-// GQA group:
-//   S^T  = K Q^T          (M=128 keys, N=128 queries, K=d)
-//   dP^T = V dO^T         (M=128 keys, N=128 queries, K=d)
+// Backward, kernel 1 (dK/dV per 128-key tile), per work item (sequence, kv head, key
+// tile), looping over the query tiles and the query heads of the GQA group:
+//   S^T  = K Q^T          (M=128 keys, N=64 queries, K=d)
+//   dP^T = V dO^T         (M=128 keys, N=64 queries, K=d)
 //   P^T  = exp(S^T - lse), dS^T = P^T * (dP^T - Delta)   (registers; thread = key row)
-//   dV  += P^T dO         (M=128, N=d, K=128 queries; A = P^T from smem)
-//   dK  += dS^T Q         (M=128, N=d, K=128 queries; A = dS^T from smem)
-//   dQ  += dS K           (M=128 queries, N=d, K=128 keys; A = dS^T read MN-major)
-// Delta = rowsum(dO * O) comes from a small pre-kernel.
+//   dV  += P^T dO         (M=128, N=d, K=queries; A = P^T from TMEM)
+//   dK  += dS^T Q         (M=128, N=d, K=queries; A = dS^T from TMEM)
+// over 64-query sub-tiles with double-buffered S^T / dP^T so MMAs overlap the softmax.
+// Kernel 2 (dQ per 128-query tile) recomputes S and dP with the forward's operand
+// patterns and accumulates dQ += dS K in TMEM, so no atomics and a deterministic result.
+// Both backward kernels run eight softmax-gradient warps (two per SM sub-partition, each
+// owning half of the tile's columns).  Delta = rowsum(dO * O) comes from a small pre-kernel.
 //
 // Semantics follow the reference (src/myk_llm/ops/flash_attn.py): queries end-aligned to
 // the keys, window (left, right) with -1 unbounded, empty rows output 0 with LSE +inf.
@@ -540,22 +542,35 @@ __device__ __forceinline__ bool decode_bwd(const FaBwdParams& p, int w, BwdItem&
 
 template <int D>
 struct DkvSmem {
-  static constexpr int kStages = D == 64 ? 2 : 1;
+  static constexpr int kStages = D == 64 ? 4 : 2;  // Q / dO ring depth
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kK = 0;
   static constexpr int kV = kK + kTile;
   static constexpr int kQ0 = kV + kTile;
   static constexpr int kDO0 = kQ0 + kStages * kTile;
-  static constexpr int kP = kDO0 + kStages * kTile;  // P^T (keys x queries)
-  static constexpr int kDS = kP + 128 * 128 * 2;     // dS^T
-  static constexpr int kLse = kDS + 128 * 128 * 2;   // [stages][128] base-2 LSE of the query tile
+  static constexpr int kLse = kDO0 + kStages * kTile;  // [stages][128] base-2 LSE of the query tile
   static constexpr int kDelta = kLse + kStages * 512;  // [stages][128] Delta of the query tile
   static constexpr int kBars = kDelta + kStages * 512;
   static constexpr int kTotal = kBars + 256;
 };
 
+// Backward kernels: producer warp, MMA warp, and two groups of four softmax-gradient warps
+// (each SM sub-partition runs one warp of each group, so one hides the other's latency).
+constexpr int kBwdSoftmaxWarps = 8;
+constexpr int kFaBwdThreads = 64 + 32 * kBwdSoftmaxWarps;
+
+// dK / dV kernel.  Each 128-query tile is processed as two 64-query sub-tiles u whose
+// S^T / dP^T accumulators alternate between two TMEM buffers, so the tensor pipe computes
+// sub-tile u + 1 (and the dV / dK products of u - 1) while the softmax warps work on u.
+// The softmax warps write P^T and dS^T back into TMEM as packed bf16 over the columns
+// they read, and dV += P^T dO, dK += dS^T Q take their A operand from TMEM.
+//
+// TMEM columns (b = u & 1):  S^T [128 b, 128 b + 64), dP^T [128 b + 64, 128 b + 128),
+// dV [256, 256 + D), dK [256 + D, 256 + 2 D).  Softmax group h (of 2) owns queries
+// [32 h, 32 h + 32) of a sub-tile and writes its 16 packed columns at the start of its own
+// 32 columns, so A for K step kk (16 queries) is at column (kk / 2) * 32 + (kk % 2) * 8.
 template <int D>
-__global__ void __launch_bounds__(kFaThreads, 1)
+__global__ void __launch_bounds__(kFaBwdThreads, 1)
 fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                    const FaBwdParams p) {
@@ -570,17 +585,15 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
   uint64_t* kv_full = bars + 0;
   uint64_t* kv_empty = bars + 1;
-  uint64_t* q_full = bars + 2;   // [ST]
-  uint64_t* q_empty = bars + 4;  // [ST]
-  uint64_t* s_full = bars + 6;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* mm_done = bars + 8;
-  uint64_t* kk_done = bars + 9;
-  uint64_t* dkv_free = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  // TMEM columns: [0,128) S^T, [128,256) dP^T, [256,256+D) dV, [256+D,256+2D) dK
+  uint64_t* q_full = bars + 2;        // [ST]
+  uint64_t* q_empty = bars + 2 + ST;  // [ST]
+  uint64_t* s_full = bars + 2 + 2 * ST;  // [2] per TMEM buffer
+  uint64_t* ds_full = s_full + 2;        // [2]
+  uint64_t* kk_done = s_full + 4;
+  uint64_t* dkv_free = s_full + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 6);
   constexpr int kCols = 512;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D;
+  constexpr uint32_t kColDV = 256, kColDK = 256 + D;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int group = p.f.group;
   if (threadIdx.x == 0) {
@@ -590,11 +603,12 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, 4);
-    mbar_init(mm_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], kBwdSoftmaxWarps);
+    }
     mbar_init(kk_done, 1);
-    mbar_init(dkv_free, 4);
+    mbar_init(dkv_free, kBwdSoftmaxWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
@@ -655,14 +669,40 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       ++items;
     }
   } else if (warp == 1) {
-    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);  // K Q^T, V dO^T
-    constexpr uint32_t idesc_kv = make_idesc_bf16(128, D, false, true);    // P^T dO, dS^T Q
+    // MMA warp.  Per sub-tile u: S^T(u), dP^T(u) into buffer u & 1, then the dV / dK
+    // products of u - 1 (whose P^T / dS^T the softmax warps have written by then).
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, false, false);  // K Q^T, V dO^T (N = 64 queries)
+    constexpr uint32_t idesc_kv = make_idesc_bf16(128, D, false, true);   // P^T dO, dS^T Q (A from TMEM)
     if (elect_one()) {
-      int stage = 0, items = 0, n = 0;
+      int stage = 0, items = 0;
       uint32_t phase = 0;
+      uint32_t u = 0;  // sub-tiles issued so far (all items)
       bool ok = true;
       const uint32_t k_addr = smem_u32(smem + S::kK), v_addr = smem_u32(smem + S::kV);
-      const uint32_t p_addr = smem_u32(smem + S::kP), ds_addr = smem_u32(smem + S::kDS);
+      // the pending sub-tile whose dV / dK products are not issued yet
+      int pend_stage = 0, pend_j = 0;
+      bool pend_last = false, pend_first = false, have_pend = false;
+      auto issue_kv = [&](uint32_t uu) -> bool {
+        const uint32_t b = uu & 1;
+        if (!mbar_wait(&ds_full[b], (uu >> 1) & 1, p.f.status, __LINE__)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + S::kQ0 + pend_stage * S::kTile);
+        const uint32_t do_addr = smem_u32(smem + S::kDO0 + pend_stage * S::kTile);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acol = b * 128 + (kk >> 1) * 32 + (kk & 1) * 8;
+          umma_bf16_ts(tmem + kColDV, tmem + acol, mnmajor_desc(do_addr, pend_j * 4 + kk), idesc_kv,
+                       (!pend_first || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acol = b * 128 + 64 + (kk >> 1) * 32 + (kk & 1) * 8;
+          umma_bf16_ts(tmem + kColDK, tmem + acol, mnmajor_desc(q_addr, pend_j * 4 + kk), idesc_kv,
+                       (!pend_first || kk > 0) ? 1u : 0u);
+        }
+        if (pend_last) umma_commit(&q_empty[pend_stage]);
+        return true;
+      };
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         BwdItem it;
         if (!decode_bwd(p, w, it) || it.qt_hi <= it.qt_lo) continue;
@@ -671,35 +711,36 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         tc_fence_after();
         bool first = true;
         for (int hh = 0; hh < group && ok; ++hh) {
-          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt, ++n) {
+          for (int qt = it.qt_lo; qt < it.qt_hi && ok; ++qt) {
             if (!mbar_wait(&q_full[stage], phase, p.f.status, __LINE__)) { ok = false; break; }
             tc_fence_after();
             const uint32_t q_addr = smem_u32(smem + S::kQ0 + stage * S::kTile);
             const uint32_t do_addr = smem_u32(smem + S::kDO0 + stage * S::kTile);
+            for (int j = 0; j < 2; ++j, ++u) {
+              const uint32_t b = u & 1;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              umma_bf16_ss(tmem + kColS, kmajor_desc(k_addr, kk), kmajor_desc(q_addr, kk), idesc_s, kk > 0);
+              for (int kk = 0; kk < D / 16; ++kk)
+                umma_bf16_ss(tmem + b * 128, kmajor_desc(k_addr, kk), kmajor_desc(q_addr + j * 8192, kk), idesc_s,
+                             kk > 0);
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              umma_bf16_ss(tmem + kColDP, kmajor_desc(v_addr, kk), kmajor_desc(do_addr, kk), idesc_s, kk > 0);
-            umma_commit(s_full);
-            if (!mbar_wait(ds_full, n & 1, p.f.status, __LINE__)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ss(tmem + kColDV, kmajor_desc(p_addr, kk), mnmajor_desc(do_addr, kk), idesc_kv,
-                           (!first || kk > 0) ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ss(tmem + kColDK, kmajor_desc(ds_addr, kk), mnmajor_desc(q_addr, kk), idesc_kv,
-                           (!first || kk > 0) ? 1u : 0u);
-            umma_commit(mm_done);
-            umma_commit(&q_empty[stage]);
+              for (int kk = 0; kk < D / 16; ++kk)
+                umma_bf16_ss(tmem + b * 128 + 64, kmajor_desc(v_addr, kk), kmajor_desc(do_addr + j * 8192, kk),
+                             idesc_s, kk > 0);
+              umma_commit(&s_full[b]);
+              if (have_pend && !issue_kv(u - 1)) { ok = false; break; }
+              pend_stage = stage;
+              pend_j = j;
+              pend_last = j == 1;
+              pend_first = first && j == 0;
+              have_pend = true;
+            }
             first = false;
             if (++stage == ST) { stage = 0; phase ^= 1; }
           }
         }
         if (!ok) break;
+        if (!issue_kv(u - 1)) break;
+        have_pend = false;
         umma_commit(kk_done);
         umma_commit(kv_empty);
         ++items;
@@ -707,11 +748,12 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
   } else {
     const int qw = warp & 3;
-    const int r = qw * 32 + lane;  // TMEM lane = key row within the tile
+    const int half = (warp - 2) >> 2;  // queries [32 half, 32 half + 32) of each 64-query sub-tile
+    const int r = qw * 32 + lane;      // TMEM lane = key row within the tile
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    uint8_t* p_tile = smem + S::kP;
-    uint8_t* ds_tile = smem + S::kDS;
-    const int64_t total_q = p.f.cu_q != nullptr ? (int64_t)p.f.cu_q[p.f.num_seqs] : 0;
+    const float* s_lse = reinterpret_cast<const float*>(smem + S::kLse);
+    const float* s_delta = reinterpret_cast<const float*>(smem + S::kDelta);
+    uint32_t u = 0;
     int n = 0, items = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
@@ -721,30 +763,28 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int kp = it.k0 + r;
       if (it.qt_hi > it.qt_lo) {
         for (int hh = 0; hh < group && ok; ++hh) {
-          const int h = it.kvh * group + hh;
-          for (int qt = it.qt_lo; qt < it.qt_hi; ++qt, ++n) {
-            const int q0 = qt * 128;
-            if (!mbar_wait_warp(s_full, n & 1, p.f.status, __LINE__)) { ok = false; break; }
-            tc_fence_after();
-            // the previous iteration's dV/dK MMAs read P^T / dS^T: wait before overwriting
-            if (n > 0 && !mbar_wait_warp(mm_done, (n - 1) & 1, p.f.status, __LINE__)) { ok = false; break; }
+          for (int qt = it.qt_lo; qt < it.qt_hi && ok; ++qt, ++n) {
             const int st_idx = n % ST;
-            const float* c_lse = reinterpret_cast<const float*>(smem + S::kLse) + st_idx * 128;
-            const float* c_delta = reinterpret_cast<const float*>(smem + S::kDelta) + st_idx * 128;
-            // every (key, query) pair of the tile visible: no per-element masks
-            const bool edge = (it.k0 + 127 >= it.g.len_k) || (q0 + 127 >= it.g.len_q) ||
-                              (p.f.right >= 0 && it.k0 + 127 > q0 + off + p.f.right) ||
-                              (p.f.left >= 0 && it.k0 < q0 + 127 + off - p.f.left);
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int j = 0; j < 2; ++j, ++u) {
+              const uint32_t b = u & 1;
+              const int q0 = qt * 128 + 64 * j;  // first query of the sub-tile
+              if (!mbar_wait_warp(&s_full[b], (u >> 1) & 1, p.f.status, __LINE__)) { ok = false; break; }
+              tc_fence_after();
               float sv[32], dp[32];
-              tmem_ld32_raw(tmem + lane_base + kColS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv));
-              tmem_ld32_raw(tmem + lane_base + kColDP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(dp));
+              tmem_ld32_raw(tmem + lane_base + b * 128 + 32 * half, *reinterpret_cast<uint32_t(*)[32]>(sv));
+              tmem_ld32_raw(tmem + lane_base + b * 128 + 64 + 32 * half, *reinterpret_cast<uint32_t(*)[32]>(dp));
+              // every (key, query) pair of the sub-tile visible: no per-element masks
+              const bool edge = (it.k0 + 127 >= it.g.len_k) || (q0 + 63 >= it.g.len_q) ||
+                                (p.f.right >= 0 && it.k0 + 127 > q0 + off + p.f.right) ||
+                                (p.f.left >= 0 && it.k0 < q0 + 63 + off - p.f.left);
+              const float* c_lse = s_lse + st_idx * 128 + 64 * j + 32 * half;
+              const float* c_delta = s_delta + st_idx * 128 + 64 * j + 32 * half;
               tmem_wait_ld();
+              uint32_t pk[16], dk[16];
 #pragma unroll
               for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 l4 = reinterpret_cast<const float4*>(c_lse + c * 32)[i4];
-                const float4 d4 = reinterpret_cast<const float4*>(c_delta + c * 32)[i4];
+                const float4 l4 = reinterpret_cast<const float4*>(c_lse)[i4];
+                const float4 d4 = reinterpret_cast<const float4*>(c_delta)[i4];
                 const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
                 const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
@@ -752,7 +792,7 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                   const int i = i4 * 4 + e;
                   float pv = exp2f(fmaf(sv[i], p.f.scale_log2, -lv[e]));
                   if (edge) {
-                    const int qi = q0 + c * 32 + i;
+                    const int qi = q0 + 32 * half + i;
                     const int qpos = qi + off;
                     bool vis = qi < it.g.len_q && kp < it.g.len_k;
                     if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
@@ -764,24 +804,18 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
               }
 #pragma unroll
-              for (int g = 0; g < 4; ++g) {
-                const int ch = c * 4 + g;
-                const int atom = ch >> 3, cc = ch & 7;
-                const uint32_t o = atom * 16384 + r * 128 + ((cc ^ (r & 7)) * 16);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p_tile) + o),
-                             "r"(pack_bf16x2(sv[g * 8 + 0], sv[g * 8 + 1])), "r"(pack_bf16x2(sv[g * 8 + 2], sv[g * 8 + 3])),
-                             "r"(pack_bf16x2(sv[g * 8 + 4], sv[g * 8 + 5])), "r"(pack_bf16x2(sv[g * 8 + 6], sv[g * 8 + 7]))
-                             : "memory");
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(ds_tile) + o),
-                             "r"(pack_bf16x2(dp[g * 8 + 0], dp[g * 8 + 1])), "r"(pack_bf16x2(dp[g * 8 + 2], dp[g * 8 + 3])),
-                             "r"(pack_bf16x2(dp[g * 8 + 4], dp[g * 8 + 5])), "r"(pack_bf16x2(dp[g * 8 + 6], dp[g * 8 + 7]))
-                             : "memory");
+              for (int m = 0; m < 16; ++m) {
+                pk[m] = pack_bf16x2(sv[2 * m], sv[2 * m + 1]);
+                dk[m] = pack_bf16x2(dp[2 * m], dp[2 * m + 1]);
               }
+              // packed P^T / dS^T over the first 16 of the 32 columns this warp group read
+              tmem_st16_raw(tmem + lane_base + b * 128 + 32 * half, pk);
+              tmem_st16_raw(tmem + lane_base + b * 128 + 64 + 32 * half, dk);
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&ds_full[b]);
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(ds_full);
           }
         }
         if (!ok) break;
@@ -792,10 +826,10 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         __nv_bfloat16* dkp = p.dk + (krow * p.f.kv_heads + it.kvh) * D;
         __nv_bfloat16* dvp = p.dv + (krow * p.f.kv_heads + it.kvh) * D;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float a[32], b[32];
+        for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
+          float a[32], bv[32];
           tmem_ld32(tmem + lane_base + kColDK + c * 32, a);
-          tmem_ld32(tmem + lane_base + kColDV + c * 32, b);
+          tmem_ld32(tmem + lane_base + kColDV + c * 32, bv);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -804,10 +838,10 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
               ka.y = pack_bf16x2(a[8 * i + 2], a[8 * i + 3]);
               ka.z = pack_bf16x2(a[8 * i + 4], a[8 * i + 5]);
               ka.w = pack_bf16x2(a[8 * i + 6], a[8 * i + 7]);
-              va.x = pack_bf16x2(b[8 * i + 0], b[8 * i + 1]);
-              va.y = pack_bf16x2(b[8 * i + 2], b[8 * i + 3]);
-              va.z = pack_bf16x2(b[8 * i + 4], b[8 * i + 5]);
-              va.w = pack_bf16x2(b[8 * i + 6], b[8 * i + 7]);
+              va.x = pack_bf16x2(bv[8 * i + 0], bv[8 * i + 1]);
+              va.y = pack_bf16x2(bv[8 * i + 2], bv[8 * i + 3]);
+              va.z = pack_bf16x2(bv[8 * i + 4], bv[8 * i + 5]);
+              va.w = pack_bf16x2(bv[8 * i + 6], bv[8 * i + 7]);
               reinterpret_cast<uint4*>(dkp + c * 32)[i] = ka;
               reinterpret_cast<uint4*>(dvp + c * 32)[i] = va;
             }
@@ -821,7 +855,7 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int64_t krow = it.g.k_start + it.k0 + r;
         __nv_bfloat16* dkp = p.dk + (krow * p.f.kv_heads + it.kvh) * D;
         __nv_bfloat16* dvp = p.dv + (krow * p.f.kv_heads + it.kvh) * D;
-        for (int i = 0; i < D / 8; ++i) {
+        for (int i = half * (D / 16); i < (half + 1) * (D / 16); ++i) {
           reinterpret_cast<uint4*>(dkp)[i] = make_uint4(0, 0, 0, 0);
           reinterpret_cast<uint4*>(dvp)[i] = make_uint4(0, 0, 0, 0);
         }
@@ -853,7 +887,7 @@ struct DqSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kFaThreads, 1)
+__global__ void __launch_bounds__(kFaBwdThreads, 1)
 fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                  const FaBwdParams p) {
@@ -885,7 +919,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(ds_full, 4);
+    mbar_init(ds_full, kBwdSoftmaxWarps);
     mbar_init(mm_done, 1);
     fence_barrier_init();
   }
@@ -961,6 +995,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     }
   } else {
     const int qw = warp & 3;
+    const int half = (warp - 2) >> 2;  // key columns [64 half, 64 half + 64)
     const int row = qw * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
     uint8_t* ds_tile = smem + S::kDS;
@@ -994,7 +1029,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                                  : 0;
         const float ps = p.scale;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
           float sv[32], dp[32];
           tmem_ld32_raw(tmem + lane_base + kColS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv));
           tmem_ld32_raw(tmem + lane_base + kColDP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(dp));
@@ -1028,7 +1063,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         if (!mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) break;
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
           float v[32];
           tmem_ld32(tmem + lane_base + kColDQ + c * 32, v);
           if (qvalid) {
@@ -1045,7 +1080,8 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         }
         tc_fence_before();
       } else if (qvalid) {
-        for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+        for (int i = half * (D / 16); i < (half + 1) * (D / 16); ++i)
+          reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
       }
     }
   }
@@ -1097,7 +1133,7 @@ static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
       configured = true;
     }
     const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
-    kern<<<std::max(1, std::min(total, sm_count())), kFaThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
+    kern<<<std::max(1, std::min(total, sm_count())), kFaBwdThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   {
@@ -1108,7 +1144,7 @@ static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
       configured = true;
     }
-    kern<<<std::max(1, std::min(p.f.total_items, sm_count())), kFaThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
+    kern<<<std::max(1, std::min(p.f.total_items, sm_count())), kFaBwdThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

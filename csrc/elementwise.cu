@@ -1,4 +1,5 @@
-// Elementwise kernels (sm_100a): SwiGLU forward/backward, interleaved-pair RoPE, token
+// Elementwise kernels (sm_100a): SwiGLU forward/backward, interleaved-pair RoPE (also fused
+// over the QKV projection), token
 // embedding gather / scatter-add.  All use 16-byte vector accesses on bf16 data.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -150,6 +151,132 @@ torch::Tensor rope(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, to
       cos_t.size(0), inverse);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return y;
+}
+
+// ------------------------------------------------------------------------ fused QKV RoPE
+// Attention input in one pass.  Forward: rows of the QKV projection (q heads, then k heads,
+// then v heads, row stride `rs` elements) -> rotated q (T, H, D), rotated k (T, KV, D) and
+// v (T, KV, D), all contiguous.  Backward: dq, dk, dv -> the QKV gradient rows, with q / k
+// rotated back.  Each thread moves one 16-byte vector (4 interleaved pairs); the cos / sin
+// tables hold one fp32 value per element (pair values repeated), so a vector reads the
+// 8 table entries at its own offset.
+template <int D, bool BWD>
+__global__ void rope_qkv_kernel(const __nv_bfloat16* __restrict__ src0, const __nv_bfloat16* __restrict__ src1,
+                                const __nv_bfloat16* __restrict__ src2, __nv_bfloat16* __restrict__ dst0,
+                                __nv_bfloat16* __restrict__ dst1, __nv_bfloat16* __restrict__ dst2,
+                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                const int64_t* __restrict__ pos, uint32_t rows, int H, int KV, int64_t rs,
+                                int64_t table_len) {
+  constexpr int kVecPerHead = D / 8;
+  const uint32_t vec_per_row = (uint32_t)(H + 2 * KV) * kVecPerHead;
+  const uint64_t total = (uint64_t)rows * vec_per_row;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t t = (uint32_t)(i / vec_per_row);
+    const uint32_t j = (uint32_t)(i - (uint64_t)t * vec_per_row);
+    const int head = (int)(j / kVecPerHead);
+    const int d0 = (int)(j % kVecPerHead) * 8;
+    // source and destination of this vector
+    const __nv_bfloat16* sp;
+    __nv_bfloat16* dp;
+    if (!BWD) {
+      sp = src0 + (int64_t)t * rs + head * D + d0;
+      if (head < H) dp = dst0 + ((int64_t)t * H + head) * D + d0;
+      else if (head < H + KV) dp = dst1 + ((int64_t)t * KV + head - H) * D + d0;
+      else dp = dst2 + ((int64_t)t * KV + head - H - KV) * D + d0;
+    } else {
+      if (head < H) sp = src0 + ((int64_t)t * H + head) * D + d0;
+      else if (head < H + KV) sp = src1 + ((int64_t)t * KV + head - H) * D + d0;
+      else sp = src2 + ((int64_t)t * KV + head - H - KV) * D + d0;
+      dp = dst0 + (int64_t)t * rs + head * D + d0;
+    }
+    bf16x8 v = *reinterpret_cast<const bf16x8*>(sp);
+    if (head < H + KV) {
+      int64_t ps = pos[t];
+      ps = ps < 0 ? 0 : (ps >= table_len ? table_len - 1 : ps);
+      const float4 c0 = *reinterpret_cast<const float4*>(cos_t + ps * D + d0);
+      const float4 c1 = *reinterpret_cast<const float4*>(cos_t + ps * D + d0 + 4);
+      const float4 s0 = *reinterpret_cast<const float4*>(sin_t + ps * D + d0);
+      const float4 s1 = *reinterpret_cast<const float4*>(sin_t + ps * D + d0 + 4);
+      const float cs[4] = {c0.x, c0.z, c1.x, c1.z};
+      const float sn[4] = {BWD ? -s0.x : s0.x, BWD ? -s0.z : s0.z, BWD ? -s1.x : s1.x, BWD ? -s1.z : s1.z};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(v.v[q]);
+        v.v[q] = __floats2bfloat162_rn(f.x * cs[q] - f.y * sn[q], f.y * cs[q] + f.x * sn[q]);
+      }
+    }
+    *reinterpret_cast<bf16x8*>(dp) = v;
+  }
+}
+
+static void check_rope_tables(const torch::Tensor& cos_t, const torch::Tensor& sin_t, int D) {
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.is_contiguous() && sin_t.is_contiguous() &&
+                  cos_t.size(-1) == D && sin_t.sizes() == cos_t.sizes(),
+              "rope_qkv: fp32 (positions, head_dim) tables");
+}
+
+template <bool BWD>
+static void launch_rope_qkv(int D, const __nv_bfloat16* s0, const __nv_bfloat16* s1, const __nv_bfloat16* s2,
+                            __nv_bfloat16* d0, __nv_bfloat16* d1, __nv_bfloat16* d2, const torch::Tensor& cos_t,
+                            const torch::Tensor& sin_t, const torch::Tensor& pos, int64_t rows, int H, int KV,
+                            int64_t rs) {
+  const int64_t total = rows * (H + 2 * KV) * (D / 8);
+  if (total == 0) return;
+  TORCH_CHECK(rows < (int64_t)UINT32_MAX, "rope_qkv: too many rows");
+  auto st = at::cuda::getCurrentCUDAStream();
+  const unsigned grid = ew_grid(total, 256);
+  if (D == 64)
+    rope_qkv_kernel<64, BWD><<<grid, 256, 0, st>>>(s0, s1, s2, d0, d1, d2, cos_t.data_ptr<float>(),
+                                                   sin_t.data_ptr<float>(), pos.data_ptr<int64_t>(), (uint32_t)rows,
+                                                   H, KV, rs, cos_t.size(0));
+  else if (D == 128)
+    rope_qkv_kernel<128, BWD><<<grid, 256, 0, st>>>(s0, s1, s2, d0, d1, d2, cos_t.data_ptr<float>(),
+                                                    sin_t.data_ptr<float>(), pos.data_ptr<int64_t>(), (uint32_t)rows,
+                                                    H, KV, rs, cos_t.size(0));
+  else
+    TORCH_CHECK(false, "rope_qkv: head_dim 64 or 128");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// qkv (B, S, (H + 2 KV) D) bf16 with unit last stride -> [q (B,S,H,D), k (B,S,KV,D), v (B,S,KV,D)].
+std::vector<torch::Tensor> rope_qkv_fwd(torch::Tensor qkv, torch::Tensor cos_t, torch::Tensor sin_t,
+                                        torch::Tensor pos, int64_t H, int64_t KV) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  TORCH_CHECK(qkv.dim() == 3 && qkv.scalar_type() == at::kBFloat16 && qkv.stride(2) == 1 &&
+                  qkv.stride(0) == qkv.size(1) * qkv.stride(1),
+              "rope_qkv: bf16 (B, S, width) with unit last stride and uniformly strided rows");
+  const int64_t B = qkv.size(0), S = qkv.size(1), D = qkv.size(2) / (H + 2 * KV);
+  TORCH_CHECK(D * (H + 2 * KV) == qkv.size(2), "rope_qkv: width is not (H + 2 KV) * head_dim");
+  TORCH_CHECK(qkv.stride(1) % 8 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0,
+              "rope_qkv: rows must be 16-byte aligned");
+  check_rope_tables(cos_t, sin_t, (int)D);
+  TORCH_CHECK(pos.is_contiguous() && pos.scalar_type() == at::kLong && pos.numel() == B * S, "rope_qkv: positions");
+  auto q = torch::empty({B, S, H, D}, qkv.options());
+  auto k = torch::empty({B, S, KV, D}, qkv.options());
+  auto v = torch::empty({B, S, KV, D}, qkv.options());
+  auto bp = [](torch::Tensor& t) { return (__nv_bfloat16*)t.data_ptr(); };
+  launch_rope_qkv<false>((int)D, (const __nv_bfloat16*)qkv.data_ptr(), nullptr, nullptr, bp(q), bp(k), bp(v), cos_t,
+                         sin_t, pos, B * S, (int)H, (int)KV, qkv.stride(1));
+  return {q, k, v};
+}
+
+// dq (B,S,H,D), dk, dv (B,S,KV,D) -> dqkv (B, S, (H + 2 KV) D), contiguous.
+torch::Tensor rope_qkv_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor cos_t,
+                           torch::Tensor sin_t, torch::Tensor pos) {
+  c10::cuda::CUDAGuard guard(dq.device());
+  dq = dq.contiguous();
+  dk = dk.contiguous();
+  dv = dv.contiguous();
+  const int64_t B = dq.size(0), S = dq.size(1), H = dq.size(2), D = dq.size(3), KV = dk.size(2);
+  TORCH_CHECK(dq.scalar_type() == at::kBFloat16 && dk.scalar_type() == at::kBFloat16 &&
+                  dv.scalar_type() == at::kBFloat16 && dk.sizes() == dv.sizes(),
+              "rope_qkv_bwd: bf16 gradients");
+  check_rope_tables(cos_t, sin_t, (int)D);
+  auto dqkv = torch::empty({B, S, (H + 2 * KV) * D}, dq.options());
+  auto bp = [](const torch::Tensor& t) { return (__nv_bfloat16*)t.data_ptr(); };
+  launch_rope_qkv<true>((int)D, bp(dq), bp(dk), bp(dv), bp(dqkv), nullptr, nullptr, cos_t, sin_t, pos, B * S, (int)H,
+                        (int)KV, (H + 2 * KV) * D);
+  return dqkv;
 }
 
 // ------------------------------------------------------------------------ embedding

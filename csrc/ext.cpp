@@ -19,6 +19,10 @@ std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, 
 torch::Tensor swiglu_fwd(torch::Tensor gu);
 torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
 torch::Tensor rope(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos, bool inverse);
+std::vector<torch::Tensor> rope_qkv_fwd(torch::Tensor qkv, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos,
+                                        int64_t H, int64_t KV);
+torch::Tensor rope_qkv_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor cos_t, torch::Tensor sin_t,
+                           torch::Tensor pos);
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
 void embedding_bwd(torch::Tensor ids, torch::Tensor dout, torch::Tensor grad);
 // loss.cu
@@ -97,6 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_fwd", &mykb::swiglu_fwd);
   m.def("swiglu_bwd", &mykb::swiglu_bwd);
   m.def("rope", &mykb::rope);
+  m.def("rope_qkv_fwd", &mykb::rope_qkv_fwd);
+  m.def("rope_qkv_bwd", &mykb::rope_qkv_bwd);
   m.def("embedding_fwd", &mykb::embedding_fwd);
   m.def("embedding_bwd", &mykb::embedding_bwd);
   m.def("ce_fwd_grad", &mykb::ce_fwd_grad);

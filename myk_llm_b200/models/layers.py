@@ -108,6 +108,10 @@ class RotaryEmbedding(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, position_ids: torch.Tensor):
         return self.rotate(q, position_ids), self.rotate(k, position_ids)
 
+    def split_qkv(self, qkv: torch.Tensor, position_ids: torch.Tensor, heads: int, kv_heads: int):
+        """Rotated q, k and v from a fused QKV projection (one pass over it)."""
+        return ops.rope_qkv(qkv, self.cos_cached, self.sin_cached, position_ids, heads, kv_heads)
+
 
 def init_linear_(module: nn.Module, std: float) -> None:
     if isinstance(module, (nn.Linear, nn.Embedding)):

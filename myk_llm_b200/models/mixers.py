@@ -82,15 +82,18 @@ class Attention(nn.Module):
                 use_cache: bool = False):
         bsz, seq, _ = x.shape
         qkv = ops.linear(x, self.qkv_proj.weight)
-        q, k, v = qkv.split(self.split, dim=-1)
-        q = q.view(bsz, seq, self.num_heads, self.head_dim)
-        k = k.view(bsz, seq, self.num_kv_heads, self.head_dim)
-        v = v.view(bsz, seq, self.num_kv_heads, self.head_dim)
-        if self.q_norm is not None and self.k_norm is not None:
-            q = self.q_norm(q, out_dtype=v.dtype)
-            k = self.k_norm(k, out_dtype=v.dtype)
-        if self.rope is not None:
-            q, k = self.rope(q, k, position_ids)
+        if self.rope is not None and self.q_norm is None and qkv.is_cuda:
+            q, k, v = self.rope.split_qkv(qkv, position_ids, self.num_heads, self.num_kv_heads)
+        else:
+            q, k, v = qkv.split(self.split, dim=-1)
+            q = q.view(bsz, seq, self.num_heads, self.head_dim)
+            k = k.view(bsz, seq, self.num_kv_heads, self.head_dim)
+            v = v.view(bsz, seq, self.num_kv_heads, self.head_dim)
+            if self.q_norm is not None and self.k_norm is not None:
+                q = self.q_norm(q, out_dtype=v.dtype)
+                k = self.k_norm(k, out_dtype=v.dtype)
+            if self.rope is not None:
+                q, k = self.rope(q, k, position_ids)
         window = (self.window - 1, 0) if self.window is not None else (-1, -1)
         new_state = KVCache(k, v) if self.shares_kv else None
         if isinstance(state, StaticKV):

@@ -165,6 +165,37 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, position_i
     return _Rope.apply(x, cos, sin, _c(pos))
 
 
+class _RopeQKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cos, sin, pos, heads: int, kv_heads: int):
+        q, k, v = ext().rope_qkv_fwd(qkv, cos, sin, pos, heads, kv_heads)
+        ctx.save_for_backward(cos, sin, pos)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos, sin, pos = ctx.saved_tensors
+        return ext().rope_qkv_bwd(dq, dk, dv, cos, sin, pos), None, None, None, None, None
+
+
+def rope_qkv(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, position_ids: torch.Tensor, heads: int,
+             kv_heads: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Split a fused QKV projection (B, S, (heads + 2 kv_heads) d) into rotated q (B, S, heads, d),
+    rotated k and v (B, S, kv_heads, d) in one pass (one kernel forward, one backward that
+    writes the QKV gradient directly)."""
+    b, s_, width = qkv.shape
+    d = width // (heads + 2 * kv_heads)
+    if not qkv.is_cuda or d not in (64, 128) or qkv.dtype != torch.bfloat16:
+        q, k, v = qkv.split((heads * d, kv_heads * d, kv_heads * d), dim=-1)
+        q, k = q.view(b, s_, heads, d), k.view(b, s_, kv_heads, d)
+        return apply_rope(q, cos, sin, position_ids), apply_rope(k, cos, sin, position_ids), \
+            v.view(b, s_, kv_heads, d)
+    pos = position_ids.expand(b, s_)
+    if pos.dtype != torch.int64:
+        pos = pos.long()
+    return _RopeQKV.apply(qkv, cos, sin, _c(pos), heads, kv_heads)
+
+
 # ---------------------------------------------------------------------------------------
 # embedding
 # ---------------------------------------------------------------------------------------

@@ -120,6 +120,37 @@ def test_rope_strided_and_inverse():
     _close(q2.grad, qr.grad, 2e-2)
 
 
+@pytest.mark.parametrize("d,heads,kv", [(64, 4, 2), (128, 8, 2)])
+def test_fused_qkv_rope_matches_split_reference(d, heads, kv):
+    from myk_llm_b200 import ops
+    from myk_llm_b200.models.layers import RotaryEmbedding
+    from myk_llm_b200.ops.reference import rope_ref
+
+    torch.manual_seed(5)
+    rope = RotaryEmbedding(d, 512, 10000.0).cuda()
+    width = (heads + 2 * kv) * d
+    # a strided row view (as a slice of a wider buffer) exercises the row stride
+    base = torch.randn(3, 45, width + 64, device="cuda", dtype=torch.bfloat16)
+    qkv = base[..., :width].detach().requires_grad_(True)
+    pos = torch.randint(0, 500, (3, 45), device="cuda")
+    q, k, v = ops.rope_qkv(qkv, rope.cos_cached, rope.sin_cached, pos, heads, kv)
+    assert q.is_contiguous() and k.is_contiguous() and v.is_contiguous()
+    gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    (q.float() * gq.float()).sum().add_((k.float() * gk.float()).sum()).add_((v.float() * gv.float()).sum()).backward()
+    ref = qkv.detach().float().requires_grad_(True)
+    rq, rk, rv = ref.split((heads * d, kv * d, kv * d), dim=-1)
+    c = rope.cos_cached[pos].unsqueeze(2)
+    s = rope.sin_cached[pos].unsqueeze(2)
+    rq = rope_ref(rq.reshape(3, 45, heads, d), c, s)
+    rk = rope_ref(rk.reshape(3, 45, kv, d), c, s)
+    rv = rv.reshape(3, 45, kv, d)
+    _close(q, rq, 1e-2)
+    _close(k, rk, 1e-2)
+    assert torch.equal(v.float(), rv)
+    ((rq * gq.float()).sum() + (rk * gk.float()).sum() + (rv * gv.float()).sum()).backward()
+    _close(qkv.grad, ref.grad, 2e-2)
+
+
 def test_embedding():
     from myk_llm_b200 import ops
 
