@@ -21,8 +21,8 @@
 //   dV  += P^T dO         (M=128, N=d, K=queries; A = P^T from TMEM)
 //   dK  += dS^T Q         (M=128, N=d, K=queries; A = dS^T from TMEM)
 // over 64-query sub-tiles with double-buffered S^T / dP^T so MMAs overlap the softmax.
-// Kernel 2 (dQ per 128-query tile) recomputes S and dP with the forward's operand
-// patterns and accumulates dQ += dS K in TMEM, so no atomics and a deterministic result.
+// Kernel 2 (dQ per 128-query tile) recomputes S and dP over 64-key sub-tiles the same way
+// and accumulates dQ += dS K in TMEM (A = dS from TMEM): no atomics, a deterministic result.
 // Both backward kernels run eight softmax-gradient warps (two per SM sub-partition, each
 // owning half of the tile's columns).  Delta = rowsum(dO * O) comes from a small pre-kernel.
 //
@@ -871,18 +871,22 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 }
 
 // ------------------------------------------------------------------ dQ per query tile
-// Same item walk and operand patterns as the forward: S = Q K^T and dP = dO V^T
-// (A, B K-major), dS = P (dP - Delta) written as a K-major tile (like P), dQ += dS K
-// (B = K tile MN-major, like V in the forward).
+// Same item walk as the forward.  Each 128-key tile is processed as two 64-key sub-tiles u
+// with S = Q K^T and dP = dO V^T (A, B K-major) double-buffered in TMEM; the softmax
+// warps (thread = query row) write dS = P (dP - Delta) back over the S columns they read
+// as packed bf16, and dQ += dS K takes A from TMEM (B = K sub-tile, MN-major).
+//
+// TMEM columns (b = u & 1): S [128 b, 128 b + 64), dP [128 b + 64, 128 b + 128),
+// dQ [256, 256 + D).  Softmax group h owns keys [32 h, 32 h + 32) of a sub-tile.
 template <int D>
 struct DqSmem {
+  static constexpr int kStages = D == 64 ? 4 : 2;  // K / V ring depth
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kQ = 0;
   static constexpr int kDO = kQ + kTile;
   static constexpr int kK0 = kDO + kTile;
-  static constexpr int kV0 = kK0 + 2 * kTile;
-  static constexpr int kDS = kV0 + 2 * kTile;
-  static constexpr int kBars = kDS + 128 * 128 * 2;
+  static constexpr int kV0 = kK0 + kStages * kTile;
+  static constexpr int kBars = kV0 + kStages * kTile;
   static constexpr int kTotal = kBars + 256;
 };
 
@@ -892,6 +896,7 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                  const FaBwdParams p) {
   using S = DqSmem<D>;
+  constexpr int ST = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem) & 1023) != 0) {
@@ -899,28 +904,32 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
-  uint64_t* kv_full = bars;       // [2]
-  uint64_t* kv_empty = bars + 2;  // [2]
-  uint64_t* q_full = bars + 4;
-  uint64_t* q_empty = bars + 5;
-  uint64_t* s_full = bars + 6;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* mm_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
-  constexpr int kCols = 512;  // S [0,128), dP [128,256), dQ [256, 256+D)
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+  uint64_t* kv_full = bars;             // [ST]
+  uint64_t* kv_empty = bars + ST;       // [ST]
+  uint64_t* q_full = bars + 2 * ST;
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* s_full = q_full + 2;        // [2]
+  uint64_t* ds_full = q_full + 4;       // [2]
+  uint64_t* dq_done = q_full + 6;
+  uint64_t* dq_free = q_full + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 8);
+  constexpr int kCols = 512;
+  constexpr uint32_t kColDQ = 256;
   const FaParams& f = p.f;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, kBwdSoftmaxWarps);
-    mbar_init(mm_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], kBwdSoftmaxWarps);
+    }
+    mbar_init(dq_done, 1);
+    mbar_init(dq_free, kBwdSoftmaxWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
@@ -948,59 +957,82 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           const int row = it.g.k_start + it.kv_lo + j * 128;
           load_tile<D>(smem + S::kK0 + stage * S::kTile, &tmK, &kv_full[stage], kvh * D, row);
           load_tile<D>(smem + S::kV0 + stage * S::kTile, &tmV, &kv_full[stage], kvh * D, row);
-          if (++stage == 2) { stage = 0; phase ^= 1; }
+          if (++stage == ST) { stage = 0; phase ^= 1; }
         }
         ++items;
       }
     }
   } else if (warp == 1) {
-    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
-    constexpr uint32_t idesc_q = make_idesc_bf16(128, D, false, true);
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, false, false);  // Q K^T, dO V^T (N = 64 keys)
+    constexpr uint32_t idesc_q = make_idesc_bf16(128, D, false, true);    // dS K (A from TMEM)
     if (elect_one()) {
-      int stage = 0, items = 0, ntile = 0;
-      uint32_t phase = 0;
+      int stage = 0, items = 0;
+      uint32_t phase = 0, u = 0;
       bool ok = true;
       const uint32_t q_addr = smem_u32(smem + S::kQ), do_addr = smem_u32(smem + S::kDO);
-      const uint32_t ds_addr = smem_u32(smem + S::kDS);
+      int pend_stage = 0, pend_j = 0;
+      bool pend_last = false, pend_first = false, have_pend = false;
+      auto issue_dq = [&](uint32_t uu) -> bool {
+        const uint32_t b = uu & 1;
+        if (!mbar_wait(&ds_full[b], (uu >> 1) & 1, f.status, __LINE__)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + S::kK0 + pend_stage * S::kTile);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acol = b * 128 + (kk >> 1) * 32 + (kk & 1) * 8;
+          umma_bf16_ts(tmem + kColDQ, tmem + acol, mnmajor_desc(k_addr, pend_j * 4 + kk), idesc_q,
+                       (!pend_first || kk > 0) ? 1u : 0u);
+        }
+        if (pend_last) umma_commit(&kv_empty[pend_stage]);
+        return true;
+      };
       for (int w = blockIdx.x; w < f.total_items && ok; w += gridDim.x) {
         Item it;
         if (!decode_item(f, w, it) || it.n_kv == 0) continue;
         if (!mbar_wait(q_full, items & 1, f.status, __LINE__)) break;
+        if (!mbar_wait(dq_free, (items & 1) ^ 1, f.status, __LINE__)) break;
         tc_fence_after();
-        for (int j = 0; j < it.n_kv && ok; ++j, ++ntile) {
+        for (int jt = 0; jt < it.n_kv && ok; ++jt) {
           if (!mbar_wait(&kv_full[stage], phase, f.status, __LINE__)) { ok = false; break; }
           tc_fence_after();
           const uint32_t k_addr = smem_u32(smem + S::kK0 + stage * S::kTile);
           const uint32_t v_addr = smem_u32(smem + S::kV0 + stage * S::kTile);
+          for (int j = 0; j < 2; ++j, ++u) {
+            const uint32_t b = u & 1;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_bf16_ss(tmem + kColS, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s, kk > 0);
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_bf16_ss(tmem + b * 128, kmajor_desc(q_addr, kk), kmajor_desc(k_addr + j * 8192, kk), idesc_s,
+                           kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_bf16_ss(tmem + kColDP, kmajor_desc(do_addr, kk), kmajor_desc(v_addr, kk), idesc_s, kk > 0);
-          umma_commit(s_full);
-          if (j == it.n_kv - 1) umma_commit(q_empty);
-          if (!mbar_wait(ds_full, ntile & 1, f.status, __LINE__)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ss(tmem + kColDQ, kmajor_desc(ds_addr, kk), mnmajor_desc(k_addr, kk), idesc_q,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(mm_done);
-          umma_commit(&kv_empty[stage]);
-          if (++stage == 2) { stage = 0; phase ^= 1; }
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_bf16_ss(tmem + b * 128 + 64, kmajor_desc(do_addr, kk), kmajor_desc(v_addr + j * 8192, kk),
+                           idesc_s, kk > 0);
+            umma_commit(&s_full[b]);
+            if (jt == it.n_kv - 1 && j == 1) umma_commit(q_empty);
+            if (have_pend && !issue_dq(u - 1)) { ok = false; break; }
+            pend_stage = stage;
+            pend_j = j;
+            pend_last = j == 1;
+            pend_first = jt == 0 && j == 0;
+            have_pend = true;
+          }
+          if (++stage == ST) { stage = 0; phase ^= 1; }
         }
+        if (!ok) break;
+        if (!issue_dq(u - 1)) break;
+        have_pend = false;
+        umma_commit(dq_done);
         ++items;
       }
     }
   } else {
     const int qw = warp & 3;
-    const int half = (warp - 2) >> 2;  // key columns [64 half, 64 half + 64)
+    const int half = (warp - 2) >> 2;  // keys [32 half, 32 half + 32) of each 64-key sub-tile
     const int row = qw * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    uint8_t* ds_tile = smem + S::kDS;
     const int64_t total_q = f.cu_q != nullptr ? (int64_t)f.cu_q[f.num_seqs] : 0;
-    int ntile = 0;
+    uint32_t u = 0;
+    int items = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < f.total_items && ok; w += gridDim.x) {
       Item it;
@@ -1016,51 +1048,47 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         lse2 = p.lse[li] * kLog2e;
         dl = p.delta[li];
       }
-      for (int j = 0; j < it.n_kv; ++j, ++ntile) {
-        if (!mbar_wait_warp(s_full, ntile & 1, f.status, __LINE__)) { ok = false; break; }
-        tc_fence_after();
-        if (j > 0 && !mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) { ok = false; break; }
-        const int k0 = it.kv_lo + j * 128;
-        const bool edge = !qvalid_tile || (k0 + 127 >= it.g.len_k) ||
-                          (f.right >= 0 && k0 + 127 > it.q0 + off + f.right) ||
-                          (f.left >= 0 && k0 < it.q0 + it.rows - 1 + off - f.left);
-        const int kmin = (f.left >= 0 ? max(0, qpos - f.left) : 0) - k0;
-        const int kspan = qvalid ? max(0, min(it.g.len_k, f.right >= 0 ? qpos + f.right + 1 : it.g.len_k) - k0 - kmin)
-                                 : 0;
-        const float ps = p.scale;
-#pragma unroll 1
-        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+      for (int jt = 0; jt < it.n_kv && ok; ++jt) {
+        for (int j = 0; j < 2; ++j, ++u) {
+          const uint32_t b = u & 1;
+          if (!mbar_wait_warp(&s_full[b], (u >> 1) & 1, f.status, __LINE__)) { ok = false; break; }
+          tc_fence_after();
           float sv[32], dp[32];
-          tmem_ld32_raw(tmem + lane_base + kColS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv));
-          tmem_ld32_raw(tmem + lane_base + kColDP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(dp));
+          tmem_ld32_raw(tmem + lane_base + b * 128 + 32 * half, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_ld32_raw(tmem + lane_base + b * 128 + 64 + 32 * half, *reinterpret_cast<uint32_t(*)[32]>(dp));
+          const int k0 = it.kv_lo + jt * 128 + 64 * j;  // first key of the sub-tile
+          const bool edge = !qvalid_tile || (k0 + 63 >= it.g.len_k) ||
+                            (f.right >= 0 && k0 + 63 > it.q0 + off + f.right) ||
+                            (f.left >= 0 && k0 < it.q0 + it.rows - 1 + off - f.left);
+          // keys visible to this row form one range; as offsets from k0:
+          const int kmin = (f.left >= 0 ? max(0, qpos - f.left) : 0) - k0;
+          const int kspan =
+              qvalid ? max(0, min(it.g.len_k, f.right >= 0 ? qpos + f.right + 1 : it.g.len_k) - k0 - kmin) : 0;
+          const float ps = p.scale;
           tmem_wait_ld();
+          uint32_t dk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float pv = exp2f(fmaf(sv[i], f.scale_log2, -lse2));
-            if (edge && (unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) pv = 0.f;
-            dp[i] = (pv * ps) * (dp[i] - dl);
+          for (int i = 0; i < 32; i += 2) {
+            float p0 = exp2f(fmaf(sv[i], f.scale_log2, -lse2));
+            float p1 = exp2f(fmaf(sv[i + 1], f.scale_log2, -lse2));
+            if (edge) {
+              if ((unsigned)(32 * half + i - kmin) >= (unsigned)kspan) p0 = 0.f;
+              if ((unsigned)(32 * half + i + 1 - kmin) >= (unsigned)kspan) p1 = 0.f;
+            }
+            dk[i >> 1] = pack_bf16x2((p0 * ps) * (dp[i] - dl), (p1 * ps) * (dp[i + 1] - dl));
           }
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int ch = c * 4 + g;
-            const int atom = ch >> 3, cc = ch & 7;
-            const uint32_t o = atom * 16384 + row * 128 + ((cc ^ (row & 7)) * 16);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(ds_tile) + o),
-                         "r"(pack_bf16x2(dp[g * 8 + 0], dp[g * 8 + 1])), "r"(pack_bf16x2(dp[g * 8 + 2], dp[g * 8 + 3])),
-                         "r"(pack_bf16x2(dp[g * 8 + 4], dp[g * 8 + 5])), "r"(pack_bf16x2(dp[g * 8 + 6], dp[g * 8 + 7]))
-                         : "memory");
-          }
+          tmem_st16_raw(tmem + lane_base + b * 128 + 32 * half, dk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ds_full[b]);
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ds_full);
       }
       if (!ok) break;
       const int64_t tok = it.g.q_start + it.q0 + row;
       __nv_bfloat16* dst = p.dq + (tok * f.heads + it.head) * D;
       if (it.n_kv > 0) {
-        if (!mbar_wait_warp(mm_done, (ntile - 1) & 1, f.status, __LINE__)) break;
+        if (!mbar_wait_warp(dq_done, items & 1, f.status, __LINE__)) break;
         tc_fence_after();
 #pragma unroll
         for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
@@ -1079,6 +1107,9 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           }
         }
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        ++items;
       } else if (qvalid) {
         for (int i = half * (D / 16); i < (half + 1) * (D / 16); ++i)
           reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
