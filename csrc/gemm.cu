@@ -50,8 +50,9 @@ struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStagingBytes = 32 * 128;  // per epilogue warp: 32 rows x 128 B
-  static constexpr int kBarOffset = STAGES * kStageBytes + kEpiWarps * kStagingBytes;
+  static constexpr int kStagingBytes = 32 * 128;  // one epilogue slab: 32 rows x 128 B
+  // two staging slabs per epilogue warp, so a slab's TMA store overlaps the next slab
+  static constexpr int kBarOffset = STAGES * kStageBytes + kEpiWarps * 2 * kStagingBytes;
   static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + alignment slack
 };
 
@@ -181,9 +182,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* stage_buf = staging + (warp - 2) * S::kStagingBytes;
-    const uint32_t stage_addr = smem_u32(stage_buf);
-    int local = 0;
+    const uint32_t stage_base = smem_u32(staging + (warp - 2) * 2 * S::kStagingBytes);
+    int local = 0, slab_ct = 0;
     for (int unit = blockIdx.x; unit < p.total_units; unit += gridDim.x, ++local) {
       int b, mt, nt, split;
       unit_coords(p, unit, b, mt, nt, split);
@@ -195,11 +195,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       // Each slab is 128 bytes of output columns: 64 bf16 or 32 fp32.
       constexpr int kSlab = OUT_F32 ? 32 : 64;
 #pragma unroll 1
-      for (int s = 0; s < BN / kSlab; ++s) {
+      for (int s = 0; s < BN / kSlab; ++s, ++slab_ct) {
+        const uint32_t stage_addr = stage_base + (slab_ct & 1) * S::kStagingBytes;
         float v[kSlab];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + s * kSlab;
-        tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
-        if constexpr (!OUT_F32) tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+        tmem_ld32_raw(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        if constexpr (!OUT_F32) tmem_ld32_raw(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
         const bool add_c = !ACCUM && p.C != nullptr && p.beta != 0.f;
 #pragma unroll
         for (int i = 0; i < kSlab; ++i) v[i] *= p.alpha;
@@ -218,8 +220,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               if (cbase + i < p.N) v[i] += p.beta * __bfloat162float(c[cbase + i]);
           }
         }
-        // The previous TMA store from this staging buffer must have finished reading it.
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        // The TMA store issued from this staging buffer two slabs ago must have finished
+        // reading it (at most one younger store may still be in flight).
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
         __syncwarp();
         // Row `lane` of the staging tile: 8 chunks of 16 bytes, chunk j stored at j ^ (lane & 7)
         // (the 128-byte swizzle the store tensor map expects).
@@ -360,8 +363,22 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   const int sms = num_sms(a.get_device());
   int split = 1;
   const int tiles = batch * p.tiles_m * p.tiles_n;
-  if (accumulate && tiles < sms) {
-    split = std::max(1, std::min(sms / tiles, p.k_blocks / 4));
+  if (accumulate) {
+    // Split K (partial sums meet in the fp32 reduce-add epilogue) when the tiles fill the
+    // SMs' waves badly: the fewest splits whose waves are >= 95% full, else the best fill,
+    // keeping >= 16 K blocks per split so the reduce epilogue stays amortised.
+    auto fill = [&](int sp) {
+      const int units = tiles * sp;
+      return (double)units / ((double)((units + sms - 1) / sms) * sms);
+    };
+    double best = fill(1);
+    for (int sp = 2; sp <= 16 && best < 0.95 && p.k_blocks / sp >= 16; ++sp) {
+      const double f = fill(sp);
+      if (f > best + 0.02) {
+        best = f;
+        split = sp;
+      }
+    }
   }
   p.kb_per_split = (p.k_blocks + split - 1) / split;
   p.split_k = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;

@@ -46,6 +46,20 @@ def build(case: str):
         b = torch.randn(4096, 4096, device=dev).bfloat16()
         return (lambda: gemm(a, b)), 2 * 16384 * 4096 * 4096, (a.numel() + b.numel() + 16384 * 4096) * 2, \
             "bf16 GEMM 16384x4096x4096, bf16 out"
+    if case == "gemm_fwd_200m":
+        # the 200M model's gate/up projection: 32768 tokens x 1024 -> 5632, bf16 out
+        x = torch.randn(32768, 1024, device=dev).bfloat16()
+        w = torch.randn(5632, 1024, device=dev).bfloat16()
+        return (lambda: gemm(x, w)), 2 * 32768 * 5632 * 1024, (x.numel() + w.numel() + 32768 * 5632) * 2, \
+            "bf16 GEMM 32768x5632x1024 (200M gate/up forward), bf16 out"
+    if case == "gemm_wgrad_200m":
+        # the 200M model's gate/up weight gradient: dW (5632 x 1024) += dy^T x over 32768 tokens
+        dy = torch.randn(32768, 5632, device=dev).bfloat16()
+        x = torch.randn(32768, 1024, device=dev).bfloat16()
+        dw = torch.zeros(5632, 1024, device=dev)
+        return (lambda: gemm(dy, x, a_major="mn", b_major="mn", out=dw, accumulate=True)), \
+            2 * 32768 * 5632 * 1024, (dy.numel() + x.numel()) * 2 + dw.numel() * 8, \
+            "bf16 GEMM wgrad 5632x1024x32768 (200M gate/up), fp32 accumulate (split-K reduce-add)"
     if case == "mxgemm":
         from . import mxfp8
 
@@ -113,7 +127,7 @@ def build(case: str):
     raise ValueError(f"unknown case {case!r}")
 
 
-CASES = ["gemm", "mxgemm", "mxquant", "fa_fwd", "fa_bwd", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
+CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fa_fwd", "fa_bwd", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
 
 
 def time_case(case: str, reps: int = 20) -> dict:

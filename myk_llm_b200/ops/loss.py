@@ -59,15 +59,38 @@ class _FusedLinearCE(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_loss, _g_ce, _g_z):
         grad_h, grad_w = ctx.saved_tensors
-        gh = (grad_h.float() * grad_loss).to(ctx.hidden_dtype)
+        # in place, scale applied in fp32 (a 0-dim fp32 factor keeps the bf16 result dtype);
+        # no host synchronisation anywhere in this backward
+        gh = grad_h.mul_(grad_loss)
+        if gh.dtype != ctx.hidden_dtype:
+            gh = gh.to(ctx.hidden_dtype)
         if ctx.has_main:
             # The weight gradient was accumulated into main_grad during forward, which is
-            # only right for an unscaled loss (loss.backward()).
-            if not bool(torch.all(grad_loss == 1)):
-                raise RuntimeError("fused CE with a main_grad buffer needs an unscaled loss.backward()")
+            # only right for an unscaled loss (loss.backward()).  Count violations on the
+            # device; check_unscaled_main_grad() reports them at the next logging sync.
+            _scale_errors(grad_loss.device).add_((grad_loss != 1).to(torch.int32))
             return gh, None, None, None, None, None, None
         gw = (grad_w * grad_loss).to(ctx.weight.dtype)
         return gh, gw, None, None, None, None, None
+
+
+_SCALE_ERRORS: dict[torch.device, torch.Tensor] = {}
+
+
+def _scale_errors(device: torch.device) -> torch.Tensor:
+    t = _SCALE_ERRORS.get(device)
+    if t is None:
+        t = _SCALE_ERRORS[device] = torch.zeros((), dtype=torch.int32, device=device)
+    return t
+
+
+def check_unscaled_main_grad() -> None:
+    """Raise if a fused CE whose weight gradient goes straight into ``main_grad`` was
+    back-propagated with a scaled loss since the last call (synchronises the device)."""
+    for t in _SCALE_ERRORS.values():
+        if int(t.item()):
+            t.zero_()
+            raise RuntimeError("fused CE with a main_grad buffer needs an unscaled loss.backward()")
 
 
 def fused_linear_cross_entropy(hidden, weight, targets, normalizer, z_loss=0.0, ignore_index=-100, chunk_size=8192):

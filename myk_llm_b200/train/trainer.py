@@ -36,6 +36,7 @@ from ..configuration import dump_yaml, load_config
 from ..data import build_fixed_batches, build_loader
 from ..data.config import Batch
 from ..models import MykLLM, generate, load_model
+from ..ops.loss import check_unscaled_main_grad
 from ..parallel.distributed import DistInfo, all_reduce_sum, init_distributed, parallelize, shutdown
 from .checkpoint import latest_checkpoint, load_checkpoint, prune_checkpoints, save_checkpoint, step_dir
 from .config import InitConfig, TrainConfig
@@ -373,6 +374,7 @@ class Trainer:
             if step % config.logging.interval == 0 or step == config.steps:
                 if info.device.type == "cuda":
                     torch.cuda.synchronize()
+                    check_unscaled_main_grad()
                 dt = time.perf_counter() - t0
                 rec = {f"train/{k[4:]}": all_reduce_sum(float(v), info.device) / max(1.0, norm_total)
                        for k, v in acc.items()}

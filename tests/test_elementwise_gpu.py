@@ -189,6 +189,38 @@ def test_fused_linear_ce(z):
     _close(w.grad, wr.grad, 5e-2)
 
 
+def test_fused_linear_ce_scaled_backward_and_main_grad_check():
+    from myk_llm_b200.ops import fused_linear_cross_entropy
+    from myk_llm_b200.ops.loss import check_unscaled_main_grad
+    from myk_llm_b200.ops.reference import linear_cross_entropy_ref
+
+    torch.manual_seed(6)
+    n, h, v = 512, 128, 2048
+    hid = (0.5 * torch.randn(n, h, device="cuda")).bfloat16().requires_grad_(True)
+    w = (0.05 * torch.randn(v, h, device="cuda")).requires_grad_(True)
+    t = torch.randint(0, v, (n,), device="cuda")
+    loss, _, _ = fused_linear_cross_entropy(hid, w, t, float(n))
+    (3.0 * loss).backward()  # a scaled loss: both gradients carry the factor
+    hr = hid.detach().float().requires_grad_(True)
+    wr = w.detach().bfloat16().float().requires_grad_(True)
+    (3.0 * linear_cross_entropy_ref(hr, wr, t, float(n), 0.0)[0]).backward()
+    _close(hid.grad, hr.grad, 5e-2)
+    _close(w.grad, wr.grad, 5e-2)
+    # with a main_grad buffer the weight gradient is added during forward: only an
+    # unscaled backward is right, and a scaled one is reported at the next check
+    w2 = w.detach().clone().requires_grad_(True)
+    w2.main_grad = torch.zeros_like(w2)
+    loss2, _, _ = fused_linear_cross_entropy(hid.detach().requires_grad_(True), w2, t, float(n))
+    loss2.backward()
+    check_unscaled_main_grad()
+    _close(w2.main_grad, wr.grad / 3.0, 5e-2)
+    loss3, _, _ = fused_linear_cross_entropy(hid.detach().requires_grad_(True), w2, t, float(n))
+    (2.0 * loss3).backward()
+    with pytest.raises(RuntimeError):
+        check_unscaled_main_grad()
+    check_unscaled_main_grad()  # the report clears the counter
+
+
 def test_adamw_multi_tensor():
     from myk_llm_b200.ops import adamw_multi_tensor
     from myk_llm_b200.ops.reference import adamw_ref
