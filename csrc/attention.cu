@@ -405,6 +405,325 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 }
 
 // -------------------------------------------------------------------------------------
+// Forward for GQA groups of even size: one work item = the same 128-query tile of two
+// query heads that share a KV head (tiles A and B), so every K / V tile is loaded once
+// for both.  Warp 0 loads, warp 1 issues MMAs, warps 2-5 run the softmax of tile A and
+// warps 6-9 that of tile B.  The MMA warp interleaves the tiles,
+//     S_A(0) S_B(0) | PV_A(0) S_A(1) | PV_B(0) S_B(1) | PV_A(1) S_A(2) | ...
+// so the tensor pipe computes one tile while the other tile's softmax runs.  P is written
+// back into the first 64 columns of its S region as packed bf16 and O += P V takes A from
+// TMEM.  A commit after S_T(j) also covers PV_T(j - 1) (issued before it), so when a
+// softmax warp sees S_T(j) it may rescale O_T and overwrite P_T.
+//
+// TMEM columns: S_A [0, 128), S_B [128, 256), O_A [256, 256 + D), O_B [256 + D, 256 + 2 D).
+// -------------------------------------------------------------------------------------
+template <int D>
+struct FaPairSmem {
+  static constexpr int kStages = D == 64 ? 3 : 2;  // K / V ring depth
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kQ = 0;                      // Q_A, then Q_B
+  static constexpr int kKV0 = 2 * kTile;            // stage s: K at kKV0 + 2 s kTile, V after it
+  static constexpr int kBars = kKV0 + kStages * 2 * kTile;
+  static constexpr int kTotal = kBars + 256;
+};
+
+constexpr int kFaPairThreads = 64 + 32 * 8;
+
+struct PairItem {
+  int seq, kvh, pair, qt;
+  SeqGeom g;
+  int q0, rows, kv_lo, n_kv;
+};
+
+__device__ __forceinline__ bool decode_pair(const FaParams& p, int w, PairItem& it) {
+  const int pairs = p.group / 2;
+  const int per_tile = p.num_seqs * p.kv_heads * pairs;
+  it.qt = p.q_tiles - 1 - w / per_tile;  // heavier (later) query tiles first
+  int rem = w % per_tile;
+  it.seq = rem / (p.kv_heads * pairs);
+  rem %= p.kv_heads * pairs;
+  it.kvh = rem / pairs;
+  it.pair = rem % pairs;
+  it.g = seq_geom(p, it.seq);
+  it.q0 = it.qt * 128;
+  if (it.q0 >= it.g.len_q) return false;
+  it.rows = min(128, it.g.len_q - it.q0);
+  const int off = it.g.len_k - it.g.len_q;
+  const int qlo = it.q0 + off, qhi = it.q0 + it.rows - 1 + off;
+  int lo = 0, hi = it.g.len_k;
+  if (p.left >= 0) lo = max(lo, qlo - p.left);
+  if (p.right >= 0) hi = min(hi, qhi + p.right + 1);
+  it.kv_lo = lo;
+  it.n_kv = hi > lo ? (hi - lo + 127) / 128 : 0;
+  return true;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFaPairThreads, 1)
+fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  using S = FaPairSmem<D>;
+  constexpr int ST = S::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023) != 0) {
+    if (threadIdx.x == 0) set_status(p.status, kMisaligned);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  uint64_t* kv_full = bars;            // [ST]
+  uint64_t* kv_empty = bars + ST;      // [ST]
+  uint64_t* q_full = bars + 2 * ST;
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* s_full = q_full + 2;       // [2] per tile
+  uint64_t* p_full = q_full + 4;       // [2]
+  uint64_t* o_full = q_full + 6;       // [2] last PV of the item done
+  uint64_t* o_free = q_full + 8;       // [2] epilogue read O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 10);
+  constexpr int kCols = 512;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int total = p.q_tiles * p.num_seqs * p.kv_heads * (p.group / 2);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+      mbar_init(&o_free[t], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0, items = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        PairItem it;
+        if (!decode_pair(p, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_empty, (items & 1) ^ 1, p.status, __LINE__)) break;
+        mbar_arrive_expect_tx(q_full, 2 * S::kTile);
+        const int h0 = it.kvh * p.group + 2 * it.pair;
+        load_tile<D>(smem + S::kQ, &tmQ, q_full, h0 * D, it.g.q_start + it.q0);
+        load_tile<D>(smem + S::kQ + S::kTile, &tmQ, q_full, (h0 + 1) * D, it.g.q_start + it.q0);
+        for (int j = 0; j < it.n_kv; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1, p.status, __LINE__)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[stage], 2 * S::kTile);
+          const int row = it.g.k_start + it.kv_lo + j * 128;
+          uint8_t* kd = smem + S::kKV0 + stage * 2 * S::kTile;
+          load_tile<D>(kd, &tmK, &kv_full[stage], it.kvh * D, row);
+          load_tile<D>(kd + S::kTile, &tmV, &kv_full[stage], it.kvh * D, row);
+          if (++stage == ST) { stage = 0; phase ^= 1; }
+        }
+        ++items;
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16(128, D, false, true);  // A = P from TMEM
+    if (elect_one()) {
+      int stage = 0, items = 0;
+      uint32_t phase = 0, ntile = 0;  // KV tiles processed so far (all items)
+      bool ok = true;
+      const uint32_t qa = smem_u32(smem + S::kQ), qb = qa + S::kTile;
+      auto k_addr = [&](int st) { return smem_u32(smem + S::kKV0 + st * 2 * S::kTile); };
+      auto issue_s = [&](int t, int st) {
+        const uint32_t q = t == 0 ? qa : qb;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16_ss(tmem + t * 128, kmajor_desc(q, kk), kmajor_desc(k_addr(st), kk), idesc_s, kk > 0);
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t v = k_addr(st) + S::kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, mnmajor_desc(v, kk), idesc_o,
+                       (acc || kk > 0) ? 1u : 0u);
+      };
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        PairItem it;
+        if (!decode_pair(p, w, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(q_full, items & 1, p.status, __LINE__)) break;
+        if (!mbar_wait(&kv_full[stage], phase, p.status, __LINE__)) break;
+        tc_fence_after();
+        issue_s(0, stage);
+        issue_s(1, stage);
+        if (it.n_kv == 1) umma_commit(q_empty);
+        for (int j = 0; j < it.n_kv && ok; ++j, ++ntile) {
+          const int cur = stage;
+          int nxt = stage + 1;
+          uint32_t nphase = phase;
+          if (nxt == ST) { nxt = 0; nphase ^= 1; }
+          const bool more = j + 1 < it.n_kv;
+          for (int t = 0; t < 2; ++t) {
+            if (j == 0 && !mbar_wait(&o_free[t], (items & 1) ^ 1, p.status, __LINE__)) { ok = false; break; }
+            if (!mbar_wait(&p_full[t], ntile & 1, p.status, __LINE__)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, cur, j > 0);
+            if (!more) umma_commit(&o_full[t]);
+            if (t == 1) umma_commit(&kv_empty[cur]);
+            if (more) {
+              if (t == 0 && !mbar_wait(&kv_full[nxt], nphase, p.status, __LINE__)) { ok = false; break; }
+              tc_fence_after();
+              issue_s(t, nxt);
+              if (t == 1 && j + 2 == it.n_kv) umma_commit(q_empty);
+            }
+          }
+          stage = nxt;
+          phase = nphase;
+        }
+        ++items;
+      }
+    }
+  } else {
+    // softmax: thread = query row of tile t; same online softmax as fa_fwd_kernel (row
+    // max over the raw scores, lazy rescale when the max grows by more than 2^8)
+    const int t = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_col = t * 128, o_col = 256 + t * D;
+    constexpr float kRescaleThreshold = 8.f;  // log2 units
+    uint32_t ntile = 0;
+    int items = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      PairItem it;
+      if (!decode_pair(p, w, it)) continue;
+      const int h = it.kvh * p.group + 2 * it.pair + t;
+      const int off = it.g.len_k - it.g.len_q;
+      const int qpos = it.q0 + row + off;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j, ++ntile) {
+        if (!mbar_wait_warp(&s_full[t], ntile & 1, p.status, __LINE__)) { ok = false; break; }
+        tc_fence_after();
+        const int k0 = it.kv_lo + j * 128;
+        const bool edge = (k0 + 127 >= it.g.len_k) || (p.right >= 0 && k0 + 127 > it.q0 + off + p.right) ||
+                          (p.left >= 0 && k0 < it.q0 + it.rows - 1 + off - p.left);
+        const int kmin = (p.left >= 0 ? max(0, qpos - p.left) : 0) - k0;
+        const int kspan = max(0, min(it.g.len_k, p.right >= 0 ? qpos + p.right + 1 : it.g.len_k) - k0 - kmin);
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t cr[32];
+          tmem_ld32_raw(tmem + lane_base + s_col + c * 32, cr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float sc = __uint_as_float(cr[i]);
+            if (edge && (unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
+            mx = fmaxf(mx, sc);
+          }
+        }
+        const float m_tile = mx * p.scale_log2;
+        const bool grow = m_tile > m_ref + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float m_new = fmaxf(m_ref, m_tile);
+          const float alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - m_new);
+          l *= alpha;
+          m_ref = m_new;
+          if (j > 0) {  // PV_t(j - 1) is complete: the commit of S_t(j) covers it
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tmem_ld32_raw(tmem + lane_base + o_col + c * 32, ov);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+              tmem_st32(tmem + lane_base + o_col + c * 32, ov);
+            }
+          }
+        }
+        const float neg = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t cr[32];
+          tmem_ld32_raw(tmem + lane_base + s_col + c * 32, cr);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float s0 = __uint_as_float(cr[i]), s1 = __uint_as_float(cr[i + 1]);
+            if (edge) {
+              if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) s0 = -INFINITY;
+              if ((unsigned)(c * 32 + i + 1 - kmin) >= (unsigned)kspan) s1 = -INFINITY;
+            }
+            const float p0 = exp2f(fmaf(s0, p.scale_log2, neg));
+            const float p1 = exp2f(fmaf(s1, p.scale_log2, neg));
+            rs += p0 + p1;
+            pk[i >> 1] = pack_bf16x2(p0, p1);
+          }
+          // P columns [16 c, 16 c + 16) lie in S columns this thread has already read
+          tmem_st16_raw(tmem + lane_base + s_col + c * 16, pk);
+        }
+        l += rs;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t tok = it.g.q_start + it.q0 + row;
+      __nv_bfloat16* dst = p.out + tok * p.out_row_stride + (int64_t)h * D;
+      if (it.n_kv > 0) {
+        if (!mbar_wait_warp(&o_full[t], items & 1, p.status, __LINE__)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld32_raw(tmem + lane_base + o_col + c * 32, ov);
+          tmem_wait_ld();
+          if (row < it.rows) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(ov[8 * i + 0]) * inv, __uint_as_float(ov[8 * i + 1]) * inv);
+              v.y = pack_bf16x2(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv);
+              v.z = pack_bf16x2(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv);
+              v.w = pack_bf16x2(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv);
+              reinterpret_cast<uint4*>(dst + c * 32)[i] = v;
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[t]);
+        ++items;
+      } else if (row < it.rows) {
+        for (int i = 0; i < D / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+      }
+      if (row < it.rows) {
+        const float lse = l > 0.f ? (m_ref + log2f(l)) * kLn2 : INFINITY;
+        if (p.cu_q != nullptr)
+          p.lse[(int64_t)h * p.cu_q[p.num_seqs] + tok] = lse;
+        else
+          p.lse[((int64_t)it.seq * p.heads + h) * p.max_q + it.q0 + row] = lse;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// -------------------------------------------------------------------------------------
 // host
 // -------------------------------------------------------------------------------------
 static int sm_count() {
@@ -436,6 +755,20 @@ static void launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
     configured = true;
+  }
+  if (p.group % 2 == 0) {
+    // GQA with an even group: two query heads per work item sharing each K / V tile
+    using SP = FaPairSmem<D>;
+    auto pk = fa_fwd_pair_kernel<D>;
+    static bool pair_configured = false;
+    if (!pair_configured) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, SP::kTotal));
+      pair_configured = true;
+    }
+    const int items = p.q_tiles * p.num_seqs * p.kv_heads * (p.group / 2);
+    pk<<<std::max(1, std::min(items, sm_count())), kFaPairThreads, SP::kTotal, st>>>(tq, tk, tv, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
   }
   const int per_sm = D == 64 ? 2 : 1;
   const int grid = std::max(1, std::min(p.total_items, sm_count() * per_sm));
@@ -1128,22 +1461,29 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 __global__ void fa_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
                                 float* __restrict__ delta, int64_t rows, int heads, int D, bool packed,
                                 int max_q) {
-  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= rows * heads) return;
-  const int64_t tok = gw / heads;
-  const int h = (int)(gw % heads);
-  const __nv_bfloat16* a = dout + gw * D;
-  const __nv_bfloat16* b = out + gw * D;
+  // D / 8 consecutive lanes share one (token, head) row: one 16-byte load of each tensor
+  // per lane, then a shuffle reduction within the group.
+  const int per = D / 8;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t gw = t / per;
+  const int sub = (int)(t % per);
+  const bool active = gw < rows * heads;
   float s = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
-    float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(b + d));
-    s += x.x * y.x + x.y * y.y;
-  }
+  if (active) {
+    const uint4 x = *reinterpret_cast<const uint4*>(dout + gw * D + sub * 8);
+    const uint4 y = *reinterpret_cast<const uint4*>(out + gw * D + sub * 8);
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
-  if (lane == 0) {
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __bfloat1622float2(xa[i]), b = __bfloat1622float2(ya[i]);
+      s = fmaf(a.x, b.x, fmaf(a.y, b.y, s));
+    }
+  }
+  for (int o = per / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
+  if (active && sub == 0) {
+    const int64_t tok = gw / heads;
+    const int h = (int)(gw % heads);
     if (packed) delta[(int64_t)h * rows + tok] = s;
     else {
       const int64_t b_ = tok / max_q, qi = tok % max_q;
@@ -1218,8 +1558,8 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
   auto delta = torch::empty_like(lse);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (q_rows > 0) {
-    const int64_t warps = q_rows * f.heads;
-    fa_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+    const int64_t threads = q_rows * f.heads * (D / 8);
+    fa_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
         (const __nv_bfloat16*)dout_c.data_ptr(), (const __nv_bfloat16*)out.data_ptr(), delta.data_ptr<float>(),
         q_rows, f.heads, D, packed, (int)max_q);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1345,8 +1685,8 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     p.dq = static_cast<__nv_bfloat16*>(dq);
     p.dk = static_cast<__nv_bfloat16*>(dk);
     p.dv = static_cast<__nv_bfloat16*>(dv);
-    const int64_t warps = (int64_t)rows_q * heads;
-    fa_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(
+    const int64_t threads = (int64_t)rows_q * heads * (head_dim / 8);
+    fa_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), sc.delta, rows_q, heads,
         head_dim, cu_seqlens != nullptr, max_q);
     err = cudaGetLastError();

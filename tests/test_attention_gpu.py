@@ -28,6 +28,9 @@ CASES = [
     (2, 300, 100, 2, 1, 64, True, (-1, -1)),
     (1, 512, 512, 2, 1, 128, True, (127, 0)),
     (1, 100, 260, 2, 2, 128, False, (50, 30)),
+    # several work items per CTA, many KV tiles, two head pairs per KV head
+    (2, 1100, 1100, 8, 2, 64, True, (-1, -1)),
+    (1, 700, 700, 16, 4, 128, True, (300, 0)),
 ]
 
 
