@@ -155,6 +155,32 @@ class ModelOutput:
     cache: list[Any] | None = None
 
 
+_NVTX = [False]
+
+
+def set_nvtx(enabled: bool) -> None:
+    """Emit NVTX ranges (per layer here, per training phase in the trainer) for timeline
+    profilers; off by default (no cost when off)."""
+    _NVTX[0] = bool(enabled)
+
+
+class nvtx_range:
+    """``with nvtx_range(name):`` pushes an NVTX range when enabled and on a CUDA build."""
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.on = _NVTX[0] and torch.cuda.is_available()
+
+    def __enter__(self):
+        if self.on:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if self.on:
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
 def build_varlen(seqlens: list[torch.Tensor], batch: int, seq_len: int, device: torch.device) -> Varlen:
     lengths = torch.cat([s.to(device="cpu", dtype=torch.int32) for s in seqlens])
     cu_cpu = F.pad(lengths.cumsum(0, dtype=torch.int32), (1, 0))
@@ -258,7 +284,8 @@ class MykLLM(nn.Module):
 
         def run(i, x):
             nonlocal shared
-            x, st = self.layers[i](x, position_ids, varlen, next(states), use_cache)
+            with nvtx_range(f"layer{i}"):
+                x, st = self.layers[i](x, position_ids, varlen, next(states), use_cache)
             if new_cache is not None:
                 new_cache.append(st)
             if i == self.cross_kv_layer:

@@ -130,6 +130,7 @@ class EvalConfig:
 class LoggingConfig:
     interval: int = 10
     tensorboard: bool = True
+    nvtx: bool = False  # NVTX ranges per layer and per training phase (for timeline profilers)
 
 
 @dataclass

@@ -36,6 +36,7 @@ from ..configuration import dump_yaml, load_config
 from ..data import build_fixed_batches, build_loader
 from ..data.config import Batch
 from ..models import MykLLM, generate, load_model
+from ..models.transformer import nvtx_range, set_nvtx
 from ..ops.loss import check_unscaled_main_grad
 from ..parallel.distributed import DistInfo, all_reduce_sum, init_distributed, parallelize, shutdown
 from .checkpoint import latest_checkpoint, load_checkpoint, prune_checkpoints, save_checkpoint, step_dir
@@ -136,6 +137,7 @@ class Trainer:
                  tokenizer: Any = None) -> None:
         self.config = config
         self.info = info = info or init_distributed()
+        set_nvtx(config.logging.nvtx)
         torch.manual_seed(config.seed)
         per_step = config.data.micro_batch_size * info.world_size
         if config.global_batch_size % per_step:
@@ -191,8 +193,10 @@ class Trainer:
 
     def forward_backward(self, batch: Batch, normalizer: float) -> dict[str, torch.Tensor]:
         batch = batch.to(self.info.device)
-        out = self.model(batch.input_ids, seqlens=batch.seqlens, head=self.objective.head(batch, normalizer))
-        out.loss.backward()
+        with nvtx_range("forward"):
+            out = self.model(batch.input_ids, seqlens=batch.seqlens, head=self.objective.head(batch, normalizer))
+        with nvtx_range("backward"):
+            out.loss.backward()
         return out.sums
 
     def clip_and_step(self) -> torch.Tensor:
@@ -262,7 +266,8 @@ class Trainer:
             s = self.forward_backward(b, normalizer)
             for k, v in s.items():
                 sums[k] = sums[k] + v if k in sums else v.clone()
-        norm = self.clip_and_step()
+        with nvtx_range("optimizer"):
+            norm = self.clip_and_step()
         self.tokens_seen += self.tokens_per_step
         out = {f"sum/{k}": v for k, v in sums.items()}
         out["loss"] = sums.get("ce", torch.zeros(())) / max(1.0, normalizer)
