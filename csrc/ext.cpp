@@ -10,7 +10,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<std::vector<torch::Tensor>> add,
                                        double eps, c10::ScalarType out_dtype);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
-                                       c10::optional<torch::Tensor> dres);
+                                       c10::optional<torch::Tensor> dres, bool bf16_copy);
 std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, c10::optional<torch::Tensor> g, torch::Tensor w,
                                              double eps, int64_t act);
 std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, c10::optional<torch::Tensor> g,

@@ -117,7 +117,7 @@ template <int NC, typename TX, typename TY>
 __global__ void __launch_bounds__(32 * kNormWarps)
 rmsnorm_bwd_kernel(const TY* __restrict__ dy, const TX* __restrict__ x, const float* __restrict__ w,
                    const float* __restrict__ rstd, const TX* __restrict__ dres, TX* __restrict__ dx,
-                   float* __restrict__ dw, int rows) {
+                   float* __restrict__ dw, int rows, __nv_bfloat16* __restrict__ dx_bf) {
   constexpr int H = NC * 128;
   __shared__ float sdw[H];
   const int lane = threadIdx.x & 31;
@@ -166,6 +166,7 @@ rmsnorm_bwd_kernel(const TY* __restrict__ dy, const TX* __restrict__ x, const fl
         for (int i = 0; i < 4; ++i) o[i] += t[i];
       }
       store4<TX>(dx + base + idx, o);
+      if (dx_bf != nullptr) store4<__nv_bfloat16>(dx_bf + base + idx, o);  // bf16 copy for a bf16 residual branch
     }
   }
 #pragma unroll
@@ -403,8 +404,10 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, c10::op
   return {y, rstd};
 }
 
+// dres: gradient arriving at the (un-normed) sum directly, added to dx.  bf16_copy: also
+// return dx rounded to bf16 (third output), written by the same kernel.
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
-                                       c10::optional<torch::Tensor> dres) {
+                                       c10::optional<torch::Tensor> dres, bool bf16_copy) {
   c10::cuda::CUDAGuard guard(x.device());
   const int rows = x.size(0), H = x.size(1);
   auto wf = w.to(at::kFloat).contiguous();
@@ -429,16 +432,21 @@ std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch:
   const int grid = norm_grid(rows);
   using bf = __nv_bfloat16;
   const bool x_f32 = x.scalar_type() == at::kFloat, y_f32 = dy.scalar_type() == at::kFloat;
+  torch::Tensor dx_bf;
+  if (bf16_copy && x_f32) dx_bf = torch::empty(x.sizes(), x.options().dtype(at::kBFloat16));
+  bf* dxb = dx_bf.defined() ? (bf*)dx_bf.data_ptr() : nullptr;
 #define MYKB_RMSB(TX, TY)                                                                                       \
   MYKB_NC_SWITCH(H, rmsnorm_bwd_kernel<NC, TX, TY><<<grid, 32 * kNormWarps, 0, st>>>(                          \
                         (const TY*)dy.data_ptr(), (const TX*)x.data_ptr(), wf.data_ptr<float>(),               \
-                        rstd.data_ptr<float>(), (const TX*)dr, (TX*)dx.data_ptr(), dw.data_ptr<float>(), rows))
+                        rstd.data_ptr<float>(), (const TX*)dr, (TX*)dx.data_ptr(), dw.data_ptr<float>(), rows, \
+                        dxb))
   if (x_f32 && y_f32) { MYKB_RMSB(float, float); }
   else if (x_f32) { MYKB_RMSB(float, bf); }
   else if (y_f32) { MYKB_RMSB(bf, float); }
   else { MYKB_RMSB(bf, bf); }
 #undef MYKB_RMSB
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (bf16_copy) return {dx, dw.to(w.scalar_type()), dx_bf.defined() ? dx_bf : dx};
   return {dx, dw.to(w.scalar_type())};
 }
 

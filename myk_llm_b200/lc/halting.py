@@ -32,6 +32,7 @@ import torch
 
 from ..configuration import load_config
 from ..models import MykLLM
+from ..models.transformer import materialize
 from ..utils.sweep import SEED_SUFFIX
 from .eval import answer_positions
 from .tasks import Example, make_example
@@ -55,7 +56,7 @@ def trace(model: MykLLM, examples: list[Example], iterations: int) -> dict[str, 
     reads: list[torch.Tensor] = []
 
     def hook(_m, _a, out):
-        x = out[0] if isinstance(out, tuple) else out
+        x = materialize(out[0] if isinstance(out, tuple) else out)
         reads.append(model.final_norm(x[rows, pos]).float())
 
     handle = model.layers[-1].register_forward_hook(hook)

@@ -51,6 +51,26 @@ def _concurrently(first: Callable[[], Any], second: Callable[[], Any], side: tor
     return a, b
 
 
+@dataclass
+class PendingResidual:
+    """A residual-stream value kept as ``base + delta`` (the block's fp32 stream and its last
+    FFN output): the next block's pre-norm (or the final norm) adds and normalises in one
+    kernel instead of an add pass followed by a norm pass."""
+
+    base: torch.Tensor
+    delta: torch.Tensor
+
+
+def materialize(x):
+    return x.base + x.delta if isinstance(x, PendingResidual) else x
+
+
+# a pytree node, so wrappers that walk module outputs (FSDP2 hooks) see both tensors
+torch.utils._pytree.register_pytree_node(
+    PendingResidual, lambda r: ([r.base, r.delta], None), lambda xs, _: PendingResidual(*xs),
+    serialized_type_name="myk_llm_b200.PendingResidual")
+
+
 class Block(nn.Module):
     """x + g1*mixer(norm(x)) then + g2*ffn(norm(x)); or parallel: x + g1*mixer(h) + g2*ffn(h)."""
 
@@ -65,6 +85,9 @@ class Block(nn.Module):
         self.ffn_gate = ResidualGate(config.residual, config.hidden_size)
         self.streams = config.parallel_streams
         self.activation_checkpointing = False
+        # set by MykLLM for its main stack: return PendingResidual instead of adding the FFN
+        # output here (the consumer fuses the add with its norm)
+        self.defer_residual = False
 
     def residual_projections(self) -> list[nn.Linear]:
         return [*self.mixer.residual_projections(), self.ffn.down_proj]
@@ -75,8 +98,12 @@ class Block(nn.Module):
         return self._forward(x, position_ids, varlen, state, use_cache)
 
     def _forward(self, x, position_ids, varlen, state, use_cache):
-        cdt = ops.compute_dtype(x)
-        h = self.mixer_norm(x, out_dtype=cdt)
+        if isinstance(x, PendingResidual):
+            cdt = ops.compute_dtype(x.base)
+            x, h = ops.add_rms_norm(x.base, x.delta, self.mixer_norm.weight, self.mixer_norm.eps, out_dtype=cdt)
+        else:
+            cdt = ops.compute_dtype(x)
+            h = self.mixer_norm(x, out_dtype=cdt)
         if self.ffn_norm is None:
             (update, state), f = self._parallel(h, position_ids, varlen, state, use_cache)
             x = self.mixer_gate(x, update, h)
@@ -87,7 +114,10 @@ class Block(nn.Module):
         else:
             x = self.mixer_gate(x, update, h)
             h = self.ffn_norm(x, out_dtype=cdt)
-        x = self.ffn_gate(x, self.ffn(h), h)
+        f = self.ffn(h)
+        if self.defer_residual and self.ffn_gate.kind == "none":
+            return PendingResidual(x, f), state
+        x = self.ffn_gate(x, f, h)
         return x, state
 
     def side_stream(self, device: torch.device) -> torch.cuda.Stream:
@@ -199,6 +229,8 @@ class MykLLM(nn.Module):
         first_global = globals_[0] if globals_ else -1
         self.layers = nn.ModuleList(Block(config, t, first_global=(i == first_global))
                                     for i, t in enumerate(config.layer_types))
+        for block in self.layers:
+            block.defer_residual = True
         self.final_norm = RMSNorm(config.hidden_size, config.norm_eps)
         self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
         if config.tie_embeddings:
@@ -297,6 +329,7 @@ class MykLLM(nn.Module):
 
         def enter(i, x):
             if i in ngram_updates:
+                x = materialize(x)
                 return x + ngram_updates[i][:, -x.size(1):]
             return x
 
@@ -305,12 +338,14 @@ class MykLLM(nn.Module):
             for i in range(start, core_start):
                 x = block(i, enter(i, x))
             if looped:
-                x = self._run_core(enter(core_start, x), block, iterations)
+                x = self._run_core(materialize(enter(core_start, x)), block, iterations)
             for i in range(core_start + loop.core if looped else end, end):
                 x = block(i, enter(i, x))
             return x
 
         x = stack(0, xs, run, bool(self_core), x)
+        if keep_last or xs < n_layers:
+            x = materialize(x)
         self_out, self_pos = x, position_ids
         if keep_last:
             x, position_ids = x[:, -keep_last:], position_ids[:, -keep_last:]
@@ -324,7 +359,12 @@ class MykLLM(nn.Module):
                 if new_cache is not None:
                     new_cache.append(None)
             x = stack(xs, n_layers, cross, cross_loop, x)
-        out = ModelOutput(self.final_norm(x, out_dtype=ops.compute_dtype(x)), x, position_ids, varlen, new_cache)
+        if isinstance(x, PendingResidual):
+            x, hidden = ops.add_rms_norm(x.base, x.delta, self.final_norm.weight, self.final_norm.eps,
+                                         out_dtype=ops.compute_dtype(x.base))
+        else:
+            hidden = self.final_norm(x, out_dtype=ops.compute_dtype(x))
+        out = ModelOutput(hidden, x, position_ids, varlen, new_cache)
         return head(self, out) if head is not None else out
 
     def num_iterations(self, iterations: int | None = None) -> int:
@@ -349,10 +389,10 @@ class MykLLM(nn.Module):
         state = torch.zeros_like(inputs)
         for it in range(iterations):
             with torch.set_grad_enabled(grad and it >= first_tracked):
-                state = inj(state, inputs)
+                state = inj(materialize(state), inputs)
                 for i in range(loop.prelude, loop.prelude + loop.core):
                     state = block(i, state)
-        return state
+        return materialize(state)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return ops.linear(hidden, self.lm_head.weight)

@@ -34,7 +34,7 @@ class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x2, w, rstd = ctx.saved_tensors
-        dx, dw = ext().rmsnorm_bwd(_c(dy.reshape(x2.shape)), x2, w, rstd, None)
+        dx, dw = ext().rmsnorm_bwd(_c(dy.reshape(x2.shape)), x2, w, rstd, None, False)
         return dx.view(ctx.shape), dw, None, None
 
 
@@ -56,7 +56,11 @@ class _AddRMSNorm(torch.autograd.Function):
     def backward(ctx, ds, dy):
         s, w, rstd = ctx.saved_tensors
         res = _c(ds.reshape(s.shape)) if ds is not None else None
-        dx, dw = ext().rmsnorm_bwd(_c(dy.reshape(s.shape)), s, w, rstd, res)
+        if ctx.u_dtype == torch.bfloat16 and s.dtype == torch.float32:
+            # the bf16 gradient of the update branch comes out of the same kernel
+            dx, dw, du = ext().rmsnorm_bwd(_c(dy.reshape(s.shape)), s, w, rstd, res, True)
+            return dx.view(ctx.shape), du.view(ctx.shape), dw, None, None
+        dx, dw = ext().rmsnorm_bwd(_c(dy.reshape(s.shape)), s, w, rstd, res, False)
         dx = dx.view(ctx.shape)
         du = dx if ctx.u_dtype == dx.dtype else dx.to(ctx.u_dtype)
         return dx, du, dw, None, None
