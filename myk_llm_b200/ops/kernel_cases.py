@@ -87,6 +87,19 @@ def build(case: str):
         do = torch.randn_like(o)
         return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), 10 * attn, \
             (q.numel() * 4 + k.numel() * 4) * 2, "FlashAttention bwd B4 L4096 16q/4kv h128 causal"
+    if case in ("fa_fwd_h64", "fa_bwd_h64"):
+        # the 200M model's attention: B8 L4096, 16 query / 4 KV heads of 64, causal
+        q = torch.randn(8, 4096, 16, 64, device=dev).bfloat16().requires_grad_()
+        k = torch.randn(8, 4096, 4, 64, device=dev).bfloat16().requires_grad_()
+        v = torch.randn(8, 4096, 4, 64, device=dev).bfloat16().requires_grad_()
+        attn = 8 * 16 * 4096 * 4096 / 2 * 64
+        if case == "fa_fwd_h64":
+            return (lambda: flash_attn_func(q, k, v, causal=True)), 4 * attn, (q.numel() * 2 + k.numel() * 2) * 2, \
+                "FlashAttention fwd B8 L4096 16q/4kv h64 causal (200M layer)"
+        o = flash_attn_func(q, k, v, causal=True)
+        do = torch.randn_like(o)
+        return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), 10 * attn, \
+            (q.numel() * 4 + k.numel() * 4) * 2, "FlashAttention bwd B8 L4096 16q/4kv h64 causal (200M layer)"
     if case == "gdn":
         from .gdn import gated_delta_rule
 
@@ -127,7 +140,7 @@ def build(case: str):
     raise ValueError(f"unknown case {case!r}")
 
 
-CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fa_fwd", "fa_bwd", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
+CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
 
 
 def time_case(case: str, reps: int = 20) -> dict:
