@@ -78,3 +78,23 @@ def test_dump_roundtrip():
 
     again = from_dict(TrainConfig, yaml.safe_load(dump_yaml(cfg)))
     assert again == cfg
+
+
+def test_every_sweep_expands_to_valid_runs():
+    """Each run of every sweep file (base config + overrides) loads with its config class."""
+    import yaml
+
+    from myk_llm_b200.arith.train import ArithConfig
+    from myk_llm_b200.configuration import load_config
+    from myk_llm_b200.lc.train import LcConfig
+    from myk_llm_b200.utils.sweep import plan
+
+    files = sorted((ROOT / "configs").rglob("sweeps/*.yaml"))
+    assert files
+    for f in files:
+        kind = f.relative_to(ROOT / "configs").parts[0]
+        cls = {"lc": LcConfig, "arith": ArithConfig}.get(kind, TrainConfig)
+        runs = plan(yaml.safe_load(f.read_text()))
+        assert runs, f
+        for _, cfg, ov in runs:
+            load_config(cls, ROOT / cfg, ov)
