@@ -279,6 +279,56 @@ torch::Tensor rope_qkv_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
   return dqkv;
 }
 
+// ------------------------------------------------------------------------ column split
+// x (rows, W) with unit last stride and row stride `rs` -> up to 4 contiguous outputs of
+// widths w[i] (sum = W, each a multiple of 8): one 16-byte vector per thread.
+struct SplitOut {
+  __nv_bfloat16* ptr[4];
+  int width[4];
+  int n;
+};
+
+__global__ void split_cols_kernel(const __nv_bfloat16* __restrict__ x, int64_t rs, uint32_t rows, int W, SplitOut o) {
+  const uint32_t vec_per_row = W / 8;
+  const uint64_t total = (uint64_t)rows * vec_per_row;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t r = (uint32_t)(i / vec_per_row);
+    int c = (int)(i - (uint64_t)r * vec_per_row) * 8;
+    const bf16x8 v = *reinterpret_cast<const bf16x8*>(x + (int64_t)r * rs + c);
+    int j = 0;
+    while (j + 1 < o.n && c >= o.width[j]) c -= o.width[j++];
+    *reinterpret_cast<bf16x8*>(o.ptr[j] + (int64_t)r * o.width[j] + c) = v;
+  }
+}
+
+std::vector<torch::Tensor> split_cols(torch::Tensor x, std::vector<int64_t> widths) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "split_cols: bf16 (rows, W) with 16-byte aligned rows");
+  TORCH_CHECK(!widths.empty() && widths.size() <= 4, "split_cols: 1 to 4 parts");
+  SplitOut o{};
+  std::vector<torch::Tensor> outs;
+  int64_t W = 0;
+  for (size_t i = 0; i < widths.size(); ++i) {
+    TORCH_CHECK(widths[i] > 0 && widths[i] % 8 == 0, "split_cols: widths must be positive multiples of 8");
+    outs.push_back(torch::empty({x.size(0), widths[i]}, x.options()));
+    o.ptr[i] = (__nv_bfloat16*)outs.back().data_ptr();
+    o.width[i] = (int)widths[i];
+    W += widths[i];
+  }
+  o.n = (int)widths.size();
+  TORCH_CHECK(W == x.size(1), "split_cols: widths must sum to the row width");
+  const int64_t total = x.size(0) * (W / 8);
+  if (total > 0) {
+    TORCH_CHECK(x.size(0) < (int64_t)UINT32_MAX, "split_cols: too many rows");
+    split_cols_kernel<<<ew_grid(total, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (uint32_t)x.size(0), (int)W, o);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  return outs;
+}
+
 // ------------------------------------------------------------------------ embedding
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
                                      float* __restrict__ out, int64_t n, int dim, int64_t vocab) {

@@ -21,6 +21,7 @@ torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
 torch::Tensor rope(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos, bool inverse);
 std::vector<torch::Tensor> rope_qkv_fwd(torch::Tensor qkv, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos,
                                         int64_t H, int64_t KV);
+std::vector<torch::Tensor> split_cols(torch::Tensor x, std::vector<int64_t> widths);
 torch::Tensor rope_qkv_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor cos_t, torch::Tensor sin_t,
                            torch::Tensor pos);
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
@@ -30,9 +31,10 @@ void ce_fwd_grad(torch::Tensor logits, torch::Tensor targets, double scale, doub
                  torch::Tensor ce_sum, torch::Tensor z_sum);
 // optim.cu
 void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
-                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd);
+                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd,
+                c10::optional<torch::Tensor> gscale);
 void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> bufs, double mu, bool nesterov,
-                  torch::Tensor out);
+                  torch::Tensor out, c10::optional<torch::Tensor> gscale);
 void muon_apply(std::vector<torch::Tensor> params, torch::Tensor orth, double decay, double step_scale);
 void frob_normalize_(torch::Tensor x, double eps);
 // attention.cu
@@ -103,6 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope", &mykb::rope);
   m.def("rope_qkv_fwd", &mykb::rope_qkv_fwd);
   m.def("rope_qkv_bwd", &mykb::rope_qkv_bwd);
+  m.def("split_cols", &mykb::split_cols);
   m.def("embedding_fwd", &mykb::embedding_fwd);
   m.def("embedding_bwd", &mykb::embedding_bwd);
   m.def("ce_fwd_grad", &mykb::ce_fwd_grad);

@@ -34,7 +34,9 @@ __device__ __forceinline__ int find_tensor(const int64_t* prefix, int n, int64_t
 template <typename TG>
 __global__ void __launch_bounds__(kOptThreads)
 adamw_kernel(TensorTable tab, int64_t total_chunks, float lr, float b1, float b2, float eps, float wd, float bc1,
-             float bc2_sqrt) {
+             float bc2_sqrt, const float* __restrict__ gscale) {
+  // gradients are scaled on load (gradient clipping), so no separate pass rewrites them
+  const float gs = gscale != nullptr ? *gscale : 1.f;
   for (int64_t chunk = blockIdx.x; chunk < total_chunks; chunk += gridDim.x) {
     const int t = find_tensor(tab.prefix, tab.n, chunk);
     const int64_t start = (chunk - tab.prefix[t]) * kChunk;
@@ -47,6 +49,7 @@ adamw_kernel(TensorTable tab, int64_t total_chunks, float lr, float b1, float b2
     for (int64_t i = start + threadIdx.x; i < end; i += kOptThreads) {
       float gi;
       if constexpr (sizeof(TG) == 4) gi = g[i]; else gi = __bfloat162float(g[i]);
+      gi *= gs;
       float pi = p[i] * (1.f - lr * wd);
       float mi = m[i] + (1.f - b1) * (gi - m[i]);
       float vi = b2 * v[i] + (1.f - b2) * gi * gi;
@@ -94,9 +97,17 @@ static torch::Tensor build_table(const std::vector<std::vector<torch::Tensor>>& 
   return d;
 }
 
+// gscale: optional fp32 scalar on the device multiplying every gradient as it is read.
 void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
-                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd) {
+                std::vector<torch::Tensor> v, int64_t step, double lr, double b1, double b2, double eps, double wd,
+                c10::optional<torch::Tensor> gscale) {
   if (params.empty()) return;
+  const float* gsp = nullptr;
+  if (gscale.has_value()) {
+    TORCH_CHECK(gscale->scalar_type() == at::kFloat && gscale->numel() == 1 && gscale->is_cuda(),
+                "adamw: gscale must be one fp32 value on the device");
+    gsp = gscale->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard guard(params[0].device());
   for (auto& p : params) TORCH_CHECK(p.scalar_type() == at::kFloat, "adamw: fp32 params");
   const bool g_bf16 = grads[0].scalar_type() == at::kBFloat16;
@@ -111,9 +122,10 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
   const float bc2s = (float)std::sqrt(1.0 - std::pow(b2, (double)step));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (g_bf16)
-    adamw_kernel<__nv_bfloat16><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s);
+    adamw_kernel<__nv_bfloat16><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s,
+                                                                          gsp);
   else
-    adamw_kernel<float><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s);
+    adamw_kernel<float><<<grid_for(chunks), kOptThreads, 0, st>>>(tab, chunks, lr, b1, b2, eps, wd, bc1, bc2s, gsp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   // keep the table alive until the kernel ran
   c10::cuda::CUDACachingAllocator::recordStream(table.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
@@ -121,7 +133,9 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
 
 // ------------------------------------------------------------------------------ Muon
 __global__ void muon_prepare_kernel(const int64_t* gptrs, const int64_t* mptrs, int n, int64_t numel, float mu,
-                                    bool nesterov, bool g_bf16, __nv_bfloat16* __restrict__ out) {
+                                    bool nesterov, bool g_bf16, __nv_bfloat16* __restrict__ out,
+                                    const float* __restrict__ gscale) {
+  const float gs = gscale != nullptr ? *gscale : 1.f;
   const int64_t total = (int64_t)n * numel;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / numel);
@@ -129,6 +143,7 @@ __global__ void muon_prepare_kernel(const int64_t* gptrs, const int64_t* mptrs, 
     float* m = reinterpret_cast<float*>(mptrs[t]);
     float g = g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(gptrs[t])[j])
                      : reinterpret_cast<const float*>(gptrs[t])[j];
+    g *= gs;
     float mv = m[j] + (1.f - mu) * (g - m[j]);
     m[j] = mv;
     float u = nesterov ? g + mu * (mv - g) : mv;
@@ -161,8 +176,14 @@ static torch::Tensor ptr_table(const std::vector<std::vector<torch::Tensor>>& li
 }
 
 void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> bufs, double mu, bool nesterov,
-                  torch::Tensor out) {
+                  torch::Tensor out, c10::optional<torch::Tensor> gscale) {
   if (grads.empty()) return;
+  const float* gsp = nullptr;
+  if (gscale.has_value()) {
+    TORCH_CHECK(gscale->scalar_type() == at::kFloat && gscale->numel() == 1 && gscale->is_cuda(),
+                "muon_prepare: gscale must be one fp32 value on the device");
+    gsp = gscale->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard guard(out.device());
   const int n = grads.size();
   const int64_t numel = grads[0].numel();
@@ -173,7 +194,7 @@ void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> b
   const int64_t total = n * numel;
   muon_prepare_kernel<<<grid_for((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       tab.data_ptr<int64_t>(), tab.data_ptr<int64_t>() + n, n, numel, (float)mu, nesterov, g_bf16,
-      (__nv_bfloat16*)out.data_ptr());
+      (__nv_bfloat16*)out.data_ptr(), gsp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   c10::cuda::CUDACachingAllocator::recordStream(tab.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
 }

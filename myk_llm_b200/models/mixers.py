@@ -338,7 +338,7 @@ class DeltaNet(nn.Module):
         else:
             qkv, new_conv = ops.silu(qkv), None
         b_, t_ = qkv.shape[:2]
-        q, k, v = qkv.split((inner.key_dim, inner.key_dim, inner.value_dim), dim=-1)
+        q, k, v = ops.split_cols(qkv, (inner.key_dim, inner.key_dim, inner.value_dim))
         q = q.reshape(b_, t_, inner.num_heads, inner.head_k_dim)
         k = k.reshape(b_, t_, inner.num_heads, inner.head_k_dim)
         v = v.reshape(b_, t_, inner.num_v_heads, inner.head_v_dim)

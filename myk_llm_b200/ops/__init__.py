@@ -8,7 +8,7 @@ the fp32 oracles of the kernel tests.  There is no other backend.
 from ._ext import available, compute_dtype, ext, is_cuda
 from .attention import flash_attn_func, flash_attn_varlen_func, flash_attn_with_kvcache
 from .elementwise import (add_rms_norm, apply_rope, rope_qkv, embedding, gated_rms_norm, ngram_lookup, rms_norm,
-                          sigmoid_gate, silu, swiglu)
+                          sigmoid_gate, silu, split_cols, swiglu)
 from .gdn import causal_conv1d, gated_delta_rule, gdn_gate, kda_gate
 from .linear import bf16_weight, gemm, invalidate_weight_cache, linear
 from .loss import fused_linear_cross_entropy
@@ -20,5 +20,5 @@ __all__ = [
     "batched_syrk", "bf16_weight", "causal_conv1d", "compute_dtype", "embedding", "ext", "flash_attn_func",
     "flash_attn_varlen_func", "flash_attn_with_kvcache", "frobenius_normalize_", "fused_linear_cross_entropy",
     "gated_delta_rule", "gated_rms_norm", "gdn_gate", "gemm", "invalidate_weight_cache", "is_cuda", "kda_gate", "linear", "muon_apply",
-    "muon_prepare", "ngram_lookup", "rms_norm", "rope_qkv", "sigmoid_gate", "silu", "swiglu",
+    "muon_prepare", "ngram_lookup", "rms_norm", "rope_qkv", "sigmoid_gate", "silu", "split_cols", "swiglu",
 ]

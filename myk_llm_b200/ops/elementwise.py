@@ -141,6 +141,28 @@ def silu(x: torch.Tensor) -> torch.Tensor:
     return F.silu(x)
 
 
+class _SplitCols(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, widths):
+        return tuple(ext().split_cols(x, list(widths)))
+
+    @staticmethod
+    def backward(ctx, *grads):
+        return torch.cat([g.contiguous() for g in grads], dim=-1), None
+
+
+def split_cols(x: torch.Tensor, widths) -> tuple[torch.Tensor, ...]:
+    """Split the last dimension of ``x`` (..., sum(widths)) into contiguous tensors in one
+    pass (a plain ``split`` returns strided views, and copying those is slow)."""
+    lead = x.shape[:-1]
+    widths = tuple(int(w) for w in widths)
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x.is_cuda or x.dtype != torch.bfloat16 or any(w % 8 for w in widths) or x2.stride(-1) != 1 \
+            or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        return tuple(t.contiguous() for t in x.split(widths, dim=-1))
+    return tuple(t.view(*lead, w) for t, w in zip(_SplitCols.apply(x2, widths), widths))
+
+
 # ---------------------------------------------------------------------------------------
 # RoPE
 # ---------------------------------------------------------------------------------------

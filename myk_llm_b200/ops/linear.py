@@ -82,6 +82,15 @@ def bf16_weight(w: torch.Tensor) -> torch.Tensor:
     return wb
 
 
+def _gemm_rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as the GEMM reads it: rows may be strided (a column slice of a wider matrix, read
+    through the TMA row stride) as long as elements are contiguous and rows 16-byte aligned;
+    anything else is copied."""
+    if t.dim() == 2 and t.stride(-1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0:
+        return t
+    return t.contiguous()
+
+
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x: torch.Tensor, w: torch.Tensor):
@@ -89,13 +98,13 @@ class _Linear(torch.autograd.Function):
         x2 = x.reshape(-1, k)
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
         wb = bf16_weight(w)
         if x2.shape[0] <= SKINNY_MAX_ROWS and k % 8 == 0:
+            x2 = x2.contiguous()
             y = torch.empty(x2.shape[0], wb.shape[0], dtype=torch.bfloat16, device=x2.device)
             ext().gemm_skinny(x2, wb, y)
         else:
+            x2 = _gemm_rows(x2)
             y = gemm(x2, wb)
         ctx.save_for_backward(x2, wb)
         ctx.w = w
@@ -110,8 +119,7 @@ class _Linear(torch.autograd.Function):
         dy2 = dy.reshape(-1, n)
         if dy2.dtype != torch.bfloat16:
             dy2 = dy2.to(torch.bfloat16)
-        if not dy2.is_contiguous():
-            dy2 = dy2.contiguous()
+        dy2 = _gemm_rows(dy2)
         dx = dw = None
         if ctx.needs_input_grad[0]:
             dx = gemm(dy2, wb, b_major="mn").view(ctx.x_shape)

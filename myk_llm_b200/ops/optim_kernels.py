@@ -69,29 +69,38 @@ def batched_newton_schulz_orthogonalize(g: torch.Tensor, steps: int, transposed:
 # AdamW
 # ---------------------------------------------------------------------------------------
 def adamw_multi_tensor(params, grads, exp_avgs, exp_avg_sqs, step: int, lr: float, beta1: float, beta2: float,
-                       eps: float, weight_decay: float) -> None:
+                       eps: float, weight_decay: float, grad_scale: torch.Tensor | None = None) -> None:
     """One AdamW step (torch.optim.AdamW semantics, decoupled decay) over lists of fp32
-    tensors, in a single kernel launch on CUDA."""
+    tensors, in a single kernel launch on CUDA.  ``grad_scale`` (a one-element fp32 device
+    tensor, e.g. the clipping coefficient) multiplies every gradient as it is read."""
     if not params:
         return
     if not params[0].is_cuda:
         for p, g, m, v in zip(params, grads, exp_avgs, exp_avg_sqs):
-            ref.adamw_ref(p, g.to(p.dtype), m, v, step, lr, beta1, beta2, eps, weight_decay)
+            g = g.to(p.dtype) if grad_scale is None else g.to(p.dtype) * grad_scale
+            ref.adamw_ref(p, g, m, v, step, lr, beta1, beta2, eps, weight_decay)
         return
     ext().adamw_step(params, grads, exp_avgs, exp_avg_sqs, int(step), float(lr), float(beta1), float(beta2),
-                     float(eps), float(weight_decay))
+                     float(eps), float(weight_decay), _scale(grad_scale))
+
+
+def _scale(t: torch.Tensor | None) -> torch.Tensor | None:
+    return None if t is None else t.reshape(1).to(torch.float32).contiguous()
 
 
 # ---------------------------------------------------------------------------------------
 # Muon momentum / update
 # ---------------------------------------------------------------------------------------
-def muon_prepare(grads, bufs, momentum: float, nesterov: bool, out: torch.Tensor) -> None:
+def muon_prepare(grads, bufs, momentum: float, nesterov: bool, out: torch.Tensor,
+                 grad_scale: torch.Tensor | None = None) -> None:
     """buf <- lerp(buf, g, 1-mu); u = lerp(g, buf, mu) if nesterov else buf; out[i] = bf16(u).
-    ``out`` is a (n, r, c) bf16 stack."""
+    ``out`` is a (n, r, c) bf16 stack; ``grad_scale`` multiplies g as it is read."""
     if out.is_cuda:
-        ext().muon_prepare(grads, bufs, float(momentum), bool(nesterov), out)
+        ext().muon_prepare(grads, bufs, float(momentum), bool(nesterov), out, _scale(grad_scale))
         return
     for i, (g, m) in enumerate(zip(grads, bufs)):
+        if grad_scale is not None:
+            g = g.to(m.dtype) * grad_scale
         m.lerp_(g.to(m.dtype), 1 - momentum)
         u = g.to(m.dtype).lerp(m, momentum) if nesterov else m
         out[i].copy_(u)

@@ -71,6 +71,9 @@ class Muon(torch.optim.Optimizer):
         # Set by the sharded runtime: fn(items, group) performs the whole update for
         # parameters it owns (items: list of (param, grad, momentum_buffer)).
         self.sharded_step: Callable | None = None
+        # Optional one-element device tensor multiplying every gradient of the next step
+        # (the clipping coefficient); the CUDA kernels apply it as they read the gradient.
+        self.grad_scale: torch.Tensor | None = None
 
     _lr_ratio = staticmethod(lr_ratio)
 
@@ -99,8 +102,13 @@ class Muon(torch.optim.Optimizer):
                     local[(tuple(p.shape), g.dtype, p.device)].append((p, g, buf))
                 else:
                     slow.append((p, g, buf))
+            scale = self.grad_scale
+            if scale is not None:  # paths without a scaling kernel scale their gradients first
+                rest = [g for its in fsdp.values() for _, g, _ in its] + [g for _, g, _ in sharded + slow]
+                if rest:
+                    torch._foreach_mul_(rest, scale)
             for items in local.values():
-                self._step_local_bucket(items, lr, wd, mu, nesterov, ns_steps, mode)
+                self._step_local_bucket(items, lr, wd, mu, nesterov, ns_steps, mode, scale)
             for items in fsdp.values():
                 self._step_fsdp_bucket(items, lr, wd, mu, nesterov, ns_steps, mode)
             if sharded:
@@ -119,11 +127,11 @@ class Muon(torch.optim.Optimizer):
                 p.add_(u.to(p.dtype), alpha=-lr * lr_ratio(p.shape, mode))
 
     @staticmethod
-    def _step_local_bucket(items, lr, wd, mu, nesterov, ns_steps, mode):
+    def _step_local_bucket(items, lr, wd, mu, nesterov, ns_steps, mode, grad_scale=None):
         params = [p for p, _, _ in items]
         rows, cols = params[0].shape
         packed = torch.empty(len(items), rows, cols, dtype=torch.bfloat16, device=params[0].device)
-        ops.muon_prepare([g for _, g, _ in items], [b for _, _, b in items], mu, nesterov, packed)
+        ops.muon_prepare([g for _, g, _ in items], [b for _, _, b in items], mu, nesterov, packed, grad_scale)
         orth = ops.batched_newton_schulz_orthogonalize(packed, ns_steps)
         ops.muon_apply(params, orth, lr, wd, -lr * lr_ratio((rows, cols), mode))
 
@@ -182,6 +190,7 @@ class AdamW(torch.optim.AdamW):
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, **kw):
         kw.pop("fused", None)
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, **kw)
+        self.grad_scale: torch.Tensor | None = None  # as Muon.grad_scale
 
     @torch.no_grad()
     def step(self, closure=None):  # type: ignore[override]
@@ -206,15 +215,16 @@ class AdamW(torch.optim.AdamW):
                 grads = [_local(p.grad) for p in ps]
                 ms = [_local(self.state[p]["exp_avg"]) for p in ps]
                 vs = [_local(self.state[p]["exp_avg_sq"]) for p in ps]
+                scale = self.grad_scale
                 if local and local[0].is_cuda and all(t.dtype == torch.float32 for t in local):
                     ops.adamw_multi_tensor(local, [g.contiguous() for g in grads], ms, vs, step, group["lr"], b1, b2,
-                                           group["eps"], group["weight_decay"])
+                                           group["eps"], group["weight_decay"], scale)
                 else:
                     from ..ops.reference import adamw_ref
 
                     for p, g, m, v in zip(local, grads, ms, vs):
-                        adamw_ref(p, g.to(p.dtype), m, v, step, group["lr"], b1, b2, group["eps"],
-                                  group["weight_decay"])
+                        g = g.to(p.dtype) if scale is None else g.to(p.dtype) * scale
+                        adamw_ref(p, g, m, v, step, group["lr"], b1, b2, group["eps"], group["weight_decay"])
 
 
 def _local(t: torch.Tensor) -> torch.Tensor:

@@ -207,16 +207,21 @@ class Trainer:
             ops.invalidate_weight_cache()
             return norm
         norm = self.grad_norm()
+        coef = None
         if grad_clip and grad_clip > 0:
+            # the clipping coefficient stays on the device and the optimizer kernels apply it
+            # as they read each gradient: no extra pass over the gradients, no host sync
             coef = torch.clamp(grad_clip / (norm + 1e-6), max=1.0)
-            gs = [p.grad for p in self._grad_owners() if p.grad is not None]
-            if self.grads is not None:
-                self.grads.flat.mul_(coef)
-                gs = [g for p, g in zip(self._grad_owners(), gs) if id(p) not in self.grads.ids]
-            if gs:
-                torch._foreach_mul_(gs, coef)
         for opt in self.optimizers:
+            if coef is not None and hasattr(opt, "grad_scale"):
+                opt.grad_scale = coef
+            elif coef is not None:  # an optimizer without the hook: scale its gradients here
+                gs = [p.grad for g in opt.param_groups for p in g["params"] if p.grad is not None]
+                if gs:
+                    torch._foreach_mul_(gs, coef)
             opt.step()
+            if hasattr(opt, "grad_scale"):
+                opt.grad_scale = None
         ops.invalidate_weight_cache()
         if self.tables is not None:
             self.tables.step()

@@ -250,3 +250,58 @@ def test_newton_schulz_matches_reference():
         out = batched_newton_schulz_orthogonalize(g, 5)
         ref = newton_schulz_ref(g, 5)
         _close(out, ref, 6e-2)
+
+
+def test_optimizer_kernels_apply_device_grad_scale():
+    from myk_llm_b200.ops import adamw_multi_tensor, muon_prepare
+
+    torch.manual_seed(9)
+    scale = torch.tensor(0.37, device="cuda")
+    ps = [torch.randn(s, device="cuda") for s in [(1000,), (37, 91)]]
+    gs = [torch.randn_like(p) for p in ps]
+    ms = [torch.randn_like(p).abs() for p in ps]
+    vs = [torch.randn_like(p).abs() for p in ps]
+    a = [[t.clone() for t in ts] for ts in (ps, ms, vs)]
+    b = [[t.clone() for t in ts] for ts in (ps, ms, vs)]
+    adamw_multi_tensor(a[0], gs, a[1], a[2], 3, 1e-2, 0.9, 0.95, 1e-8, 0.1, grad_scale=scale)
+    adamw_multi_tensor(b[0], [g * scale for g in gs], b[1], b[2], 3, 1e-2, 0.9, 0.95, 1e-8, 0.1)
+    for x, y in zip(a[0] + a[1] + a[2], b[0] + b[1] + b[2]):
+        assert torch.allclose(x, y, atol=1e-6, rtol=1e-5)
+    g2 = [torch.randn(64, 96, device="cuda") for _ in range(3)]
+    m1 = [torch.randn(64, 96, device="cuda") for _ in range(3)]
+    m2 = [m.clone() for m in m1]
+    o1 = torch.empty(3, 64, 96, device="cuda", dtype=torch.bfloat16)
+    o2 = torch.empty_like(o1)
+    muon_prepare(g2, m1, 0.95, True, o1, grad_scale=scale)
+    muon_prepare([g * scale for g in g2], m2, 0.95, True, o2)
+    assert torch.equal(o1, o2)
+    for x, y in zip(m1, m2):
+        assert torch.allclose(x, y, atol=1e-6)
+
+
+def test_split_cols_and_strided_linear():
+    from myk_llm_b200 import ops
+
+    torch.manual_seed(10)
+    base = torch.randn(2, 300, 96 + 64 + 32 + 8, device="cuda", dtype=torch.bfloat16)
+    x = base[..., :192].detach().requires_grad_(True)  # strided rows
+    a, b, c = ops.split_cols(x, (96, 64, 32))
+    assert a.is_contiguous() and b.shape == (2, 300, 64)
+    ra, rb, rc = x.detach().split((96, 64, 32), dim=-1)
+    assert torch.equal(a, ra) and torch.equal(b, rb) and torch.equal(c, rc)
+    ga, gb, gc = torch.randn_like(a), torch.randn_like(b), torch.randn_like(c)
+    ((a.float() * ga.float()).sum() + (b.float() * gb.float()).sum() + (c.float() * gc.float()).sum()).backward()
+    assert torch.equal(x.grad, torch.cat([ga, gb, gc], -1))
+    # a linear reading a column slice of a wider activation (strided rows, no copy)
+    w = (0.05 * torch.randn(128, 64, device="cuda")).requires_grad_(True)
+    xs = base[..., 96:160].detach().requires_grad_(True)
+    y = ops.linear(xs, w)
+    gy = torch.randn_like(y)
+    (y.float() * gy.float()).sum().backward()
+    xr = xs.detach().float().requires_grad_(True)
+    wr = w.detach().bfloat16().float().requires_grad_(True)
+    yr = xr @ wr.t()
+    (yr * gy.float()).sum().backward()
+    _close(y, yr, 1e-2)
+    _close(xs.grad, xr.grad, 2e-2)
+    _close(w.grad, wr.grad, 2e-2)

@@ -63,3 +63,23 @@ def test_split_parameters():
     assert all(names[id(p)].startswith("layers") for p in g.muon)
     assert any(names[id(p)] == "lm_head.weight" for p in g.no_decay)
     assert any("conv1d" in names[id(p)] for p in g.decay)
+
+
+@pytest.mark.parametrize("kind", ["adamw", "muon"])
+def test_grad_scale_equals_prescaled_gradients(kind):
+    """The clipping coefficient handed to the optimizer equals multiplying the gradients first."""
+    torch.manual_seed(2)
+    p1 = torch.nn.Parameter(torch.randn(16, 32))
+    p2 = torch.nn.Parameter(p1.detach().clone())
+    make = (lambda p: AdamW([p], lr=1e-2, weight_decay=0.1)) if kind == "adamw" else \
+        (lambda p: Muon([p], lr=0.02, weight_decay=0.1))
+    o1, o2 = make(p1), make(p2)
+    for i in range(3):
+        g = torch.randn(16, 32)
+        scale = torch.tensor(0.3 + 0.2 * i)
+        p1.grad, p2.grad = g.clone(), g * scale
+        o1.grad_scale = scale
+        o1.step()
+        o1.grad_scale = None
+        o2.step()
+    assert torch.allclose(p1, p2, atol=1e-6)
