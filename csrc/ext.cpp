@@ -5,7 +5,7 @@ namespace mykb {
 int64_t take_status();
 // gemm.cu
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
-          double alpha, double beta, bool accumulate);
+          double alpha, double beta, bool accumulate, bool symmetric);
 // norm.cu
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<std::vector<torch::Tensor>> add,
                                        double eps, c10::ScalarType out_dtype);

@@ -36,6 +36,7 @@ struct GemmParams {
   const void* C;  // optional epilogue input, same layout/dtype as D
   int64_t ldc, c_batch_stride;
   float alpha, beta;
+  int symmetric;  // D = D^T (M == N): tiles strictly above the diagonal are skipped, then mirrored
   int* status;
 };
 
@@ -44,6 +45,11 @@ constexpr int kBK = 64;
 constexpr int kGroupM = 8;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+// A tile of a symmetric product whose every element lies above the diagonal (column > row).
+__device__ __forceinline__ bool skip_tile(const GemmParams& p, int mt, int nt, int bn) {
+  return p.symmetric && nt * bn >= (mt + 1) * kBM;
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -118,6 +124,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x) {
         int b, mt, nt, split;
         unit_coords(p, unit, b, mt, nt, split);
+        if (skip_tile(p, mt, nt, BN)) continue;
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -150,9 +157,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x) {
         int b, mt, nt, split;
         unit_coords(p, unit, b, mt, nt, split);
+        if (skip_tile(p, mt, nt, BN)) continue;
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         const int buf = local & 1;
@@ -177,6 +185,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         if (!ok) break;
         umma_commit(&acc_full[buf]);
+        ++local;
       }
     }
   } else {
@@ -184,9 +193,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t stage_base = smem_u32(staging + (warp - 2) * 2 * S::kStagingBytes);
     int local = 0, slab_ct = 0;
-    for (int unit = blockIdx.x; unit < p.total_units; unit += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < p.total_units; unit += gridDim.x) {
       int b, mt, nt, split;
       unit_coords(p, unit, b, mt, nt, split);
+      if (skip_tile(p, mt, nt, BN)) continue;
       const int buf = local & 1;
       if (!mbar_wait_warp(&acc_full[buf], (local >> 1) & 1, p.status, __LINE__)) break;
       tc_fence_after();
@@ -266,6 +276,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      ++local;
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
@@ -331,9 +342,30 @@ static void dispatch_layout(bool a_mn, bool b_mn, bool out_f32, bool accum, cons
 #undef MYKB_GEMM_CASE
 }
 
+// Symmetric mode: copy the lower triangle onto the upper one (D[i][j] = D[j][i], j > i), which
+// also fills the tiles the GEMM skipped.  One thread per element pair, 32x32 tiles through
+// shared memory so both the reads and the writes are coalesced.
+template <typename T>
+__global__ void mirror_lower_kernel(T* __restrict__ d, int n, int64_t ld, int64_t bstride) {
+  __shared__ T tile[32][33];
+  const int bi = blockIdx.y, bj = blockIdx.x;  // destination tile (rows bi, cols bj), bj > bi
+  if (bj < bi) return;
+  T* m = d + (int64_t)blockIdx.z * bstride;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int r = ty; r < 32; r += blockDim.y) {  // read the source tile (rows bj, cols bi)
+    const int i = bj * 32 + r, j = bi * 32 + tx;
+    if (i < n && j < n) tile[r][tx] = m[(int64_t)i * ld + j];
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += blockDim.y) {
+    const int i = bi * 32 + r, j = bj * 32 + tx;
+    if (i < n && j < n && j > i) m[(int64_t)i * ld + j] = tile[tx][r];
+  }
+}
+
 // a: (batch?, M, K) or (batch?, K, M); b: (batch?, N, K) or (batch?, K, N); d: (batch?, M, N)
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
-          double alpha, double beta, bool accumulate) {
+          double alpha, double beta, bool accumulate, bool symmetric) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands required");
   TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm: D must be bf16 or fp32");
@@ -394,6 +426,10 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
     p.c_batch_stride = batched ? c->stride(0) : 0;
   }
   p.status = device_status();
+  if (symmetric) {
+    TORCH_CHECK(M == N && !accumulate && split == 1, "gemm: symmetric mode needs M == N and a stored product");
+    p.symmetric = 1;
+  }
 
   // Tensor maps (dims innermost first): A/B tiles of 64 elements (128 B) along the
   // contiguous dim; D boxes of 128 bytes x 32 rows.
@@ -416,6 +452,15 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
     dispatch_layout<128>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
   } else {
     dispatch_layout<256>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
+  }
+  if (symmetric && M > 0) {
+    const int tiles32 = (M + 31) / 32;
+    dim3 mg(tiles32, tiles32, batch), mb(32, 8);
+    if (out_f32)
+      mirror_lower_kernel<float><<<mg, mb, 0, stream>>>(d.data_ptr<float>(), M, d.stride(-2), d_bs);
+    else
+      mirror_lower_kernel<__nv_bfloat16><<<mg, mb, 0, stream>>>((__nv_bfloat16*)d.data_ptr(), M, d.stride(-2), d_bs);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
 

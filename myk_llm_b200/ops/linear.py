@@ -28,9 +28,12 @@ from ._ext import ext
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_major: str = "k", b_major: str = "k",
          out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
-         beta: float = 0.0, c: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+         beta: float = 0.0, c: torch.Tensor | None = None, accumulate: bool = False,
+         symmetric: bool = False) -> torch.Tensor:
     """See module docstring.  ``a`` is (.., M, K) for K-major or (.., K, M) for M-major; ``b`` is
-    (.., N, K) for K-major or (.., K, N) for N-major.  Leading dims are a batch."""
+    (.., N, K) for K-major or (.., K, N) for N-major.  Leading dims are a batch.  ``symmetric``
+    promises a symmetric result (e.g. X X^T): tiles above the diagonal are not computed and
+    the lower triangle is mirrored onto them."""
     a_mn, b_mn = a_major == "mn", b_major == "mn"
     if not a.is_cuda:
         am = a.transpose(-1, -2) if a_mn else a
@@ -49,8 +52,23 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_major: str = "k", b_major: str =
     n = b.shape[-1] if b_mn else b.shape[-2]
     if out is None:
         out = torch.empty(*a.shape[:-2], m, n, dtype=out_dtype, device=a.device)
-    ext().gemm(a, b, out, c, a_mn, b_mn, float(alpha), float(beta), bool(accumulate))
+    for name, t in (("a", a), ("b", b), ("out", out), ("c", c)):
+        _check_tma_operand(name, t)
+    ext().gemm(a, b, out, c, a_mn, b_mn, float(alpha), float(beta), bool(accumulate), bool(symmetric))
     return out
+
+
+def _check_tma_operand(name: str, t: torch.Tensor | None) -> None:
+    """The GEMM moves every operand with TMA: 16-byte aligned base, unit inner stride and
+    row / batch strides that are multiples of 16 bytes (e.g. bf16 rows of a multiple of 8)."""
+    if t is None:
+        return
+    es = t.element_size()
+    ok = t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and (t.stride(-2) * es) % 16 == 0 and \
+        (t.dim() < 3 or t.size(0) == 1 or (t.stride(0) * es) % 16 == 0)
+    if not ok:
+        raise ValueError(f"gemm: operand {name} {tuple(t.shape)} strides {t.stride()} ({t.dtype}) does not meet the "
+                         "TMA layout rules (unit inner stride, 16-byte aligned rows and base)")
 
 
 _WEIGHT_EPOCH = [0]

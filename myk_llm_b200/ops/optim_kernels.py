@@ -28,7 +28,7 @@ def batched_syrk(x: torch.Tensor, alpha: float = 1.0, beta: float = 0.0, bias: t
         if bias is not None:
             out = out + beta * bias.float()
         return out.to(x.dtype)
-    return gemm(x, x, alpha=alpha, beta=beta, c=bias)
+    return gemm(x, x, alpha=alpha, beta=beta, c=bias, symmetric=bias is None and x.shape[-2] >= 2048)
 
 
 def frobenius_normalize_(x: torch.Tensor, eps: float = 1e-7) -> torch.Tensor:
@@ -53,14 +53,18 @@ def batched_newton_schulz_orthogonalize(g: torch.Tensor, steps: int, transposed:
     frobenius_normalize_(x, eps)
     r, cdim = x.shape[-2], x.shape[-1]
     tall = (r > cdim) if transposed is None else transposed
+    # The Gram matrix and the polynomial in it are symmetric, so their tiles above the
+    # diagonal can be skipped and mirrored.  Measured on B200 this pays from 2048-wide Grams
+    # (~6% of the iteration); for 1024-wide ones the mirror pass costs more than it saves.
+    sym = min(r, cdim) >= 2048
     for _ in range(steps):
         if tall:
-            gram = gemm(x, x, a_major="mn", b_major="mn")  # (c, c) = Y^T Y
-            poly = gemm(gram, gram, alpha=c, beta=b, c=gram)
+            gram = gemm(x, x, a_major="mn", b_major="mn", symmetric=sym)  # (c, c) = Y^T Y
+            poly = gemm(gram, gram, alpha=c, beta=b, c=gram, symmetric=sym)
             x = gemm(x, poly, alpha=1.0, beta=a, c=x)  # Y poly (poly symmetric)
         else:
-            gram = gemm(x, x)  # (r, r) = X X^T
-            poly = gemm(gram, gram, alpha=c, beta=b, c=gram)
+            gram = gemm(x, x, symmetric=sym)  # (r, r) = X X^T
+            poly = gemm(gram, gram, alpha=c, beta=b, c=gram, symmetric=sym)
             x = gemm(poly, x, b_major="mn", alpha=1.0, beta=a, c=x)
     return x
 

@@ -112,3 +112,37 @@ def test_linear_uses_skinny_rows():
     x = torch.randn(2, 3, 512, device="cuda", generator=g).bfloat16()
     w = torch.randn(768, 512, device="cuda", generator=g)
     _close(linear(x, w), x.float() @ w.bfloat16().float().t())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,batch", [(128, 256, 1), (312, 512, 2), (1024, 1536, 3), (2048, 640, 1)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_symmetric_gemm_matches_full(m, k, batch, out_dtype):
+    """Symmetric mode (X X^T, and a symmetric product with a symmetric C) skips the tiles above
+    the diagonal and mirrors the lower triangle: it must equal the full product."""
+    from myk_llm_b200.ops import gemm
+
+    torch.manual_seed(m + k)
+    x = torch.randn(batch, m, k, device="cuda").bfloat16()
+    full = gemm(x, x, out_dtype=out_dtype)
+    sym = gemm(x, x, out_dtype=out_dtype, symmetric=True)
+    ref = x.float() @ x.float().transpose(-1, -2)
+    assert torch.equal(sym, sym.transpose(-1, -2))
+    tol = 2e-2 if out_dtype == torch.bfloat16 else 1e-3
+    assert ((sym.float() - ref).abs().max() / ref.abs().max()) < tol
+    lower = torch.tril(torch.ones(m, m, device="cuda", dtype=torch.bool))
+    assert torch.equal(sym[:, lower], full[:, lower])
+    g = sym if out_dtype == torch.bfloat16 else sym.bfloat16()
+    poly = gemm(g, g, alpha=0.5, beta=-1.5, c=g, symmetric=True)
+    poly_ref = 0.5 * (g.float() @ g.float()) - 1.5 * g.float()
+    assert torch.equal(poly, poly.transpose(-1, -2))
+    assert ((poly.float() - poly_ref).abs().max() / poly_ref.abs().max()) < 2e-2
+
+
+def test_gemm_rejects_layouts_tma_cannot_move():
+    """Rows that are not a multiple of 16 bytes are refused with a clear error up front."""
+    from myk_llm_b200.ops import gemm
+
+    x = torch.randn(2, 300, 64, device="cuda").bfloat16()
+    with pytest.raises(ValueError):
+        gemm(x, x)  # output rows of 300 bf16 = 600 bytes
