@@ -620,11 +620,16 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           uint32_t cr[32];
           tmem_ld32_raw(tmem + lane_base + s_col + c * 32, cr);
           tmem_wait_ld();
+          if (edge) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float sc = __uint_as_float(cr[i]);
-            if (edge && (unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
-            mx = fmaxf(mx, sc);
+            for (int i = 0; i < 32; ++i) {
+              float sc = __uint_as_float(cr[i]);
+              if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
+              mx = fmaxf(mx, sc);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(cr[i]), __uint_as_float(cr[i + 1]));
           }
         }
         const float m_tile = mx * p.scale_log2;
@@ -647,7 +652,8 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           }
         }
         const float neg = (m_ref == -INFINITY) ? 0.f : -m_ref;
-        float rs = 0.f;
+        const float2 scale2 = make_float2(p.scale_log2, p.scale_log2), neg2 = make_float2(neg, neg);
+        float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t cr[32];
@@ -661,15 +667,15 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
               if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) s0 = -INFINITY;
               if ((unsigned)(c * 32 + i + 1 - kmin) >= (unsigned)kspan) s1 = -INFINITY;
             }
-            const float p0 = exp2f(fmaf(s0, p.scale_log2, neg));
-            const float p1 = exp2f(fmaf(s1, p.scale_log2, neg));
-            rs += p0 + p1;
-            pk[i >> 1] = pack_bf16x2(p0, p1);
+            const float2 a = ffma2(make_float2(s0, s1), scale2, neg2);  // both exponents in one FMA
+            const float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
+            rs2 = fadd2(rs2, pv);
+            pk[i >> 1] = pack_bf16x2(pv.x, pv.y);
           }
           // P columns [16 c, 16 c + 16) lie in S columns this thread has already read
           tmem_st16_raw(tmem + lane_base + s_col + c * 16, pk);
         }
-        l += rs;
+        l += rs2.x + rs2.y;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -1114,26 +1120,34 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
               const float* c_delta = s_delta + st_idx * 128 + 64 * j + 32 * half;
               tmem_wait_ld();
               uint32_t pk[16], dk[16];
+              const float2 sc2 = make_float2(p.f.scale_log2, p.f.scale_log2), ps2 = make_float2(p.scale, p.scale);
 #pragma unroll
               for (int i4 = 0; i4 < 8; ++i4) {
                 const float4 l4 = reinterpret_cast<const float4*>(c_lse)[i4];
                 const float4 d4 = reinterpret_cast<const float4*>(c_delta)[i4];
-                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-                const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+                const float2 nl[2] = {make_float2(-l4.x, -l4.y), make_float2(-l4.z, -l4.w)};
+                const float2 nd[2] = {make_float2(-d4.x, -d4.y), make_float2(-d4.z, -d4.w)};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
+                for (int e = 0; e < 4; e += 2) {
                   const int i = i4 * 4 + e;
-                  float pv = exp2f(fmaf(sv[i], p.f.scale_log2, -lv[e]));
+                  const float2 a = ffma2(make_float2(sv[i], sv[i + 1]), sc2, nl[e >> 1]);
+                  float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
                   if (edge) {
-                    const int qi = q0 + 32 * half + i;
-                    const int qpos = qi + off;
-                    bool vis = qi < it.g.len_q && kp < it.g.len_k;
-                    if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
-                    if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
-                    pv = vis ? pv : 0.f;
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                      const int qi = q0 + 32 * half + i + u;
+                      const int qpos = qi + off;
+                      bool vis = qi < it.g.len_q && kp < it.g.len_k;
+                      if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
+                      if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
+                      if (!vis) (u == 0 ? pv.x : pv.y) = 0.f;
+                    }
                   }
-                  sv[i] = pv;
-                  dp[i] = (pv * p.scale) * (dp[i] - dv[e]);
+                  sv[i] = pv.x;
+                  sv[i + 1] = pv.y;
+                  const float2 d = fmul2(fmul2(pv, ps2), fadd2(make_float2(dp[i], dp[i + 1]), nd[e >> 1]));
+                  dp[i] = d.x;
+                  dp[i + 1] = d.y;
                 }
               }
 #pragma unroll
@@ -1400,15 +1414,18 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           const float ps = p.scale;
           tmem_wait_ld();
           uint32_t dk[16];
+          const float2 sc2 = make_float2(f.scale_log2, f.scale_log2), nl2 = make_float2(-lse2, -lse2);
+          const float2 ps2 = make_float2(ps, ps), nd2 = make_float2(-dl, -dl);
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            float p0 = exp2f(fmaf(sv[i], f.scale_log2, -lse2));
-            float p1 = exp2f(fmaf(sv[i + 1], f.scale_log2, -lse2));
+            const float2 a = ffma2(make_float2(sv[i], sv[i + 1]), sc2, nl2);
+            float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
             if (edge) {
-              if ((unsigned)(32 * half + i - kmin) >= (unsigned)kspan) p0 = 0.f;
-              if ((unsigned)(32 * half + i + 1 - kmin) >= (unsigned)kspan) p1 = 0.f;
+              if ((unsigned)(32 * half + i - kmin) >= (unsigned)kspan) pv.x = 0.f;
+              if ((unsigned)(32 * half + i + 1 - kmin) >= (unsigned)kspan) pv.y = 0.f;
             }
-            dk[i >> 1] = pack_bf16x2((p0 * ps) * (dp[i] - dl), (p1 * ps) * (dp[i + 1] - dl));
+            const float2 d = fmul2(fmul2(pv, ps2), fadd2(make_float2(dp[i], dp[i + 1]), nd2));
+            dk[i >> 1] = pack_bf16x2(d.x, d.y);
           }
           tmem_st16_raw(tmem + lane_base + b * 128 + 32 * half, dk);
           tmem_wait_st();
