@@ -343,23 +343,40 @@ static void dispatch_layout(bool a_mn, bool b_mn, bool out_f32, bool accum, cons
 }
 
 // Symmetric mode: copy the lower triangle onto the upper one (D[i][j] = D[j][i], j > i), which
-// also fills the tiles the GEMM skipped.  One thread per element pair, 32x32 tiles through
-// shared memory so both the reads and the writes are coalesced.
+// also fills the tiles the GEMM skipped.  A block moves one 64 x 64 tile: 16-byte vector loads
+// of the source tile (below the diagonal) into shared memory, transposed 16-byte vector stores
+// of the destination tile (above it).  Rows must be 16-byte aligned (checked by the caller).
 template <typename T>
-__global__ void mirror_lower_kernel(T* __restrict__ d, int n, int64_t ld, int64_t bstride) {
-  __shared__ T tile[32][33];
-  const int bi = blockIdx.y, bj = blockIdx.x;  // destination tile (rows bi, cols bj), bj > bi
+__global__ void __launch_bounds__(256) mirror_lower_kernel(T* __restrict__ d, int n, int64_t ld, int64_t bstride) {
+  constexpr int V = 16 / sizeof(T);  // elements per vector
+  __shared__ alignas(16) T tile[64][64 + V];
+  const int bi = blockIdx.y, bj = blockIdx.x;  // destination tile: rows 64 bi.., cols 64 bj..
   if (bj < bi) return;
   T* m = d + (int64_t)blockIdx.z * bstride;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int r = ty; r < 32; r += blockDim.y) {  // read the source tile (rows bj, cols bi)
-    const int i = bj * 32 + r, j = bi * 32 + tx;
-    if (i < n && j < n) tile[r][tx] = m[(int64_t)i * ld + j];
+  constexpr int kVecRow = 64 / V;
+  for (int v = threadIdx.x; v < 64 * kVecRow; v += blockDim.x) {  // source tile: rows 64 bj.., cols 64 bi..
+    const int r = v / kVecRow, c = (v % kVecRow) * V;
+    const int i = bj * 64 + r, j = bi * 64 + c;
+    if (i < n && j + V <= n) {
+      *reinterpret_cast<uint4*>(&tile[r][c]) = *reinterpret_cast<const uint4*>(m + (int64_t)i * ld + j);
+    } else if (i < n) {
+      for (int e = 0; e < V && j + e < n; ++e) tile[r][c + e] = m[(int64_t)i * ld + j + e];
+    }
   }
   __syncthreads();
-  for (int r = ty; r < 32; r += blockDim.y) {
-    const int i = bi * 32 + r, j = bj * 32 + tx;
-    if (i < n && j < n && j > i) m[(int64_t)i * ld + j] = tile[tx][r];
+  for (int v = threadIdx.x; v < 64 * kVecRow; v += blockDim.x) {
+    const int r = v / kVecRow, c = (v % kVecRow) * V;  // destination row 64 bi + r, cols 64 bj + c ..
+    const int i = bi * 64 + r, j = bj * 64 + c;
+    if (i >= n) continue;
+    alignas(16) T out[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) out[e] = tile[c + e][r];
+    if (j > i && j + V <= n) {
+      *reinterpret_cast<uint4*>(m + (int64_t)i * ld + j) = *reinterpret_cast<const uint4*>(out);
+    } else {
+      for (int e = 0; e < V; ++e)
+        if (j + e > i && j + e < n) m[(int64_t)i * ld + j + e] = out[e];
+    }
   }
 }
 
@@ -454,12 +471,12 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
     dispatch_layout<256>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
   }
   if (symmetric && M > 0) {
-    const int tiles32 = (M + 31) / 32;
-    dim3 mg(tiles32, tiles32, batch), mb(32, 8);
+    const int tiles64 = (M + 63) / 64;
+    dim3 mg(tiles64, tiles64, batch);
     if (out_f32)
-      mirror_lower_kernel<float><<<mg, mb, 0, stream>>>(d.data_ptr<float>(), M, d.stride(-2), d_bs);
+      mirror_lower_kernel<float><<<mg, 256, 0, stream>>>(d.data_ptr<float>(), M, d.stride(-2), d_bs);
     else
-      mirror_lower_kernel<__nv_bfloat16><<<mg, mb, 0, stream>>>((__nv_bfloat16*)d.data_ptr(), M, d.stride(-2), d_bs);
+      mirror_lower_kernel<__nv_bfloat16><<<mg, 256, 0, stream>>>((__nv_bfloat16*)d.data_ptr(), M, d.stride(-2), d_bs);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
