@@ -219,15 +219,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           const int cbase = col0 + s * kSlab;
           if (OUT_F32) {
             const float* c = reinterpret_cast<const float*>(p.C) + b * p.c_batch_stride + (int64_t)row * p.ldc;
+            if (cbase + kSlab <= p.N) {  // whole slab in range: 16-byte loads (rows are 16-byte aligned)
 #pragma unroll
-            for (int i = 0; i < kSlab; ++i)
-              if (cbase + i < p.N) v[i] += p.beta * c[cbase + i];
+              for (int i = 0; i < kSlab; i += 4) {
+                const float4 cv = *reinterpret_cast<const float4*>(c + cbase + i);
+                v[i] += p.beta * cv.x;
+                v[i + 1] += p.beta * cv.y;
+                v[i + 2] += p.beta * cv.z;
+                v[i + 3] += p.beta * cv.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < kSlab; ++i)
+                if (cbase + i < p.N) v[i] += p.beta * c[cbase + i];
+            }
           } else {
             const __nv_bfloat16* c =
                 reinterpret_cast<const __nv_bfloat16*>(p.C) + b * p.c_batch_stride + (int64_t)row * p.ldc;
+            if (cbase + kSlab <= p.N) {
 #pragma unroll
-            for (int i = 0; i < kSlab; ++i)
-              if (cbase + i < p.N) v[i] += p.beta * __bfloat162float(c[cbase + i]);
+              for (int i = 0; i < kSlab; i += 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(c + cbase + i);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 f = __bfloat1622float2(h[j]);
+                  v[i + 2 * j] += p.beta * f.x;
+                  v[i + 2 * j + 1] += p.beta * f.y;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < kSlab; ++i)
+                if (cbase + i < p.N) v[i] += p.beta * __bfloat162float(c[cbase + i]);
+            }
           }
         }
         // The TMA store issued from this staging buffer two slabs ago must have finished

@@ -54,9 +54,10 @@ def batched_newton_schulz_orthogonalize(g: torch.Tensor, steps: int, transposed:
     r, cdim = x.shape[-2], x.shape[-1]
     tall = (r > cdim) if transposed is None else transposed
     # The Gram matrix and the polynomial in it are symmetric, so their tiles above the
-    # diagonal can be skipped and mirrored.  Measured on B200 this pays from 2048-wide Grams
-    # (~6% of the iteration); for 1024-wide ones the mirror pass costs more than it saves.
-    sym = min(r, cdim) >= 2048
+    # diagonal can be skipped and mirrored.  Measured on B200 this pays for wide matrices
+    # (2048 x 11264: 1.5x per iteration) and not for near-square ones (aspect <= 3, where
+    # the mirror pass and uneven tile counts cost what the skipped tiles save).
+    sym = min(r, cdim) >= 2048 and max(r, cdim) >= 4 * min(r, cdim)
     for _ in range(steps):
         if tall:
             gram = gemm(x, x, a_major="mn", b_major="mn", symmetric=sym)  # (c, c) = Y^T Y
