@@ -1204,22 +1204,31 @@ __global__ void conv1d_fwd_kernel(const bf16* __restrict__ x, const float* __res
   float2 win[K];
   conv_prime<K>(win, xb, init, b, c, D, t0, start, docs.cu == nullptr);
   const int t1 = min(T, t0 + kConvTile);
-  for (int t = t0; t < t1; ++t) {
-    if (t >= end) {
-      docs.find(t, T, start, end, d);
+  constexpr int kPre = 8;  // time steps loaded ahead: 8 independent loads in flight per thread
+  for (int tb = t0; tb < t1; tb += kPre) {
+    float2 xin[kPre];
 #pragma unroll
-      for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
+    for (int u = 0; u < kPre; ++u) xin[u] = tb + u < t1 ? ld2(xb + (int64_t)(tb + u) * D) : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int t = tb + u;
+      if (t >= t1) break;
+      if (t >= end) {
+        docs.find(t, T, start, end, d);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
+      }
+      win[K - 1] = xin[u];
+      float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        z0 = fmaf(w0[i], win[i].x, z0);
+        z1 = fmaf(w1[i], win[i].y, z1);
+      }
+      st2(y + ((int64_t)b * T + t) * D + c, z0 / (1.f + __expf(-z0)), z1 / (1.f + __expf(-z1)));
+#pragma unroll
+      for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
     }
-    win[K - 1] = ld2(xb + (int64_t)t * D);
-    float z0 = 0.f, z1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < K; ++i) {
-      z0 = fmaf(w0[i], win[i].x, z0);
-      z1 = fmaf(w1[i], win[i].y, z1);
-    }
-    st2(y + ((int64_t)b * T + t) * D + c, z0 / (1.f + __expf(-z0)), z1 / (1.f + __expf(-z1)));
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
   }
 }
 
@@ -1255,53 +1264,66 @@ __global__ void conv1d_bwd_kernel(const bf16* __restrict__ dy, const bf16* __res
     dd[i] = -1;
   }
   const int tend = t0 + kConvTile + K - 1;
-  for (int t = t0; t < tend; ++t) {
+  constexpr int kPre = 8;  // time steps of x and dy loaded ahead
+  for (int tb = t0; tb < tend; tb += kPre) {
+    float2 xin[kPre], gin[kPre];
 #pragma unroll
-    for (int i = 0; i < K - 1; ++i) {
-      dz[i] = dz[i + 1];
-      dd[i] = dd[i + 1];
+    for (int v = 0; v < kPre; ++v) {
+      const bool in = tb + v < T && tb + v < tend;
+      xin[v] = in ? ld2(xb + (int64_t)(tb + v) * D) : make_float2(0.f, 0.f);
+      gin[v] = in ? ld2(dyb + (int64_t)(tb + v) * D) : make_float2(0.f, 0.f);
     }
-    if (t < T) {
-      if (t >= end) {
-        docs.find(t, T, start, end, d);
 #pragma unroll
-        for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
-      }
-      win[K - 1] = ld2(xb + (int64_t)t * D);
-      float z0 = 0.f, z1 = 0.f;
+    for (int u = 0; u < kPre; ++u) {
+      const int t = tb + u;
+      if (t >= tend) break;
 #pragma unroll
-      for (int i = 0; i < K; ++i) {
-        z0 = fmaf(w0[i], win[i].x, z0);
-        z1 = fmaf(w1[i], win[i].y, z1);
+      for (int i = 0; i < K - 1; ++i) {
+        dz[i] = dz[i + 1];
+        dd[i] = dd[i + 1];
       }
-      const float2 gy = ld2(dyb + (int64_t)t * D);
-      const float s0 = 1.f / (1.f + __expf(-z0)), s1 = 1.f / (1.f + __expf(-z1));
-      dz[K - 1] = make_float2(gy.x * s0 * (1.f + z0 * (1.f - s0)), gy.y * s1 * (1.f + z1 * (1.f - s1)));
-      dd[K - 1] = d;
-      if (t < t0 + kConvTile) {
+      if (t < T) {
+        if (t >= end) {
+          docs.find(t, T, start, end, d);
+#pragma unroll
+          for (int i = 0; i < K - 1; ++i) win[i] = make_float2(0.f, 0.f);
+        }
+        win[K - 1] = xin[u];
+        float z0 = 0.f, z1 = 0.f;
 #pragma unroll
         for (int i = 0; i < K; ++i) {
-          g0[i] = fmaf(dz[K - 1].x, win[i].x, g0[i]);
-          g1[i] = fmaf(dz[K - 1].y, win[i].y, g1[i]);
+          z0 = fmaf(w0[i], win[i].x, z0);
+          z1 = fmaf(w1[i], win[i].y, z1);
         }
-      }
+        const float2 gy = gin[u];
+        const float s0 = 1.f / (1.f + __expf(-z0)), s1 = 1.f / (1.f + __expf(-z1));
+        dz[K - 1] = make_float2(gy.x * s0 * (1.f + z0 * (1.f - s0)), gy.y * s1 * (1.f + z1 * (1.f - s1)));
+        dd[K - 1] = d;
+        if (t < t0 + kConvTile) {
 #pragma unroll
-      for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
-    } else {
-      dz[K - 1] = make_float2(0.f, 0.f);
-      dd[K - 1] = -1;
-    }
-    const int tp = t - (K - 1);  // the dx position completed at this step: dz[m] is tp + m
-    if (tp >= t0 && tp < T && tp < t0 + kConvTile) {
-      float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < K; ++m) {
-        if (dd[m] == dd[0]) {
-          a0 = fmaf(w0[K - 1 - m], dz[m].x, a0);
-          a1 = fmaf(w1[K - 1 - m], dz[m].y, a1);
+          for (int i = 0; i < K; ++i) {
+            g0[i] = fmaf(dz[K - 1].x, win[i].x, g0[i]);
+            g1[i] = fmaf(dz[K - 1].y, win[i].y, g1[i]);
+          }
         }
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) win[i] = win[i + 1];
+      } else {
+        dz[K - 1] = make_float2(0.f, 0.f);
+        dd[K - 1] = -1;
       }
-      st2(dx + ((int64_t)b * T + tp) * D + c, a0, a1);
+      const int tp = t - (K - 1);  // the dx position completed at this step: dz[m] is tp + m
+      if (tp >= t0 && tp < T && tp < t0 + kConvTile) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int m = 0; m < K; ++m) {
+          if (dd[m] == dd[0]) {
+            a0 = fmaf(w0[K - 1 - m], dz[m].x, a0);
+            a1 = fmaf(w1[K - 1 - m], dz[m].y, a1);
+          }
+        }
+        st2(dx + ((int64_t)b * T + tp) * D + c, a0, a1);
+      }
     }
   }
 #pragma unroll
