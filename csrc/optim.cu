@@ -46,17 +46,52 @@ adamw_kernel(TensorTable tab, int64_t total_chunks, float lr, float b1, float b2
     float* m = reinterpret_cast<float*>(tab.ptrs[4 * t + 2]);
     float* v = reinterpret_cast<float*>(tab.ptrs[4 * t + 3]);
     const int64_t end = min(n, start + kChunk);
-    for (int64_t i = start + threadIdx.x; i < end; i += kOptThreads) {
+    auto update = [&](float gi, float& pi, float& mi, float& vi) {
+      gi *= gs;
+      pi *= 1.f - lr * wd;
+      mi += (1.f - b1) * (gi - mi);
+      vi = b2 * vi + (1.f - b2) * gi * gi;
+      pi -= (lr / bc1) * mi / (sqrtf(vi) / bc2_sqrt + eps);
+    };
+    // 16-byte accesses when every stream is aligned (tensors can be views at any offset of a
+    // flat buffer, so this is checked per tensor), scalar ones otherwise and for the tail
+    const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) &
+                      15) == 0 && (reinterpret_cast<uintptr_t>(g) & (4 * sizeof(TG) - 1)) == 0;
+    int64_t tail = start;
+    if (vec) {
+      const int64_t nv = (end - start) / 4;
+      for (int64_t j = threadIdx.x; j < nv; j += kOptThreads) {
+        const int64_t i = start + 4 * j;
+        float4 pv = *reinterpret_cast<float4*>(p + i), mv = *reinterpret_cast<float4*>(m + i),
+               vv = *reinterpret_cast<float4*>(v + i);
+        float gv[4];
+        if constexpr (sizeof(TG) == 4) {
+          const float4 t = *reinterpret_cast<const float4*>(g + i);
+          gv[0] = t.x, gv[1] = t.y, gv[2] = t.z, gv[3] = t.w;
+        } else {
+          const uint2 t = *reinterpret_cast<const uint2*>(g + i);
+          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.x));
+          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.y));
+          gv[0] = a.x, gv[1] = a.y, gv[2] = b.x, gv[3] = b.y;
+        }
+        update(gv[0], pv.x, mv.x, vv.x);
+        update(gv[1], pv.y, mv.y, vv.y);
+        update(gv[2], pv.z, mv.z, vv.z);
+        update(gv[3], pv.w, mv.w, vv.w);
+        *reinterpret_cast<float4*>(p + i) = pv;
+        *reinterpret_cast<float4*>(m + i) = mv;
+        *reinterpret_cast<float4*>(v + i) = vv;
+      }
+      tail = start + 4 * nv;
+    }
+    for (int64_t i = tail + threadIdx.x; i < end; i += kOptThreads) {
       float gi;
       if constexpr (sizeof(TG) == 4) gi = g[i]; else gi = __bfloat162float(g[i]);
-      gi *= gs;
-      float pi = p[i] * (1.f - lr * wd);
-      float mi = m[i] + (1.f - b1) * (gi - m[i]);
-      float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+      float pi = p[i], mi = m[i], vi = v[i];
+      update(gi, pi, mi, vi);
+      p[i] = pi;
       m[i] = mi;
       v[i] = vi;
-      const float denom = sqrtf(vi) / bc2_sqrt + eps;
-      p[i] = pi - (lr / bc1) * mi / denom;
     }
   }
 }
