@@ -167,34 +167,97 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
 }
 
 // ------------------------------------------------------------------------------ Muon
+// Muon kernels over a bucket of same-shape tensors: blockIdx.y is the tensor, blocks in x
+// stride over its elements.  VEC: 4 elements per access (16-byte fp32 / 8-byte bf16), used
+// when every pointer of the bucket is aligned and numel is a multiple of 4.
+__device__ __forceinline__ void load4f(const float* p, float (&v)[4]) {
+  const float4 t = *reinterpret_cast<const float4*>(p);
+  v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+}
+__device__ __forceinline__ void load4b(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 t = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.y));
+  v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+}
+__device__ __forceinline__ void store4b(__nv_bfloat16* p, const float (&v)[4]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 t;
+  t.x = *reinterpret_cast<uint32_t*>(&a);
+  t.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = t;
+}
+
+template <bool VEC>
 __global__ void muon_prepare_kernel(const int64_t* gptrs, const int64_t* mptrs, int n, int64_t numel, float mu,
                                     bool nesterov, bool g_bf16, __nv_bfloat16* __restrict__ out,
                                     const float* __restrict__ gscale) {
   const float gs = gscale != nullptr ? *gscale : 1.f;
-  const int64_t total = (int64_t)n * numel;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / numel);
-    const int64_t j = i - (int64_t)t * numel;
-    float* m = reinterpret_cast<float*>(mptrs[t]);
-    float g = g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(gptrs[t])[j])
-                     : reinterpret_cast<const float*>(gptrs[t])[j];
-    g *= gs;
-    float mv = m[j] + (1.f - mu) * (g - m[j]);
-    m[j] = mv;
-    float u = nesterov ? g + mu * (mv - g) : mv;
-    out[i] = __float2bfloat16(u);
+  const int t = blockIdx.y;
+  float* m = reinterpret_cast<float*>(mptrs[t]);
+  const float* gf = reinterpret_cast<const float*>(gptrs[t]);
+  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(gptrs[t]);
+  __nv_bfloat16* o = out + (int64_t)t * numel;
+  constexpr int W = VEC ? 4 : 1;
+  for (int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * W; j < numel; j += (int64_t)gridDim.x * blockDim.x * W) {
+    float g[W], mv[W], u[W];
+    if constexpr (VEC) {
+      if (g_bf16) load4b(gb + j, g); else load4f(gf + j, g);
+      load4f(m + j, mv);
+    } else {
+      g[0] = g_bf16 ? __bfloat162float(gb[j]) : gf[j];
+      mv[0] = m[j];
+    }
+#pragma unroll
+    for (int e = 0; e < W; ++e) {
+      g[e] *= gs;
+      mv[e] += (1.f - mu) * (g[e] - mv[e]);
+      u[e] = nesterov ? g[e] + mu * (mv[e] - g[e]) : mv[e];
+    }
+    if constexpr (VEC) {
+      *reinterpret_cast<float4*>(m + j) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+      store4b(o + j, u);
+    } else {
+      m[j] = mv[0];
+      o[j] = __float2bfloat16(u[0]);
+    }
   }
 }
 
+template <bool VEC>
 __global__ void muon_apply_kernel(const int64_t* pptrs, int n, int64_t numel, float decay, float step_scale,
                                   const __nv_bfloat16* __restrict__ orth) {
-  const int64_t total = (int64_t)n * numel;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / numel);
-    const int64_t j = i - (int64_t)t * numel;
-    float* p = reinterpret_cast<float*>(pptrs[t]);
-    p[j] = p[j] * (1.f - decay) + step_scale * __bfloat162float(orth[i]);
+  const int t = blockIdx.y;
+  float* p = reinterpret_cast<float*>(pptrs[t]);
+  const __nv_bfloat16* o = orth + (int64_t)t * numel;
+  constexpr int W = VEC ? 4 : 1;
+  for (int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * W; j < numel; j += (int64_t)gridDim.x * blockDim.x * W) {
+    if constexpr (VEC) {
+      float pv[4], ov[4];
+      load4f(p + j, pv);
+      load4b(o + j, ov);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pv[e] = pv[e] * (1.f - decay) + step_scale * ov[e];
+      *reinterpret_cast<float4*>(p + j) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+    } else {
+      p[j] = p[j] * (1.f - decay) + step_scale * __bfloat162float(o[j]);
+    }
   }
+}
+
+static bool aligned16(const std::vector<torch::Tensor>& ts) {
+  for (auto& t : ts)
+    if (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) return false;
+  return true;
+}
+
+static dim3 bucket_grid(int64_t numel, int n, int width) {
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t need = (numel / width + 255) / 256;
+  const int64_t cap = std::max<int64_t>(1, (int64_t)sms * 8 / std::max(1, n));
+  return dim3((unsigned)std::max<int64_t>(1, std::min(need, cap)), (unsigned)n);
 }
 
 static torch::Tensor ptr_table(const std::vector<std::vector<torch::Tensor>>& lists, torch::Device dev) {
@@ -226,10 +289,18 @@ void muon_prepare(std::vector<torch::Tensor> grads, std::vector<torch::Tensor> b
   for (auto& b : bufs) TORCH_CHECK(b.scalar_type() == at::kFloat, "muon_prepare: fp32 momentum");
   const bool g_bf16 = grads[0].scalar_type() == at::kBFloat16;
   auto tab = ptr_table({grads, bufs}, out.device());
-  const int64_t total = n * numel;
-  muon_prepare_kernel<<<grid_for((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      tab.data_ptr<int64_t>(), tab.data_ptr<int64_t>() + n, n, numel, (float)mu, nesterov, g_bf16,
-      (__nv_bfloat16*)out.data_ptr(), gsp);
+  TORCH_CHECK(n <= 65535, "muon_prepare: too many tensors in one bucket");
+  const bool vec = numel % 4 == 0 && aligned16(bufs) && aligned16({out}) &&
+                   [&] { for (auto& g : grads) if (reinterpret_cast<uintptr_t>(g.data_ptr()) % (g_bf16 ? 8 : 16)) return false; return true; }();
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (vec)
+    muon_prepare_kernel<true><<<bucket_grid(numel, n, 4), 256, 0, st>>>(
+        tab.data_ptr<int64_t>(), tab.data_ptr<int64_t>() + n, n, numel, (float)mu, nesterov, g_bf16,
+        (__nv_bfloat16*)out.data_ptr(), gsp);
+  else
+    muon_prepare_kernel<false><<<bucket_grid(numel, n, 1), 256, 0, st>>>(
+        tab.data_ptr<int64_t>(), tab.data_ptr<int64_t>() + n, n, numel, (float)mu, nesterov, g_bf16,
+        (__nv_bfloat16*)out.data_ptr(), gsp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   c10::cuda::CUDACachingAllocator::recordStream(tab.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
 }
@@ -241,9 +312,15 @@ void muon_apply(std::vector<torch::Tensor> params, torch::Tensor orth, double de
   const int64_t numel = params[0].numel();
   for (auto& p : params) TORCH_CHECK(p.scalar_type() == at::kFloat, "muon_apply: fp32 params");
   auto tab = ptr_table({params}, orth.device());
-  const int64_t total = n * numel;
-  muon_apply_kernel<<<grid_for((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      tab.data_ptr<int64_t>(), n, numel, (float)decay, (float)step_scale, (const __nv_bfloat16*)orth.data_ptr());
+  TORCH_CHECK(n <= 65535, "muon_apply: too many tensors in one bucket");
+  const bool vec = numel % 4 == 0 && aligned16(params) && aligned16({orth});
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (vec)
+    muon_apply_kernel<true><<<bucket_grid(numel, n, 4), 256, 0, st>>>(
+        tab.data_ptr<int64_t>(), n, numel, (float)decay, (float)step_scale, (const __nv_bfloat16*)orth.data_ptr());
+  else
+    muon_apply_kernel<false><<<bucket_grid(numel, n, 1), 256, 0, st>>>(
+        tab.data_ptr<int64_t>(), n, numel, (float)decay, (float)step_scale, (const __nv_bfloat16*)orth.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   c10::cuda::CUDACachingAllocator::recordStream(tab.storage().data_ptr(), at::cuda::getCurrentCUDAStream());
 }
@@ -253,7 +330,18 @@ __global__ void sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t per, f
   const int b = blockIdx.y;
   const __nv_bfloat16* xb = x + (int64_t)b * per;
   float s = 0.f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t per8 = (reinterpret_cast<uintptr_t>(xb) % 16 == 0) ? per / 8 : 0;  // 16-byte part
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 u = reinterpret_cast<const uint4*>(xb)[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      s += f.x * f.x + f.y * f.y;
+    }
+  }
+  for (int64_t i = per8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per;
+       i += (int64_t)gridDim.x * blockDim.x) {
     float v = __bfloat162float(xb[i]);
     s += v * v;
   }
@@ -273,7 +361,19 @@ __global__ void scale_kernel(__nv_bfloat16* __restrict__ x, int64_t per, const f
   const int b = blockIdx.y;
   __nv_bfloat16* xb = x + (int64_t)b * per;
   const float inv = 1.f / fmaxf(sqrtf(ss[b]), eps);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x)
+  const int64_t per8 = (reinterpret_cast<uintptr_t>(xb) % 16 == 0) ? per / 8 : 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per8; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u = reinterpret_cast<uint4*>(xb)[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      h[e] = __floats2bfloat162_rn(f.x * inv, f.y * inv);
+    }
+    reinterpret_cast<uint4*>(xb)[i] = u;
+  }
+  for (int64_t i = per8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per;
+       i += (int64_t)gridDim.x * blockDim.x)
     xb[i] = __float2bfloat16(__bfloat162float(xb[i]) * inv);
 }
 
@@ -283,7 +383,8 @@ void frob_normalize_(torch::Tensor x, double eps) {
   const int B = x.size(0);
   const int64_t per = x.size(1) * x.size(2);
   auto ss = torch::zeros({B}, x.options().dtype(at::kFloat));
-  dim3 grid((unsigned)std::min<int64_t>(64, (per + 255) / 256), B);
+  dim3 grid((unsigned)std::max<int64_t>(1, std::min<int64_t>(std::max<int64_t>(64, 1184 / std::max(1, B)),
+                                                               (per / 8 + 255) / 256)), B);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   sumsq_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x.data_ptr(), per, ss.data_ptr<float>());
   scale_kernel<<<grid, 256, 0, st>>>((__nv_bfloat16*)x.data_ptr(), per, ss.data_ptr<float>(), (float)eps);
