@@ -156,8 +156,9 @@ class _Linear(torch.autograd.Function):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM, or the block-scaled MXFP8 GEMMs for
-    weights converted by ``convert_to_mxfp8_training``; CPU: ``F.linear`` in x's dtype."""
+    """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM, the block-scaled MXFP8 GEMMs for
+    weights converted by ``convert_to_mxfp8_training``, or the float8 GEMMs for weights
+    converted by ``convert_to_float8_training``; CPU: ``F.linear`` in x's dtype."""
     if not x.is_cuda:
         return F.linear(x, weight.to(x.dtype))
     fmt = getattr(weight, "_mykb_mxfp8", None)
@@ -166,4 +167,10 @@ def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
         if eligible_shapes(x, weight) and x.numel() // x.shape[-1] > SKINNY_MAX_ROWS:
             return mx_linear(x, weight, fmt)
+    recipe = getattr(weight, "_mykb_fp8", None)
+    if recipe is not None:
+        from .float8 import eligible_shapes as fp8_eligible, fp8_linear
+
+        if fp8_eligible(x, weight) and x.numel() // x.shape[-1] > SKINNY_MAX_ROWS:
+            return fp8_linear(x, weight, recipe)
     return _Linear.apply(x, weight)

@@ -91,20 +91,28 @@ def uses_sharded(config, info: DistInfo) -> bool:
 
 
 def convert_float8(model: nn.Module, recipe: str, *, skip_down_proj: bool = False, grad_dtype: str = "e4m3") -> int:
-    """Swap eligible block linears for MXFP8 training modules; returns the count.  Skips
+    """Swap eligible block linears for float8 training modules; returns the count.  Skips
     the output head, DeltaNet a/b/f projections, optionally ``down_proj`` and linears
-    whose dimensions are not multiples of 32 (reference selection rules,
-    ``src/myk_llm/train/distributed.py:71-105``)."""
-    if recipe != "mxfp8":
-        raise NotImplementedError(f"float8 recipe {recipe!r}: this framework implements block-scaled mxfp8")
-    from ..ops.mxfp8 import convert_to_mxfp8_training
+    whose dimensions are not multiples of 32 (MXFP8) or 16 (per-tensor / per-row float8)
+    (reference selection rules, ``src/myk_llm/train/distributed.py:71-105``).  ``mxfp8``
+    uses the block-scaled tcgen05 GEMMs; ``tensorwise``, ``rowwise`` and
+    ``rowwise_with_gw_hp`` the dynamic-scaling linears of ``ops.float8``."""
+    from ..ops import float8 as f8
+
+    if recipe != "mxfp8" and recipe not in f8.RECIPES:
+        raise ValueError(f"unknown float8 recipe {recipe!r}")
+    align = 32 if recipe == "mxfp8" else 16
 
     def eligible(m: nn.Module, fqn: str) -> bool:
         return (type(m) is nn.Linear and fqn != "lm_head" and not fqn.endswith((".a_proj", ".b_proj"))
                 and ".f_proj." not in fqn and not (skip_down_proj and fqn.endswith(".down_proj"))
-                and m.in_features % 32 == 0 and m.out_features % 32 == 0)
+                and m.in_features % align == 0 and m.out_features % align == 0)
 
-    return convert_to_mxfp8_training(model, module_filter_fn=eligible, grad_dtype=grad_dtype)
+    if recipe == "mxfp8":
+        from ..ops.mxfp8 import convert_to_mxfp8_training
+
+        return convert_to_mxfp8_training(model, module_filter_fn=eligible, grad_dtype=grad_dtype)
+    return f8.convert_to_float8_training(model, recipe, module_filter_fn=eligible)
 
 
 def parallelize(model, config, info: DistInfo):
