@@ -45,8 +45,8 @@ def test_conversion_keeps_parameters_and_rules():
             assert not isinstance(mod, mxfp8.MXFP8Linear), name
         if isinstance(mod, mxfp8.MXFP8Linear):
             assert mod.weight._mykb_mxfp8 == "e5m2"
-    with pytest.raises(NotImplementedError):
-        convert_float8(nn.Sequential(nn.Linear(64, 64)), "tensorwise")
+    with pytest.raises(ValueError):
+        convert_float8(nn.Sequential(nn.Linear(64, 64)), "blockwise")
 
 
 # ------------------------------------------------------------------------------ GPU
