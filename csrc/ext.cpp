@@ -26,6 +26,10 @@ torch::Tensor rope_qkv_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
                            torch::Tensor pos);
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
 void embedding_bwd(torch::Tensor ids, torch::Tensor dout, torch::Tensor grad);
+// fp8.cu
+std::vector<torch::Tensor> fp8_quant_rows(torch::Tensor x, bool e5m2, bool pow2);
+std::vector<torch::Tensor> fp8_quant_tensor(torch::Tensor x, bool e5m2);
+std::vector<torch::Tensor> fp8_quant_cols_t(torch::Tensor x, bool e5m2, bool pow2);
 // loss.cu
 void ce_fwd_grad(torch::Tensor logits, torch::Tensor targets, double scale, double z_coef, int64_t ignore_index,
                  torch::Tensor ce_sum, torch::Tensor z_sum);
@@ -106,6 +110,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_qkv_fwd", &mykb::rope_qkv_fwd);
   m.def("rope_qkv_bwd", &mykb::rope_qkv_bwd);
   m.def("split_cols", &mykb::split_cols);
+  m.def("fp8_quant_rows", &mykb::fp8_quant_rows);
+  m.def("fp8_quant_tensor", &mykb::fp8_quant_tensor);
+  m.def("fp8_quant_cols_t", &mykb::fp8_quant_cols_t);
   m.def("embedding_fwd", &mykb::embedding_fwd);
   m.def("embedding_bwd", &mykb::embedding_bwd);
   m.def("ce_fwd_grad", &mykb::ce_fwd_grad);

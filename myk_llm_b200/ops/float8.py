@@ -16,8 +16,11 @@ implementation of those three scaling statements for the three GEMMs of a linear
   (the weight gradient keeps high precision), accumulated into ``main_grad`` by the
   tcgen05 GEMM epilogue when the parameter has one.
 
-The float8 GEMMs are cuBLASLt's scaled matmul (``torch._scaled_mm``), a plain library GEMM
-with the dequantisation scales applied to the fp32 accumulator.  On the CPU the same
+Activations and gradients are quantised by this framework's kernels (``csrc/fp8.cu``: a
+fused per-row amax+cast, a per-tensor amax then cast, and a per-column amax then
+transposing cast for the weight-gradient operands).  The float8 GEMMs are cuBLASLt's
+scaled matmul (``torch._scaled_mm``), a plain library GEMM with the dequantisation scales
+applied to the fp32 accumulator.  On the CPU the same
 statement ``(a * s_a) @ (b * s_b)`` is evaluated in fp32, so the CPU tests check the
 scaling rules exactly.  The quantised weight (both orientations) is cached on the
 parameter and rebuilt after each optimizer step, like the bf16 weight copy of the plain
@@ -45,10 +48,36 @@ def quantize(x: torch.Tensor, dtype: torch.dtype, rowwise: bool) -> tuple[torch.
     a = x.abs()
     amax = (a.amax(dim=-1, keepdim=True) if rowwise else a.amax()).float().clamp_min(_AMAX_EPS)
     inv = fmax / amax
-    if rowwise:
-        inv = torch.exp2(torch.floor(torch.log2(inv)))
+    if rowwise:   # keep the exponent bits alone: inv rounded down to a power of two
+        inv = (inv.view(torch.int32) & 0x7F800000).view(torch.float32)
     q = (x.float() * inv).clamp_(-fmax, fmax).to(dtype)
     return q, inv.reciprocal()
+
+
+def _kernel_ok(x: torch.Tensor) -> bool:
+    return (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous()
+            and x.shape[1] % 8 == 0 and x.data_ptr() % 16 == 0)
+
+
+def quantize_act(x: torch.Tensor, dtype: torch.dtype, rowwise: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """:func:`quantize` of an activation or gradient; contiguous bf16 CUDA tensors go through
+    the fused quantiser kernels (``csrc/fp8.cu``), which compute the same statement."""
+    if _kernel_ok(x):
+        from ._ext import ext
+
+        e5 = dtype == E5M2
+        return tuple(ext().fp8_quant_rows(x, e5, True) if rowwise else ext().fp8_quant_tensor(x, e5))
+    return quantize(x, dtype, rowwise)
+
+
+def quantize_act_t(x: torch.Tensor, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row :func:`quantize` of ``x^T`` (one scale per column of ``x``), written transposed;
+    the fused column-amax + transposing cast kernels for contiguous bf16 CUDA tensors."""
+    if _kernel_ok(x) and x.shape[0] % 16 == 0:
+        from ._ext import ext
+
+        return tuple(ext().fp8_quant_cols_t(x, dtype == E5M2, True))
+    return quantize(x.t().contiguous(), dtype, True)
 
 
 def scaled_mm(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor,
@@ -95,7 +124,7 @@ class _Fp8Linear(torch.autograd.Function):
         x2 = x.reshape(-1, k)
         rowwise = recipe != "tensorwise"
         q, s, qt, st = _WeightCache.get(w, rowwise)
-        xq, xs = quantize(x2, E4M3, rowwise)
+        xq, xs = quantize_act(x2, E4M3, rowwise)
         y = scaled_mm(xq, xs, q, s, torch.bfloat16)
         ctx.recipe, ctx.w = recipe, w
         ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
@@ -109,13 +138,13 @@ class _Fp8Linear(torch.autograd.Function):
     def backward(ctx, dy: torch.Tensor):
         w, recipe = ctx.w, ctx.recipe
         n = w.shape[0]
-        dy2 = dy.reshape(-1, n)
+        dy2 = dy.reshape(-1, n).contiguous()
         rowwise = recipe != "tensorwise"
         _, _, qt, st = _WeightCache.get(w, rowwise)
         dx = dw = None
         if recipe == "tensorwise":
             xq, xs = ctx.saved_tensors
-            gq, gs = quantize(dy2, E5M2, False)
+            gq, gs = quantize_act(dy2, E5M2, False)
             if ctx.needs_input_grad[0]:
                 dx = scaled_mm(gq, gs, qt, st, torch.bfloat16)
             if ctx.needs_input_grad[1]:
@@ -123,12 +152,12 @@ class _Fp8Linear(torch.autograd.Function):
         else:
             (x2,) = ctx.saved_tensors
             if ctx.needs_input_grad[0]:
-                gq, gs = quantize(dy2, E4M3, True)
+                gq, gs = quantize_act(dy2, E4M3, True)
                 dx = scaled_mm(gq, gs, qt, st, torch.bfloat16)
             if ctx.needs_input_grad[1]:
                 if recipe == "rowwise":
-                    gtq, gts = quantize(dy2.t().contiguous(), E4M3, True)
-                    xtq, xts = quantize(x2.t().contiguous(), E4M3, True)
+                    gtq, gts = quantize_act_t(dy2, E4M3)
+                    xtq, xts = quantize_act_t(x2, E4M3)
                     dw = scaled_mm(gtq, gts, xtq, xts, torch.bfloat16).float()
                 else:
                     dw = _high_precision_wgrad(dy2, x2, w)

@@ -91,6 +91,31 @@ def test_convert_float8_rules():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(256, 512), (4096, 1024), (80, 200), (1040, 3072)])
+@pytest.mark.parametrize("dtype", [f8.E4M3, f8.E5M2])
+def test_quantizer_kernels_match_statement(shape, dtype):
+    """The fused quantisers reproduce the PyTorch statement bit for bit."""
+    from myk_llm_b200.ops._ext import ext
+
+    torch.manual_seed(5)
+    r, c = shape
+    x = (torch.randn(r, c, device="cuda") * torch.logspace(-3, 3, r, device="cuda")[:, None]).to(torch.bfloat16)
+    x[0, :8] = 0   # a partly zero row
+    e5 = dtype == f8.E5M2
+    for rowwise in (False, True):
+        q, s = ext().fp8_quant_rows(x, e5, True) if rowwise else ext().fp8_quant_tensor(x, e5)
+        qr, sr = f8.quantize(x, dtype, rowwise)
+        assert q.dtype == dtype and s.shape == sr.shape
+        assert torch.equal(s, sr)
+        assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
+    if r % 16 == 0:
+        qt, st = ext().fp8_quant_cols_t(x, e5, True)
+        qr, sr = f8.quantize(x.t().contiguous(), dtype, True)
+        assert torch.equal(st, sr)
+        assert torch.equal(qt.view(torch.uint8), qr.view(torch.uint8))
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("recipe", f8.RECIPES)
 def test_fp8_linear_gpu_matches_statement(recipe):
     torch.manual_seed(3)
