@@ -333,7 +333,7 @@ def main():
     else:
         device, step, batch_cls, _ = build_ours(world, a.layers, a.model, a.set)
 
-    total_steps = a.warmup + 2 * a.steps + 1
+    total_steps = a.warmup + a.steps + 1
     batches = synthetic_batches(total_steps, 0, rank, world, batch_cls, seq_len, micro)
     bi = iter(batches)
     for _ in range(a.warmup):
@@ -360,8 +360,10 @@ def main():
     dev_ms = max_over_ranks(dev_ms, device)
     loss_val = float(last) if last is not None else float("nan")
 
-    # ---- end-to-end loop (public API, H2D + D2H every step)
-    e2e_batches = [next(bi) for _ in range(a.steps)]
+    # ---- end-to-end loop (public API, H2D + D2H every step).  It replays the timed loop's
+    # host batches: packed documents of random lengths make the attention cost differ from
+    # batch to batch, so the two loops must run the same batches to be comparable.
+    e2e_batches = timed
     barrier_sync(device)
     t0 = time.perf_counter()
     for b in e2e_batches:
