@@ -75,6 +75,13 @@ def build(case: str):
         a = torch.randn(16384, 4096, device=dev).bfloat16()
         return (lambda: mxfp8.mx_quantize(a, "e4m3", True, True)), 0, a.numel() * (2 + 1 + 1), \
             "MXFP8 quantize 16384x4096 bf16 -> fp8 rows + fp8 transpose"
+    if case in ("fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t"):
+        # the 200M model's down-projection input (32768 tokens x 2816), 185 MB of bf16
+        a = torch.randn(32768, 2816, device=dev).bfloat16()
+        fn = {"fp8quant_rows": lambda: ext().fp8_quant_rows(a, False, True),
+              "fp8quant_tensor": lambda: ext().fp8_quant_tensor(a, False),
+              "fp8quant_cols_t": lambda: ext().fp8_quant_cols_t(a, False, True)}[case]
+        return fn, 0, a.numel() * (2 + 1), f"float8 quantise ({case[9:]}) 32768x2816 bf16 -> e4m3"
     if case in ("fa_fwd", "fa_bwd"):
         q = torch.randn(4, 4096, 16, 128, device=dev).bfloat16().requires_grad_()
         k = torch.randn(4, 4096, 4, 128, device=dev).bfloat16().requires_grad_()
@@ -140,7 +147,7 @@ def build(case: str):
     raise ValueError(f"unknown case {case!r}")
 
 
-CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
+CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
 
 
 def time_case(case: str, reps: int = 20) -> dict:
