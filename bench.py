@@ -183,6 +183,17 @@ def max_over_ranks(x: float, device) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(x: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier_sync(device):
     import torch
     import torch.distributed as dist
@@ -358,7 +369,8 @@ def main():
     clk = clocks.stop()
     dev_ms = ev0.elapsed_time(ev1)
     dev_ms = max_over_ranks(dev_ms, device)
-    loss_val = float(last) if last is not None else float("nan")
+    # each rank's step returns its share of the loss (local CE sum / global target count)
+    loss_val = sum_over_ranks(float(last) if last is not None else float("nan"), device)
 
     # ---- end-to-end loop (public API, H2D + D2H every step).  It replays the timed loop's
     # host batches: packed documents of random lengths make the attention cost differ from
