@@ -1,4 +1,4 @@
-"""Training-throughput benchmark: train tokens/s of the 200M dense config.
+"""Training-throughput benchmark: train tokens/s of the 200M dense pretraining config.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
@@ -35,7 +35,7 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_TOKS = None  # BASELINE.md publishes no number for this metric/config on any GPU
+BASELINE_TOKS = None  # the reference publishes no number for this metric and config on any GPU
 
 _COMMON = ["objective.z_loss=1e-4", "optimizer.name=muon", "optimizer.muon_ns_steps=5"]
 
@@ -283,6 +283,30 @@ def build_reference(world: int, layers: int, model: str, compile_blocks: bool = 
     return info.device, step, Batch, None
 
 
+def _parallel_desc(trainer, world: int) -> str:
+    if world == 1 or trainer is None:
+        return ""
+    rt = trainer.model
+    if getattr(rt, "shard_params", False):
+        how = "re-gathered at every use" if rt.reshard_after_forward else "gathered once per step"
+        return f" (block weights row-sharded, all-gather fused into the tcgen05 GEMMs, {how})"
+    return " (parameters replicated, optimizer state sharded)"
+
+
+def _compile_failure_reason(err: BaseException) -> str:
+    """One line naming why Inductor could not build the reference's step.  The known case on
+    this image (torch 2.11, Triton 3.6): Inductor re-emits the reference's own Triton
+    FlashAttention kernel with the Python-float softmax scale typed fp64, so the scores, the
+    running max / rescale factor and the rescaled accumulator become fp64, and Triton's
+    ``tl.dot(p, v, acc)`` rejects an fp64 accumulator for an fp32 product."""
+    text = f"{type(err).__name__}: {err}"
+    if "tl.dot" in text or "_fwd_inner" in text or "acc * alpha" in text:
+        return ("Inductor recompiles the reference's Triton FlashAttention with the float softmax scale typed fp64; "
+                "the fp64 accumulator then fails tl.dot's accumulator-type check (Triton 3.6)")
+    first = text.strip().splitlines()[0] if text.strip() else type(err).__name__
+    return first[:300]
+
+
 def main():
     a = parse()
     rank, world, local = dist_env()
@@ -295,6 +319,7 @@ def main():
 
     _, seq_len, micro, model_desc = MODELS[a.model]
     compile_on = None
+    trainer = None
     if a.impl == "reference":
         ref_dir = os.path.join(ROOT, "baseline", "_ref", "myk_llm")
         if not os.path.isdir(ref_dir):
@@ -319,6 +344,7 @@ def main():
                                       f"flash-linear-attention has none ({err})"}))
                 return
         compile_on = a.ref_compile in ("auto", "on")
+        compile_error = None
         device, step, batch_cls, _ = build_reference(world, a.layers, a.model, compile_on)
         if a.ref_compile == "auto":
             # try one step with torch.compile; if Inductor cannot build the reference's
@@ -329,7 +355,8 @@ def main():
                 step(probe)
             except Exception as err:  # noqa: BLE001
                 ok = False
-                print(f"reference with torch.compile failed ({type(err).__name__}); using parallel.compile=false",
+                compile_error = _compile_failure_reason(err)
+                print(f"reference with torch.compile failed ({compile_error}); using parallel.compile=false",
                       file=sys.stderr)
             if dist.is_initialized():
                 t = torch.tensor([1.0 if ok else 0.0], device=device)
@@ -342,7 +369,7 @@ def main():
                 compile_on = False
                 device, step, batch_cls, _ = build_reference(world, a.layers, a.model, False)
     else:
-        device, step, batch_cls, _ = build_ours(world, a.layers, a.model, a.set)
+        device, step, batch_cls, trainer = build_ours(world, a.layers, a.model, a.set)
 
     total_steps = a.warmup + a.steps + 1
     batches = synthetic_batches(total_steps, 0, rank, world, batch_cls, seq_len, micro)
@@ -389,6 +416,10 @@ def main():
         launches = count_launches(lambda: step(launch_batch), "mykb") * a.steps
     barrier_sync(device)
 
+    peak_gb = max_over_ranks(torch.cuda.max_memory_allocated(device) / 2 ** 30, device)
+    mem_detail = None
+    if trainer is not None and hasattr(trainer.model, "memory_bytes"):
+        mem_detail = trainer.model.memory_bytes()
     tokens_per_step = micro * seq_len * world
     value = tokens_per_step * a.steps / (dev_ms / 1000.0)
     e2e = tokens_per_step * a.steps / e2e_s
@@ -404,7 +435,7 @@ def main():
             "data": "synthetic packed documents (geometric mean 1024, uniform ids, EOS), random-init weights",
             "config": {"model": model_desc,
                        "global_batch": micro * world, "seq_len": seq_len, "micro_batch_per_gpu": micro,
-                       "parallelism": f"dp{world}" + ("" if world == 1 else " (sharded)"),
+                       "parallelism": f"dp{world}" + _parallel_desc(trainer, world),
                        "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
                        "l2": "working set >> 126 MB L2 (no flush inserted)",
                        "layers": a.layers, **({"overrides": a.set} if a.set else {})},
@@ -412,10 +443,15 @@ def main():
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
             "loss": loss_val,
+            "peak_mem_gb_per_gpu": peak_gb,
         }
+        if mem_detail:
+            rec["config"]["memory_per_gpu_bytes"] = mem_detail
         if a.impl == "reference":
             rec["impl"] = "reference"
             rec["config"]["reference_compile"] = compile_on
+            if compile_error:
+                rec["config"]["reference_compile_error"] = compile_error
             rec.pop("gpu_launches")
         print(json.dumps(rec))
     if dist.is_initialized():

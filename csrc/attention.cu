@@ -757,20 +757,14 @@ static void launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
                        cudaStream_t st) {
   using S = FaSmem<D>;
   auto kern = fa_fwd_kernel<D>;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-    configured = true;
-  }
+  static SmemOptIn configured;
+  C10_CUDA_CHECK(configured.ensure(kern, S::kTotal));
   if (p.group % 2 == 0) {
     // GQA with an even group: two query heads per work item sharing each K / V tile
     using SP = FaPairSmem<D>;
     auto pk = fa_fwd_pair_kernel<D>;
-    static bool pair_configured = false;
-    if (!pair_configured) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, SP::kTotal));
-      pair_configured = true;
-    }
+    static SmemOptIn pair_configured;
+    C10_CUDA_CHECK(pair_configured.ensure(pk, SP::kTotal));
     const int items = p.q_tiles * p.num_seqs * p.kv_heads * (p.group / 2);
     pk<<<std::max(1, std::min(items, sm_count())), kFaPairThreads, SP::kTotal, st>>>(tq, tk, tv, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1515,11 +1509,8 @@ static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   {
     using S = DkvSmem<D>;
     auto kern = fa_bwd_dkdv_kernel<D>;
-    static bool configured = false;
-    if (!configured) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-      configured = true;
-    }
+    static SmemOptIn configured;
+    C10_CUDA_CHECK(configured.ensure(kern, S::kTotal));
     const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
     kern<<<std::max(1, std::min(total, sm_count())), kFaBwdThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1527,11 +1518,8 @@ static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   {
     using S = DqSmem<D>;
     auto kern = fa_bwd_dq_kernel<D>;
-    static bool configured = false;
-    if (!configured) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-      configured = true;
-    }
+    static SmemOptIn configured;
+    C10_CUDA_CHECK(configured.ensure(kern, S::kTotal));
     kern<<<std::max(1, std::min(p.f.total_items, sm_count())), kFaBwdThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
@@ -1616,7 +1604,7 @@ namespace mykb {
 namespace {
 // Working memory of mykb_flash_attn_bwd_noalloc: Delta (one float per query row and head)
 // and the status word its bounded waits write.  Every GPU that loads this library holds
-// these (4 MB + 4 B) until the process exits.
+// these (4 MB + 256 B) until the process exits.
 static __device__ __align__(256) float g_noalloc_delta[MYKB_NOALLOC_MAX_ROWS_X_HEADS];
 static __device__ __align__(256) int g_noalloc_status[64];
 
@@ -1628,8 +1616,10 @@ struct NoallocScratch {
 };
 
 // Host-side stand-ins of the arrays are not device addresses: look the addresses up once
-// per device (with that device current) and pass them to the kernels.
+// per device (with that device current) and pass them to the kernels.  The mutex makes
+// first calls from several host threads safe.
 NoallocScratch noalloc_scratch(int dev, cudaError_t* err) {
+  static std::mutex mu;
   static NoallocScratch cache[64];
   static bool ready[64] = {false};
   *err = cudaSuccess;
@@ -1637,6 +1627,7 @@ NoallocScratch noalloc_scratch(int dev, cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return {};
   }
+  std::lock_guard<std::mutex> lock(mu);
   if (!ready[dev]) {
     NoallocScratch s;
     *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.delta), g_noalloc_delta);
@@ -1670,14 +1661,27 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
   g_noalloc_err[0] = 0;
   if (head_dim != 64 && head_dim != 128) return noalloc_fail(1, "head_dim must be 64 or 128");
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads) return noalloc_fail(2, "heads must be a multiple of kv_heads");
+  if (rows_q <= 0 || rows_k <= 0 || num_seqs <= 0 || max_q <= 0 || max_k <= 0)
+    return noalloc_fail(4, "empty problem");
+  const bool packed = cu_seqlens != nullptr;
+  if (packed) {
+    // One cu_seqlens serves queries and keys, so both sides hold the same documents.
+    if (rows_k != rows_q) return noalloc_fail(9, "packed layout: q and k share cu_seqlens, so rows_k must equal rows_q");
+  } else {
+    if ((int64_t)num_seqs * max_q != rows_q || (int64_t)num_seqs * max_k != rows_k)
+      return noalloc_fail(10, "batch layout: rows_q must equal num_seqs * max_q and rows_k num_seqs * max_k");
+  }
+  // Delta holds one float per (query row, head) in either layout.
   if ((int64_t)rows_q * heads > MYKB_NOALLOC_MAX_ROWS_X_HEADS)
     return noalloc_fail(3, "rows_q * heads exceeds MYKB_NOALLOC_MAX_ROWS_X_HEADS (the built-in scratch size)");
-  if (rows_q <= 0 || rows_k <= 0 || num_seqs <= 0) return noalloc_fail(4, "empty problem");
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return noalloc_fail(5, cudaGetErrorString(err));
   NoallocScratch sc = noalloc_scratch(dev, &err);
   if (err != cudaSuccess) return noalloc_fail(6, cudaGetErrorString(err));
+  // A wait that gave up in an earlier call must not make this call's waits give up too.
+  err = cudaMemsetAsync(sc.status, 0, sizeof(int), stream);
+  if (err != cudaSuccess) return noalloc_fail(7, cudaGetErrorString(err));
   try {
     FaBwdParams p{};
     FaParams& f = p.f;
@@ -1705,7 +1709,7 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     const int64_t threads = (int64_t)rows_q * heads * (head_dim / 8);
     fa_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), sc.delta, rows_q, heads,
-        head_dim, cu_seqlens != nullptr, max_q);
+        head_dim, packed, max_q);
     err = cudaGetLastError();
     if (err != cudaSuccess) return noalloc_fail(7, cudaGetErrorString(err));
     CUtensorMap tq = raw_token_map(q, rows_q, heads, head_dim), tk = raw_token_map(k, rows_k, kv_heads, head_dim),
@@ -1721,3 +1725,29 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
 }
 
 extern "C" const char* mykb_noalloc_last_error(void) { return mykb::g_noalloc_err; }
+
+extern "C" int mykb_noalloc_status(int clear) {
+  using namespace mykb;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return -noalloc_fail(5, cudaGetErrorString(err));
+  NoallocScratch sc = noalloc_scratch(dev, &err);
+  if (err != cudaSuccess) return -noalloc_fail(6, cudaGetErrorString(err));
+  int h = 0;
+  err = cudaMemcpy(&h, sc.status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return -noalloc_fail(7, cudaGetErrorString(err));
+  if (clear && h != 0) {
+    err = cudaMemset(sc.status, 0, sizeof(int));
+    if (err != cudaSuccess) return -noalloc_fail(7, cudaGetErrorString(err));
+  }
+  return h;
+}
+
+extern "C" void* mykb_noalloc_status_address(void) {
+  using namespace mykb;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return nullptr;
+  NoallocScratch sc = noalloc_scratch(dev, &err);
+  return err == cudaSuccess ? sc.status : nullptr;
+}

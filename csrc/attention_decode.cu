@@ -332,20 +332,13 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   p.tickets = ticket_region(B * Hkv);
   const int grid = B * Hkv * ctas;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  static bool attr[2] = {false, false};
+  static SmemOptIn attr64, attr128;
   const size_t smem = (size_t)(ROWS + 4 * WARPS * KEYS) * (D + 8) * sizeof(bf16);
   if (D == 64) {
-    if (!attr[0]) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(fa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr[0] = true;
-    }
+    C10_CUDA_CHECK(attr64.ensure(fa_decode_kernel<64>, (int)smem));
     fa_decode_kernel<64><<<grid, WARPS * 32, smem, st>>>(p);
   } else {
-    if (!attr[1]) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(fa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-      attr[1] = true;
-    }
+    C10_CUDA_CHECK(attr128.ensure(fa_decode_kernel<128>, (int)smem));
     fa_decode_kernel<128><<<grid, WARPS * 32, smem, st>>>(p);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

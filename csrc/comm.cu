@@ -215,6 +215,55 @@ dp_muon_apply_allgather_kernel(const int64_t* __restrict__ param_ptrs, int rank,
   }
 }
 
+// Muon, owned row-sharded matrices (parameter-sharded mode): orth[t] is the full update of
+// matrix t; row `row` of it lives on rank row / rows_per_rank.  The owner reads that rank's
+// fp32 master row (peer load), applies p <- p (1 - lr wd) + step_scale * orth, and stores the
+// fp32 master and its bf16 compute copy back into that rank's shard buffers (peer stores).
+// Vectorised by 4 (cols is a multiple of 8).
+__global__ void __launch_bounds__(256)
+dp_muon_apply_shards_kernel(const int64_t* __restrict__ param_ptrs, const int64_t* __restrict__ bf16_ptrs,
+                            const int64_t* __restrict__ poffs, const int64_t* __restrict__ boffs, int n, int rows,
+                            int cols, int rows_per_rank, float decay, float step_scale,
+                            const __nv_bfloat16* __restrict__ orth) {
+  const int64_t numel = (int64_t)rows * cols;
+  const int64_t total4 = (int64_t)n * numel / 4;
+  for (int64_t i4 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i4 < total4; i4 += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = i4 * 4;
+    const int t = (int)(i / numel);
+    const int64_t j = i - (int64_t)t * numel;
+    const int row = (int)(j / cols), col = (int)(j - (int64_t)row * cols);
+    const int r = row / rows_per_rank;
+    const int64_t local = (int64_t)(row - r * rows_per_rank) * cols + col;
+    float4* pm = reinterpret_cast<float4*>(reinterpret_cast<float*>(param_ptrs[r]) + poffs[t] + local);
+    uint2* pb = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(bf16_ptrs[r]) + boffs[t] + local);
+    const uint2 ov = *reinterpret_cast<const uint2*>(orth + i);
+    const float2 o01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ov.x));
+    const float2 o23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ov.y));
+    float4 p = *pm;
+    p.x = p.x * (1.f - decay) + step_scale * o01.x;
+    p.y = p.y * (1.f - decay) + step_scale * o01.y;
+    p.z = p.z * (1.f - decay) + step_scale * o23.x;
+    p.w = p.w * (1.f - decay) + step_scale * o23.y;
+    *pm = p;
+    *pb = make_uint2(pack_bf16x2(p.x, p.y), pack_bf16x2(p.z, p.w));
+  }
+}
+
+// Parameter-sharded mode, set-up and checkpoint load: bf16 compute copy of this rank's
+// fp32 master shards (ranges of the flat buffers, multiples of 4 elements).
+__global__ void __launch_bounds__(256)
+cast_ranges_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, RangeTable src_tab,
+                        const int64_t* __restrict__ dst_offs) {
+  const int64_t total4 = src_tab.prefix[src_tab.n] / 4;
+  for (int64_t i4 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i4 < total4; i4 += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = i4 * 4;
+    const int k = find_range(src_tab.prefix, src_tab.n, i);
+    const int64_t within = i - src_tab.prefix[k];
+    const float4 v = *reinterpret_cast<const float4*>(src + src_tab.offset[k] + within);
+    *reinterpret_cast<uint2*>(dst + dst_offs[k] + within) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
 // -------------------------------------------------------------------------------------
 // host wrappers
 // -------------------------------------------------------------------------------------
@@ -278,6 +327,30 @@ void dp_muon_apply_allgather(torch::Tensor param_ptrs, int64_t rank, int64_t wor
   dp_muon_apply_allgather_kernel<<<comm_grid((int64_t)n * numel), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       param_ptrs.data_ptr<int64_t>(), (int)rank, (int)world, offs.data_ptr<int64_t>(), n, numel, (float)decay,
       (float)step_scale, (const __nv_bfloat16*)orth.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dp_muon_apply_shards(torch::Tensor param_ptrs, torch::Tensor bf16_ptrs, torch::Tensor poffs,
+                          torch::Tensor boffs, int64_t rows, int64_t cols, int64_t rows_per_rank, double decay,
+                          double step_scale, torch::Tensor orth) {
+  const int n = poffs.numel();
+  if (n == 0) return;
+  TORCH_CHECK(cols % 8 == 0 && rows_per_rank > 0, "dp_muon_apply_shards: cols must be a multiple of 8");
+  TORCH_CHECK(orth.is_contiguous() && orth.numel() == (int64_t)n * rows * cols, "dp_muon_apply_shards: orth shape");
+  dp_muon_apply_shards_kernel<<<comm_grid((int64_t)n * rows * cols / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      param_ptrs.data_ptr<int64_t>(), bf16_ptrs.data_ptr<int64_t>(), poffs.data_ptr<int64_t>(),
+      boffs.data_ptr<int64_t>(), n, (int)rows, (int)cols, (int)rows_per_rank, (float)decay, (float)step_scale,
+      (const __nv_bfloat16*)orth.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void cast_ranges_bf16(torch::Tensor src, torch::Tensor dst, torch::Tensor src_offsets, torch::Tensor prefix,
+                      torch::Tensor dst_offsets, int64_t total) {
+  RangeTable tab{src_offsets.data_ptr<int64_t>(), prefix.data_ptr<int64_t>(), (int)src_offsets.numel()};
+  if (total == 0 || tab.n == 0) return;
+  TORCH_CHECK(src.scalar_type() == at::kFloat && dst.scalar_type() == at::kBFloat16, "cast_ranges_bf16: dtypes");
+  cast_ranges_bf16_kernel<<<comm_grid(total / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      src.data_ptr<float>(), (__nv_bfloat16*)dst.data_ptr(), tab, dst_offsets.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

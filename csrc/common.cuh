@@ -12,7 +12,31 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace mykb {
+
+// Raises a kernel's dynamic shared-memory limit.  The attribute belongs to the device, so
+// each call site keeps one flag per device; the mutex makes first calls from several host
+// threads safe.  Returns the CUDA error of the attribute call (cudaSuccess when already set).
+struct SmemOptIn {
+  std::mutex mu;
+  bool done[64] = {};
+  template <typename Kern>
+  cudaError_t ensure(Kern kern, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e != cudaSuccess) return e;
+      done[dev] = true;
+    }
+    return cudaSuccess;
+  }
+};
 
 // -------------------------------------------------------------------------------------
 // status word

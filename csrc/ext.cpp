@@ -2,8 +2,17 @@
 #include <torch/extension.h>
 
 namespace mykb {
+void dp_muon_apply_shards(torch::Tensor param_ptrs, torch::Tensor bf16_ptrs, torch::Tensor poffs,
+                          torch::Tensor boffs, int64_t rows, int64_t cols, int64_t rows_per_rank, double decay,
+                          double step_scale, torch::Tensor orth);
+void cast_ranges_bf16(torch::Tensor src, torch::Tensor dst, torch::Tensor src_offsets, torch::Tensor prefix,
+                      torch::Tensor dst_offsets, int64_t total);
 int64_t take_status();
 // gemm.cu
+void gemm_gather(torch::Tensor a, torch::Tensor w, torch::Tensor d, bool b_mn, torch::Tensor src_ptrs,
+                 int64_t src_offset, int64_t rows_per_rank, int64_t rank, torch::Tensor ready, int64_t epoch);
+void shard_gather(torch::Tensor w, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
+                  torch::Tensor ready, int64_t epoch);
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
           double alpha, double beta, bool accumulate, bool symmetric);
 // norm.cu
@@ -100,6 +109,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "myk_llm_b200 sm_100a kernels";
   m.def("take_status", &mykb::take_status, "read and clear the device status word");
   m.def("gemm", &mykb::gemm, "tcgen05 bf16 GEMM");
+  m.def("gemm_gather", &mykb::gemm_gather, "tcgen05 bf16 GEMM with the all-gather of its sharded weight fused in");
+  m.def("shard_gather", &mykb::shard_gather, "all-gather of a row-sharded bf16 weight over peer memory");
   m.def("rmsnorm_fwd", &mykb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &mykb::rmsnorm_bwd);
   m.def("gated_rmsnorm_fwd", &mykb::gated_rmsnorm_fwd);
@@ -139,4 +150,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_adamw_allgather", &mykb::dp_adamw_allgather);
   m.def("dp_muon_prepare", &mykb::dp_muon_prepare);
   m.def("dp_muon_apply_allgather", &mykb::dp_muon_apply_allgather);
+  m.def("dp_muon_apply_shards", &mykb::dp_muon_apply_shards);
+  m.def("cast_ranges_bf16", &mykb::cast_ranges_bf16);
 }

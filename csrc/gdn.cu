@@ -1464,11 +1464,6 @@ static gdnk::Geo make_geo(const torch::Tensor& q, const torch::Tensor& v, const 
   return g;
 }
 
-template <typename Kern>
-static void set_smem(Kern kern, size_t bytes) {
-  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-}
-
 static void gdn_check(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const char* who) {
   TORCH_CHECK(q.dim() == 4 && q.size(3) == gdnk::DK && k.sizes() == q.sizes() && v.size(3) == gdnk::DV &&
                   v.size(2) == q.size(2) && v.size(1) == q.size(1),
@@ -1505,13 +1500,10 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
   auto bf = beta.to(at::kFloat).contiguous();
   torch::Tensor init_f;
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
-  static bool configured = false;
-  if (!configured) {
-    set_smem(gdnk::gdn_prep_kernel, sizeof(gdnk::PrepSm));
-    set_smem(gdnk::gdn_state_kernel, sizeof(gdnk::StateSm));
-    set_smem(gdnk::gdn_out_kernel, sizeof(gdnk::OutSm));
-    configured = true;
-  }
+  static SmemOptIn a_prep, a_state, a_out;
+  C10_CUDA_CHECK(a_prep.ensure(gdnk::gdn_prep_kernel, (int)sizeof(gdnk::PrepSm)));
+  C10_CUDA_CHECK(a_state.ensure(gdnk::gdn_state_kernel, (int)sizeof(gdnk::StateSm)));
+  C10_CUDA_CHECK(a_out.ensure(gdnk::gdn_out_kernel, (int)sizeof(gdnk::OutSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (rows > 0 && g.num_seqs > 0) {
@@ -1561,12 +1553,9 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
   auto dinit = torch::empty({g.num_seqs, H, gdnk::DK, gdnk::DV}, f32);
   torch::Tensor dfin_f;
   if (dfinal.has_value()) dfin_f = dfinal->to(at::kFloat).contiguous();
-  static bool configured = false;
-  if (!configured) {
-    set_smem(gdnk::gdn_dstate_kernel, sizeof(gdnk::DStateSm));
-    set_smem(gdnk::gdn_grad_kernel, sizeof(gdnk::GradSm));
-    configured = true;
-  }
+  static SmemOptIn a_dstate, a_grad;
+  C10_CUDA_CHECK(a_dstate.ensure(gdnk::gdn_dstate_kernel, (int)sizeof(gdnk::DStateSm)));
+  C10_CUDA_CHECK(a_grad.ensure(gdnk::gdn_grad_kernel, (int)sizeof(gdnk::GradSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int64_t rows = (int64_t)q.size(0) * q.size(1);
@@ -1602,11 +1591,8 @@ std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
   const int smem = (dk * dv + 2 * dk + 32 + dv) * 4;
   TORCH_CHECK(smem <= 227 * 1024, "gdn_recurrent: state too large");
-  static bool configured = false;
-  if (!configured) {
-    set_smem(gdnk::gdn_recurrent_kernel, 227 * 1024);
-    configured = true;
-  }
+  static SmemOptIn a_rec;
+  C10_CUDA_CHECK(a_rec.ensure(gdnk::gdn_recurrent_kernel, 227 * 1024));
   gdnk::gdn_recurrent_kernel<<<B * H, gdnk::NT, smem, at::cuda::getCurrentCUDAStream()>>>(
       (const bf16*)qc.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), gf.data_ptr<float>(),
       bf.data_ptr<float>(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)out.data_ptr(),

@@ -29,6 +29,31 @@
 
 namespace mykb {
 
+// All-gather fused into the GEMM (parameter-sharded data parallelism): the B operand is a
+// weight whose rows are spread over `world` GPUs (rank r holds rows [r*R, (r+1)*R) in its
+// shard buffer, at the same element offset on every rank).  Extra "gather" warps of every
+// CTA copy 64-row chunks of it from the owners' memory (16-byte peer loads over NVLink,
+// local loads for this rank's own rows) into a local full-size copy `dst`, which the TMA
+// producer then reads; a chunk counter per 64 rows (release add by the gather warp,
+// acquire load by the producer, proxy fences on both sides for the TMA read) orders them.
+// The copy starts at this rank's own chunks and the tile order (forward: output columns;
+// data gradient: the reduction loop) starts there too, so the first tiles run on rows that
+// are local while the remote rows cross NVLink.
+struct GatherParams {
+  const int64_t* src_ptrs;  // [world] base addresses (bf16) of every rank's shard buffer
+  int64_t src_offset;       // element offset of this weight's shard in each buffer (multiple of 8)
+  int rows_per_rank;        // R
+  int rows, cols;           // gathered weight: rows x cols, row-major (cols multiple of 8)
+  __nv_bfloat16* dst;       // local full-size copy
+  uint32_t* ready;          // [chunks] counters, one per 64 rows of dst
+  uint32_t target;          // counter value once this call has copied the whole chunk
+  int pieces_per_chunk, rows_per_piece;
+  int first_chunk, chunks;
+};
+
+constexpr int kGatherWarps = 4;
+constexpr int kGatherUnroll = 8;
+
 struct GemmParams {
   int M, N, K, batch;
   int tiles_m, tiles_n, k_blocks, split_k, kb_per_split;
@@ -38,6 +63,9 @@ struct GemmParams {
   float alpha, beta;
   int symmetric;  // D = D^T (M == N): tiles strictly above the diagonal are skipped, then mirrored
   int* status;
+  int rot_n;      // gather mode, B K-major: output column tiles start at this one
+  int rot_k;      // gather mode, B MN-major: the reduction loop starts at this K block
+  GatherParams g;
 };
 
 constexpr int kBM = 128;
@@ -75,10 +103,92 @@ __device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& 
   int in_group = tile % group_span;
   mt = first_m + in_group % gsize;
   nt = in_group / gsize;
+  if (p.rot_n) nt = (nt + p.rot_n) % p.tiles_n;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Gather warps: copy pieces (rows_per_piece whole rows) of the sharded weight into dst,
+// chunk by chunk starting at this rank's first chunk, and count each finished piece on its
+// chunk's counter.  gw / n_gw: this warp's index among all gather warps of the grid.
+__device__ __forceinline__ void gather_rows(const GatherParams& g, int gw, int n_gw, int lane) {
+  const int vpr = g.cols / 8;  // 16-byte vectors per row
+  const int total = g.chunks * g.pieces_per_chunk;
+  uint4* dst = reinterpret_cast<uint4*>(g.dst);
+  for (int pi = gw; pi < total; pi += n_gw) {
+    const int chunk = (g.first_chunk + pi / g.pieces_per_chunk) % g.chunks;
+    const int row0 = chunk * 64 + (pi % g.pieces_per_chunk) * g.rows_per_piece;
+    const int row1 = min(row0 + g.rows_per_piece, g.rows);
+    const int nvec = max(0, row1 - row0) * vpr;
+    for (int base = 0; base < nvec; base += 32 * kGatherUnroll) {
+      uint4 v[kGatherUnroll];
+      int64_t at[kGatherUnroll];
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        const int i = base + u * 32 + lane;
+        at[u] = -1;
+        if (i < nvec) {
+          const int row = row0 + i / vpr, c = i % vpr;
+          const int r = row / g.rows_per_rank, lr = row - r * g.rows_per_rank;
+          const uint4* src = reinterpret_cast<const uint4*>(g.src_ptrs[r]) + (g.src_offset + (int64_t)lr * g.cols) / 8;
+          v[u] = src[c];
+          at[u] = (int64_t)row * vpr + c;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u)
+        if (at[u] >= 0) dst[at[u]] = v[u];
+    }
+    // the copied rows are read next by TMA (the async proxy) in other CTAs
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence();
+      red_release_add(g.ready + chunk, 1u);
+    }
+  }
+}
+
+// Producer side: wait (bounded) until every chunk of rows [r0, r1) is complete in this call.
+// `seen` caches chunks already found complete (the first 256).
+__device__ __forceinline__ bool wait_rows_ready(const GatherParams& g, int r0, int r1, uint32_t* seen, int* status,
+                                                int code) {
+  const int c0 = r0 / 64, c1 = min(g.chunks, (r1 + 63) / 64);
+  bool waited = false;
+  for (int c = c0; c < c1; ++c) {
+    if (c < 256 && (seen[c >> 5] >> (c & 31) & 1u)) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acquire_gpu(g.ready + c) - g.target) < 0) {
+      if (status_failed(status)) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        set_status(status, code);
+        return false;
+      }
+    }
+    if (c < 256) seen[c >> 5] |= 1u << (c & 31);
+    waited = true;
+  }
+  if (waited) fence_proxy_async_global();
+  return true;
+}
+
+template <bool GATHER>
+constexpr int gemm_threads() {
+  return kThreads + (GATHER ? 32 * kGatherWarps : 0);
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM, bool GATHER>
+__global__ void __launch_bounds__(gemm_threads<GATHER>(), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   using S = GemmSmem<BN, STAGES>;
@@ -121,13 +231,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint32_t seen[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int unit = blockIdx.x; unit < p.total_units && ok; unit += gridDim.x) {
         int b, mt, nt, split;
         unit_coords(p, unit, b, mt, nt, split);
         if (skip_tile(p, mt, nt, BN)) continue;
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        if (GATHER && !B_MN && !wait_rows_ready(p.g, nt * BN, nt * BN + BN, seen, p.status, __LINE__)) {
+          ok = false;
+          break;
+        }
+        const int nkb = kb1 - kb0;
+        for (int it = 0; it < nkb; ++it) {
+          const int kb = GATHER ? kb0 + (it + p.rot_k) % nkb : kb0 + it;
+          if (GATHER && B_MN && !wait_rows_ready(p.g, kb * kBK, kb * kBK + kBK, seen, p.status, __LINE__)) {
+            ok = false;
+            break;
+          }
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status, __LINE__)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
@@ -167,7 +288,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (!mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, p.status, __LINE__)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {  // only the count matters here: the producer orders the K blocks
           if (!mbar_wait(&full[stage], phase, p.status, __LINE__)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * S::kStageBytes);
@@ -188,6 +309,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         ++local;
       }
     }
+  } else if (GATHER && warp >= 2 + kEpiWarps) {
+    // ---------------------------------------------------------------- gather warps
+    gather_rows(p.g, blockIdx.x * kGatherWarps + (warp - 2 - kEpiWarps), gridDim.x * kGatherWarps, lane);
   } else {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -325,28 +449,25 @@ static int num_sms(int device) {
   return cached[device];
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM, bool GATHER>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const GemmParams& p,
                         int grid, cudaStream_t stream) {
   using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, OUT_F32, ACCUM>;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-    configured = true;
-  }
-  kern<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, td, p);
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, OUT_F32, ACCUM, GATHER>;
+  static SmemOptIn configured;
+  C10_CUDA_CHECK(configured.ensure(kern, S::kTotal));
+  kern<<<grid, gemm_threads<GATHER>(), S::kTotal, stream>>>(ta, tb, td, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM>
+template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool ACCUM, bool GATHER = false>
 static void dispatch_stages(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const GemmParams& p,
                             int grid, cudaStream_t stream) {
   // 4 stages for BN=256 (48 KB each), 6 for BN=128 (32 KB each).
   if constexpr (BN == 256) {
-    launch_gemm<BN, 4, A_MN, B_MN, OUT_F32, ACCUM>(ta, tb, td, p, grid, stream);
+    launch_gemm<BN, 4, A_MN, B_MN, OUT_F32, ACCUM, GATHER>(ta, tb, td, p, grid, stream);
   } else {
-    launch_gemm<BN, 6, A_MN, B_MN, OUT_F32, ACCUM>(ta, tb, td, p, grid, stream);
+    launch_gemm<BN, 6, A_MN, B_MN, OUT_F32, ACCUM, GATHER>(ta, tb, td, p, grid, stream);
   }
 }
 
@@ -406,8 +527,11 @@ __global__ void __launch_bounds__(256) mirror_lower_kernel(T* __restrict__ d, in
 }
 
 // a: (batch?, M, K) or (batch?, K, M); b: (batch?, N, K) or (batch?, K, N); d: (batch?, M, N)
-void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
-          double alpha, double beta, bool accumulate, bool symmetric) {
+// gather != nullptr: all-gather mode (2-D, A K-major, bf16 D, stored product); b is the local
+// full-size copy the kernel fills from the shards while it multiplies.
+static void run_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& d, c10::optional<torch::Tensor> c,
+                     bool a_mn, bool b_mn, double alpha, double beta, bool accumulate, bool symmetric,
+                     const GatherParams* gather) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands required");
   TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "gemm: D must be bf16 or fp32");
@@ -472,6 +596,16 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
     TORCH_CHECK(M == N && !accumulate && split == 1, "gemm: symmetric mode needs M == N and a stored product");
     p.symmetric = 1;
   }
+  if (gather != nullptr) {
+    TORCH_CHECK(!batched && !a_mn && !out_f32 && !accumulate && !symmetric && split == 1,
+                "gemm_gather: 2-D, A K-major, bf16 D, stored product");
+    p.g = *gather;
+    if (b_mn) {
+      p.rot_k = p.k_blocks > 0 ? gather->first_chunk % p.k_blocks : 0;  // a chunk is one 64-row K block
+    } else {
+      p.rot_n = p.tiles_n > 0 ? (gather->first_chunk * 64 / BN) % p.tiles_n : 0;
+    }
+  }
 
   // Tensor maps (dims innermost first): A/B tiles of 64 elements (128 B) along the
   // contiguous dim; D boxes of 128 bytes x 32 rows.
@@ -490,6 +624,16 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
                                           d.stride(-2), d_bs, 64, 32);
   const int grid = std::min(p.total_units, sms);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (gather != nullptr) {
+    if (BN == 128) {
+      if (b_mn) dispatch_stages<128, false, true, false, false, true>(ta, tb, td, p, grid, stream);
+      else dispatch_stages<128, false, false, false, false, true>(ta, tb, td, p, grid, stream);
+    } else {
+      if (b_mn) dispatch_stages<256, false, true, false, false, true>(ta, tb, td, p, grid, stream);
+      else dispatch_stages<256, false, false, false, false, true>(ta, tb, td, p, grid, stream);
+    }
+    return;
+  }
   if (BN == 128) {
     dispatch_layout<128>(a_mn, b_mn, out_f32, accumulate, ta, tb, td, p, grid, stream);
   } else {
@@ -504,6 +648,90 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
       mirror_lower_kernel<__nv_bfloat16><<<mg, 256, 0, stream>>>((__nv_bfloat16*)d.data_ptr(), M, d.stride(-2), d_bs);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
+          double alpha, double beta, bool accumulate, bool symmetric) {
+  run_gemm(a, b, d, c, a_mn, b_mn, alpha, beta, accumulate, symmetric, nullptr);
+}
+
+// Fused all-gather + GEMM.  `w` (rows x cols bf16, local) receives the gathered weight;
+// forward (b_mn false): d = a w^T with w (N x K); data gradient (b_mn true): d = a w with
+// w (K x N).  src_ptrs: int64 [world] base addresses of every rank's bf16 shard buffer;
+// the weight's shard starts at element src_offset of each and holds rows_per_rank rows.
+// ready: int32 [ceil(rows / 64)] counters owned by `w` (zeroed once at allocation); epoch:
+// the number of gathers into `w` so far including this one.
+void gemm_gather(torch::Tensor a, torch::Tensor w, torch::Tensor d, bool b_mn, torch::Tensor src_ptrs,
+                 int64_t src_offset, int64_t rows_per_rank, int64_t rank, torch::Tensor ready, int64_t epoch) {
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "gemm_gather: w 2-D bf16");
+  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && src_ptrs.is_cuda(), "gemm_gather: int64 CUDA src_ptrs");
+  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.is_cuda() && ready.is_contiguous(), "gemm_gather: ready");
+  const int rows = w.size(0), cols = w.size(1);
+  const int world = src_ptrs.numel();
+  TORCH_CHECK(cols % 8 == 0 && src_offset % 8 == 0, "gemm_gather: rows and shards must be 16-byte aligned");
+  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * world >= rows && rank >= 0 && rank < world,
+              "gemm_gather: shards do not cover the weight");
+  const int chunks = (rows + 63) / 64;
+  TORCH_CHECK(ready.numel() >= chunks, "gemm_gather: ready needs one counter per 64 rows");
+  GatherParams g{};
+  g.src_ptrs = src_ptrs.data_ptr<int64_t>();
+  g.src_offset = src_offset;
+  g.rows_per_rank = (int)rows_per_rank;
+  g.rows = rows;
+  g.cols = cols;
+  g.dst = (__nv_bfloat16*)w.data_ptr();
+  g.ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int>());
+  // pieces of whole rows of about 16 KB, a power of two per 64-row chunk
+  int rpp = 64;
+  while (rpp > 1 && (int64_t)rpp * cols * 2 > 16384) rpp >>= 1;
+  g.rows_per_piece = rpp;
+  g.pieces_per_chunk = 64 / rpp;
+  g.target = (uint32_t)((uint64_t)epoch * (uint64_t)g.pieces_per_chunk);
+  g.chunks = chunks;
+  g.first_chunk = (int)((rank * rows_per_rank) / 64) % std::max(1, chunks);
+  run_gemm(a, w, d, c10::nullopt, false, b_mn, 1.0, 0.0, false, false, &g);
+}
+
+// Gather only (no product): the same copy as gemm_gather's gather warps, with a grid of its
+// own.  Used where a sharded weight is needed outside a large GEMM (decode-sized products,
+// checkpoints) and as the unfused comparison in tests.
+__global__ void __launch_bounds__(32 * kGatherWarps) shard_gather_kernel(const GatherParams g) {
+  gather_rows(g, blockIdx.x * kGatherWarps + threadIdx.x / 32, gridDim.x * kGatherWarps, threadIdx.x % 32);
+}
+
+void shard_gather(torch::Tensor w, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
+                  torch::Tensor ready, int64_t epoch) {
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "shard_gather: w 2-D bf16");
+  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && src_ptrs.is_cuda(), "shard_gather: int64 CUDA src_ptrs");
+  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.is_cuda() && ready.is_contiguous(), "shard_gather: ready");
+  const int rows = w.size(0), cols = w.size(1);
+  const int world = src_ptrs.numel();
+  TORCH_CHECK(cols % 8 == 0 && src_offset % 8 == 0, "shard_gather: rows and shards must be 16-byte aligned");
+  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * world >= rows && rank >= 0 && rank < world,
+              "shard_gather: shards do not cover the weight");
+  const int chunks = (rows + 63) / 64;
+  TORCH_CHECK(ready.numel() >= chunks, "shard_gather: ready needs one counter per 64 rows");
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard guard(w.device());
+  GatherParams g{};
+  g.src_ptrs = src_ptrs.data_ptr<int64_t>();
+  g.src_offset = src_offset;
+  g.rows_per_rank = (int)rows_per_rank;
+  g.rows = rows;
+  g.cols = cols;
+  g.dst = (__nv_bfloat16*)w.data_ptr();
+  g.ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int>());
+  int rpp = 64;
+  while (rpp > 1 && (int64_t)rpp * cols * 2 > 16384) rpp >>= 1;
+  g.rows_per_piece = rpp;
+  g.pieces_per_chunk = 64 / rpp;
+  g.target = (uint32_t)((uint64_t)epoch * (uint64_t)g.pieces_per_chunk);
+  g.chunks = chunks;
+  g.first_chunk = (int)((rank * rows_per_rank) / 64) % chunks;
+  const int pieces = chunks * g.pieces_per_chunk;
+  const int blocks = std::max(1, std::min((pieces + kGatherWarps - 1) / kGatherWarps, 4 * num_sms(w.get_device())));
+  shard_gather_kernel<<<blocks, 32 * kGatherWarps, 0, at::cuda::getCurrentCUDAStream()>>>(g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace mykb

@@ -186,12 +186,8 @@ template <int MT, int WM>
 static void skinny_launch(const skinny::Params& p, int grid, cudaStream_t st) {
   using namespace skinny;
   const size_t smem = (size_t)STAGES * (WM * MT * 16 + BN) * LDS * sizeof(bf16);
-  static bool attr = false;
-  if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(skinny_gemm_kernel<MT, WM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)smem));
-    attr = true;
-  }
+  static SmemOptIn attr;
+  C10_CUDA_CHECK(attr.ensure(skinny_gemm_kernel<MT, WM>, (int)smem));
   skinny_gemm_kernel<MT, WM><<<grid, THREADS * WM, smem, st>>>(p);
 }
 

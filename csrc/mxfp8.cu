@@ -409,11 +409,8 @@ template <bool AE, bool BE, bool F32, bool ACC>
 static void mx_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const mx::GemmArgs& p,
                       int grid, cudaStream_t st) {
   auto kern = mx::mx_gemm_kernel<AE, BE, F32, ACC>;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, mx::SMEM_TOTAL));
-    configured = true;
-  }
+  static SmemOptIn configured;
+  C10_CUDA_CHECK(configured.ensure(kern, mx::SMEM_TOTAL));
   kern<<<grid, mx::THREADS, mx::SMEM_TOTAL, st>>>(ta, tb, td, p);
 }
 

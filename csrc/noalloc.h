@@ -26,9 +26,19 @@ extern "C" {
 // (packed) or (num_seqs, heads, max_q) (batch).  window_left / window_right: -1 = unbounded
 // (causal is window_right = 0).  head_dim must be 64 or 128.
 //
-// Returns 0 on success.  A non-zero return is an error code and
-// mykb_noalloc_last_error() describes it; sizes beyond MYKB_NOALLOC_MAX_ROWS_X_HEADS are
-// rejected without launching anything.
+// Packed layout: the one cu_seqlens array gives the document boundaries of both queries
+// and keys, so rows_k must equal rows_q.  Batch layout: rows_q must equal num_seqs * max_q
+// and rows_k must equal num_seqs * max_k.  Calls that break either rule are rejected.
+//
+// Returns 0 when the work was enqueued on `stream`.  A non-zero return is an error code
+// and mykb_noalloc_last_error() describes it (the message is kept per host thread); sizes
+// beyond MYKB_NOALLOC_MAX_ROWS_X_HEADS are rejected without launching anything.
+//
+// The kernels' waits are bounded: a wait that gives up records a non-zero code in this
+// device's status word and the kernels wind down, leaving dq / dk / dv incomplete.  The
+// call itself cannot see that (it does not synchronise), so read the word with
+// mykb_noalloc_status() after synchronising the stream.  Each call clears the word on its
+// stream before its kernels run.
 //
 // The first call on a device looks up the device address of the scratch arrays
 // (cudaGetSymbolAddress) for that device; make that first call before any stream
@@ -43,6 +53,17 @@ int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, const void* k, 
                                 int window_right, cudaStream_t stream);
 
 const char* mykb_noalloc_last_error(void);
+
+// Status word of the current device's allocation-free calls: 0 when every wait of the
+// calls since the last clear completed, else the code of the wait that gave up.  It
+// synchronises with the device (a blocking copy), so call it after the stream sync.
+// clear != 0 also resets the word.  A negative value is an error (see
+// mykb_noalloc_last_error).
+int mykb_noalloc_status(int clear);
+
+// Device address of the current device's status word (NULL on error), for callers that
+// read it asynchronously into their own pinned memory.
+void* mykb_noalloc_status_address(void);
 
 #ifdef __cplusplus
 }

@@ -7,10 +7,16 @@
 
 namespace mykb {
 
+namespace {
+std::mutex g_pool_mu;  // guards the per-device lazily created buffers below
+}
+
 int* device_status() {
   static int* ptrs[64] = {nullptr};
   int dev = 0;
-  cudaGetDevice(&dev);
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  TORCH_CHECK(dev >= 0 && dev < 64, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_pool_mu);
   if (ptrs[dev] == nullptr) {
     C10_CUDA_CHECK(cudaMalloc(&ptrs[dev], sizeof(int)));
     C10_CUDA_CHECK(cudaMemset(ptrs[dev], 0, sizeof(int)));
@@ -37,7 +43,9 @@ int* ticket_region(int count) {
   static int next[64] = {0};
   TORCH_CHECK(count > 0 && count <= kTicketPool / 4, "ticket_region: too many tickets (", count, ")");
   int dev = 0;
-  cudaGetDevice(&dev);
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  TORCH_CHECK(dev >= 0 && dev < 64, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_pool_mu);
   if (pools[dev] == nullptr) {
     C10_CUDA_CHECK(cudaMalloc(&pools[dev], sizeof(int) * kTicketPool));
     C10_CUDA_CHECK(cudaMemset(pools[dev], 0, sizeof(int) * kTicketPool));

@@ -10,6 +10,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Literal
 
+import numpy as np
 import torch
 
 from .filters import DocFilter
@@ -59,30 +60,80 @@ class DataConfig:
 
 @dataclass
 class Batch:
+    """One rank's micro-batch on the host (or, after ``to``, on the device).  Loaders that
+    build batches with ``RowPacker`` keep inputs and targets in one pinned ``(2, B, S)``
+    tensor (``staged``), so moving a batch to the GPU is a single asynchronous copy."""
+
     input_ids: torch.Tensor  # (batch, seq) int64
     targets: torch.Tensor  # (batch, seq) int64, IGNORE_INDEX where unsupervised
-    seqlens: list[torch.Tensor] | None = None  # per-row document lengths
+    seqlens: list[torch.Tensor] | None = None  # per-row document lengths (int32)
+    staged: torch.Tensor | None = None
 
     def to(self, device: torch.device) -> "Batch":
+        if self.staged is not None and torch.device(device).type == "cuda":
+            both = self.staged.to(device, non_blocking=True)
+            return Batch(both[0], both[1], self.seqlens)
         return Batch(self.input_ids.to(device, non_blocking=True), self.targets.to(device, non_blocking=True),
                      self.seqlens)
 
     def pin_memory(self) -> "Batch":
-        return Batch(self.input_ids.pin_memory(), self.targets.pin_memory(), self.seqlens)
+        if self.staged is not None and self.staged.is_pinned():
+            return self
+        both = torch.stack([self.input_ids, self.targets]).pin_memory()
+        return Batch(both[0], both[1], self.seqlens, both)
 
     @property
     def num_targets(self) -> int:
-        return int((self.targets != IGNORE_INDEX).sum())
+        return int(torch.count_nonzero(self.targets != IGNORE_INDEX))
 
     @property
     def nbytes(self) -> int:
-        return self.input_ids.numel() * self.input_ids.element_size() + self.targets.numel() * self.targets.element_size()
+        return 2 * self.input_ids.numel() * self.input_ids.element_size()
 
 
-def collate(rows: list[dict]) -> Batch:
-    import numpy as np
+def _pinned_ok() -> bool:
+    return torch.cuda.is_available()
 
-    ids = torch.as_tensor(np.stack([r["input_ids"] for r in rows]), dtype=torch.long)
-    tg = torch.as_tensor(np.stack([r["targets"] for r in rows]), dtype=torch.long)
-    seqlens = [torch.as_tensor(r["seqlens"], dtype=torch.int32) for r in rows] if "seqlens" in rows[0] else None
-    return Batch(ids, tg, seqlens)
+
+class RowPacker:
+    """Writes the rows of one batch straight into a pinned host tensor: row ``i`` is a
+    window of ``seq_len + 1`` tokens; its inputs are the first ``seq_len``, its targets the
+    last ``seq_len`` with ``IGNORE_INDEX`` where ``ignore`` is set.  Document cut points
+    (offsets inside the window where a document ends) become per-row ``seqlens``.  Pinned
+    blocks come from torch's caching host allocator, which does not hand a block out again
+    while an asynchronous copy from it may still be running."""
+
+    def __init__(self, rows: int, seq_len: int, pin: bool | None = None) -> None:
+        pin = _pinned_ok() if pin is None else pin
+        self.seq_len = seq_len
+        self.host = torch.empty((2, rows, seq_len), dtype=torch.long, pin_memory=pin)
+        self.view = self.host.numpy()
+        self.seqlens: list[torch.Tensor] = []
+        self.masked = False
+
+    def put(self, i: int, window: np.ndarray, ignore: np.ndarray | None = None,
+            cuts: np.ndarray | None = None) -> None:
+        self.view[0, i] = window[:-1]
+        self.view[1, i] = window[1:]
+        if ignore is not None:
+            self.view[1, i][ignore] = IGNORE_INDEX
+        if cuts is not None:
+            self.masked = True
+            bounds = np.concatenate(([0], np.asarray(cuts, dtype=np.int64), [self.seq_len]))
+            self.seqlens.append(torch.from_numpy(np.diff(bounds).astype(np.int32)))
+
+    def batch(self) -> Batch:
+        return Batch(self.host[0], self.host[1], self.seqlens if self.masked else None, self.host)
+
+
+def collate(rows: list[dict], pin: bool | None = None) -> Batch:
+    """Batch from row dicts (``input_ids``, ``targets``, optional ``seqlens``).  Data-loader
+    worker processes pass ``pin=False`` (a forked worker must not touch CUDA)."""
+    packer = RowPacker(len(rows), len(rows[0]["input_ids"]), pin)
+    for i, r in enumerate(rows):
+        packer.view[0, i] = r["input_ids"]
+        packer.view[1, i] = r["targets"]
+        if "seqlens" in r:
+            packer.masked = True
+            packer.seqlens.append(torch.as_tensor(np.asarray(r["seqlens"], dtype=np.int32)))
+    return packer.batch()

@@ -1,10 +1,15 @@
 """Supervised fine-tuning data: chat transcripts with an assistant-only loss mask.
 
-File layout (shared with the reference, ``src/myk_llm/data/sft.py:60-83``):
-``P.tokens.bin`` (uint32), ``P.loss_mask.bin`` (uint8, 1 on assistant tokens),
-``P.spans.npy`` (int64 [start, end) per conversation) and ``P.meta.json``.
-``ChatLoader`` draws window starts from a generator seeded with (seed, step), so its
-only state is the step.
+Files of a tokenised chat set with prefix ``P`` (an interface shared with the reference,
+``src/myk_llm/data/sft.py:1-13``): ``P.tokens.bin`` (uint32 ids, conversations back to
+back), ``P.loss_mask.bin`` (uint8, 1 where the token is supervised: assistant content and
+its end-of-turn), ``P.spans.npy`` (int64 ``[start, end)`` per conversation) and
+``P.meta.json``.
+
+Training windows start at positions drawn from ``default_rng([seed, step])`` over the
+whole token array, so conversations are packed rather than padded and the loader's only
+state is the step; with document masking the conversation ends inside a window cut it.
+Batches are assembled straight into pinned host memory (``RowPacker``).
 """
 
 from __future__ import annotations
@@ -15,89 +20,125 @@ from typing import Any, Iterable, Iterator
 
 import numpy as np
 
-from .config import IGNORE_INDEX, Batch, DataConfig, collate
+from .config import Batch, DataConfig, RowPacker
 
-ROLE_ALIASES = {"human": "user", "user": "user", "gpt": "assistant", "assistant": "assistant", "bot": "assistant",
-                "system": "system"}
+# role spellings of the two accepted transcript schemas, folded to chat-template roles
+_ROLES = {"human": "user", "user": "user", "gpt": "assistant", "bot": "assistant", "assistant": "assistant",
+          "system": "system"}
+# (list key, role key, text key) of the accepted schemas: OpenAI-style and ShareGPT
+_SCHEMAS = (("messages", "role", "content"), ("conversations", "from", "value"))
 
 
 def normalize_messages(example: dict[str, Any]) -> list[dict[str, str]]:
-    """{'messages': [{role, content}]} or ShareGPT {'conversations': [{from, value}]}."""
-    msgs = example.get("messages", example.get("conversations"))
-    if not isinstance(msgs, list) or not msgs:
-        raise ValueError("chat examples need a non-empty 'messages' or 'conversations' list")
-    out = []
-    for m in msgs:
-        role, content = m.get("role", m.get("from")), m.get("content", m.get("value"))
-        if not isinstance(role, str) or not isinstance(content, str):
-            raise ValueError("chat messages need string role/content (or from/value)")
-        out.append({"role": ROLE_ALIASES.get(role.lower(), role), "content": content})
-    return out
+    """``{"messages": [{"role", "content"}]}`` or ShareGPT ``{"conversations": [{"from",
+    "value"}]}`` as a list of ``{"role", "content"}`` with canonical role names."""
+    for list_key, role_key, text_key in _SCHEMAS:
+        turns = example.get(list_key)
+        if turns is None:
+            continue
+        if not isinstance(turns, list) or not turns:
+            break
+        out = []
+        for turn in turns:
+            role = turn.get(role_key, turn.get("role", turn.get("from")))
+            text = turn.get(text_key, turn.get("content", turn.get("value")))
+            if not (isinstance(role, str) and isinstance(text, str)):
+                raise ValueError("chat messages need string role/content (or from/value)")
+            out.append({"role": _ROLES.get(role.lower(), role), "content": text})
+        return out
+    raise ValueError("chat examples need a non-empty 'messages' or 'conversations' list")
 
 
-def encode_chat(tokenizer, messages: list[dict[str, str]]) -> tuple[list[int], list[int]]:
-    """Token ids and the assistant mask produced by a chat template with
-    ``{% generation %}`` blocks."""
+def encode_chat(tokenizer, messages: list[dict[str, str]]) -> tuple[np.ndarray, np.ndarray]:
+    """Token ids (uint32) and loss mask (uint8) from a chat template whose assistant turns
+    are wrapped in ``{% generation %}`` (which is what makes the mask exact)."""
     enc = tokenizer.apply_chat_template(messages, tokenize=True, add_generation_prompt=False, return_dict=True,
                                         return_assistant_tokens_mask=True)
-    ids = [int(t) for t in enc["input_ids"]]
+    ids = np.asarray(enc["input_ids"], dtype=np.uint32)
     mask = enc.get("assistant_masks")
-    if not mask or len(mask) != len(ids):
+    if mask is None or len(mask) != ids.size or ids.size == 0:
         raise ValueError("the chat template did not produce an assistant mask ({% generation %} tags missing?)")
-    return ids, [int(m) for m in mask]
+    return ids, np.asarray(mask, dtype=np.uint8)
+
+
+class _Growing:
+    """An append-only numpy array that doubles its storage."""
+
+    def __init__(self, dtype) -> None:
+        self.data = np.empty(1 << 16, dtype=dtype)
+        self.size = 0
+
+    def extend(self, values: np.ndarray) -> None:
+        need = self.size + values.size
+        if need > self.data.size:
+            grown = np.empty(max(need, 2 * self.data.size), dtype=self.data.dtype)
+            grown[:self.size] = self.data[:self.size]
+            self.data = grown
+        self.data[self.size:need] = values
+        self.size = need
+
+    def array(self) -> np.ndarray:
+        return self.data[:self.size]
 
 
 def write_chat_dataset(tokenizer, examples: Iterable[dict[str, Any]], prefix, tokenizer_path: str) -> dict[str, Any]:
-    prefix = Path(prefix)
-    prefix.parent.mkdir(parents=True, exist_ok=True)
-    toks: list[int] = []
-    mask: list[int] = []
+    """Tokenise transcripts into the chat-set files; conversations with fewer than two
+    tokens or no supervised token are skipped and counted.  Returns the meta record."""
+    toks, mask = _Growing(np.uint32), _Growing(np.uint8)
     spans: list[tuple[int, int]] = []
     skipped = 0
-    for ex in examples:
-        ids, m = encode_chat(tokenizer, normalize_messages(ex))
-        if len(ids) < 2 or not any(m):
+    for example in examples:
+        ids, m = encode_chat(tokenizer, normalize_messages(example))
+        if ids.size < 2 or not m.any():
             skipped += 1
             continue
-        spans.append((len(toks), len(toks) + len(ids)))
+        spans.append((toks.size, toks.size + ids.size))
         toks.extend(ids)
         mask.extend(m)
-    write_chat_arrays(prefix, toks, mask, spans, tokenizer_path, skipped)
-    return json.loads(Path(f"{prefix}.meta.json").read_text())
+    return write_chat_arrays(prefix, toks.array(), mask.array(), spans, tokenizer_path, skipped)
 
 
-def write_chat_arrays(prefix, toks, mask, spans, tokenizer_path: str = "", skipped: int = 0) -> None:
-    np.asarray(toks, dtype=np.uint32).tofile(f"{prefix}.tokens.bin")
-    np.asarray(mask, dtype=np.uint8).tofile(f"{prefix}.loss_mask.bin")
+def write_chat_arrays(prefix, toks, mask, spans, tokenizer_path: str = "", skipped: int = 0) -> dict[str, Any]:
+    prefix = Path(prefix)
+    prefix.parent.mkdir(parents=True, exist_ok=True)
+    toks = np.asarray(toks, dtype=np.uint32)
+    np.ascontiguousarray(toks).tofile(f"{prefix}.tokens.bin")
+    np.ascontiguousarray(np.asarray(mask, dtype=np.uint8)).tofile(f"{prefix}.loss_mask.bin")
     np.save(f"{prefix}.spans.npy", np.asarray(spans, dtype=np.int64).reshape(-1, 2))
-    meta = {"mode": "chat", "tokenizer": tokenizer_path, "num_tokens": len(toks), "num_spans": len(spans),
+    meta = {"mode": "chat", "tokenizer": tokenizer_path, "num_tokens": int(toks.size), "num_spans": len(spans),
             "token_dtype": "uint32", "has_loss_mask": True, "skipped": skipped}
     Path(f"{prefix}.meta.json").write_text(json.dumps(meta, indent=2), encoding="utf-8")
+    return meta
 
 
 class ChatDataset:
+    """Memory-mapped chat set."""
+
     def __init__(self, prefix) -> None:
         meta = json.loads(Path(f"{prefix}.meta.json").read_text(encoding="utf-8"))
         if not meta.get("has_loss_mask"):
             raise ValueError(f"{prefix} has no loss mask; tokenize it as chat data")
-        self.num_tokens = int(meta["num_tokens"])
-        self.tokens = np.memmap(f"{prefix}.tokens.bin", dtype=np.uint32, mode="r", shape=(self.num_tokens,))
-        self.loss_mask = np.memmap(f"{prefix}.loss_mask.bin", dtype=np.uint8, mode="r", shape=(self.num_tokens,))
+        n = self.num_tokens = int(meta["num_tokens"])
+        self.tokens = np.memmap(f"{prefix}.tokens.bin", dtype=np.uint32, mode="r", shape=(n,))
+        self.loss_mask = np.memmap(f"{prefix}.loss_mask.bin", dtype=np.uint8, mode="r", shape=(n,))
         self.doc_ends = np.load(f"{prefix}.spans.npy")[:, 1]
 
-    def window(self, start: int, seq_len: int, document_masking: bool) -> dict[str, np.ndarray]:
-        chunk = np.asarray(self.tokens[start:start + seq_len + 1], dtype=np.int64)
-        m = np.asarray(self.loss_mask[start + 1:start + seq_len + 1], dtype=bool)
-        row = {"input_ids": chunk[:-1], "targets": np.where(m, chunk[1:], IGNORE_INDEX)}
+    def fill(self, packer: RowPacker, row: int, start: int, document_masking: bool) -> None:
+        """Window of ``seq_len + 1`` tokens at ``start`` into a batch row: targets are the
+        supervised next tokens only; conversation ends inside the window cut it."""
+        seq = packer.seq_len
+        chunk = np.asarray(self.tokens[start:start + seq + 1], dtype=np.int64)
+        unsupervised = self.loss_mask[start + 1:start + seq + 1] == 0
+        cuts = None
         if document_masking:
-            lo, hi = start, start + seq_len
             e = self.doc_ends
-            cuts = e[np.searchsorted(e, lo, side="right"):np.searchsorted(e, hi, side="left")]
-            row["seqlens"] = np.diff(np.concatenate(([lo], cuts, [hi]))).astype(np.int32)
-        return row
+            cuts = e[np.searchsorted(e, start, side="right"):np.searchsorted(e, start + seq, side="left")] - start
+        packer.put(row, chunk, ignore=unsupervised, cuts=cuts)
 
 
 class ChatLoader:
+    """SFT batches for this rank; the state is the step counter."""
+
     def __init__(self, config: DataConfig, rank: int = 0, world_size: int = 1) -> None:
         if len(config.sources) != 1 or not config.sources[0].path:
             raise ValueError("sft data takes exactly one source with a tokenized `path` prefix")
@@ -108,16 +149,17 @@ class ChatLoader:
         self.step = 0
 
     def batch_at(self, step: int) -> Batch:
-        per = self.config.micro_batch_size
-        rng = np.random.default_rng([self.config.seed, step])
-        starts = rng.integers(0, self.dataset.num_tokens - self.config.seq_len, size=per * self.world_size)
-        mine = starts[self.rank * per:(self.rank + 1) * per]
-        return collate([self.dataset.window(int(s), self.config.seq_len, self.config.document_masking) for s in mine])
+        per, seq = self.config.micro_batch_size, self.config.seq_len
+        starts = np.random.default_rng([self.config.seed, step]).integers(
+            0, self.dataset.num_tokens - seq, size=per * self.world_size)
+        packer = RowPacker(per, seq)
+        for row, start in enumerate(starts[self.rank * per:(self.rank + 1) * per]):
+            self.dataset.fill(packer, row, int(start), self.config.document_masking)
+        return packer.batch()
 
     def next_batch(self) -> Batch:
-        b = self.batch_at(self.step)
         self.step += 1
-        return b
+        return self.batch_at(self.step - 1)
 
     def __iter__(self) -> Iterator[Batch]:
         while True:

@@ -20,6 +20,8 @@ tokenizer at load time and resume by cursor.
 
 from __future__ import annotations
 
+import functools
+
 import glob
 from pathlib import Path
 from typing import Any, Iterator
@@ -237,7 +239,7 @@ class StreamLoader:
         workers = config.num_workers
         self.loader = StatefulDataLoader(
             PackedStreamDataset(config, eos_id, rank, world_size, **dataset_kw), batch_size=config.micro_batch_size,
-            num_workers=workers, collate_fn=collate, pin_memory=workers > 0, drop_last=True,
+            num_workers=workers, collate_fn=functools.partial(collate, pin=False), pin_memory=workers > 0, drop_last=True,
             persistent_workers=workers > 0, prefetch_factor=4 if workers > 0 else None)
         self._it: Iterator[Batch] | None = None
 

@@ -18,7 +18,7 @@ from typing import Any, Iterator
 import numpy as np
 import torch
 
-from .config import IGNORE_INDEX, Batch, DataConfig
+from .config import IGNORE_INDEX, Batch, DataConfig, collate
 
 
 def packed_row(rng: np.random.Generator, seq_len: int, vocab: int, mean: int, eos: int,
@@ -60,10 +60,7 @@ class SyntheticLoader:
             global_row = (step * self.world_size + self.rank) * c.micro_batch_size + i
             rng = np.random.default_rng([c.seed, global_row])
             rows.append(packed_row(rng, c.seq_len, s.vocab_size, s.mean_doc_len, s.eos_id, c.document_masking))
-        ids = torch.as_tensor(np.stack([r["input_ids"] for r in rows]))
-        tg = torch.as_tensor(np.stack([r["targets"] for r in rows]))
-        seqlens = [torch.as_tensor(r["seqlens"]) for r in rows] if c.document_masking else None
-        return Batch(ids, tg, seqlens)
+        return collate(rows)
 
     def next_batch(self) -> Batch:
         b = self.batch_at(self.step)

@@ -158,7 +158,12 @@ class _Linear(torch.autograd.Function):
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """y = x W^T (no bias).  CUDA: bf16 tcgen05 GEMM, the block-scaled MXFP8 GEMMs for
     weights converted by ``convert_to_mxfp8_training``, or the float8 GEMMs for weights
-    converted by ``convert_to_float8_training``; CPU: ``F.linear`` in x's dtype."""
+    converted by ``convert_to_float8_training``; CPU: ``F.linear`` in x's dtype.  A weight
+    row-sharded by the parameter-sharded runtime goes through its handle, whose GEMMs
+    gather the weight from the other GPUs as they run."""
+    shard = getattr(weight, "_mykb_shard", None)
+    if shard is not None:  # a row-sharded weight of the parameter-sharded runtime
+        return shard.linear(x, weight)
     if not x.is_cuda:
         return F.linear(x, weight.to(x.dtype))
     fmt = getattr(weight, "_mykb_mxfp8", None)

@@ -11,9 +11,12 @@ data-parallel runtime:
 * ``fsdp``: torch FSDP2 (``fully_shard`` per block + root, fp32 gradient reduction as a
   sum, as in the reference ``src/myk_llm/train/distributed.py:108-134``): the NCCL
   baseline.
-* ``sharded`` (and ``auto`` with more than one rank): this framework's sharded data
-  parallel (:mod:`myk_llm_b200.parallel.sharded`), whose all-gather and reduce-scatter
-  run inside sm_100a kernels over peer memory.
+* ``sharded`` (and ``auto`` with more than one rank): this framework's parameter-sharded
+  data parallel (:mod:`myk_llm_b200.parallel.sharded`): block weights row-sharded over the
+  ranks and gathered inside the GEMMs that consume them, the gradient reduce-scatter fused
+  with the clipping norm and the optimizer update, all over peer memory;
+* ``replicated``: the same runtime with every parameter replicated (optimizer state and
+  work still sharded).
 """
 
 from __future__ import annotations
@@ -87,7 +90,7 @@ def uses_fsdp(config, info: DistInfo) -> bool:
 
 
 def uses_sharded(config, info: DistInfo) -> bool:
-    return config.strategy == "sharded" or (config.strategy == "auto" and info.enabled)
+    return config.strategy in ("sharded", "replicated") or (config.strategy == "auto" and info.enabled)
 
 
 def convert_float8(model: nn.Module, recipe: str, *, skip_down_proj: bool = False, grad_dtype: str = "e4m3") -> int:
@@ -136,5 +139,6 @@ def parallelize(model, config, info: DistInfo):
     if uses_sharded(config, info) and info.enabled:
         from .sharded import shard_model
 
-        return shard_model(model, info, reshard_after_forward=config.reshard_after_forward)
+        return shard_model(model, info, reshard_after_forward=config.reshard_after_forward,
+                           shard_params=config.strategy != "replicated")
     return model

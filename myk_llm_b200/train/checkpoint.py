@@ -63,6 +63,9 @@ def save_checkpoint(directory: Path, model, optimizers, trainer_state: dict, dat
     torch.save(data_state, directory / f"data_rank{info.rank}.pt")
     if export_weights:
         export_model(directory, model, info, tokenizer, extra_weights)
+    done = getattr(model, "after_checkpoint_save", None)
+    if done is not None:
+        done()
     barrier()
     if info.is_main:
         (directory / "trainer.json").write_text(json.dumps(trainer_state, indent=2), encoding="utf-8")
@@ -82,6 +85,9 @@ def load_checkpoint(directory: Path, model, optimizers, info: DistInfo):
     """Load model (+ optimizer) state in place; returns (trainer_state, this rank's data state)."""
     directory = Path(directory)
     base = _unwrap(model)
+    prepare = getattr(model, "before_checkpoint_load", None)
+    if prepare is not None:
+        prepare()
     if optimizers:
         state = _app_state(model, optimizers)
         dcp.load(state, checkpoint_id=str(directory))

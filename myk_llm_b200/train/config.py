@@ -86,9 +86,11 @@ class InitConfig:
 
 @dataclass
 class ParallelConfig:
-    # auto: this framework's sharded data parallel when world_size > 1; fsdp: torch FSDP2
-    # (NCCL baseline); sharded: always the own runtime; none: replicate nothing.
-    strategy: Literal["auto", "fsdp", "sharded", "none"] = "auto"
+    # auto: this framework's parameter-sharded data parallel when world_size > 1; sharded:
+    # always that runtime; replicated: the same runtime with every parameter replicated
+    # (only optimizer state and work sharded); fsdp: torch FSDP2 (NCCL baseline); none:
+    # no data-parallel wrapper.
+    strategy: Literal["auto", "fsdp", "sharded", "replicated", "none"] = "auto"
     param_dtype: Literal["fp32", "bf16"] = "fp32"
     reshard_after_forward: bool = True
     compile: bool = True

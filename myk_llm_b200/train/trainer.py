@@ -280,6 +280,21 @@ class Trainer:
         out["normalizer"] = torch.tensor(normalizer)
         return out
 
+    def check_health(self, loss: float, grad_norm: float, step: int) -> None:
+        """Called at a point where the host has already synchronised with the device (the
+        logging sync of ``fit``): raises if a bounded device wait gave up since the last
+        check (a peer that never arrived, a stalled pipeline: the kernels wound down and
+        left results incomplete) or if the loss or the gradient norm is not finite."""
+        if self.info.device.type == "cuda":
+            code = int(ops.ext().take_status())
+            if code != 0:
+                raise RuntimeError(f"step {step}: a device wait gave up (status {code}: the source line of the wait "
+                                   "in csrc/); the step's results are incomplete")
+        if not math.isfinite(loss):
+            raise FloatingPointError(f"step {step}: non-finite training loss {loss}")
+        if not math.isfinite(grad_norm):
+            raise FloatingPointError(f"step {step}: non-finite gradient norm {grad_norm}")
+
     # ---------------------------------------------------------------------------------
     @torch.no_grad()
     def validate(self, val_sets: dict[str, list[Batch]], token_bytes: torch.Tensor | None) -> dict[str, float]:
@@ -398,6 +413,7 @@ class Trainer:
                             "tokens": self.tokens_seen})
                 if self.tables is not None:
                     rec.update(self.tables.pop_stats())
+                self.check_health(rec["train/loss"], rec["train/grad_norm"], step)
                 if metrics is not None:
                     metrics.log(step, rec)
                 log0(info, f"step {step:6d} loss {rec['train/loss']:.4f} lr {rec['train/lr']:.2e} "

@@ -1,7 +1,8 @@
 """Builds the sm_100a extension in place: ``python setup.py build_ext --inplace``.
 
-Every kernel is compiled for ``sm_100a`` only (``-gencode arch=compute_100a,code=sm_100a``);
-torch's own architecture list is bypassed.
+Every kernel is compiled for ``sm_100a`` only (``-gencode arch=compute_100a,code=sm_100a``).
+torch's extension builder adds no architecture flags of its own when the nvcc flags
+already name an architecture, so the flag below is the only one.
 """
 
 import glob
@@ -29,14 +30,6 @@ nvcc_flags = [
 ]
 
 
-class Build(BuildExtension):
-    def build_extensions(self):
-        # Drop any -gencode torch adds from its arch list; the nvcc flags above decide.
-        for ext in self.extensions:
-            ext.extra_compile_args["nvcc"] = [f for f in ext.extra_compile_args["nvcc"]]
-        super().build_extensions()
-
-
 setup(
     name="myk_llm_b200",
     ext_modules=[
@@ -47,5 +40,5 @@ setup(
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc_flags},
         )
     ],
-    cmdclass={"build_ext": Build.with_options(use_ninja=True)},
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -68,7 +68,8 @@ def test_token_balanced_sources(tmp_path):
                                   SourceConfig(name="b", path=str(tmp_path / "b"), weight=3.0)])
     ld = build_loader(cfg)
     [ld.next_batch() for _ in range(10)]
-    a, b = ld.cursors[0].consumed, ld.cursors[1].consumed
+    cur = ld.state_dict()["cursors"]
+    a, b = cur[0]["consumed"], cur[1]["consumed"]
     assert abs(b / max(a, 1) - 3.0) < 0.6
 
 

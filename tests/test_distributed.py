@@ -1,6 +1,7 @@
-"""Multi-process data parallelism on CPU (gloo, world size 2): the sharded runtime
-(optimizer state partitioned, gradient reduce-scatter + parameter all-gather per step)
-trains exactly like one process on the whole global batch, for Muon + AdamW.  Also torch
+"""Multi-process data parallelism on CPU (gloo, world size 2): the sharded runtime trains
+exactly like one process on the whole global batch, for Muon + AdamW, in its three
+layouts: row-sharded block weights gathered at every use (the FSDP2 default) or once per
+step, and every parameter replicated with only optimizer state and work partitioned.  Also torch
 FSDP2 (the NCCL-baseline strategy) over gloo on the tiny config, and the host-side
 failure path: a rank that raises makes the other rank's next collective fail instead of
 hanging."""
@@ -38,16 +39,20 @@ def _run_steps(trainer, world, rank, steps=3):
     for s in range(1, steps + 1):
         batches = [ld.batch_at((s - 1) * trainer.grad_accum + i) for i in range(trainer.grad_accum)]
         trainer.train_step(batches, s)
+    full = getattr(trainer.model, "full_named_parameters", None)
+    if full is not None:
+        return full()
     return {n: p.detach().clone() for n, p in trainer.raw_model.named_parameters()}
 
 
-def _worker(rank, world, port, out_path, strategy):
+def _worker(rank, world, port, out_path, strategy, reshard=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="60")
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from myk_llm_b200.train.trainer import Trainer
 
-    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OVERRIDES + [f"parallel.strategy={strategy}", "parallel.reshard_after_forward=false"])
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml",
+                      OVERRIDES + [f"parallel.strategy={strategy}", f"parallel.reshard_after_forward={str(reshard).lower()}"])
     tr = Trainer(cfg, DistInfo(rank, world, rank, torch.device("cpu")), build_data=False)
     params = _run_steps(tr, world, rank)
     if strategy == "fsdp":
@@ -68,11 +73,12 @@ def _single(tmp):
     return _run_steps(tr, 1, 0)
 
 
-@pytest.mark.parametrize("strategy", ["sharded", pytest.param("fsdp", marks=pytest.mark.skip(
+@pytest.mark.parametrize("strategy,reshard", [("sharded", True), ("sharded", False), ("replicated", False),
+                                              pytest.param("fsdp", False, marks=pytest.mark.skip(
     reason="torch FSDP2's sum reduction uses ReduceOp.PREMUL_SUM, which gloo does not implement"))])
-def test_world2_matches_single_process(strategy, tmp_path):
+def test_world2_matches_single_process(strategy, reshard, tmp_path):
     out = str(tmp_path / "p.pt")
-    mp.spawn(_worker, args=(2, _port(), out, strategy), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), out, strategy, reshard), nprocs=2, join=True)
     dp = torch.load(out)
     ref = _single(tmp_path)
     for n, p in ref.items():

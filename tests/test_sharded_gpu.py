@@ -1,6 +1,8 @@
-"""The sharded data-parallel runtime on 2 GPUs (peer-memory reduce-scatter fused with the
-norm, AdamW / Muon fused with the parameter all-gather) trains like one GPU on the whole
-global batch.  Skipped with fewer than 2 GPUs."""
+"""The sharded data-parallel runtime on 2 GPUs trains like one GPU on the whole global
+batch, in its three layouts: block weights row-sharded and gathered inside the GEMMs at
+every use or once per step, and every parameter replicated (the peer-memory reduce-scatter
+fused with the norm and the optimizer update in all three).  Skipped with fewer than 2
+GPUs."""
 
 import os
 import socket
@@ -32,10 +34,12 @@ def _steps(tr, world, rank, n=3):
     for s in range(1, n + 1):
         tr.train_step([ld.batch_at((s - 1) * tr.grad_accum + i) for i in range(tr.grad_accum)], s)
     torch.cuda.synchronize()
-    return {k: v.detach().float().cpu().clone() for k, v in tr.raw_model.named_parameters()}
+    full = getattr(tr.model, "full_named_parameters", None)
+    params = full() if full is not None else {k: v.detach() for k, v in tr.raw_model.named_parameters()}
+    return {k: v.float().cpu().clone() for k, v in params.items()}
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, strategy, reshard):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
     from myk_llm_b200.configuration import load_config
@@ -45,7 +49,8 @@ def _worker(rank, world, port, out):
     from myk_llm_b200.train.trainer import Trainer
 
     info = init_distributed()
-    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OV + ["parallel.strategy=sharded"])
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml",
+                      OV + [f"parallel.strategy={strategy}", f"parallel.reshard_after_forward={reshard}"])
     tr = Trainer(cfg, info, build_data=False)
     params = _steps(tr, world, rank)
     status = ext().take_status()
@@ -56,9 +61,10 @@ def _worker(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_two_gpus_matches_one(tmp_path):
+@pytest.mark.parametrize("strategy,reshard", [("sharded", "true"), ("sharded", "false"), ("replicated", "false")])
+def test_sharded_two_gpus_matches_one(strategy, reshard, tmp_path):
     out = str(tmp_path / "p.pt")
-    mp.spawn(_worker, args=(2, _port(), out), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), out, strategy, reshard), nprocs=2, join=True)
     got = torch.load(out)
     assert got["status"] == 0
     from myk_llm_b200.configuration import load_config

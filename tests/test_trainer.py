@@ -1,4 +1,4 @@
-"""Trainer on CPU: steps run, loss falls, DCP checkpoints resume
+"""Trainer on CPU (the tiny dense correctness config): steps run, loss falls, DCP checkpoints resume
 bit-exactly, incomplete checkpoints are ignored, and the portable export loads."""
 
 import json
@@ -71,3 +71,13 @@ def test_export_loads(tmp_path):
     assert (d / "model.safetensors").exists() and (d / "trainer.json").exists()
     assert json.loads((d / "trainer.json").read_text())["step"] == 6
     assert m.config.hidden_size == 256
+
+
+def test_non_finite_loss_stops_the_run(tmp_path):
+    """A non-finite loss or gradient norm is caught at the next logging sync."""
+    cfg = _cfg(tmp_path)
+    tr = Trainer(cfg, CPU)
+    with torch.no_grad():
+        next(tr.model.parameters()).fill_(float("nan"))
+    with pytest.raises(FloatingPointError, match="non-finite"):
+        tr.fit("none")
