@@ -9,8 +9,9 @@ void cast_ranges_bf16(torch::Tensor src, torch::Tensor dst, torch::Tensor src_of
                       torch::Tensor dst_offsets, int64_t total);
 int64_t take_status();
 // gemm.cu
-void gemm_gather(torch::Tensor a, torch::Tensor w, torch::Tensor d, bool b_mn, torch::Tensor src_ptrs,
-                 int64_t src_offset, int64_t rows_per_rank, int64_t rank, torch::Tensor ready, int64_t epoch);
+void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor d, bool a_mn, bool b_mn, bool accumulate,
+                 torch::Tensor gw, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
+                 torch::Tensor ready, int64_t epoch);
 void shard_gather(torch::Tensor w, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
                   torch::Tensor ready, int64_t epoch);
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch::Tensor> c, bool a_mn, bool b_mn,
@@ -83,6 +84,10 @@ void mx_gemm(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, to
              torch::Tensor d, bool accumulate);
 // gemm_skinny.cu
 void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d);
+// ngram.cu (fused hashed n-gram embedding)
+std::vector<torch::Tensor> ngram_embed_fwd(torch::Tensor tokens, std::vector<torch::Tensor> tables,
+                                           std::vector<int64_t> orders, int64_t context);
+void ngram_embed_bwd(torch::Tensor rows, torch::Tensor dout, std::vector<torch::Tensor> grads);
 // ngram.cu
 torch::Tensor ngram_stage(torch::Tensor ids, torch::Tensor W, torch::Tensor M, torch::Tensor V, torch::Tensor last,
                           int64_t step, double lr, double wd, double b1, double b2, double eps, bool rowwise,
@@ -139,6 +144,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
   m.def("ngram_stage", &mykb::ngram_stage);
+  m.def("ngram_embed_fwd", &mykb::ngram_embed_fwd, "hashed n-gram embedding: hash, gather and sum in one kernel");
+  m.def("ngram_embed_bwd", &mykb::ngram_embed_bwd, "hashed n-gram embedding backward: scatter-add per order");
   m.def("gemm_skinny", &mykb::gemm_skinny);
   m.def("mx_quantize", &mykb::mx_quantize);
   m.def("mx_gemm", &mykb::mx_gemm);

@@ -49,6 +49,7 @@ struct GatherParams {
   uint32_t target;          // counter value once this call has copied the whole chunk
   int pieces_per_chunk, rows_per_piece;
   int first_chunk, chunks;
+  int wait_b;  // 1: dst is this GEMM's B operand (the producer waits per chunk); 0: prefetch of a later GEMM's weight
 };
 
 constexpr int kGatherWarps = 4;
@@ -238,14 +239,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (skip_tile(p, mt, nt, BN)) continue;
         int kb0 = split * p.kb_per_split;
         int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
-        if (GATHER && !B_MN && !wait_rows_ready(p.g, nt * BN, nt * BN + BN, seen, p.status, __LINE__)) {
+        if (GATHER && !B_MN && p.g.wait_b && !wait_rows_ready(p.g, nt * BN, nt * BN + BN, seen, p.status, __LINE__)) {
           ok = false;
           break;
         }
         const int nkb = kb1 - kb0;
         for (int it = 0; it < nkb; ++it) {
           const int kb = GATHER ? kb0 + (it + p.rot_k) % nkb : kb0 + it;
-          if (GATHER && B_MN && !wait_rows_ready(p.g, kb * kBK, kb * kBK + kBK, seen, p.status, __LINE__)) {
+          if (GATHER && B_MN && p.g.wait_b && !wait_rows_ready(p.g, kb * kBK, kb * kBK + kBK, seen, p.status, __LINE__)) {
             ok = false;
             break;
           }
@@ -597,13 +598,18 @@ static void run_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tens
     p.symmetric = 1;
   }
   if (gather != nullptr) {
-    TORCH_CHECK(!batched && !a_mn && !out_f32 && !accumulate && !symmetric && split == 1,
-                "gemm_gather: 2-D, A K-major, bf16 D, stored product");
+    const bool store_layout = !a_mn && !out_f32 && !accumulate;  // forward / data-gradient products
+    const bool wgrad_layout = a_mn && b_mn && accumulate;        // weight-gradient products
+    TORCH_CHECK(!batched && !symmetric && (store_layout || wgrad_layout),
+                "gemm_gather: 2-D forward (A, B K-major), data-gradient (B MN-major) or weight-gradient layouts");
+    TORCH_CHECK(!gather->wait_b || (store_layout && split == 1), "gemm_gather: B can be gathered only by a stored product");
     p.g = *gather;
-    if (b_mn) {
-      p.rot_k = p.k_blocks > 0 ? gather->first_chunk % p.k_blocks : 0;  // a chunk is one 64-row K block
-    } else {
-      p.rot_n = p.tiles_n > 0 ? (gather->first_chunk * 64 / BN) % p.tiles_n : 0;
+    if (gather->wait_b) {  // start where this rank's own rows are
+      if (b_mn) {
+        p.rot_k = p.k_blocks > 0 ? gather->first_chunk % p.k_blocks : 0;  // a chunk is one 64-row K block
+      } else {
+        p.rot_n = p.tiles_n > 0 ? (gather->first_chunk * 64 / BN) % p.tiles_n : 0;
+      }
     }
   }
 
@@ -626,10 +632,12 @@ static void run_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tens
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (gather != nullptr) {
     if (BN == 128) {
-      if (b_mn) dispatch_stages<128, false, true, false, false, true>(ta, tb, td, p, grid, stream);
+      if (accumulate) dispatch_stages<128, true, true, true, true, true>(ta, tb, td, p, grid, stream);
+      else if (b_mn) dispatch_stages<128, false, true, false, false, true>(ta, tb, td, p, grid, stream);
       else dispatch_stages<128, false, false, false, false, true>(ta, tb, td, p, grid, stream);
     } else {
-      if (b_mn) dispatch_stages<256, false, true, false, false, true>(ta, tb, td, p, grid, stream);
+      if (accumulate) dispatch_stages<256, true, true, true, true, true>(ta, tb, td, p, grid, stream);
+      else if (b_mn) dispatch_stages<256, false, true, false, false, true>(ta, tb, td, p, grid, stream);
       else dispatch_stages<256, false, false, false, false, true>(ta, tb, td, p, grid, stream);
     }
     return;
@@ -655,24 +663,19 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor d, c10::optional<torch
   run_gemm(a, b, d, c, a_mn, b_mn, alpha, beta, accumulate, symmetric, nullptr);
 }
 
-// Fused all-gather + GEMM.  `w` (rows x cols bf16, local) receives the gathered weight;
-// forward (b_mn false): d = a w^T with w (N x K); data gradient (b_mn true): d = a w with
-// w (K x N).  src_ptrs: int64 [world] base addresses of every rank's bf16 shard buffer;
-// the weight's shard starts at element src_offset of each and holds rows_per_rank rows.
-// ready: int32 [ceil(rows / 64)] counters owned by `w` (zeroed once at allocation); epoch:
-// the number of gathers into `w` so far including this one.
-void gemm_gather(torch::Tensor a, torch::Tensor w, torch::Tensor d, bool b_mn, torch::Tensor src_ptrs,
-                 int64_t src_offset, int64_t rows_per_rank, int64_t rank, torch::Tensor ready, int64_t epoch) {
-  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "gemm_gather: w 2-D bf16");
-  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && src_ptrs.is_cuda(), "gemm_gather: int64 CUDA src_ptrs");
-  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.is_cuda() && ready.is_contiguous(), "gemm_gather: ready");
+static GatherParams make_gather(const torch::Tensor& w, const torch::Tensor& src_ptrs, int64_t src_offset,
+                                int64_t rows_per_rank, int64_t rank, const torch::Tensor& ready, int64_t epoch,
+                                const char* who) {
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, who, ": gathered weight 2-D bf16");
+  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && src_ptrs.is_cuda(), who, ": int64 CUDA src_ptrs");
+  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.is_cuda() && ready.is_contiguous(), who, ": ready counters");
   const int rows = w.size(0), cols = w.size(1);
   const int world = src_ptrs.numel();
-  TORCH_CHECK(cols % 8 == 0 && src_offset % 8 == 0, "gemm_gather: rows and shards must be 16-byte aligned");
-  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * world >= rows && rank >= 0 && rank < world,
-              "gemm_gather: shards do not cover the weight");
+  TORCH_CHECK(cols % 8 == 0 && src_offset % 8 == 0, who, ": rows and shards must be 16-byte aligned");
+  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * world >= rows && rank >= 0 && rank < world, who,
+              ": shards do not cover the weight");
   const int chunks = (rows + 63) / 64;
-  TORCH_CHECK(ready.numel() >= chunks, "gemm_gather: ready needs one counter per 64 rows");
+  TORCH_CHECK(ready.numel() >= chunks, who, ": ready needs one counter per 64 rows");
   GatherParams g{};
   g.src_ptrs = src_ptrs.data_ptr<int64_t>();
   g.src_offset = src_offset;
@@ -688,8 +691,25 @@ void gemm_gather(torch::Tensor a, torch::Tensor w, torch::Tensor d, bool b_mn, t
   g.pieces_per_chunk = 64 / rpp;
   g.target = (uint32_t)((uint64_t)epoch * (uint64_t)g.pieces_per_chunk);
   g.chunks = chunks;
-  g.first_chunk = (int)((rank * rows_per_rank) / 64) % std::max(1, chunks);
-  run_gemm(a, w, d, c10::nullopt, false, b_mn, 1.0, 0.0, false, false, &g);
+  g.first_chunk = chunks > 0 ? (int)((rank * rows_per_rank) / 64) % chunks : 0;
+  return g;
+}
+
+// GEMM with an all-gather fused in.  `gw` (rows x cols bf16, local) receives a row-sharded
+// weight: src_ptrs holds every rank's bf16 shard-buffer base address (int64 [world]), the
+// weight's shard starts at element src_offset of each and holds rows_per_rank rows; ready
+// are int32 counters owned by gw (one per 64 rows, zeroed once at allocation) and epoch
+// counts the gathers into gw so far including this one.  When `b` is `gw` the product
+// waits for the rows it reads (forward d = a gw^T, or data gradient d = a gw with b_mn);
+// otherwise the gather is a prefetch for a later product and `b` is any operand, in the
+// forward, data-gradient or weight-gradient layouts of `gemm`.
+void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor d, bool a_mn, bool b_mn, bool accumulate,
+                 torch::Tensor gw, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
+                 torch::Tensor ready, int64_t epoch) {
+  GatherParams g = make_gather(gw, src_ptrs, src_offset, rows_per_rank, rank, ready, epoch, "gemm_gather");
+  g.wait_b = b.data_ptr() == gw.data_ptr() ? 1 : 0;
+  TORCH_CHECK(!g.wait_b || b.sizes() == gw.sizes(), "gemm_gather: b aliases gw with another shape");
+  run_gemm(a, b, d, c10::nullopt, a_mn, b_mn, 1.0, 0.0, accumulate, false, &g);
 }
 
 // Gather only (no product): the same copy as gemm_gather's gather warps, with a grid of its
@@ -701,34 +721,10 @@ __global__ void __launch_bounds__(32 * kGatherWarps) shard_gather_kernel(const G
 
 void shard_gather(torch::Tensor w, torch::Tensor src_ptrs, int64_t src_offset, int64_t rows_per_rank, int64_t rank,
                   torch::Tensor ready, int64_t epoch) {
-  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "shard_gather: w 2-D bf16");
-  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && src_ptrs.is_cuda(), "shard_gather: int64 CUDA src_ptrs");
-  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.is_cuda() && ready.is_contiguous(), "shard_gather: ready");
-  const int rows = w.size(0), cols = w.size(1);
-  const int world = src_ptrs.numel();
-  TORCH_CHECK(cols % 8 == 0 && src_offset % 8 == 0, "shard_gather: rows and shards must be 16-byte aligned");
-  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * world >= rows && rank >= 0 && rank < world,
-              "shard_gather: shards do not cover the weight");
-  const int chunks = (rows + 63) / 64;
-  TORCH_CHECK(ready.numel() >= chunks, "shard_gather: ready needs one counter per 64 rows");
-  if (rows == 0) return;
+  GatherParams g = make_gather(w, src_ptrs, src_offset, rows_per_rank, rank, ready, epoch, "shard_gather");
+  if (g.rows == 0) return;
   c10::cuda::CUDAGuard guard(w.device());
-  GatherParams g{};
-  g.src_ptrs = src_ptrs.data_ptr<int64_t>();
-  g.src_offset = src_offset;
-  g.rows_per_rank = (int)rows_per_rank;
-  g.rows = rows;
-  g.cols = cols;
-  g.dst = (__nv_bfloat16*)w.data_ptr();
-  g.ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int>());
-  int rpp = 64;
-  while (rpp > 1 && (int64_t)rpp * cols * 2 > 16384) rpp >>= 1;
-  g.rows_per_piece = rpp;
-  g.pieces_per_chunk = 64 / rpp;
-  g.target = (uint32_t)((uint64_t)epoch * (uint64_t)g.pieces_per_chunk);
-  g.chunks = chunks;
-  g.first_chunk = (int)((rank * rows_per_rank) / 64) % chunks;
-  const int pieces = chunks * g.pieces_per_chunk;
+  const int pieces = g.chunks * g.pieces_per_chunk;
   const int blocks = std::max(1, std::min((pieces + kGatherWarps - 1) / kGatherWarps, 4 * num_sms(w.get_device())));
   shard_gather_kernel<<<blocks, 32 * kGatherWarps, 0, at::cuda::getCurrentCUDAStream()>>>(g);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -169,4 +169,149 @@ void ngram_adam(torch::Tensor ids, torch::Tensor grad, torch::Tensor W, torch::T
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------------
+// Hashed n-gram embedding, forward and backward in one kernel each.
+//
+// Row ids: for each order n (table k) and position t, the rolling hash of the n tokens
+// ending at t (tokens[t], tokens[t-1], ...; missing left context is the sentinel id):
+//   h = n;  for o in 0..n-1:  h = h * M[o % 4] + tok[t - o] + 1;  h ^= h >> 29  (wrapping
+//   int64, arithmetic shift);  row = (h mod buckets, in [0, buckets)) + k * buckets.
+// This is the bucket function of the reference model, so checkpoints' n-gram tables are
+// addressed identically.  The forward writes the sum over orders of the rows (fp32) and
+// the row ids (for the backward and for lazy tables); the backward scatter-adds the output
+// gradient into every order's gradient rows.
+// ------------------------------------------------------------------------------------
+__constant__ uint64_t kNgramMul[4] = {0x1F3D5B79A2C4E681ull, 0x0DDC0FFEEBADF00Dull, 0x1B873593CC9E2D51ull,
+                                      0x0000000100000001B3ull};
+
+constexpr int kNgramMaxOrders = 8;
+
+struct NgramTables {
+  const float* table[kNgramMaxOrders];
+  float* grad[kNgramMaxOrders];
+  int order[kNgramMaxOrders];
+  int k;
+};
+
+__device__ __forceinline__ int64_t ngram_row(const int64_t* tok, int order, int64_t buckets) {
+  int64_t h = order;
+  for (int o = 0; o < order; ++o) {
+    const uint64_t u = (uint64_t)h * kNgramMul[o & 3] + (uint64_t)tok[-o] + 1ull;
+    h = (int64_t)u;
+    h ^= h >> 29;
+  }
+  int64_t r = h % buckets;
+  return r < 0 ? r + buckets : r;
+}
+
+// One warp per position: lane 0..k-1 hash one order each, then the warp sums the rows with
+// 16-byte loads.  tokens: (batch, context + seq) with `context` columns of left context.
+__global__ void __launch_bounds__(256)
+ngram_embed_fwd_kernel(const int64_t* __restrict__ tokens, int64_t batch, int64_t seq, int context, int64_t buckets,
+                       NgramTables t, int dim, float* __restrict__ out, int64_t* __restrict__ rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = batch * seq;
+  for (int64_t pos = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; pos < n;
+       pos += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t b = pos / seq, s = pos - b * seq;
+    const int64_t* tok = tokens + b * (seq + context) + context + s;
+    int64_t my = 0;
+    if (lane < t.k) {
+      my = ngram_row(tok, t.order[lane], buckets);
+      rows[(int64_t)lane * n + pos] = my + lane * buckets;
+    }
+    const float4* src[kNgramMaxOrders];
+#pragma unroll
+    for (int j = 0; j < kNgramMaxOrders; ++j) {  // every lane takes part in every shuffle
+      const int64_t r = __shfl_sync(0xffffffff, my, j < t.k ? j : 0);
+      src[j] = j < t.k ? reinterpret_cast<const float4*>(t.table[j] + r * dim) : nullptr;
+    }
+    float4* o4 = reinterpret_cast<float4*>(out + pos * dim);
+    for (int c = lane; c < dim / 4; c += 32) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < t.k; ++j) {
+        const float4 v = src[j][c];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      o4[c] = acc;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+ngram_embed_bwd_kernel(const int64_t* __restrict__ rows, int64_t n, int64_t buckets, NgramTables t, int dim,
+                       const float* __restrict__ dout) {
+  const int64_t total = n * dim;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pos = i / dim;
+    const int c = (int)(i - pos * dim);
+    const float g = dout[i];
+    for (int j = 0; j < t.k; ++j) {
+      const int64_t r = rows[(int64_t)j * n + pos] - j * buckets;
+      atomicAdd(t.grad[j] + r * dim + c, g);
+    }
+  }
+}
+
+static NgramTables ngram_tables(const std::vector<torch::Tensor>& tabs, const std::vector<int64_t>& orders) {
+  TORCH_CHECK(!tabs.empty() && tabs.size() == orders.size() && (int)tabs.size() <= kNgramMaxOrders,
+              "ngram_embed: one table per order, at most 8");
+  NgramTables t{};
+  t.k = (int)tabs.size();
+  for (int j = 0; j < t.k; ++j) {
+    TORCH_CHECK(tabs[j].scalar_type() == at::kFloat && tabs[j].is_contiguous() && tabs[j].dim() == 2 &&
+                    tabs[j].sizes() == tabs[0].sizes(),
+                "ngram_embed: fp32 contiguous tables of one shape");
+    t.table[j] = tabs[j].data_ptr<float>();
+    t.order[j] = (int)orders[j];
+    TORCH_CHECK(orders[j] >= 1 && orders[j] <= 32, "ngram_embed: order out of range");
+  }
+  return t;
+}
+
+// tokens: (batch, context + seq) int64.  Returns (batch * seq, dim) fp32 sums and the
+// (orders, batch * seq) int64 stacked row ids.
+std::vector<torch::Tensor> ngram_embed_fwd(torch::Tensor tokens, std::vector<torch::Tensor> tables,
+                                           std::vector<int64_t> orders, int64_t context) {
+  c10::cuda::CUDAGuard guard(tokens.device());
+  TORCH_CHECK(tokens.scalar_type() == at::kLong && tokens.dim() == 2 && tokens.is_contiguous(),
+              "ngram_embed: (batch, context + seq) int64 tokens");
+  NgramTables t = ngram_tables(tables, orders);
+  const int64_t batch = tokens.size(0), seq = tokens.size(1) - context;
+  for (int j = 0; j < t.k; ++j) TORCH_CHECK(orders[j] - 1 <= context, "ngram_embed: context shorter than an order");
+  const int dim = tables[0].size(1);
+  TORCH_CHECK(dim % 4 == 0, "ngram_embed: dim must be a multiple of 4");
+  const int64_t buckets = tables[0].size(0), n = batch * seq;
+  auto out = torch::empty({n, dim}, tables[0].options());
+  auto rows = torch::empty({t.k, n}, tokens.options());
+  if (n == 0) return {out, rows};
+  const int64_t warps = n;
+  const int blocks = (int)std::min<int64_t>((warps * 32 + 255) / 256, 65535);
+  ngram_embed_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      tokens.data_ptr<int64_t>(), batch, seq, (int)context, buckets, t, dim, out.data_ptr<float>(),
+      rows.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {out, rows};
+}
+
+// Scatter-add of dout (n, dim) fp32 into every order's fp32 gradient table.
+void ngram_embed_bwd(torch::Tensor rows, torch::Tensor dout, std::vector<torch::Tensor> grads) {
+  c10::cuda::CUDAGuard guard(dout.device());
+  TORCH_CHECK(dout.scalar_type() == at::kFloat && dout.is_contiguous(), "ngram_embed_bwd: fp32 contiguous dout");
+  std::vector<int64_t> orders(grads.size(), 1);
+  NgramTables t = ngram_tables(grads, orders);
+  for (int j = 0; j < t.k; ++j) t.grad[j] = grads[j].data_ptr<float>();
+  const int64_t n = dout.size(0);
+  const int dim = dout.size(1);
+  if (n == 0) return;
+  const int64_t total = n * dim;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  ngram_embed_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      rows.data_ptr<int64_t>(), n, grads[0].size(0), t, dim, dout.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace mykb

@@ -1,9 +1,10 @@
 """Model hyper-parameters.
 
-Field names, defaults and validation rules follow the upstream schema
-(reference: ``src/myk_llm/model/config.py:17-263``) so a ``model:`` section written for
-the reference describes the same network here, and ``model.yaml`` files exported by
-either side load in the other.
+Field names and defaults are the reference's schema (``src/myk_llm/model/config.py:17-175``)
+so a ``model:`` section written for the reference describes the same network here, and
+``model.yaml`` files exported by either side load in the other; the same configurations
+are rejected (the rules are the table ``_RULES`` at the end of this file), and the
+derived layout properties keep the reference's names and meaning.
 
 Layer codes (one character per block, the pattern repeats to ``num_layers``):
 
@@ -130,92 +131,129 @@ class ModelConfig:
     cross: CrossDecoderConfig = field(default_factory=CrossDecoderConfig)
 
     def __post_init__(self) -> None:
-        self._validate()
+        for rule in _RULES:
+            problem = rule(self)
+            if problem:
+                raise ValueError(problem)
 
-    # -- validation --------------------------------------------------------------------
-    def _validate(self) -> None:
-        pattern = self.layer_pattern
-        if not pattern or any(c not in LAYER_CODES for c in pattern):
-            raise ValueError(f"layer_pattern must use only {LAYER_CODES}, got {pattern!r}")
-        att = self.attention
-        if att.num_heads % att.num_kv_heads:
-            raise ValueError("attention.num_heads must be divisible by attention.num_kv_heads")
-        ng = self.ngram
-        if any(o < 2 for o in ng.orders):
-            raise ValueError("ngram.orders must be >= 2 (order 1 is the token embedding)")
-        if ng.orders:
-            ok = bool(ng.layers) and len(set(ng.layers)) == len(ng.layers)
-            ok = ok and all(0 <= i < self.num_layers for i in ng.layers)
-            if not ok:
-                raise ValueError(f"ngram.layers must be distinct block indices in [0, {self.num_layers}), got {ng.layers}")
-        if self.mtp.layer not in (GLOBAL_ATTENTION, LOCAL_ATTENTION, DELTANET):
-            raise ValueError(f"mtp.layer must be one of {LAYER_CODES[:-1]}")
-        kinds, xs = self.layer_types, self.cross_start
-        loop = self.loop
-        if xs < self.num_layers:
-            tail_ok = set(kinds[xs:]) == {CROSS_ATTENTION} and CROSS_ATTENTION not in kinds[:xs]
-            if xs == 0 or not tail_ok:
-                raise ValueError(
-                    "cross-decoder ('X') blocks must be the last blocks after at least one other, "
-                    f"got {''.join(kinds)} (write the pattern out in full, e.g. LLLLXXXX)")
-            if loop.core and loop.prelude < xs < loop.prelude + loop.core:
-                raise ValueError(
-                    f"the loop core (blocks {loop.prelude}-{loop.prelude + loop.core - 1}) must lie "
-                    f"either before the cross-decoder or inside it (from block {xs})")
-            if self.cross.kv == "layer" and GLOBAL_ATTENTION not in kinds[:xs]:
-                raise ValueError("cross.kv=layer needs a global ('G') layer in the self-decoder")
-        if loop.core < 0 or loop.prelude < 0 or loop.prelude + loop.core > self.num_layers:
-            raise ValueError(f"need loop.core, loop.prelude >= 0 and prelude + core <= num_layers ({self.num_layers})")
-        if loop.core:
-            if loop.iterations < 1 or loop.backprop_iterations < 0:
-                raise ValueError("need loop.iterations >= 1 and loop.backprop_iterations >= 0")
-            ti = loop.train_iterations
-            if ti and (len(ti) != 2 or not 1 <= ti[0] <= ti[1]):
-                raise ValueError(f"loop.train_iterations must be [min, max] with 1 <= min <= max, got {ti}")
-            inside = range(loop.prelude + 1, loop.prelude + loop.core)
-            if ng.orders and any(i in inside for i in ng.layers):
-                raise ValueError("ngram.layers cannot point inside the loop core (except at its first block)")
-
-    # -- derived properties ------------------------------------------------------------
+    # -- derived layout (the names are the reference's public properties) ---------------
     @property
     def layer_types(self) -> list[str]:
-        p = self.layer_pattern
-        return [p[i % len(p)] for i in range(self.num_layers)]
+        """One layer code per block: the pattern repeated to ``num_layers``."""
+        reps = -(-self.num_layers // len(self.layer_pattern))
+        return list((self.layer_pattern * reps)[:self.num_layers])
 
     @property
     def cross_start(self) -> int:
-        kinds = self.layer_types
-        return kinds.index(CROSS_ATTENTION) if CROSS_ATTENTION in kinds else self.num_layers
+        """Index of the first cross-decoder block (``num_layers`` when there is none)."""
+        return "".join(self.layer_types).find(CROSS_ATTENTION) % (self.num_layers + 1)
 
     @property
     def cross_kv_layer(self) -> int | None:
-        xs = self.cross_start
-        if xs == self.num_layers or self.cross.kv != "layer":
+        """The self-decoder block whose keys / values the cross-decoder reuses
+        (``cross.kv == "layer"``): the last global block before the cross-decoder."""
+        start = self.cross_start
+        if start == self.num_layers or self.cross.kv != "layer":
             return None
-        return max(i for i, t in enumerate(self.layer_types[:xs]) if t == GLOBAL_ATTENTION)
+        return "".join(self.layer_types[:start]).rfind(GLOBAL_ATTENTION)
+
+    def rotates(self, block: int) -> bool:
+        """Whether the attention of a G / L block applies RoPE: local blocks always; global
+        blocks by ``attention.global_rope`` (all, only the first global block, or none)."""
+        kind = self.layer_types[block]
+        if kind == LOCAL_ATTENTION:
+            return True
+        mode = self.attention.global_rope
+        return mode == "all" or (mode == "first" and block == "".join(self.layer_types).find(GLOBAL_ATTENTION))
 
     @property
     def cross_rope(self) -> bool:
-        mode = self.attention.global_rope
-        globals_ = [i for i, t in enumerate(self.layer_types) if t == GLOBAL_ATTENTION]
+        """Whether the shared keys (and so the cross-decoder queries) are rotated: as the
+        source block when the KV comes from a layer, else as a first global block would be
+        (rotated under "first" only when the model has no global block at all)."""
         src = self.cross_kv_layer
-        is_first = (src == globals_[0]) if src is not None else not globals_
-        return mode == "all" or (mode == "first" and is_first)
+        if src is not None:
+            return self.rotates(src)
+        mode = self.attention.global_rope
+        return mode == "all" or (mode == "first" and GLOBAL_ATTENTION not in self.layer_types)
 
     @property
     def effective_layers(self) -> int:
+        """Blocks run per forward pass at the default iteration count."""
         return self.num_layers + self.loop.core * (self.loop.iterations - 1)
 
     @property
     def layout(self) -> str:
-        kinds, loop = "".join(self.layer_types), self.loop
-        if not loop.core:
-            return kinds
-        end = loop.prelude + loop.core
-        return f"{kinds[:loop.prelude]}({kinds[loop.prelude:end]})x{loop.iterations}{kinds[end:]}"
+        """Layer codes with the looped core marked, e.g. ``D(GD)x4G``."""
+        codes, lp = "".join(self.layer_types), self.loop
+        if not lp.core:
+            return codes
+        a, b = lp.prelude, lp.prelude + lp.core
+        return f"{codes[:a]}({codes[a:b]})x{lp.iterations}{codes[b:]}"
 
     @property
     def ffn_hidden_size(self) -> int:
-        raw = int(self.hidden_size * self.ffn.multiplier)
-        m = self.ffn.multiple_of
-        return m * ((raw + m - 1) // m)
+        """``hidden_size * ffn.multiplier`` rounded up to a multiple of ``ffn.multiple_of``."""
+        raw, unit = int(self.hidden_size * self.ffn.multiplier), self.ffn.multiple_of
+        return -(-raw // unit) * unit
+
+
+# -- validation rules: each returns an error message or None ----------------------------
+def _rule_pattern(c: ModelConfig):
+    if not c.layer_pattern or not set(c.layer_pattern) <= set(LAYER_CODES):
+        return f"layer_pattern must use only {LAYER_CODES}, got {c.layer_pattern!r}"
+
+
+def _rule_heads(c: ModelConfig):
+    if c.attention.num_heads % c.attention.num_kv_heads:
+        return "attention.num_heads must be divisible by attention.num_kv_heads"
+
+
+def _rule_ngram(c: ModelConfig):
+    ng = c.ngram
+    if min(ng.orders, default=2) < 2:
+        return "ngram.orders must be >= 2 (order 1 is the token embedding)"
+    if ng.orders and not (ng.layers and len(set(ng.layers)) == len(ng.layers)
+                          and all(0 <= i < c.num_layers for i in ng.layers)):
+        return f"ngram.layers must be distinct block indices in [0, {c.num_layers}), got {ng.layers}"
+
+
+def _rule_mtp(c: ModelConfig):
+    if c.mtp.layer not in (GLOBAL_ATTENTION, LOCAL_ATTENTION, DELTANET):
+        return f"mtp.layer must be one of {LAYER_CODES[:-1]}"
+
+
+def _rule_loop_bounds(c: ModelConfig):
+    lp = c.loop
+    if min(lp.core, lp.prelude) < 0 or lp.prelude + lp.core > c.num_layers:
+        return f"need loop.core, loop.prelude >= 0 and prelude + core <= num_layers ({c.num_layers})"
+    if not lp.core:
+        return None
+    if lp.iterations < 1 or lp.backprop_iterations < 0:
+        return "need loop.iterations >= 1 and loop.backprop_iterations >= 0"
+    ti = lp.train_iterations
+    if ti and not (len(ti) == 2 and 1 <= ti[0] <= ti[1]):
+        return f"loop.train_iterations must be [min, max] with 1 <= min <= max, got {ti}"
+    # a core block after the first runs on the loop state, which has no single input to
+    # inject into; the first core block's injection joins the loop input
+    if c.ngram.orders and any(lp.prelude < i < lp.prelude + lp.core for i in c.ngram.layers):
+        return "ngram.layers cannot point inside the loop core (except at its first block)"
+
+
+def _rule_cross(c: ModelConfig):
+    codes = "".join(c.layer_types)
+    start = c.cross_start
+    if start == c.num_layers:
+        return None
+    if start == 0 or codes[start:].strip(CROSS_ATTENTION):
+        return ("cross-decoder ('X') blocks must be the last blocks after at least one other, "
+                f"got {codes} (write the pattern out in full, e.g. LLLLXXXX)")
+    lp = c.loop
+    if lp.core and lp.prelude < start < lp.prelude + lp.core:
+        return (f"the loop core (blocks {lp.prelude}-{lp.prelude + lp.core - 1}) must lie either before the "
+                f"cross-decoder or inside it (from block {start})")
+    if c.cross.kv == "layer" and GLOBAL_ATTENTION not in codes[:start]:
+        return "cross.kv=layer needs a global ('G') layer in the self-decoder"
+
+
+_RULES = (_rule_pattern, _rule_heads, _rule_ngram, _rule_mtp, _rule_cross, _rule_loop_bounds)

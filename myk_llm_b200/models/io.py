@@ -1,8 +1,9 @@
-"""Portable model directory: ``model.safetensors`` + ``model.yaml`` (+ tokenizer files).
+"""Portable model directories: ``model.safetensors`` + ``model.yaml`` (+ tokenizer files).
 
-The layout is the reference's (``src/myk_llm/model/io.py:23-61``) so exported models
-load on either side: the tied ``lm_head.weight`` is dropped when embeddings are tied, and
-loading is non-strict only for that key.
+The directory layout is an interface shared with the reference
+(``src/myk_llm/model/io.py:23-61``): a model exported by either framework loads in the
+other.  With tied embeddings the output head is the token embedding, so
+``lm_head.weight`` is not written and is the only key a load may find missing.
 """
 
 from __future__ import annotations
@@ -19,38 +20,64 @@ from .transformer import MykLLM
 
 WEIGHTS_FILE = "model.safetensors"
 CONFIG_FILE = "model.yaml"
+TIED_KEY = "lm_head.weight"
+
+
+class ModelDirectory:
+    """One exported model on disk."""
+
+    def __init__(self, path) -> None:
+        self.path = Path(path)
+
+    @property
+    def weights(self) -> Path:
+        return self.path / WEIGHTS_FILE
+
+    @property
+    def config_file(self) -> Path:
+        return self.path / CONFIG_FILE
+
+    def write(self, config: ModelConfig, tensors: dict[str, torch.Tensor], tokenizer: str | None = None) -> None:
+        self.path.mkdir(parents=True, exist_ok=True)
+        host = {name: t.detach().cpu().contiguous() for name, t in tensors.items()
+                if not (config.tie_embeddings and name == TIED_KEY)}
+        save_file(host, str(self.weights))
+        self.config_file.write_text(yaml.safe_dump(to_dict(config), sort_keys=False), encoding="utf-8")
+        if tokenizer:
+            from transformers import AutoTokenizer
+
+            AutoTokenizer.from_pretrained(tokenizer).save_pretrained(str(self.path))
+
+    def config(self) -> ModelConfig:
+        return from_dict(ModelConfig, yaml.safe_load(self.config_file.read_text(encoding="utf-8")))
+
+    def tensors(self) -> dict[str, torch.Tensor]:
+        return load_file(str(self.weights))
+
+    def instantiate(self, device="cuda", max_seq_len: int | None = None) -> MykLLM:
+        cfg = self.config()
+        if max_seq_len is not None:
+            cfg.max_seq_len = max_seq_len
+        model = MykLLM(cfg).to(device)
+        result = model.load_state_dict(self.tensors(), strict=False)
+        missing = set(result.missing_keys) - ({TIED_KEY} if cfg.tie_embeddings else set())
+        if missing or result.unexpected_keys:
+            raise KeyError(f"weight mismatch loading {self.path}: missing={sorted(missing)} "
+                           f"unexpected={result.unexpected_keys}")
+        return model.eval()
 
 
 def save_model(directory, config: ModelConfig, state_dict: dict[str, torch.Tensor], tokenizer: str | None = None):
-    directory = Path(directory)
-    directory.mkdir(parents=True, exist_ok=True)
-    tensors = {k: t.detach().to("cpu").contiguous() for k, t in state_dict.items()}
-    if config.tie_embeddings:
-        tensors.pop("lm_head.weight", None)
-    save_file(tensors, str(directory / WEIGHTS_FILE))
-    (directory / CONFIG_FILE).write_text(yaml.safe_dump(to_dict(config), sort_keys=False), encoding="utf-8")
-    if tokenizer:
-        from transformers import AutoTokenizer
-
-        AutoTokenizer.from_pretrained(tokenizer).save_pretrained(str(directory))
+    ModelDirectory(directory).write(config, state_dict, tokenizer)
 
 
 def load_model_config(directory) -> ModelConfig:
-    tree = yaml.safe_load((Path(directory) / CONFIG_FILE).read_text(encoding="utf-8"))
-    return from_dict(ModelConfig, tree)
+    return ModelDirectory(directory).config()
 
 
 def load_state_dict(directory) -> dict[str, torch.Tensor]:
-    return load_file(str(Path(directory) / WEIGHTS_FILE))
+    return ModelDirectory(directory).tensors()
 
 
 def load_model(directory, device="cuda", max_seq_len: int | None = None) -> MykLLM:
-    config = load_model_config(directory)
-    if max_seq_len is not None:
-        config.max_seq_len = max_seq_len
-    model = MykLLM(config).to(device)
-    missing, unexpected = model.load_state_dict(load_state_dict(directory), strict=False)
-    missing = [k for k in missing if not (config.tie_embeddings and k == "lm_head.weight")]
-    if missing or unexpected:
-        raise KeyError(f"weight mismatch loading {directory}: missing={missing} unexpected={unexpected}")
-    return model.eval()
+    return ModelDirectory(directory).instantiate(device, max_seq_len)

@@ -97,28 +97,29 @@ class Block(nn.Module):
             return checkpoint(Block._forward, self, x, position_ids, varlen, state, False, use_reentrant=False)
         return self._forward(x, position_ids, varlen, state, use_cache)
 
-    def _forward(self, x, position_ids, varlen, state, use_cache):
+    def _enter(self, x):
+        """(residual stream, normed mixer input): a pending FFN output from the previous
+        block is added here, in the same kernel as this block's pre-norm."""
         if isinstance(x, PendingResidual):
-            cdt = ops.compute_dtype(x.base)
-            x, h = ops.add_rms_norm(x.base, x.delta, self.mixer_norm.weight, self.mixer_norm.eps, out_dtype=cdt)
-        else:
-            cdt = ops.compute_dtype(x)
-            h = self.mixer_norm(x, out_dtype=cdt)
-        if self.ffn_norm is None:
+            return ops.add_rms_norm(x.base, x.delta, self.mixer_norm.weight, self.mixer_norm.eps,
+                                    out_dtype=ops.compute_dtype(x.base))
+        return x, self.mixer_norm(x, out_dtype=ops.compute_dtype(x))
+
+    def _forward(self, x, position_ids, varlen, state, use_cache):
+        x, h = self._enter(x)
+        if self.ffn_norm is None:  # parallel block: one norm, both branches read it
             (update, state), f = self._parallel(h, position_ids, varlen, state, use_cache)
-            x = self.mixer_gate(x, update, h)
-            return self.ffn_gate(x, f, h), state
+            return self.ffn_gate(self.mixer_gate(x, update, h), f, h), state
         update, state = self.mixer(h, position_ids, varlen, state, use_cache)
-        if self.mixer_gate.kind == "none":
-            x, h = ops.add_rms_norm(x, update, self.ffn_norm.weight, self.ffn_norm.eps, out_dtype=cdt)
+        if self.mixer_gate.kind == "none":  # residual add fused with the FFN pre-norm
+            x, h = ops.add_rms_norm(x, update, self.ffn_norm.weight, self.ffn_norm.eps, out_dtype=h.dtype)
         else:
             x = self.mixer_gate(x, update, h)
-            h = self.ffn_norm(x, out_dtype=cdt)
+            h = self.ffn_norm(x, out_dtype=ops.compute_dtype(x))
         f = self.ffn(h)
         if self.defer_residual and self.ffn_gate.kind == "none":
-            return PendingResidual(x, f), state
-        x = self.ffn_gate(x, f, h)
-        return x, state
+            return PendingResidual(x, f), state  # the next norm adds it
+        return self.ffn_gate(x, f, h), state
 
     def side_stream(self, device: torch.device) -> torch.cuda.Stream:
         s = self.__dict__.get("_side_stream")
@@ -220,6 +221,90 @@ def build_varlen(seqlens: list[torch.Tensor], batch: int, seq_len: int, device: 
     return Varlen(cu_seqlens=cu, max_seqlen=seq_len, cu_seqlens_cpu=cu_cpu)
 
 
+class _Pass:
+    """One forward pass's walk over the blocks.
+
+    Cache layout (what ``use_cache`` returns and ``cache`` must match): one entry per
+    self-decoder block call in execution order (the looped core contributes one entry per
+    block per iteration), then the projected shared KV (``cross.kv = project``), then one
+    empty entry per cross-decoder block.  The cross-decoder reads the shared KV (projected,
+    or the state of block ``cross_kv_layer``) and keeps no state of its own.
+    """
+
+    def __init__(self, model: "MykLLM", positions, varlen, cache, use_cache: bool, injections: dict, iterations: int):
+        cfg = model.config
+        self.model, self.positions, self.varlen, self.use_cache = model, positions, varlen, use_cache
+        self.injections, self.iterations, self.loop = injections, iterations, cfg.loop
+        n, start = len(model.layers), model.cross_start
+        self.has_cross = start < n
+        # a loop whose core lies in the cross-decoder repeats stateless cross blocks only
+        self.core_in_cross = bool(self.loop.core) and self.loop.prelude >= start
+        repeated = 0 if self.core_in_cross else self.loop.core * (iterations - 1)
+        calls = n + repeated + (model.shared_kv is not None)
+        if cache is not None and len(cache) != calls:
+            raise ValueError(f"cache has {len(cache)} entries but this pass runs {calls} blocks "
+                             "(iteration count changed?)")
+        self.states = iter(cache) if cache is not None else None
+        self.new_cache: list[Any] | None = [] if use_cache else None
+        self.shared: Any = None
+
+    def _state(self):
+        return next(self.states) if self.states is not None else None
+
+    def _keep(self, state) -> None:
+        if self.new_cache is not None:
+            self.new_cache.append(state)
+
+    def _inject(self, i: int, x):
+        update = self.injections.get(i)
+        if update is None:
+            return x
+        x = materialize(x)
+        return x + update[:, -x.shape[1]:]
+
+    def self_block(self, i: int, x):
+        with nvtx_range(f"layer{i}"):
+            x, state = self.model.layers[i](x, self.positions, self.varlen, self._state(), self.use_cache)
+        self._keep(state)
+        if i == self.model.cross_kv_layer:
+            self.shared = state
+        return x
+
+    def cross_block(self, i: int, x):
+        with nvtx_range(f"layer{i}"):
+            return self.model.layers[i](x, self.positions, self.varlen, self.shared)[0]
+
+    def _span(self, lo: int, hi: int, call, looped: bool, x):
+        """Blocks [lo, hi) with n-gram injections; the loop core in it runs looped."""
+        core_lo, core_hi = (self.loop.prelude, self.loop.prelude + self.loop.core) if looped else (hi, hi)
+        for i in range(lo, core_lo):
+            x = call(i, self._inject(i, x))
+        if looped:
+            x = self.model._run_core(materialize(self._inject(core_lo, x)), call, self.iterations)
+        for i in range(core_hi, hi):
+            x = call(i, self._inject(i, x))
+        return x
+
+    def self_decoder(self, x):
+        looped = bool(self.loop.core) and not self.core_in_cross
+        return self._span(0, self.model.cross_start, self.self_block, looped, x)
+
+    def cross_decoder(self, x, keep_last: int):
+        """Shared KV from the full self-decoder output, then the cross blocks on the last
+        ``keep_last`` positions (all of them when 0)."""
+        model = self.model
+        full_x, full_pos = x, self.positions
+        if model.shared_kv is not None:
+            self.shared = model.shared_kv(full_x, full_pos, self._state())
+            self._keep(self.shared)
+        for _ in range(model.cross_start, len(model.layers)):
+            self._state()
+            self._keep(None)
+        if keep_last:
+            x, self.positions = x[:, -keep_last:], self.positions[:, -keep_last:]
+        return self._span(model.cross_start, len(model.layers), self.cross_block, self.core_in_cross, x)
+
+
 class MykLLM(nn.Module):
     def __init__(self, config: ModelConfig) -> None:
         super().__init__()
@@ -295,76 +380,27 @@ class MykLLM(nn.Module):
         bsz, seq = input_ids.shape
         if position_ids is None:
             position_ids = torch.arange(seq, device=input_ids.device).expand(bsz, -1)
-        varlen = None
-        if seqlens is not None:
-            if use_cache or keep_last:
-                raise ValueError("document masking (seqlens) cannot be combined with a cache or keep_last")
-            varlen = build_varlen(seqlens, bsz, seq, input_ids.device)
-        x, ngram_updates = self.embed(input_ids, prefix_ids)
+        if seqlens is not None and (use_cache or keep_last):
+            raise ValueError("document masking (seqlens) cannot be combined with a cache or keep_last")
+        varlen = build_varlen(seqlens, bsz, seq, input_ids.device) if seqlens is not None else None
+        x, injections = self.embed(input_ids, prefix_ids)
         if embed_offset is not None:
             x = x + embed_offset
-        loop, xs, n_layers = self.config.loop, self.cross_start, len(self.layers)
-        iterations = self.num_iterations(iterations)
-        cross_loop = bool(loop.core) and loop.prelude >= xs
-        self_core = 0 if cross_loop else loop.core
-        n_calls = n_layers + self_core * (iterations - 1) + (self.shared_kv is not None)
-        if cache is not None and len(cache) != n_calls:
-            raise ValueError(f"cache has {len(cache)} entries but this pass runs {n_calls} blocks (iteration count changed?)")
-        states = iter(cache if cache is not None else [None] * n_calls)
-        new_cache: list[Any] | None = [] if use_cache else None
-        shared: Any = None
-
-        def run(i, x):
-            nonlocal shared
-            with nvtx_range(f"layer{i}"):
-                x, st = self.layers[i](x, position_ids, varlen, next(states), use_cache)
-            if new_cache is not None:
-                new_cache.append(st)
-            if i == self.cross_kv_layer:
-                shared = st
-            return x
-
-        def cross(i, x):
-            return self.layers[i](x, position_ids, varlen, shared)[0]
-
-        def enter(i, x):
-            if i in ngram_updates:
-                x = materialize(x)
-                return x + ngram_updates[i][:, -x.size(1):]
-            return x
-
-        def stack(start, end, block, looped, x):
-            core_start = loop.prelude if looped else end
-            for i in range(start, core_start):
-                x = block(i, enter(i, x))
-            if looped:
-                x = self._run_core(materialize(enter(core_start, x)), block, iterations)
-            for i in range(core_start + loop.core if looped else end, end):
-                x = block(i, enter(i, x))
-            return x
-
-        x = stack(0, xs, run, bool(self_core), x)
-        if keep_last or xs < n_layers:
+        run = _Pass(self, position_ids, varlen, cache, use_cache, injections, self.num_iterations(iterations))
+        x = run.self_decoder(x)
+        if keep_last or run.has_cross:
             x = materialize(x)
-        self_out, self_pos = x, position_ids
-        if keep_last:
-            x, position_ids = x[:, -keep_last:], position_ids[:, -keep_last:]
-        if xs < n_layers:
-            if self.shared_kv is not None:
-                shared = self.shared_kv(self_out, self_pos, next(states))
-                if new_cache is not None:
-                    new_cache.append(shared)
-            for _ in range(xs, n_layers):
-                next(states)
-                if new_cache is not None:
-                    new_cache.append(None)
-            x = stack(xs, n_layers, cross, cross_loop, x)
+        if run.has_cross:
+            x = run.cross_decoder(x, keep_last)
+        elif keep_last:
+            x = x[:, -keep_last:]
+        positions = position_ids[:, -keep_last:] if keep_last else position_ids
         if isinstance(x, PendingResidual):
             x, hidden = ops.add_rms_norm(x.base, x.delta, self.final_norm.weight, self.final_norm.eps,
                                          out_dtype=ops.compute_dtype(x.base))
         else:
             hidden = self.final_norm(x, out_dtype=ops.compute_dtype(x))
-        out = ModelOutput(hidden, x, position_ids, varlen, new_cache)
+        out = ModelOutput(hidden, x, positions, varlen, run.new_cache)
         return head(self, out) if head is not None else out
 
     def num_iterations(self, iterations: int | None = None) -> int:

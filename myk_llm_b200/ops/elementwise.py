@@ -257,12 +257,14 @@ def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 def ngram_lookup(tokens, tables, orders, context, num_buckets):
-    """Sum over orders of table_k[hash_k(tokens)] -> (batch, seq, dim)."""
-    from ..models.embeddings import ngram_bucket_ids
+    """Sum over orders of ``table_k[hash_k(tokens)]`` -> (batch, seq, dim); ``tokens`` carries
+    ``context`` columns of left context.  CUDA: the fused hash + gather + sum kernel."""
+    from ..models.embeddings import _NgramEmbed, ngram_bucket_ids
 
+    if tokens.is_cuda:
+        return _NgramEmbed.apply(tokens, context, tuple(orders), *tables)
     total = None
-    for k, (n, table) in enumerate(zip(orders, tables)):
-        ids = ngram_bucket_ids(tokens, n, context, num_buckets)
-        rows = embedding(ids, table)
+    for n, table in zip(orders, tables):
+        rows = F.embedding(ngram_bucket_ids(tokens, n, context, num_buckets), table)
         total = rows if total is None else total + rows
     return total

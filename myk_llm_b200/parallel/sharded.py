@@ -94,6 +94,26 @@ class GatherBuffer:
         self.holder: tuple[int, int] | None = None
 
 
+class UseTrace:
+    """Order in which row-sharded weights are used by forward products, recorded over one
+    optimizer step and replayed as prefetch hints in the next (a wrong hint only costs a
+    gather: every use checks what its buffer holds)."""
+
+    def __init__(self) -> None:
+        self.previous: list["ShardedWeight"] = []
+        self.current: list["ShardedWeight"] = []
+
+    def next_after(self, w: "ShardedWeight") -> "ShardedWeight | None":
+        pos = len(self.current)
+        self.current.append(w)
+        if pos + 1 < len(self.previous) and self.previous[pos] is w:
+            return self.previous[pos + 1]
+        return None
+
+    def end_step(self) -> None:
+        self.previous, self.current = self.current, []
+
+
 class ShardedWeight:
     """Run-time handle of one row-sharded weight, attached to its parameter as
     ``_mykb_shard``; ``ops.linear`` routes the parameter's products through it."""
@@ -113,31 +133,55 @@ class ShardedWeight:
         return self.buf.holder == self._key()
 
     def _gather_args(self):
+        """Arguments of a gather into this weight's buffer; marks the buffer as holding it
+        (every later use is ordered after the gather on the stream)."""
         rt, s = self.rt, self.slot
         self.buf.epoch += 1
         self.buf.holder = self._key()
-        return rt.bf16_ptrs, s.boff, s.rows_per_rank, rt.rank, self.buf.ready, self.buf.epoch
+        return self.buf.w, rt.bf16_ptrs, s.boff, s.rows_per_rank, rt.rank, self.buf.ready, self.buf.epoch
+
+    def can_prefetch_during(self, other: "ShardedWeight") -> bool:
+        return self is not other and not self.holds() and self.buf is not other.buf
 
     def forward_gemm(self, x2: torch.Tensor) -> torch.Tensor:
-        """y = x W^T, gathering W inside the GEMM unless the buffer already holds it."""
-        if self.holds():
-            return ops.gemm(x2, self.buf.w)
+        """y = x W^T.  W not gathered yet: the GEMM gathers it and waits per 64 rows.  W
+        gathered: the GEMM's gather warps prefetch the weight the next forward product
+        uses (learned from the previous step's order of uses)."""
+        rt = self.rt
+        nxt = rt.trace.next_after(self)
         y = torch.empty(x2.shape[0], self.rows, dtype=torch.bfloat16, device=x2.device)
-        ops.ext().gemm_gather(x2, self.buf.w, y, False, *self._gather_args())
+        if not self.holds():
+            ops.ext().gemm_gather(x2, self.buf.w, y, False, False, False, *self._gather_args())
+        elif nxt is not None and nxt.can_prefetch_during(self):
+            ops.ext().gemm_gather(x2, self.buf.w, y, False, False, False, *nxt._gather_args())
+        else:
+            ops.gemm(x2, self.buf.w, out=y)
         return y
 
-    def dgrad_gemm(self, dy2: torch.Tensor) -> torch.Tensor:
-        """dx = dy W, gathering W inside the GEMM unless the buffer already holds it."""
-        if self.holds():
-            return ops.gemm(dy2, self.buf.w, b_major="mn")
+    def backward_gemms(self, dy2: torch.Tensor, x2: torch.Tensor, main_grad: torch.Tensor | None,
+                       need_dx: bool) -> torch.Tensor | None:
+        """Weight gradient (accumulated into ``main_grad``) and data gradient ``dy W``.  If W
+        was released since the forward, the weight-gradient GEMM, which does not need W,
+        gathers it with its spare warps, so the data-gradient GEMM finds it local."""
+        ext = ops.ext()
+        if main_grad is not None:
+            if not self.holds() and need_dx:
+                ext.gemm_gather(dy2, x2, main_grad, True, True, True, *self._gather_args())
+            else:
+                ops.gemm(dy2, x2, a_major="mn", b_major="mn", out=main_grad, accumulate=True)
+        if not need_dx:
+            return None
         dx = torch.empty(dy2.shape[0], self.cols, dtype=torch.bfloat16, device=dy2.device)
-        ops.ext().gemm_gather(dy2, self.buf.w, dx, True, *self._gather_args())
+        if self.holds():
+            ops.gemm(dy2, self.buf.w, b_major="mn", out=dx)
+        else:
+            ext.gemm_gather(dy2, self.buf.w, dx, False, True, False, *self._gather_args())
         return dx
 
     def full(self) -> torch.Tensor:
         """The whole bf16 weight (gathered by the standalone kernel if needed)."""
         if not self.holds():
-            ops.ext().shard_gather(self.buf.w, *self._gather_args())
+            ops.ext().shard_gather(*self._gather_args())
         return self.buf.w
 
     # -- CPU (gloo) --------------------------------------------------------------------
@@ -186,13 +230,12 @@ class _ShardedLinear(torch.autograd.Function):
         if dy2.dtype != torch.bfloat16:
             dy2 = dy2.to(torch.bfloat16)
         dy2 = dy2.contiguous()
-        dx = None
-        if ctx.needs_input_grad[0]:
-            dx = shard.dgrad_gemm(dy2).view(ctx.x_shape)
+        main = w.main_grad if ctx.needs_input_grad[1] else None
+        dx = shard.backward_gemms(dy2, x2, main, ctx.needs_input_grad[0])
+        if dx is not None:
+            dx = dx.view(ctx.x_shape)
             if ctx.x_dtype != torch.bfloat16:
                 dx = dx.to(ctx.x_dtype)
-        if ctx.needs_input_grad[1]:
-            ops.gemm(dy2, x2, a_major="mn", b_major="mn", out=w.main_grad, accumulate=True)
         return dx, None, None
 
 
@@ -240,6 +283,7 @@ class ShardedDataParallel(nn.Module):
         self.last_norm = torch.zeros((), device=info.device)
         self.slots: list[Slot] = []
         self._linear_weights = {id(m.weight) for m in model.modules() if type(m) is nn.Linear}
+        self.trace = UseTrace()
 
     # -- module plumbing ----------------------------------------------------------------
     def forward(self, *args, **kwargs):
@@ -493,6 +537,7 @@ class ShardedDataParallel(nn.Module):
         self.step_count += 1
         norm = self._step_cuda(grad_clip) if self.cuda else self._step_reference(grad_clip)
         self.version += 1
+        self.trace.end_step()
         return norm
 
     def _step_cuda(self, grad_clip: float) -> torch.Tensor:

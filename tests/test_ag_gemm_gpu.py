@@ -55,7 +55,7 @@ def test_gather_gemm_one_gpu_emulated_ranks(world, m, n, k):
             x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
             y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
             full.fill_(float("nan"))  # every element must come from the shards
-            ext().gemm_gather(x, full, y, False, ptrs, 16, r, rank, ready, epoch)
+            ext().gemm_gather(x, full, y, False, False, False, full, ptrs, 16, r, rank, ready, epoch)
             torch.cuda.synchronize()
             assert ext().take_status() == 0
             assert torch.equal(full, w)
@@ -65,7 +65,7 @@ def test_gather_gemm_one_gpu_emulated_ranks(world, m, n, k):
             dy = torch.randn(m, n, device="cuda", generator=g).bfloat16()
             dx = torch.empty(m, k, dtype=torch.bfloat16, device="cuda")
             full.fill_(float("nan"))
-            ext().gemm_gather(dy, full, dx, True, ptrs, 16, r, rank, ready, epoch)
+            ext().gemm_gather(dy, full, dx, False, True, False, full, ptrs, 16, r, rank, ready, epoch)
             torch.cuda.synchronize()
             assert ext().take_status() == 0
             assert torch.equal(full, w)
@@ -74,6 +74,45 @@ def test_gather_gemm_one_gpu_emulated_ranks(world, m, n, k):
         ext().shard_gather(full, ptrs, 16, r, rank, ready, 5)
         torch.cuda.synchronize()
         assert torch.equal(full, w)
+    del bufs
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_gather_as_prefetch_inside_unrelated_products(world):
+    """The gather warps fill another weight's buffer while the GEMM multiplies operands
+    that do not depend on it: forward, data-gradient and weight-gradient layouts."""
+    from myk_llm_b200.ops import ext
+
+    g = torch.Generator(device="cuda").manual_seed(world)
+    w = (torch.randn(2816, 1024, device="cuda", generator=g) * 0.05).bfloat16()
+    bufs, ptrs, r = _shards(w, world)
+    full = torch.empty_like(w)
+    ready = torch.zeros((w.shape[0] + 63) // 64, dtype=torch.int32, device="cuda")
+    m, n, k = 2048, 1536, 1024
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    b = (torch.randn(n, k, device="cuda", generator=g) * 0.05).bfloat16()
+    epoch = 0
+    for layout in ("fwd", "dgrad", "wgrad"):
+        epoch += 1
+        full.zero_()
+        if layout == "fwd":
+            d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            ext().gemm_gather(x, b, d, False, False, False, full, ptrs, 16, r, 1 % world, ready, epoch)
+            ref = x.float() @ b.float().t()
+        elif layout == "dgrad":
+            dy = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+            d = torch.empty(m, k, dtype=torch.bfloat16, device="cuda")
+            ext().gemm_gather(dy, b, d, False, True, False, full, ptrs, 16, r, 1 % world, ready, epoch)
+            ref = dy.float() @ b.float()
+        else:
+            dy = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+            d = torch.ones(n, k, dtype=torch.float32, device="cuda")
+            ext().gemm_gather(dy, x, d, True, True, True, full, ptrs, 16, r, 1 % world, ready, epoch)
+            ref = 1.0 + dy.float().t() @ x.float()
+        torch.cuda.synchronize()
+        assert ext().take_status() == 0
+        assert torch.equal(full, w), layout
+        _close(d, ref)
     del bufs
 
 
@@ -115,12 +154,12 @@ def _worker(rank, world, port, out):
         full = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
         ready = torch.zeros((n + 63) // 64, dtype=torch.int32, device=dev)
         y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        ext().gemm_gather(x, full, y, False, ptrs, 0, r, rank, ready, 1)
+        ext().gemm_gather(x, full, y, False, False, False, full, ptrs, 0, r, rank, ready, 1)
         dy = torch.randn(m, n, device=dev, generator=gx).bfloat16()
         dx = torch.empty(m, k, dtype=torch.bfloat16, device=dev)
         full2 = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
         ready2 = torch.zeros_like(ready)
-        ext().gemm_gather(dy, full2, dx, True, ptrs, 0, r, rank, ready2, 1)
+        ext().gemm_gather(dy, full2, dx, False, True, False, full2, ptrs, 0, r, rank, ready2, 1)
         # the unfused baseline: NCCL all-gather of the padded shards, then the GEMM
         gathered = torch.empty(world * r * k, dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(gathered, shard[:r * k].clone())

@@ -305,3 +305,34 @@ def test_split_cols_and_strided_linear():
     _close(y, yr, 1e-2)
     _close(xs.grad, xr.grad, 2e-2)
     _close(w.grad, wr.grad, 2e-2)
+
+
+def test_fused_ngram_embedding_matches_statement():
+    """Hash + gather + sum in one kernel: the same rows as the integer-op statement of the
+    bucket function, the same sums, and the scatter-add backward into every order's
+    gradient rows (also with left context from a prefix)."""
+    import torch.nn as nn
+
+    from myk_llm_b200.models.embeddings import NgramEmbedding
+    from myk_llm_b200.models.config import NgramEmbeddingConfig
+
+    torch.manual_seed(0)
+    cfg = NgramEmbeddingConfig(orders=[2, 3, 4], num_buckets=1000, dim=64, layers=[0])
+    emb = NgramEmbedding(cfg, vocab_size=500, hidden_size=64).cuda()
+    for t in emb.tables:
+        nn.init.normal_(t.weight)
+    ids = torch.randint(0, 500, (3, 37), device="cuda")
+    prefix = torch.randint(0, 500, (3, 2), device="cuda")
+    for pre in (None, prefix):
+        got = emb.lookup(ids, pre)
+        rows = emb.row_ids(ids, pre)
+        want = sum(emb.tables[k].weight[rows[k] - k * cfg.num_buckets] for k in range(3))
+        assert torch.equal(got, want)
+        g = torch.randn_like(got)
+        for t in emb.tables:
+            t.weight.grad = None
+        got.backward(g)
+        for k, t in enumerate(emb.tables):
+            ref = torch.zeros_like(t.weight).index_add_(0, (rows[k] - k * cfg.num_buckets).reshape(-1),
+                                                        g.reshape(-1, 64))
+            assert torch.allclose(t.weight.grad, ref, atol=1e-5)
