@@ -1,64 +1,98 @@
-"""Chat or plain text completion with an exported model directory.
+"""Chat (or plain continuation) with an exported model directory.
 
     python -m myk_llm_b200.chat runs/200m-sft/export
     python -m myk_llm_b200.chat runs/200m-pt/export --raw --prompt "Once upon a time"
     python -m myk_llm_b200.chat runs/200m-pt/export --raw --prompt "..." --speculative   # MTP + CUDA graph
 
-The directory holds ``model.safetensors``, ``model.yaml`` and the tokenizer files
-(:func:`myk_llm_b200.models.io.save_model`).  Turns use the tokenizer's chat template
-(SFT models) or raw continuation (base models); the oldest context is dropped once the
-prompt plus the reply would exceed ``max_seq_len``.  ``--speculative`` decodes greedily
-through the static-cache MTP engine (:class:`myk_llm_b200.infer.StaticDecoder`).
-
-Interface of the reference's ``src/myk_llm/chat.py:19-86``.
+The directory is a portable export (``model.safetensors``, ``model.yaml``, tokenizer files).
+A ``ChatSession`` keeps the conversation: SFT models get the tokenizer's chat template over
+the whole history, base models (``--raw``) a plain continuation of the last text.  When
+prompt plus reply would pass ``max_seq_len`` the oldest tokens are dropped.
+``--speculative`` decodes greedily through the static-cache MTP engine
+(:class:`myk_llm_b200.infer.StaticDecoder`, CUDA graphs).  The command line and the
+helper functions ``build_prompt_ids`` / ``generate_reply`` are the reference's interface
+(``src/myk_llm/chat.py:19-86``).
 """
 
 from __future__ import annotations
 
 import argparse
+from dataclasses import dataclass, field
 
 import torch
 
 from .models import MykLLM, generate
 from .models.io import load_model
 
-EXIT_COMMANDS = {"exit", "quit", ":q"}
+EXIT_COMMANDS = frozenset({"exit", "quit", ":q"})
+
+
+def _turns(history: list[tuple[str, str]], user_text: str) -> list[dict[str, str]]:
+    msgs = [m for u, a in history for m in ({"role": "user", "content": u}, {"role": "assistant", "content": a})]
+    return msgs + [{"role": "user", "content": user_text}]
 
 
 def build_prompt_ids(model: MykLLM, tokenizer, history: list[tuple[str, str]], user_text: str,
                      raw: bool) -> torch.Tensor:
-    """Token ids of the next turn: chat template (with the history) or raw text."""
+    """(1, n) token ids of the next turn on the model's device."""
     if raw:
         ids = tokenizer(user_text, add_special_tokens=False, return_tensors="pt")["input_ids"]
     else:
-        messages = []
-        for u, a in history:
-            messages.append({"role": "user", "content": u})
-            messages.append({"role": "assistant", "content": a})
-        messages.append({"role": "user", "content": user_text})
-        ids = tokenizer.apply_chat_template(messages, add_generation_prompt=True, return_tensors="pt",
-                                            return_dict=True)["input_ids"]
-    return ids.to(next(model.parameters()).device)
+        ids = tokenizer.apply_chat_template(_turns(history, user_text), add_generation_prompt=True,
+                                            return_tensors="pt", return_dict=True)["input_ids"]
+    return ids.to(model.device)
 
 
 def generate_reply(model: MykLLM, tokenizer, prompt_ids: torch.Tensor, max_tokens: int, speculative: bool = False,
                    **sampling) -> tuple[str, list[int], bool]:
-    """(reply text, reply ids, whether the end-of-turn token was produced)."""
-    keep = model.config.max_seq_len - max_tokens
-    prompt_ids = prompt_ids[:, -keep:]
+    """(reply text, reply ids up to the end-of-turn token, whether that token came)."""
+    budget = model.config.max_seq_len - max_tokens
+    prompt_ids = prompt_ids[:, -budget:]  # drop the oldest context
     eos = tokenizer.eos_token_id
     if speculative:
         from .infer import StaticDecoder
 
-        dec = StaticDecoder(model, batch_size=1, max_len=prompt_ids.size(1) + max_tokens + 8)
-        out, _ = dec.generate(prompt_ids, max_tokens)
+        engine = StaticDecoder(model, batch_size=1, max_len=prompt_ids.shape[1] + max_tokens + 8)
+        tokens, _ = engine.generate(prompt_ids, max_tokens)
     else:
-        out = generate(model, prompt_ids, max_tokens, eos_token_id=eos, **sampling)
-    ids = out[0, prompt_ids.size(1):].tolist()
-    stopped = eos is not None and eos in ids
+        tokens = generate(model, prompt_ids, max_tokens, eos_token_id=eos, **sampling)
+    reply = tokens[0, prompt_ids.shape[1]:].tolist()
+    stopped = eos is not None and eos in reply
     if stopped:
-        ids = ids[:ids.index(eos)]
-    return tokenizer.decode(ids, skip_special_tokens=True).strip(), ids, stopped
+        reply = reply[:reply.index(eos)]
+    return tokenizer.decode(reply, skip_special_tokens=True).strip(), reply, stopped
+
+
+@dataclass
+class ChatSession:
+    model: MykLLM
+    tokenizer: object
+    raw: bool = False
+    max_tokens: int = 256
+    speculative: bool = False
+    sampling: dict = field(default_factory=dict)
+    history: list[tuple[str, str]] = field(default_factory=list)
+
+    @torch.no_grad()
+    def say(self, text: str) -> str:
+        ids = build_prompt_ids(self.model, self.tokenizer, [] if self.raw else self.history, text, self.raw)
+        reply, _, _ = generate_reply(self.model, self.tokenizer, ids, self.max_tokens, self.speculative,
+                                     **self.sampling)
+        self.history.append((text, reply))
+        return reply
+
+
+def _repl(session: ChatSession) -> None:
+    print("Type 'exit' to quit.")
+    while True:
+        try:
+            text = input("user> ").strip()
+        except EOFError:
+            return
+        if text.lower() in EXIT_COMMANDS:
+            return
+        if text:
+            print(f"assistant> {session.say(text)}")
 
 
 def main(argv: list[str] | None = None) -> None:
@@ -77,30 +111,14 @@ def main(argv: list[str] | None = None) -> None:
 
     from transformers import AutoTokenizer
 
-    model = load_model(args.model, device=args.device).eval()
-    tokenizer = AutoTokenizer.from_pretrained(args.model)
-    sampling = dict(temperature=args.temperature, top_k=args.top_k, top_p=args.top_p,
-                    repetition_penalty=args.repetition_penalty)
-    with torch.no_grad():
-        if args.prompt:
-            ids = build_prompt_ids(model, tokenizer, [], args.prompt, args.raw)
-            print(generate_reply(model, tokenizer, ids, args.max_tokens, args.speculative, **sampling)[0])
-            return
-        history: list[tuple[str, str]] = []
-        print("Type 'exit' to quit.")
-        while True:
-            try:
-                text = input("user> ").strip()
-            except EOFError:
-                break
-            if not text:
-                continue
-            if text.lower() in EXIT_COMMANDS:
-                break
-            ids = build_prompt_ids(model, tokenizer, history, text, args.raw)
-            reply, _, _ = generate_reply(model, tokenizer, ids, args.max_tokens, args.speculative, **sampling)
-            print(f"assistant> {reply}")
-            history.append((text, reply))
+    session = ChatSession(load_model(args.model, device=args.device).eval(), AutoTokenizer.from_pretrained(args.model),
+                          raw=args.raw, max_tokens=args.max_tokens, speculative=args.speculative,
+                          sampling=dict(temperature=args.temperature, top_k=args.top_k, top_p=args.top_p,
+                                        repetition_penalty=args.repetition_penalty))
+    if args.prompt:
+        print(session.say(args.prompt))
+    else:
+        _repl(session)
 
 
 if __name__ == "__main__":

@@ -1,19 +1,19 @@
-"""Draft acceptance of a model's multi-token-prediction (MTP) heads for greedy
-speculative decoding with K = 0..depth drafts (the quantity ``MTPDecoder`` /
-``StaticDecoder`` turn into speed).
+"""How often a model's multi-token-prediction (MTP) drafts would be accepted by greedy
+speculative decoding with K = 0 .. depth drafts per step (the quantity the speculative
+decoders turn into speed).
 
-At position i the main model's greedy token is g(i) and MTP depth k drafts d_k(i) (the
-token at i + 1 + k).  Draft k is accepted when d_j(i) == g(i + j) for every j <= k (a
-chain).  Per K it reports the chained acceptance a_k, tokens per verify iteration
-E = 1 + a_1 + ... + a_K, bytes per iteration, and the sampling (T = 1) acceptance of the
-greedy drafts, prod_j p(d_j(i) | x_<=i+j).  Two text sources, like the reference's
-``scripts/eval_mtp_acceptance.py``:
+At position ``i`` the main model's greedy token is ``g(i)`` and MTP head ``k`` drafts
+``d_k(i)`` for position ``i + 1 + k``.  Draft ``k`` is accepted when ``d_j(i) = g(i + j)``
+for every ``j <= k`` (a chain).  Per K the report gives the chained acceptance ``a_k``,
+tokens per verify step ``E = 1 + a_1 + ... + a_K``, bytes per step, and the sampling
+(T = 1) acceptance of the greedy drafts, ``prod_j p(d_j(i) | x_<=i+j)``.  As in the
+reference's ``scripts/eval_mtp_acceptance.py``, two texts are measured: teacher-forced
+validation text (``text``), and the model's own greedy continuation of validation prompts
+(``greedy``, exact for greedy speculative decoding; ``repeat`` is the share of repeated
+4-grams in it).
 
-* ``text``   teacher-forced validation text (a proxy: decoding conditions on the model's
-  own continuation);
-* ``greedy`` the model continues validation prompts greedily, then the same measurement
-  runs on its own continuation (exact for greedy speculative decoding on that text;
-  ``repeat`` is the share of repeated 4-grams, which small models produce a lot of).
+All depths are scored at once: drafts and greedy targets are (K, T) tensors, the chain is
+a cumulative product along K and the T = 1 acceptance a cumulative sum of log-probs.
 
     python -m myk_llm_b200.infer.eval_mtp_acceptance runs/sweeps/ngram-mtp/v32k-none
 """
@@ -29,65 +29,86 @@ import torch
 import yaml
 
 
+def _ahead(x: torch.Tensor, k: int, fill) -> torch.Tensor:
+    """``x`` shifted left by ``k`` along the last dim, padded with ``fill``."""
+    out = torch.full_like(x, fill)
+    if k < x.shape[-1]:
+        out[..., :x.shape[-1] - k] = x[..., k:]
+    return out
+
+
 @torch.no_grad()
 def row_acceptance(model, ids: torch.Tensor, targets: torch.Tensor, seqlens, token_bytes: torch.Tensor,
                    start: int = 0) -> dict[str, np.ndarray]:
-    """For one row (1, T): accepted[k, i] (chained), p_accepted[k, i], bytes of each draft
-    and of the verified token, over positions whose next depth + 1 targets are in-document."""
+    """One row (1, T): accepted[k, i] (chained), p_accepted[k, i], the bytes of each draft
+    and of the verified token, over positions whose next ``depth + 1`` targets are all
+    in-document (and at or after ``start``)."""
     from ..data.config import IGNORE_INDEX
     from ..train.objectives import mtp_targets
 
-    depth = len(model.mtp)
     out = model(ids, seqlens=seqlens)
     heads = model.mtp_hidden(out, ids)
-    logits = model.logits(out.hidden[0]).float()
-    greedy = logits.argmax(-1)
-    logp = logits.log_softmax(-1)
-    T = greedy.numel()
+    depth = len(heads)
+    logp = model.logits(out.hidden[0]).float().log_softmax(-1)          # (T, V)
+    greedy = logp.argmax(-1)                                              # (T,)
+    drafts = torch.stack([model.logits(h[0]).float().argmax(-1) for h in heads])  # (K, T)
+    wanted = torch.stack([_ahead(greedy, k, -1) for k in range(1, depth + 1)])
+    chained = (drafts == wanted).long().cumprod(0).bool()
+    # log p of draft k under the main model at the position it is verified (i + k)
+    draft_lp = torch.stack([_verify_logp(logp, drafts[k - 1], k) for k in range(1, depth + 1)])
+    p_chain = draft_lp.cumsum(0).exp()
     keep = mtp_targets(targets, depth)[0] != IGNORE_INDEX
     keep[:start] = False
-    chain = torch.ones(T, dtype=torch.bool, device=ids.device)
-    pchain = torch.ones(T, device=ids.device)
-    acc, pacc, nbytes = [], [], []
     tb = token_bytes.to(ids.device)
-    for k, h in enumerate(heads, start=1):
-        draft = model.logits(h[0]).float().argmax(-1)
-        want = torch.full_like(greedy, -1)
-        want[:-k] = greedy[k:]
-        chain = chain & (draft == want)
-        lp = torch.full((T,), float("-inf"), device=ids.device)
-        lp[:-k] = logp[k:].gather(1, draft[:-k, None])[:, 0]
-        pchain = pchain * lp.exp()
-        acc.append(chain[keep].float())
-        pacc.append(pchain[keep])
-        nbytes.append(tb[draft][keep])
-    return {"accepted": torch.stack(acc).cpu().numpy(), "p_accepted": torch.stack(pacc).cpu().numpy(),
-            "bytes": torch.stack(nbytes).cpu().numpy(), "first_bytes": tb[greedy][keep].cpu().numpy()}
+    return {"accepted": chained[:, keep].float().cpu().numpy(), "p_accepted": p_chain[:, keep].cpu().numpy(),
+            "bytes": tb[drafts][:, keep].cpu().numpy(), "first_bytes": tb[greedy][keep].cpu().numpy()}
+
+
+def _verify_logp(logp: torch.Tensor, draft: torch.Tensor, k: int) -> torch.Tensor:
+    """``log p(draft(i) | x_<=i+k)``: row ``i + k`` of the main model's log-probs at the
+    draft's token; ``-inf`` where ``i + k`` is past the end."""
+    t = logp.shape[0]
+    out = torch.full((t,), float("-inf"), device=logp.device)
+    if k < t:
+        out[:t - k] = logp[k:].gather(1, draft[:t - k, None])[:, 0]
+    return out
 
 
 def summarize(parts: list[dict[str, np.ndarray]]) -> dict:
-    """Per K in 0..depth: a_k, expected tokens / bytes per iteration, T = 1 acceptance."""
+    """Per K in 0..depth: a_k, expected tokens / bytes per step, T = 1 acceptance."""
     cat = {key: np.concatenate([p[key] for p in parts], axis=-1) for key in parts[0]}
-    a, p, b = cat["accepted"], cat["p_accepted"], cat["bytes"]
-    rows = []
-    for K in range(a.shape[0] + 1):
-        rows.append({"K": K,
-                     "a_k": float(a[K - 1].mean()) if K else 1.0,
-                     "tokens_per_iter": float((1 + a[:K].sum(0)).mean()),
-                     "bytes_per_iter": float((cat["first_bytes"] + (a[:K] * b[:K]).sum(0)).mean()),
-                     "p_accept_k": float(p[K - 1].mean()) if K else 1.0,
-                     "p_tokens_per_iter": float((1 + p[:K].sum(0)).mean())})
-    return {"positions": int(a.shape[1]), "rows": rows}
+    acc, pacc, nbytes, first = cat["accepted"], cat["p_accepted"], cat["bytes"], cat["first_bytes"]
+    run_tokens = np.concatenate([np.zeros((1, acc.shape[1])), np.cumsum(acc, 0)])
+    run_bytes = np.concatenate([np.zeros((1, acc.shape[1])), np.cumsum(acc * nbytes, 0)])
+    run_p = np.concatenate([np.zeros((1, acc.shape[1])), np.cumsum(pacc, 0)])
+    rows = [{"K": k,
+             "a_k": float(acc[k - 1].mean()) if k else 1.0,
+             "tokens_per_iter": float((1 + run_tokens[k]).mean()),
+             "bytes_per_iter": float((first + run_bytes[k]).mean()),
+             "p_accept_k": float(pacc[k - 1].mean()) if k else 1.0,
+             "p_tokens_per_iter": float((1 + run_p[k]).mean())} for k in range(acc.shape[0] + 1)]
+    return {"positions": int(acc.shape[1]), "rows": rows}
 
 
 def repeat_fraction(ids: list[int], n: int = 4) -> float:
     """Share of n-grams that already occurred earlier in the sequence."""
-    grams = [tuple(ids[i:i + n]) for i in range(len(ids) - n + 1)]
-    seen, rep = set(), 0
-    for g in grams:
-        rep += g in seen
-        seen.add(g)
-    return rep / max(1, len(grams))
+    grams = list(zip(*(ids[i:] for i in range(n))))
+    first_seen = {}
+    for pos, g in enumerate(grams):
+        first_seen.setdefault(g, pos)
+    repeats = sum(1 for pos, g in enumerate(grams) if first_seen[g] < pos)
+    return repeats / max(1, len(grams))
+
+
+def _report(name: str, text: dict, greedy: dict, reps: list[float]) -> None:
+    print(f"\n{name}: text {text['positions']} positions; greedy {greedy['positions']} positions, "
+          f"repeated 4-grams {100 * np.mean(reps):.0f}%")
+    print("| K | text a_k | text tok/iter | text B/iter | p_accept_k (T=1) | greedy a_k | greedy tok/iter "
+          "| greedy B/iter |")
+    print("|---|---|---|---|---|---|---|---|")
+    for t, g in zip(text["rows"], greedy["rows"]):
+        print(f"| {t['K']} | {t['a_k']:.3f} | {t['tokens_per_iter']:.3f} | {t['bytes_per_iter']:.2f} | "
+              f"{t['p_accept_k']:.3f} | {g['a_k']:.3f} | {g['tokens_per_iter']:.3f} | {g['bytes_per_iter']:.2f} |")
 
 
 def main(argv: list[str] | None = None) -> None:
@@ -103,12 +124,16 @@ def main(argv: list[str] | None = None) -> None:
     from ..configuration import from_dict
     from ..data import IGNORE_INDEX, build_fixed_batches
     from ..models import generate, load_model
+    from ..train.checkpoint import latest_checkpoint
     from ..train.config import TrainConfig
     from ..train.trainer import token_byte_lengths
 
     for run in map(Path, args.run_dirs):
         cfg = from_dict(TrainConfig, yaml.safe_load((run / "config.yaml").read_text()))
-        ckpt = sorted((run / "checkpoints").glob("step_*"))[-1]
+        ckpt = latest_checkpoint(run)
+        if ckpt is None:
+            print(f"{run.name}: no complete checkpoint")
+            continue
         model = load_model(ckpt)
         if not len(model.mtp):
             print(f"{run.name}: no MTP heads")
@@ -125,19 +150,10 @@ def main(argv: list[str] | None = None) -> None:
             for b in batches[:args.prompts]:
                 ids = generate(model, b.input_ids[:, :args.prompt_len].cuda(), args.new, temperature=0.0)
                 tgt = torch.cat([ids[:, 1:], torch.full_like(ids[:, :1], IGNORE_INDEX)], 1)
-                parts.append(row_acceptance(model, ids, tgt, [torch.tensor([ids.size(1)], device="cuda")], tb,
+                parts.append(row_acceptance(model, ids, tgt, [torch.tensor([ids.shape[1]], device="cuda")], tb,
                                             start=args.prompt_len))
                 reps.append(repeat_fraction(ids[0, args.prompt_len:].tolist()))
-            greedy = summarize(parts)
-            print(f"\n{val.name}: text {text['positions']} positions; greedy {greedy['positions']} positions, "
-                  f"repeated 4-grams {100 * np.mean(reps):.0f}%")
-            print("| K | text a_k | text tok/iter | text B/iter | p_accept_k (T=1) | greedy a_k | greedy tok/iter "
-                  "| greedy B/iter |")
-            print("|---|---|---|---|---|---|---|---|")
-            for t, g in zip(text["rows"], greedy["rows"]):
-                print(f"| {t['K']} | {t['a_k']:.3f} | {t['tokens_per_iter']:.3f} | {t['bytes_per_iter']:.2f} | "
-                      f"{t['p_accept_k']:.3f} | {g['a_k']:.3f} | {g['tokens_per_iter']:.3f} | "
-                      f"{g['bytes_per_iter']:.2f} |")
+            _report(val.name, text, summarize(parts), reps)
 
 
 if __name__ == "__main__":

@@ -89,89 +89,109 @@ class Example:
 
 
 def _keys(rng: np.random.Generator, count: int, key_len: int) -> list[list[int]]:
-    """``count`` distinct keys of ``key_len`` key symbols."""
-    if count > KEY_SYMBOLS ** key_len:
-        raise ValueError(f"{count} keys needed, only {KEY_SYMBOLS ** key_len} exist; raise key_len")
-    codes = rng.choice(KEY_SYMBOLS ** key_len, size=count, replace=False)
-    place = KEY_SYMBOLS ** np.arange(key_len - 1, -1, -1)
-    return ((codes[:, None] // place) % KEY_SYMBOLS + KEY_BASE).tolist()
+    """``count`` distinct keys of ``key_len`` key symbols: distinct integers below
+    ``KEY_SYMBOLS ** key_len`` written in base ``KEY_SYMBOLS``, most significant first."""
+    space = KEY_SYMBOLS ** key_len
+    if count > space:
+        raise ValueError(f"{count} keys needed, only {space} exist; raise key_len")
+    codes = rng.choice(space, size=count, replace=False)
+    symbols = np.empty((count, key_len), dtype=np.int64)
+    for j in range(key_len - 1, -1, -1):
+        codes, symbols[:, j] = np.divmod(codes, KEY_SYMBOLS)
+    return (symbols + KEY_BASE).tolist()
+
+
+@dataclass
+class _Item:
+    chain: list[list[int]]   # the keys of its hops, in order
+    value: list[int]
+
+    def records(self) -> list[list[int]]:
+        """``k_i k_{i+1} ;`` for each hop, then ``k_last v... ;``."""
+        links = [a + b + [SEP] for a, b in zip(self.chain, self.chain[1:])]
+        return links + [self.chain[-1] + self.value + [SEP]]
+
+    def query(self, cot: bool) -> tuple[list[int], list[int]]:
+        """(prompt ``? k_0``, answer: the later keys when ``cot``, the value, ``$``)."""
+        middle = [t for key in self.chain[1:] for t in key] if cot else []
+        return [QUERY] + self.chain[0], middle + self.value + [EOS]
+
+
+class _Layout:
+    """Writes records at random offsets into noise, then the queries, into one array."""
+
+    def __init__(self, length: int) -> None:
+        self.ids = np.empty(length, dtype=np.int64)
+        self.pos = 0
+
+    def put(self, tokens) -> int:
+        start = self.pos
+        self.ids[start:start + len(tokens)] = tokens
+        self.pos += len(tokens)
+        return start
 
 
 def make_example(rng: np.random.Generator, task: TaskConfig, length: int, records: int | None = None) -> Example:
-    """One example of exactly ``length`` tokens."""
+    """One example of exactly ``length`` tokens.  The order of random draws (hop counts,
+    keys, values, queried items, record order, gaps, noise) is fixed, so a seed gives the
+    same example as the reference's generator."""
     n = task.records_at(length, records)
-    q = min(task.num_queries, n)
     hops = rng.choice(task.hops, size=n)
     keys = _keys(rng, int(hops.sum()), task.key_len)
     values = (rng.integers(0, VALUE_SYMBOLS, size=(n, task.value_len)) + VALUE_BASE).tolist()
-    chains, recs, k = [], [], 0
-    for item, h in enumerate(hops.tolist()):
-        chain = keys[k:k + h]
-        k += h
-        chains.append(chain)
-        for a, b in zip(chain, chain[1:]):
-            recs.append((item, a + b + [SEP]))
-        recs.append((item, chain[-1] + values[item] + [SEP]))
-    queried = rng.choice(n, size=q, replace=False).tolist()
-    queries = []
-    for item in queried:
-        middle = [t for key in chains[item][1:] for t in key] if task.cot else []
-        queries.append(([QUERY] + chains[item][0], middle + values[item] + [EOS]))
-    q_tokens = sum(len(p) + len(a) for p, a in queries)
-    context = length - q_tokens
+    bounds = np.concatenate(([0], np.cumsum(hops))).tolist()
+    items = [_Item(keys[bounds[i]:bounds[i + 1]], values[i]) for i in range(n)]
+    recs = [(i, r) for i, item in enumerate(items) for r in item.records()]
+    queried = rng.choice(n, size=min(task.num_queries, n), replace=False).tolist()
+    queries = [items[i].query(task.cot) for i in queried]
+    context = length - sum(len(p) + len(a) for p, a in queries)
     noise = context - sum(len(r) for _, r in recs)
     if noise < 0:
         raise ValueError(f"{n} items and their queries do not fit in {length} tokens")
     order = rng.permutation(len(recs)).tolist()
-    gaps = np.sort(rng.integers(0, noise + 1, size=len(recs))).tolist()  # noise before each record
-    noise_ids = rng.integers(NOISE_BASE, NOISE_BASE + NOISE_SYMBOLS, size=noise)
-    ids = np.empty(length, dtype=np.int64)
-    first = [context] * n
-    pos = used = 0
-    for ri, g in zip(order, gaps):
-        ids[pos:pos + g - used] = noise_ids[used:g]
-        pos += g - used
-        used = g
-        item, toks = recs[ri]
-        first[item] = min(first[item], pos)
-        ids[pos:pos + len(toks)] = toks
-        pos += len(toks)
-    ids[pos:context] = noise_ids[used:]
-    pos = context
-    answers, depths = [], []
-    for (prompt, ans), item in zip(queries, queried):
-        ids[pos:pos + len(prompt)] = prompt
-        pos += len(prompt)
-        ids[pos:pos + len(ans)] = ans
-        answers.append((pos, pos + len(ans)))
-        pos += len(ans)
-        depths.append(first[item] / context)
-    return Example(ids, answers, depths, [int(hops[i]) for i in queried])
+    gaps = np.sort(rng.integers(0, noise + 1, size=len(recs))).tolist()  # noise tokens before each record
+    filler = rng.integers(NOISE_BASE, NOISE_BASE + NOISE_SYMBOLS, size=noise)
+    out = _Layout(length)
+    first_seen = [context] * n
+    taken = 0
+    for r, gap in zip(order, gaps):
+        out.put(filler[taken:gap])
+        taken = gap
+        item, tokens = recs[r]
+        first_seen[item] = min(first_seen[item], out.put(tokens))
+    out.put(filler[taken:])
+    answers = []
+    for prompt, answer in queries:
+        out.put(prompt)
+        start = out.put(answer)
+        answers.append((start, start + len(answer)))
+    return Example(out.ids, answers, [first_seen[i] / context for i in queried], [int(hops[i]) for i in queried])
 
 
 def make_copy_example(rng: np.random.Generator, task: TaskConfig) -> Example:
-    """A random span then the same span; the repeat after its first token is the answer."""
-    span = rng.integers(KEY_BASE, VOCAB_SIZE, size=int(rng.integers(task.copy_min, task.copy_max + 1)))
-    ids = np.concatenate([span, span])
-    return Example(ids, [(len(span) + 1, len(ids))], [0.0], [0])
+    """A random span followed by the same span; the repeat after its first token is the answer."""
+    width = int(rng.integers(task.copy_min, task.copy_max + 1))
+    span = rng.integers(KEY_BASE, VOCAB_SIZE, size=width)
+    return Example(np.concatenate([span, span]), [(width + 1, 2 * width)], [0.0], [0])
 
 
 def resolve(ids: np.ndarray, query_key: list[int], key_len: int) -> list[int]:
-    """Follow the records of the context from ``query_key`` to its value (a direct
-    statement of the task, for tests)."""
+    """Follow the context's records from ``query_key`` to its value: a direct statement of
+    the task used by the tests.  A record starts with a key symbol right after a
+    separator, a noise token or the beginning."""
     toks = ids.tolist()
     toks = toks[:toks.index(QUERY)]
-    table: dict[tuple[int, ...], list[int]] = {}
+    lookup: dict[tuple[int, ...], list[int]] = {}
     i = 0
     while i < len(toks):
-        starts_record = KEY_BASE <= toks[i] < VALUE_BASE and (i == 0 or toks[i - 1] == SEP or toks[i - 1] >= NOISE_BASE)
-        if starts_record:
+        boundary = i == 0 or toks[i - 1] == SEP or toks[i - 1] >= NOISE_BASE
+        if KEY_BASE <= toks[i] < VALUE_BASE and boundary:
             end = toks.index(SEP, i)
-            table[tuple(toks[i:i + key_len])] = toks[i + key_len:end]
+            lookup[tuple(toks[i:i + key_len])] = toks[i + key_len:end]
             i = end + 1
         else:
             i += 1
-    out = table[tuple(query_key)]
-    while all(KEY_BASE <= t < VALUE_BASE for t in out):
-        out = table[tuple(out)]
-    return out
+    target = lookup[tuple(query_key)]
+    while all(KEY_BASE <= t < VALUE_BASE for t in target):  # a link to the next key
+        target = lookup[tuple(target)]
+    return target

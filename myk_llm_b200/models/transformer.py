@@ -330,6 +330,8 @@ class MykLLM(nn.Module):
             assert isinstance(src, Attention)
             src.shares_kv = True
         self._iteration_rng = random.Random(torch.initial_seed())
+        # analysis hook: called as fn(iteration, loop state) after every pass of a looped core
+        self.core_observer: Callable[[int, torch.Tensor], None] | None = None
         self.init_weights()
 
     @torch.no_grad()
@@ -428,6 +430,9 @@ class MykLLM(nn.Module):
                 state = inj(materialize(state), inputs)
                 for i in range(loop.prelude, loop.prelude + loop.core):
                     state = block(i, state)
+            if self.core_observer is not None:
+                state = materialize(state)
+                self.core_observer(it, state)
         return materialize(state)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
