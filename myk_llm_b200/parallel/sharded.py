@@ -719,11 +719,11 @@ class ShardedDataParallel(nn.Module):
         self._dematerialise_sharded()
 
     def before_checkpoint_load(self) -> None:
-        """DCP loads in place: give row-sharded parameters full-size storage to load into."""
-        with torch.no_grad():
-            for s in self.slots:
-                if s.sharded:
-                    s.param.data = torch.empty(s.rows, s.cols, dtype=torch.float32, device=self.info.device)
+        """DCP loads in place into the tensors of the current state: give row-sharded
+        parameters full-size storage, and the torch optimizers full per-parameter state
+        (the gradients are the runtime's buffers, so torch cannot create that state with a
+        trial step)."""
+        self.sync_params_for_checkpoint()
 
     def after_checkpoint_load(self) -> None:
         """Scatter loaded values and per-parameter optimizer state back into the shards."""

@@ -114,3 +114,70 @@ def test_dead_rank_fails_fast():
         p.join(timeout=60)
     assert all(not p.is_alive() for p in ps)
     assert q.get(timeout=5) != "no error"
+
+
+RESUME_OV = ["model.num_layers=2", "data.seq_len=64", "data.micro_batch_size=2", "global_batch_size=4",
+             "model.max_seq_len=64", "optimizer.name=muon", "steps=6", "checkpoint.interval=2",
+             "checkpoint.final=true", "checkpoint.keep_last=0", "logging.interval=1"]
+
+
+def _fit_worker(rank, world, port, run_root, die_at, out_path):
+    """Runs ``Trainer.fit`` as rank ``rank``; with ``die_at`` rank 1 exits abruptly when it
+    reaches that step (between steps: nothing of its in flight)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    from myk_llm_b200.train.trainer import Trainer
+
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", RESUME_OV + [f"output_dir={run_root}"])
+    tr = Trainer(cfg, DistInfo(rank, world, rank, torch.device("cpu")))
+    if die_at is not None and rank == 1:
+        step_fn = tr.train_step
+
+        def dying(batches, step=None):
+            if step == die_at:
+                os._exit(7)
+            return step_fn(batches, step)
+
+        tr.train_step = dying
+    tr.fit("auto")
+    full = tr.model.full_named_parameters() if hasattr(tr.model, "full_named_parameters") else \
+        {n: p.detach().clone() for n, p in tr.raw_model.named_parameters()}
+    if rank == 0 and out_path:
+        torch.save(full, out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_fit(world, run_root, die_at=None, out_path=None):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_fit_worker, args=(r, world, port, str(run_root), die_at, out_path))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung instead of failing"
+    return [p.exitcode for p in procs]
+
+
+def test_killed_rank_fails_fast_and_the_job_resumes_bit_exactly(tmp_path):
+    """A rank dies at step 5 (checkpoints at 2 and 4): every rank ends with an error rather
+    than hanging; re-running the same command resumes from step 4 and ends with exactly the
+    parameters of an uninterrupted run."""
+    from myk_llm_b200.train.checkpoint import latest_checkpoint
+
+    codes = _run_fit(2, tmp_path / "crashed", die_at=5)
+    assert codes[1] == 7 and codes[0] != 0
+    assert latest_checkpoint(tmp_path / "crashed" / "tiny-cpu").name == "step_0000004"
+    assert _run_fit(2, tmp_path / "crashed", out_path=str(tmp_path / "resumed.pt")) == [0, 0]
+    assert _run_fit(2, tmp_path / "clean", out_path=str(tmp_path / "clean.pt")) == [0, 0]
+    resumed, clean = torch.load(tmp_path / "resumed.pt"), torch.load(tmp_path / "clean.pt")
+    for name, p in clean.items():
+        assert torch.equal(resumed[name], p), name
