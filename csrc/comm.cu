@@ -124,6 +124,45 @@ dp_reduce_sumsq_kernel(const int64_t* __restrict__ grad_ptrs, int rank, int worl
   }
 }
 
+// The same reduce-scatter through NVSwitch multicast (NVLS): one `multimem.ld_reduce`
+// per 16 bytes reads the element from every rank's gradient buffer and returns the sum,
+// reduced inside the switch, so each owned element crosses NVLink once instead of once
+// per rank.  `mc` is the multicast address of the gradient buffer (same offsets as the
+// per-rank buffers).
+__device__ __forceinline__ float4 multimem_sum_f32x4(const float4* addr) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256)
+dp_reduce_sumsq_multimem_kernel(const float4* __restrict__ mc, float4* __restrict__ own, RangeTable tab,
+                                float* __restrict__ partial) {
+  const int64_t total4 = tab.prefix[tab.n] / 4;
+  float ss = 0.f;
+  for (int64_t i4 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i4 < total4; i4 += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = i4 * 4;
+    const int k = find_range(tab.prefix, tab.n, i);
+    const int64_t e = (tab.offset[k] + (i - tab.prefix[k])) / 4;
+    const float4 acc = multimem_sum_f32x4(mc + e);
+    own[e] = acc;
+    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    atomicAdd(partial, t);
+  }
+}
+
 // Clip coefficient from every rank's partial squared norm (partials[r] points at rank r's
 // float) plus the replicated-parameter part `extra_sq` (already global).
 __device__ __forceinline__ float clip_coef(const int64_t* partial_ptrs, int world, float extra_sq, float max_norm,
@@ -288,6 +327,17 @@ void dp_reduce_sumsq(torch::Tensor grad_ptrs, int64_t rank, int64_t world, torch
   if (total == 0 || tab.n == 0) return;
   dp_reduce_sumsq_kernel<<<comm_grid(total / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       grad_ptrs.data_ptr<int64_t>(), (int)rank, (int)world, tab, partial.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dp_reduce_sumsq_multimem(int64_t grad_mc, torch::Tensor own_grad, torch::Tensor offsets, torch::Tensor prefix,
+                              torch::Tensor partial, int64_t total) {
+  RangeTable tab{offsets.data_ptr<int64_t>(), prefix.data_ptr<int64_t>(), (int)offsets.numel()};
+  if (total == 0 || tab.n == 0) return;
+  TORCH_CHECK(grad_mc != 0 && grad_mc % 16 == 0, "dp_reduce_multimem: a 16-byte aligned multicast address");
+  dp_reduce_sumsq_multimem_kernel<<<comm_grid(total / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const float4*>(grad_mc), reinterpret_cast<float4*>(own_grad.data_ptr<float>()), tab,
+      partial.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -382,4 +382,29 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dout, torch::Tensor grad) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------ fp32 -> bf16
+// The bf16 compute copy of an fp32 master weight (once per optimizer step and weight):
+// 16-byte loads, 8-byte stores, round to nearest even.
+__global__ void __launch_bounds__(256) cast_bf16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst,
+                                                        int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = src[i];
+    dst[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+torch::Tensor cast_bf16(torch::Tensor src) {
+  c10::cuda::CUDAGuard guard(src.device());
+  TORCH_CHECK(src.scalar_type() == at::kFloat && src.is_contiguous(), "cast_bf16: contiguous fp32 input");
+  auto out = torch::empty(src.sizes(), src.options().dtype(at::kBFloat16));
+  const int64_t n = src.numel();
+  if (n == 0) return out;
+  TORCH_CHECK(n % 4 == 0 && reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0,
+              "cast_bf16: 16-byte aligned input of a multiple of 4 elements");
+  cast_bf16_kernel<<<ew_grid(n / 4, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const float4*>(src.data_ptr<float>()), reinterpret_cast<uint2*>(out.data_ptr()), n / 4);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 }  // namespace mykb

@@ -2,6 +2,9 @@
 #include <torch/extension.h>
 
 namespace mykb {
+torch::Tensor cast_bf16(torch::Tensor src);
+void dp_reduce_sumsq_multimem(int64_t grad_mc, torch::Tensor own_grad, torch::Tensor offsets, torch::Tensor prefix,
+                              torch::Tensor partial, int64_t total);
 void dp_muon_apply_shards(torch::Tensor param_ptrs, torch::Tensor bf16_ptrs, torch::Tensor poffs,
                           torch::Tensor boffs, int64_t rows, int64_t cols, int64_t rows_per_rank, double decay,
                           double step_scale, torch::Tensor orth);
@@ -126,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_qkv_fwd", &mykb::rope_qkv_fwd);
   m.def("rope_qkv_bwd", &mykb::rope_qkv_bwd);
   m.def("split_cols", &mykb::split_cols);
+  m.def("cast_bf16", &mykb::cast_bf16, "fp32 -> bf16 copy (round to nearest even)");
   m.def("fp8_quant_rows", &mykb::fp8_quant_rows);
   m.def("fp8_quant_tensor", &mykb::fp8_quant_tensor);
   m.def("fp8_quant_cols_t", &mykb::fp8_quant_cols_t);
@@ -154,6 +158,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ngram_adam", &mykb::ngram_adam);
   m.def("peer_barrier", &mykb::peer_barrier);
   m.def("dp_reduce_sumsq", &mykb::dp_reduce_sumsq);
+  m.def("dp_reduce_sumsq_multimem", &mykb::dp_reduce_sumsq_multimem,
+        "gradient reduce-scatter + squared norm through NVSwitch multicast (multimem.ld_reduce)");
   m.def("dp_adamw_allgather", &mykb::dp_adamw_allgather);
   m.def("dp_muon_prepare", &mykb::dp_muon_prepare);
   m.def("dp_muon_apply_allgather", &mykb::dp_muon_apply_allgather);

@@ -52,6 +52,33 @@ def build(case: str):
         w = torch.randn(5632, 1024, device=dev).bfloat16()
         return (lambda: gemm(x, w)), 2 * 32768 * 5632 * 1024, (x.numel() + w.numel() + 32768 * 5632) * 2, \
             "bf16 GEMM 32768x5632x1024 (200M gate/up forward), bf16 out"
+    if case in ("gemm_gather_self_200m", "gemm_gather_prefetch_200m"):
+        # the gate/up forward with the fused all-gather of a row-sharded weight, "ranks"
+        # emulated as 8 buffers of this GPU: `self` gathers its own B operand (the producer
+        # waits per 64 rows), `prefetch` gathers another weight while multiplying a held one
+        world, n, k = 8, 5632, 1024
+        x = torch.randn(32768, k, device=dev).bfloat16()
+        w = torch.randn(n, k, device=dev).bfloat16()
+        r = -(-n // world)
+        shards = [torch.zeros(r * k, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+        for i, sh in enumerate(shards):
+            part = w[i * r:(i + 1) * r].reshape(-1)
+            sh[:part.numel()] = part
+        ptrs = torch.tensor([sh.data_ptr() for sh in shards], dtype=torch.int64, device=dev)
+        full = torch.empty_like(w)
+        ready = torch.zeros((n + 63) // 64, dtype=torch.int32, device=dev)
+        y = torch.empty(32768, n, device=dev, dtype=torch.bfloat16)
+        held = w.clone()
+        epoch = [0]
+
+        def run():
+            epoch[0] += 1
+            b = full if case == "gemm_gather_self_200m" else held
+            ext().gemm_gather(x, b, y, False, False, False, full, ptrs, 0, r, 3, ready, epoch[0])
+
+        run.keep = shards  # the shards must outlive the closure
+        return run, 2 * 32768 * n * k, (x.numel() + 2 * w.numel() + 32768 * n) * 2, \
+            f"bf16 GEMM 32768x{n}x{k} with the fused gather of a {n}x{k} weight from {world} emulated ranks ({case})"
     if case == "gemm_wgrad_200m":
         # the 200M model's gate/up weight gradient: dW (5632 x 1024) += dy^T x over 32768 tokens
         dy = torch.randn(32768, 5632, device=dev).bfloat16()
@@ -147,7 +174,7 @@ def build(case: str):
     raise ValueError(f"unknown case {case!r}")
 
 
-CASES = ["gemm", "gemm_fwd_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
+CASES = ["gemm", "gemm_fwd_200m", "gemm_gather_self_200m", "gemm_gather_prefetch_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
 
 
 def time_case(case: str, reps: int = 20) -> dict:

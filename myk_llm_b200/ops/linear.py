@@ -92,7 +92,12 @@ def bf16_weight(w: torch.Tensor) -> torch.Tensor:
     key = (w._version, _WEIGHT_EPOCH[0], w.data_ptr())
     if cache is not None and cache[0] == key:
         return cache[1]
-    wb = w.detach().to(torch.bfloat16).contiguous()
+    wd = w.detach()
+    if wd.is_cuda and wd.dtype == torch.float32 and wd.is_contiguous() and wd.numel() % 4 == 0 \
+            and wd.data_ptr() % 16 == 0:
+        wb = ext().cast_bf16(wd)
+    else:
+        wb = wd.to(torch.bfloat16).contiguous()
     try:
         w._mykb_bf16 = (key, wb)
     except AttributeError:  # pragma: no cover - tensors that refuse attributes

@@ -24,7 +24,9 @@ into it).  Each optimizer step (``optimizer_step``):
 1. peer barrier (every rank finished its backward passes);
 2. ``dp_reduce_sumsq``: each rank sums, from every peer's gradient buffer, the element
    ranges it owns (whole matrices for Muon, even slices of the AdamW space) and
-   accumulates their squared norm: the reduce-scatter fused with the clipping norm;
+   accumulates their squared norm: the reduce-scatter fused with the clipping norm.  With
+   NVSwitch multicast (NVLS) available, ``dp_reduce_sumsq_multimem`` reads each owned
+   element once through the switch, which adds up every rank's copy (``multimem.ld_reduce``);
 3. peer barrier; the clip coefficient is formed on the device from all partial norms;
 4. ``dp_adamw_allgather``: AdamW on the owned slices, the result stored into every rank's
    replicated copy.  Muon: momentum / Nesterov / bf16 pack of the owned matrices, batched
@@ -284,6 +286,7 @@ class ShardedDataParallel(nn.Module):
         self.slots: list[Slot] = []
         self._linear_weights = {id(m.weight) for m in model.modules() if type(m) is nn.Linear}
         self.trace = UseTrace()
+        self.grad_mc = 0  # NVSwitch multicast address of the gradient buffer (0: peer loads)
 
     # -- module plumbing ----------------------------------------------------------------
     def forward(self, *args, **kwargs):
@@ -377,10 +380,30 @@ class ShardedDataParallel(nn.Module):
             self.partial_ptrs = self.flag_ptrs + 32 * 4
             self.partial = self.ctrl[32:33].view(torch.float32)
             self._handles = handles
+            self.grad_mc = self._multicast_address(handles[1], self.flat_grad)
         else:
             self.flat_param = torch.zeros(self.param_total, dtype=torch.float32, device=dev)
             self.flat_grad = torch.zeros(self.grad_total, dtype=torch.float32, device=dev)
             self.flat_bf16 = torch.zeros(self.bf16_total, dtype=torch.bfloat16, device=dev)
+
+    def _multicast_address(self, handle, tensor: torch.Tensor) -> int:
+        """NVSwitch multicast address of a symmetric buffer when every rank's GPU supports
+        NVLS (and ``MYKB_NVLS`` is not ``0``), else 0: the gradient reduce-scatter then reads
+        through the switch (``multimem.ld_reduce``) instead of from every peer."""
+        import os
+
+        from torch._C._autograd import DeviceType
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        ok = os.environ.get("MYKB_NVLS", "1") != "0" and \
+            _SymmetricMemory.has_multicast_support(DeviceType.CUDA, tensor.device.index)
+        mc = int(handle.multicast_ptr) if ok else 0
+        flag = torch.tensor([1 if mc else 0], dtype=torch.int32, device=tensor.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)  # all ranks take the same path
+        if not int(flag):
+            return 0
+        delta = tensor.data_ptr() - int(handle.buffer_ptrs[self.rank])
+        return mc + delta
 
     def _load_params_into_buffers(self) -> None:
         """Copy the (identical on every rank after the broadcast) initial values into the
@@ -544,8 +567,12 @@ class ShardedDataParallel(nn.Module):
         ext = ops.ext()
         self.partial.zero_()
         self._barrier()
-        ext.dp_reduce_sumsq(self.grad_ptrs, self.rank, self.world, self.red_offsets, self.red_prefix, self.partial,
-                            self.red_total)
+        if self.grad_mc:
+            ext.dp_reduce_sumsq_multimem(self.grad_mc, self.flat_grad, self.red_offsets, self.red_prefix, self.partial,
+                                         self.red_total)
+        else:
+            ext.dp_reduce_sumsq(self.grad_ptrs, self.rank, self.world, self.red_offsets, self.red_prefix,
+                                self.partial, self.red_total)
         self._barrier()
         b1, b2, eps = self._adam_hparams()
         dev = self.info.device

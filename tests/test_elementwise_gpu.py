@@ -336,3 +336,20 @@ def test_fused_ngram_embedding_matches_statement():
             ref = torch.zeros_like(t.weight).index_add_(0, (rows[k] - k * cfg.num_buckets).reshape(-1),
                                                         g.reshape(-1, 64))
             assert torch.allclose(t.weight.grad, ref, atol=1e-5)
+
+
+def test_cast_bf16_matches_torch_rounding():
+    """The weight cast kernel rounds like torch (nearest even), including infinities,
+    NaN, denormals and values at the rounding midpoints."""
+    from myk_llm_b200.ops import ext
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(4096 * 1024 + 16, device="cuda", generator=g) * 3.0
+    x[:8] = torch.tensor([float("inf"), -float("inf"), 0.0, -0.0, 1e-40, -1e-42, 3.4e38, 1.00390625], device="cuda")
+    x[8] = float("nan")
+    mid = torch.arange(1, 8, device="cuda", dtype=torch.int32) * 65536 + 32768  # exact midpoints
+    x[16:23] = mid.view(torch.float32)
+    got = ext().cast_bf16(x)
+    want = x.to(torch.bfloat16)
+    same = (got.view(torch.int16) == want.view(torch.int16)) | (got.isnan() & want.isnan())
+    assert bool(same.all())

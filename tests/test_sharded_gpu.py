@@ -39,9 +39,9 @@ def _steps(tr, world, rank, n=3):
     return {k: v.float().cpu().clone() for k, v in params.items()}
 
 
-def _worker(rank, world, port, out, strategy, reshard):
+def _worker(rank, world, port, out, strategy, reshard, nvls="0"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
+                      LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0", MYKB_NVLS=nvls)
     from myk_llm_b200.configuration import load_config
     from myk_llm_b200.ops import ext
     from myk_llm_b200.parallel.distributed import init_distributed
@@ -61,10 +61,13 @@ def _worker(rank, world, port, out, strategy, reshard):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("strategy,reshard", [("sharded", "true"), ("sharded", "false"), ("replicated", "false")])
-def test_sharded_two_gpus_matches_one(strategy, reshard, tmp_path):
+@pytest.mark.parametrize("strategy,reshard,nvls", [("sharded", "true", "0"), ("sharded", "false", "0"),
+                                                   ("replicated", "false", "0"), ("sharded", "true", "1")])
+def test_sharded_two_gpus_matches_one(strategy, reshard, nvls, tmp_path):
+    """nvls=1: the gradient reduce-scatter reads through NVSwitch multicast where the GPUs
+    support it (peer loads otherwise)."""
     out = str(tmp_path / "p.pt")
-    mp.spawn(_worker, args=(2, _port(), out, strategy, reshard), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), out, strategy, reshard, nvls), nprocs=2, join=True)
     got = torch.load(out)
     assert got["status"] == 0
     from myk_llm_b200.configuration import load_config
