@@ -26,8 +26,9 @@ namespace fadec {
 
 typedef __nv_bfloat16 bf16;
 constexpr int ROWS = 16;        // query rows per KV head (GQA group x queries)
-constexpr int KEYS = 32;        // keys per tile; a warp walks `tiles` consecutive tiles
+constexpr int KEYS = 32;        // keys per tile; a warp walks consecutive tiles
 constexpr int WARPS = 4;
+constexpr int STAGES = 3;       // tiles per warp in its shared-memory ring (two in flight while one is used)
 
 struct Params {
   const bf16* q;       // (B, L, H, D) with strides
@@ -80,12 +81,19 @@ __device__ __forceinline__ bool visible(const Params& p, int r, int j, int rows,
   return true;
 }
 
+// Shared-memory tiles are unpadded rows of D bf16 with the 16-byte chunks of row r stored
+// at chunk index c ^ (r & 7): the eight rows an ldmatrix phase reads then hit eight
+// different bank groups.
+template <int D>
+__device__ __forceinline__ int swz(int r, int col) {
+  return r * D + ((((col >> 3) ^ (r & 7)) << 3) | (col & 7));
+}
+
 template <int D>
 __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
-  constexpr int LDK = D + 8;
-  extern __shared__ __align__(16) unsigned char smraw[];
-  bf16* Qs = reinterpret_cast<bf16*>(smraw);  // [ROWS][LDK]
-  bf16* KV = Qs + ROWS * LDK;                  // [WARPS][2 buffers][K, V][KEYS][LDK]
+  extern __shared__ __align__(128) unsigned char smraw[];
+  bf16* Qs = reinterpret_cast<bf16*>(smraw);  // [ROWS][D] (swizzled)
+  bf16* KV = Qs + ROWS * D;                    // [WARPS][STAGES][K, V][KEYS][D] (swizzled)
   __shared__ int last;
   __shared__ float rowM[ROWS], rowL[ROWS];
   __shared__ float wM[WARPS][ROWS], wL[WARPS][ROWS];
@@ -95,8 +103,9 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
   const int G = p.H / p.Hkv, rows = G * p.L;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kv_len = min(p.seqused[b], p.cap);
-  const int T = p.tiles;
-  const int key0 = (cta * WARPS + warp) * KEYS * T;  // this warp's contiguous key range
+  // this warp's contiguous key range: the visible keys split evenly over all warps of (b, hk)
+  const int T = (kv_len + ctas * WARPS * KEYS - 1) / (ctas * WARPS * KEYS);
+  const int key0 = (cta * WARPS + warp) * KEYS * T;
   const int64_t kv_row = (int64_t)p.Hkv * D;
   const bf16* kb = p.k + ((int64_t)b * p.cap) * kv_row + (int64_t)hk * D;
   const bf16* vb = p.v + ((int64_t)b * p.cap) * kv_row + (int64_t)hk * D;
@@ -104,27 +113,32 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
     const int r = e / (D / 8), c = (e % (D / 8)) * 8;
     const bool ok = r < rows;
     const int g = ok ? r / p.L : 0, i = ok ? r % p.L : 0;
-    cp16(Qs + r * LDK + c, p.q + b * p.q_sb + i * p.q_st + (int64_t)(hk * G + g) * p.q_sh + c, ok);
+    cp16(Qs + swz<D>(r, c), p.q + b * p.q_sb + i * p.q_st + (int64_t)(hk * G + g) * p.q_sh + c, ok);
   }
-  bf16* wbuf = KV + warp * 2 * 2 * KEYS * LDK;
-  auto load_tile = [&](int t, int buf) {
-    bf16* ks = wbuf + buf * 2 * KEYS * LDK;
-    bf16* vs = ks + KEYS * LDK;
+  bf16* wbuf = KV + warp * STAGES * 2 * KEYS * D;
+  auto load_tile = [&](int t) {
+    bf16* ks = wbuf + (t % STAGES) * 2 * KEYS * D;
+    bf16* vs = ks + KEYS * D;
     const int base = key0 + t * KEYS;
+#pragma unroll 4
     for (int e = lane; e < KEYS * (D / 8); e += 32) {
       const int r = e / (D / 8), c = (e % (D / 8)) * 8;
       const bool ok = base + r < kv_len;
       const int64_t off = (int64_t)(ok ? base + r : 0) * kv_row + c;
-      cp16(ks + r * LDK + c, kb + off, ok);
-      cp16(vs + r * LDK + c, vb + off, ok);
+      cp16(ks + swz<D>(r, c), kb + off, ok);
+      cp16(vs + swz<D>(r, c), vb + off, ok);
     }
   };
   asm volatile("cp.async.commit_group;" ::: "memory");  // group: Q
   // tiles past the visible keys are skipped (they would only be masked)
   const int nt = max(0, min(T, (kv_len - key0 + KEYS - 1) / KEYS));
-  if (nt > 0) load_tile(0, 0);
-  asm volatile("cp.async.commit_group;" ::: "memory");  // group: tile 0
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  // prologue: STAGES - 1 tiles in flight (empty groups keep the group count uniform)
+#pragma unroll
+  for (int t = 0; t < STAGES - 1; ++t) {
+    if (t < nt) load_tile(t);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 1) : "memory");
   __syncthreads();  // Q is visible to every warp
   const int rr = lane & 7, mat = lane >> 3, gq = lane >> 2, cq = (lane & 3) * 2;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
@@ -132,23 +146,23 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   for (int t = 0; t < nt; ++t) {
-    if (t + 1 < nt) load_tile(t + 1, (t + 1) & 1);
+    if (t + STAGES - 1 < nt) load_tile(t + STAGES - 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(STAGES - 1) : "memory");  // tile t has landed
     __syncwarp();
-    const bf16* ks = wbuf + (t & 1) * 2 * KEYS * LDK;
-    const bf16* vs = ks + KEYS * LDK;
+    const bf16* ks = wbuf + (t % STAGES) * 2 * KEYS * D;
+    const bf16* vs = ks + KEYS * D;
     float s[KEYS / 8][4];
 #pragma unroll
     for (int j = 0; j < KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
     for (int k0 = 0; k0 < D; k0 += 16) {
       uint32_t a[4];
-      ldsm4(a, Qs + (lane & 15) * LDK + k0 + (lane >> 4) * 8);
+      ldsm4(a, Qs + swz<D>(lane & 15, k0 + (lane >> 4) * 8));
 #pragma unroll
       for (int j = 0; j < KEYS / 8; j += 2) {
         uint32_t bq[4];
-        ldsm4(bq, ks + (j * 8 + rr + (mat >> 1) * 8) * LDK + k0 + (mat & 1) * 8);
+        ldsm4(bq, ks + swz<D>(j * 8 + rr + (mat >> 1) * 8, k0 + (mat & 1) * 8));
         mma(s[j], a, bq[0], bq[1]);
         mma(s[j + 1], a, bq[2], bq[3]);
       }
@@ -201,12 +215,12 @@ __global__ void __launch_bounds__(WARPS * 32) fa_decode_kernel(Params p) {
 #pragma unroll
       for (int n = 0; n < D / 8; n += 2) {
         uint32_t bv[4];
-        ldsm4t(bv, vs + (kt * 16 + (mat & 1) * 8 + rr) * LDK + n * 8 + (mat >> 1) * 8);
+        ldsm4t(bv, vs + swz<D>(kt * 16 + (mat & 1) * 8 + rr, n * 8 + (mat >> 1) * 8));
         mma(o[n], a, bv[0], bv[1]);
         mma(o[n + 1], a, bv[2], bv[3]);
       }
     }
-    __syncwarp();  // this buffer is refilled by the load two tiles ahead
+    __syncwarp();  // this stage is refilled by the load STAGES - 1 tiles ahead
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   // merge the warps of this CTA through shared memory (reusing the K/V buffers)
@@ -333,7 +347,7 @@ torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   const int grid = B * Hkv * ctas;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   static SmemOptIn attr64, attr128;
-  const size_t smem = (size_t)(ROWS + 4 * WARPS * KEYS) * (D + 8) * sizeof(bf16);
+  const size_t smem = (size_t)(ROWS + STAGES * 2 * WARPS * KEYS) * D * sizeof(bf16);
   if (D == 64) {
     C10_CUDA_CHECK(attr64.ensure(fa_decode_kernel<64>, (int)smem));
     fa_decode_kernel<64><<<grid, WARPS * 32, smem, st>>>(p);
