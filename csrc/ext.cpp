@@ -2,6 +2,8 @@
 #include <torch/extension.h>
 
 namespace mykb {
+void fp8_scaled_gemm(torch::Tensor a, torch::Tensor unit_sa, bool a_e5m2, torch::Tensor b, torch::Tensor unit_sb,
+                     bool b_e5m2, torch::Tensor row_scale, torch::Tensor col_scale, torch::Tensor d);
 torch::Tensor cast_bf16(torch::Tensor src);
 void dp_reduce_sumsq_multimem(int64_t grad_mc, torch::Tensor own_grad, torch::Tensor offsets, torch::Tensor prefix,
                               torch::Tensor partial, int64_t total);
@@ -153,6 +155,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_skinny", &mykb::gemm_skinny);
   m.def("mx_quantize", &mykb::mx_quantize);
   m.def("mx_gemm", &mykb::mx_gemm);
+  m.def("fp8_scaled_gemm", &mykb::fp8_scaled_gemm, "per-tensor / per-row scaled float8 GEMM on tcgen05");
   m.def("fa_decode", &mykb::fa_decode);
   m.def("kv_append", &mykb::kv_append);
   m.def("ngram_adam", &mykb::ngram_adam);

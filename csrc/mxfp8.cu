@@ -140,6 +140,11 @@ struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, k_blocks, total_tiles;
   int* status;
+  // optional dequantisation of per-tensor / per-row float8 operands, applied in the
+  // epilogue: D[m, n] = acc[m, n] * row_scale[m or 0] * col_scale[n or 0]
+  const float* row_scale;
+  const float* col_scale;
+  int row_scale_n, col_scale_n;  // 1 (scalar) or M / N
 };
 
 // block-scaled instruction descriptor (kind::mxf8f6f4, scale vector 1X, E8M0 scales)
@@ -304,6 +309,14 @@ mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + s * kSlab;
         tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
         if constexpr (!OUT_F32) tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+        if (p.row_scale != nullptr) {
+          const int row = mt * BM + q * 32 + lane;
+          const float rs = p.row_scale[p.row_scale_n == 1 ? 0 : min(row, p.M - 1)];
+          const int c0 = nt * BN + s * kSlab;
+#pragma unroll
+          for (int i = 0; i < kSlab; ++i)
+            v[i] *= rs * p.col_scale[p.col_scale_n == 1 ? 0 : min(c0 + i, p.N - 1)];
+        }
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncwarp();
 #pragma unroll
@@ -415,9 +428,34 @@ static void mx_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
 }
 
 // d (M, N) = a (M, K) . b (N, K)^T: a, b fp8 bits (uint8) with scale atoms sa, sb from
-// mx_quantize; d bf16 or fp32; accumulate adds into fp32 d.
+// mx_quantize; d bf16 or fp32; accumulate adds into fp32 d.  row_scale / col_scale
+// (optional fp32, 1 or M / N entries) multiply the product in the epilogue.
+static void mx_gemm_impl(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, torch::Tensor sb,
+                         bool b_e5m2, torch::Tensor d, bool accumulate, const torch::Tensor* row_scale,
+                         const torch::Tensor* col_scale);
+
 void mx_gemm(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, torch::Tensor sb, bool b_e5m2,
              torch::Tensor d, bool accumulate) {
+  mx_gemm_impl(a, sa, a_e5m2, b, sb, b_e5m2, d, accumulate, nullptr, nullptr);
+}
+
+// Per-tensor / per-row scaled float8 GEMM (the float8 training recipes' matmul):
+// d = (a * row_scale) . (b * col_scale)^T with a (M, K), b (N, K) fp8 bits, K a multiple
+// of 128.  The tensor cores run the block-scaled instruction with every block scale 2^0
+// (unit atoms, built once per shape by the caller) and the epilogue applies the scales.
+void fp8_scaled_gemm(torch::Tensor a, torch::Tensor unit_sa, bool a_e5m2, torch::Tensor b, torch::Tensor unit_sb,
+                     bool b_e5m2, torch::Tensor row_scale, torch::Tensor col_scale, torch::Tensor d) {
+  TORCH_CHECK(row_scale.scalar_type() == at::kFloat && col_scale.scalar_type() == at::kFloat &&
+                  row_scale.is_contiguous() && col_scale.is_contiguous() && row_scale.is_cuda() && col_scale.is_cuda(),
+              "fp8_scaled_gemm: fp32 CUDA scales");
+  TORCH_CHECK(row_scale.numel() == 1 || row_scale.numel() == a.size(0), "fp8_scaled_gemm: row scale 1 or M");
+  TORCH_CHECK(col_scale.numel() == 1 || col_scale.numel() == b.size(0), "fp8_scaled_gemm: column scale 1 or N");
+  mx_gemm_impl(a, unit_sa, a_e5m2, b, unit_sb, b_e5m2, d, false, &row_scale, &col_scale);
+}
+
+static void mx_gemm_impl(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, torch::Tensor sb,
+                         bool b_e5m2, torch::Tensor d, bool accumulate, const torch::Tensor* row_scale,
+                         const torch::Tensor* col_scale) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && d.is_cuda() && a.dim() == 2 && b.dim() == 2 && d.dim() == 2,
               "mx_gemm: 2-D CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kByte && b.scalar_type() == at::kByte, "mx_gemm: uint8 fp8 operands");
@@ -441,6 +479,12 @@ void mx_gemm(torch::Tensor a, torch::Tensor sa, bool a_e5m2, torch::Tensor b, to
   p.k_blocks = K / mx::BK;
   p.total_tiles = p.tiles_m * p.tiles_n;
   p.status = device_status();
+  if (row_scale != nullptr) {
+    p.row_scale = row_scale->data_ptr<float>();
+    p.col_scale = col_scale->data_ptr<float>();
+    p.row_scale_n = (int)row_scale->numel();
+    p.col_scale_n = (int)col_scale->numel();
+  }
   if (p.total_tiles == 0) return;
   CUtensorMap ta = make_tmap_3d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, 1, K, 0, mx::BK, mx::BM);
   CUtensorMap tb = make_tmap_3d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, 1, K, 0, mx::BK, mx::BN);

@@ -18,9 +18,10 @@ implementation of those three scaling statements for the three GEMMs of a linear
 
 Activations and gradients are quantised by this framework's kernels (``csrc/fp8.cu``: a
 fused per-row amax+cast, a per-tensor amax then cast, and a per-column amax then
-transposing cast for the weight-gradient operands).  The float8 GEMMs are cuBLASLt's
-scaled matmul (``torch._scaled_mm``), a plain library GEMM with the dequantisation scales
-applied to the fp32 accumulator.  On the CPU the same
+transposing cast for the weight-gradient operands).  The float8 GEMMs are this
+framework's tcgen05 block-scaled GEMM (``csrc/mxfp8.cu``) run with unit block scales, the
+per-tensor / per-row dequantisation scales applied to the fp32 accumulator in its
+epilogue (``fp8_scaled_gemm``).  On the CPU the same
 statement ``(a * s_a) @ (b * s_b)`` is evaluated in fp32, so the CPU tests check the
 scaling rules exactly.  The quantised weight (both orientations) is cached on the
 parameter and rebuilt after each optimizer step, like the bf16 weight copy of the plain
@@ -80,14 +81,37 @@ def quantize_act_t(x: torch.Tensor, dtype: torch.dtype) -> tuple[torch.Tensor, t
     return quantize(x.t().contiguous(), dtype, True)
 
 
+_UNIT_ATOMS: dict[tuple, torch.Tensor] = {}
+
+
+def _unit_atoms(rows: int, k: int, device) -> torch.Tensor:
+    """Block-scale atoms of value 2^0 (E8M0 127) for an fp8 operand of ``rows`` x ``k``."""
+    key = ((rows + 127) // 128, k // 128, str(device))
+    atoms = _UNIT_ATOMS.get(key)
+    if atoms is None:
+        atoms = _UNIT_ATOMS[key] = torch.full((key[0] * key[1] * 512,), 127, dtype=torch.uint8, device=device)
+    return atoms
+
+
 def scaled_mm(a: torch.Tensor, sa: torch.Tensor, b: torch.Tensor, sb: torch.Tensor,
               out_dtype: torch.dtype) -> torch.Tensor:
     """``(a * sa) @ (b * sb)^T`` for fp8 ``a`` (M, K) and ``b`` (N, K), both K-contiguous;
-    ``sa`` is a scalar or (M, 1), ``sb`` a scalar or (N, 1)."""
-    sbt = sb if sb.numel() == 1 else sb.reshape(1, -1)
-    if a.is_cuda:
-        return torch._scaled_mm(a, b.t(), sa, sbt, out_dtype=out_dtype)
-    return ((a.float() * sa) @ (b.float() * sb).t()).to(out_dtype)
+    ``sa`` is a scalar or (M, 1), ``sb`` a scalar or (N, 1).  CUDA: the tcgen05 block-scaled
+    GEMM with unit block scales and the per-tensor / per-row scales applied in its
+    epilogue (``fp8_scaled_gemm``); K must be a multiple of 128 (``eligible_shapes``)."""
+    if not a.is_cuda:
+        return ((a.float() * sa) @ (b.float() * sb).t()).to(out_dtype)
+    from ._ext import ext
+
+    m, k = a.shape
+    n = b.shape[0]
+    if k % 128:
+        raise ValueError(f"float8 GEMM needs the reduction size to be a multiple of 128, got {k}")
+    d = torch.empty(m, n, dtype=out_dtype, device=a.device)
+    ext().fp8_scaled_gemm(a.contiguous().view(torch.uint8), _unit_atoms(m, k, a.device), a.dtype == E5M2,
+                          b.contiguous().view(torch.uint8), _unit_atoms(n, k, b.device), b.dtype == E5M2,
+                          sa.reshape(-1).float().contiguous(), sb.reshape(-1).float().contiguous(), d)
+    return d
 
 
 class _WeightCache:
@@ -200,10 +224,11 @@ def fp8_linear(x: torch.Tensor, w: torch.Tensor, recipe: str) -> torch.Tensor:
 
 
 def eligible_shapes(x: torch.Tensor, w: torch.Tensor) -> bool:
-    """cuBLASLt's float8 GEMM wants every dimension (K, N and, for ``dW``, the token count M)
-    a multiple of 16."""
+    """The tcgen05 float8 GEMMs reduce over K (forward), N (data gradient) and the token
+    count M (weight gradient) in blocks of 128, so all three must be multiples of 128;
+    other linears stay in bf16."""
     rows = x.numel() // max(x.shape[-1], 1)
-    return w.shape[0] % 16 == 0 and w.shape[1] % 16 == 0 and x.shape[-1] == w.shape[1] and rows % 16 == 0
+    return w.shape[0] % 128 == 0 and w.shape[1] % 128 == 0 and x.shape[-1] == w.shape[1] and rows % 128 == 0
 
 
 class Float8Linear(nn.Linear):
