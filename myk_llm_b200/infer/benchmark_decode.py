@@ -1,8 +1,13 @@
-"""MTP speculative-decode benchmark (one GPU, random weights).
+"""MTP speculative-decode benchmark (random weights), one GPU or data-parallel replicas.
 
     python -m myk_llm_b200.infer.benchmark_decode                       # 200M + 2 MTP heads
     python -m myk_llm_b200.infer.benchmark_decode --batch 1 8 64 --prompt 2048 --new 256
     python -m myk_llm_b200.infer.benchmark_decode --impl reference      # the reference's own timing
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m myk_llm_b200.infer.benchmark_decode  # 8 replicas
+
+With several ranks every GPU runs an independent replica (its own model copy, prompts
+and decoder); rank 0 reports the sum of the replicas' tokens over the slowest replica's
+time (prefill and decode timed separately, max over ranks).
 
 Ours: :class:`~myk_llm_b200.infer.engine.StaticDecoder` prefills random prompts into
 static KV caches, then decodes greedily with the model's MTP heads drafting K tokens per
@@ -121,6 +126,29 @@ def bench_reference(batch: int, prompt: int, new: int, acceptance: float, seed: 
             "acceptance_assumed": acceptance}
 
 
+def _replicas(result: dict, world: int) -> dict:
+    """Aggregate one replica per rank: times are the max over ranks, token rates the sum of
+    the replicas' tokens over that time."""
+    import torch.distributed as dist
+
+    if world == 1 or "unavailable" in result:
+        return result
+    keys = [k for k in ("prefill_ms", "decode_ms", "iteration_ms") if k in result]
+    t = torch.tensor([result[k] for k in keys], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    out = dict(result, replicas=world)
+    for k, v in zip(keys, t.tolist()):
+        out[k] = v
+    b, new, prompt = result["batch"], result["new_tokens"], result["prompt"]
+    out["prefill_tokens_per_s"] = world * b * prompt / (out["prefill_ms"] / 1e3)
+    if "decode_ms" in out:
+        out["decode_tokens_per_s"] = world * b * new / (out["decode_ms"] / 1e3)
+    else:
+        tokens_per_it = sum(result["acceptance_assumed"] ** i for i in range(result["draft_depth"] + 1))
+        out["decode_tokens_per_s"] = world * b * tokens_per_it / (out["iteration_ms"] / 1e3)
+    return out
+
+
 def main(argv: list[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--batch", type=int, nargs="+", default=[1, 8, 64])
@@ -129,14 +157,30 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--impl", choices=["ours", "reference", "both"], default="ours")
     args = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
     for b in args.batch:
         acc = 0.0
         if args.impl in ("ours", "both"):
-            r = bench_ours(b, args.prompt, args.new)
+            r = _replicas(bench_ours(b, args.prompt, args.new, seed=rank), world)
             acc = r["acceptance"]
-            print(json.dumps(r), flush=True)
+            if rank == 0:
+                print(json.dumps(r), flush=True)
         if args.impl in ("reference", "both"):
-            print(json.dumps(bench_reference(b, args.prompt, args.new, acc)), flush=True)
+            r = _replicas(bench_reference(b, args.prompt, args.new, acc, seed=rank), world)
+            if rank == 0:
+                print(json.dumps(r), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
