@@ -74,6 +74,13 @@ MODELS = {
 }
 
 
+def _model_layers(model: str) -> int:
+    for o in MODELS[model][0]:
+        if o.startswith("model.num_layers="):
+            return int(o.split("=", 1)[1])
+    raise KeyError(model)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -83,7 +90,8 @@ def parse():
     ap.add_argument("--model", default="200m", choices=sorted(MODELS), help="benchmark config (default: 200m)")
     ap.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
                     help="(experiments only) extra config overrides for our arm, e.g. parallel.float8=none")
-    ap.add_argument("--layers", type=int, default=24, help="(debug only) fewer layers; results are not comparable")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="(debug only) override the model's layer count; results are not comparable")
     ap.add_argument("--ref-compile", default="auto", choices=["auto", "on", "off"],
                     help="reference arm: its parallel.compile switch (auto: on, falling back to off if Inductor fails)")
     return ap.parse_args()
@@ -231,7 +239,9 @@ def build_ours(world: int, layers: int, model: str, extra: list[str] | None = No
 
     ov, _, micro, _ = MODELS[model]
     ov = ov + list(extra or []) + [f"global_batch_size={micro * world}", "steps=1000", "schedule.warmup_ratio=0.0",
-                            "data.kind=synthetic", "logging.tensorboard=false", f"model.num_layers={layers}"]
+                                   "data.kind=synthetic", "logging.tensorboard=false"]
+    if layers is not None:
+        ov.append(f"model.num_layers={layers}")
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
     tr = Trainer(cfg, info, build_data=False)
@@ -257,8 +267,9 @@ def build_reference(world: int, layers: int, model: str, compile_blocks: bool = 
     from myk_llm.train.optim import build_optimizers
 
     ov, _, micro, _ = MODELS[model]
-    ov = list(ov) + [f"global_batch_size={micro * world}", f"model.num_layers={layers}",
-                                         f"parallel.compile={'true' if compile_blocks else 'false'}"]
+    ov = list(ov) + [f"global_batch_size={micro * world}", f"parallel.compile={'true' if compile_blocks else 'false'}"]
+    if layers is not None:
+        ov.append(f"model.num_layers={layers}")
     cfg = from_dict(TrainConfig, apply_overrides({}, ov))
     info = init_distributed()
     torch.manual_seed(cfg.seed)
@@ -438,7 +449,8 @@ def main():
                        "parallelism": f"dp{world}" + _parallel_desc(trainer, world),
                        "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
                        "l2": "working set >> 126 MB L2 (no flush inserted)",
-                       "layers": a.layers, **({"overrides": a.set} if a.set else {})},
+                       "layers": a.layers if a.layers is not None else _model_layers(a.model),
+                       **({"overrides": a.set} if a.set else {})},
             "clocks": clk,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
             "gpu_launches": launches,

@@ -742,13 +742,19 @@ static int sm_count() {
 // 2-D (token rows, head*d cols) tensor map of a (.., tokens, heads, d) tensor.
 static CUtensorMap token_map(const torch::Tensor& t) {
   const int64_t d = t.size(-1), h = t.size(-2);
-  TORCH_CHECK(t.stride(-1) == 1 && t.stride(-2) == d, "attention: heads must be packed (stride d)");
-  const int64_t row_stride = t.stride(-3);
+  // size-1 dimensions may carry any stride: only strides that address data are checked
+  TORCH_CHECK(t.stride(-1) == 1 && (h == 1 || t.stride(-2) == d), "attention: heads must be packed (stride d)");
+  int64_t row_stride = t.stride(-3);
   int64_t rows = t.size(-3);
   if (t.dim() == 4) {
-    TORCH_CHECK(t.stride(0) == t.size(1) * row_stride, "attention: batch rows must be uniformly strided");
+    if (t.size(1) == 1)
+      row_stride = t.stride(0);  // one token per sequence: rows step over the batch
+    else
+      TORCH_CHECK(t.size(0) == 1 || t.stride(0) == t.size(1) * row_stride,
+                  "attention: batch rows must be uniformly strided");
     rows *= t.size(0);
   }
+  if (rows == 1) row_stride = h * d;
   return make_tmap_3d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, h * d, rows, 1, row_stride, 0, 64, 128);
 }
 

@@ -78,6 +78,9 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
                                          c10::optional<torch::Tensor> dfinal, bool per_channel);
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel);
+torch::Tensor gdn_spec_window(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                              torch::Tensor state, torch::Tensor pq, torch::Tensor pk, torch::Tensor pv,
+                              torch::Tensor pg, torch::Tensor pbeta, torch::Tensor pending, bool per_channel);
 // attention_decode.cu
 torch::Tensor fa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor seqused,
                         double scale, int64_t left, int64_t right);
@@ -149,6 +152,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_fwd", &mykb::gdn_chunk_fwd_entry);
   m.def("gdn_chunk_bwd", &mykb::gdn_chunk_bwd);
   m.def("gdn_recurrent", &mykb::gdn_recurrent);
+  m.def("gdn_spec_window", &mykb::gdn_spec_window);
   m.def("ngram_stage", &mykb::ngram_stage);
   m.def("ngram_embed_fwd", &mykb::ngram_embed_fwd, "hashed n-gram embedding: hash, gather and sum in one kernel");
   m.def("ngram_embed_bwd", &mykb::ngram_embed_bwd, "hashed n-gram embedding backward: scatter-add per order");

@@ -1079,73 +1079,135 @@ __global__ void __launch_bounds__(NT) gdn_grad_kernel(
 
 // ---------------------------------------------------------------------- recurrence
 // Token-by-token decoding: one CTA per (batch row, head); state (dk x dv) fp32 in shared
-// memory; q/k normalised in-kernel.  Returns the outputs and the final state.
-__global__ void __launch_bounds__(NT)
-gdn_recurrent_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
-                     const float* __restrict__ gg, const float* __restrict__ bb, const float* __restrict__ init,
-                     bf16* __restrict__ out, float* __restrict__ fin, int T, int H, int dk, int dv, float qscale,
-                     bool per_channel) {
-  extern __shared__ float sm[];
-  float* S = sm;            // [dk][dv]
-  float* kv = S + dk * dv;  // [dk] normalised k
-  float* qv = kv + dk;      // [dk]
-  float* red = qv + dk;     // [32]
-  float* u = red + 32;      // [dv]
-  const int b = blockIdx.x / H, h = blockIdx.x % H;
+// memory; q/k normalised in-kernel.
+
+struct RecSmem {
+  float* S;    // [dk][dv]
+  float* kv;   // [dk] normalised k
+  float* qv;   // [dk] normalised, scaled q
+  float* red;  // [32]
+  float* u;    // [dv]
+  __device__ RecSmem(float* sm, int dk, int dv)
+      : S(sm), kv(sm + dk * dv), qv(sm + dk * dv + dk), red(sm + dk * dv + 2 * dk), u(sm + dk * dv + 2 * dk + 32) {}
+};
+
+// One token of the gated delta rule on the CTA's state:
+//   S <- exp(g) S;  u = beta (v - S^T k);  S <- S + k u^T;  o = S^T q  (when o != nullptr).
+// q/k/v point at this (token, head)'s vectors, g at its decay (one value, or dk values when
+// per_channel).  Ends with a barrier, so S may be read or written right after.
+__device__ __forceinline__ void rec_step(const RecSmem& s, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                         const bf16* __restrict__ v, const float* __restrict__ g, float beta, int dk,
+                                         int dv, float qscale, bool per_channel, bf16* __restrict__ o) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < dk * dv; i += blockDim.x) S[i] = init != nullptr ? init[((int64_t)b * H + h) * dk * dv + i] : 0.f;
-  for (int t = 0; t < T; ++t) {
-    const int64_t row = (int64_t)b * T + t;
-    __syncthreads();
-    if (tid < 32) {
-      float sk = 0.f, sq = 0.f;
-      for (int i = tid; i < dk; i += 32) {
-        const float a_ = __bfloat162float(k[(row * H + h) * dk + i]);
-        const float c_ = __bfloat162float(q[(row * H + h) * dk + i]);
-        kv[i] = a_;
-        qv[i] = c_;
-        sk += a_ * a_;
-        sq += c_ * c_;
-      }
+  __syncthreads();
+  if (tid < 32) {
+    float sk = 0.f, sq = 0.f;
+    for (int i = tid; i < dk; i += 32) {
+      const float a_ = __bfloat162float(k[i]);
+      const float c_ = __bfloat162float(q[i]);
+      s.kv[i] = a_;
+      s.qv[i] = c_;
+      sk += a_ * a_;
+      sq += c_ * c_;
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        sk += __shfl_xor_sync(0xffffffff, sk, o);
-        sq += __shfl_xor_sync(0xffffffff, sq, o);
-      }
-      if (tid == 0) {
-        red[0] = 1.f / fmaxf(sqrtf(sk), 1e-6f);
-        red[1] = qscale / fmaxf(sqrtf(sq), 1e-6f);
-      }
+    for (int off = 16; off > 0; off >>= 1) {
+      sk += __shfl_xor_sync(0xffffffff, sk, off);
+      sq += __shfl_xor_sync(0xffffffff, sq, off);
     }
-    __syncthreads();
-    for (int i = tid; i < dk; i += blockDim.x) {
-      kv[i] *= red[0];
-      qv[i] *= red[1];
-    }
-    __syncthreads();
-    const float beta = bb[row * H + h];
-    for (int i = tid; i < dk * dv; i += blockDim.x) {
-      const int r = i / dv;
-      const float dec = per_channel ? __expf(gg[(row * H + h) * dk + r]) : __expf(gg[row * H + h]);
-      S[i] *= dec;
-    }
-    __syncthreads();
-    for (int c = tid; c < dv; c += blockDim.x) {
-      float acc = 0.f;
-      for (int r = 0; r < dk; ++r) acc = fmaf(S[r * dv + c], kv[r], acc);
-      u[c] = beta * (__bfloat162float(v[(row * H + h) * dv + c]) - acc);
-    }
-    __syncthreads();
-    for (int i = tid; i < dk * dv; i += blockDim.x) S[i] = fmaf(kv[i / dv], u[i % dv], S[i]);
-    __syncthreads();
-    for (int c = tid; c < dv; c += blockDim.x) {
-      float acc = 0.f;
-      for (int r = 0; r < dk; ++r) acc = fmaf(S[r * dv + c], qv[r], acc);
-      out[(row * H + h) * dv + c] = __float2bfloat16(acc);
+    if (tid == 0) {
+      s.red[0] = 1.f / fmaxf(sqrtf(sk), 1e-6f);
+      s.red[1] = qscale / fmaxf(sqrtf(sq), 1e-6f);
     }
   }
   __syncthreads();
-  for (int i = tid; i < dk * dv; i += blockDim.x) fin[((int64_t)b * H + h) * dk * dv + i] = S[i];
+  for (int i = tid; i < dk; i += blockDim.x) {
+    s.kv[i] *= s.red[0];
+    s.qv[i] *= s.red[1];
+  }
+  __syncthreads();
+  for (int i = tid; i < dk * dv; i += blockDim.x) {
+    const float dec = per_channel ? __expf(g[i / dv]) : __expf(g[0]);
+    s.S[i] *= dec;
+  }
+  __syncthreads();
+  for (int c = tid; c < dv; c += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < dk; ++r) acc = fmaf(s.S[r * dv + c], s.kv[r], acc);
+    s.u[c] = beta * (__bfloat162float(v[c]) - acc);
+  }
+  __syncthreads();
+  for (int i = tid; i < dk * dv; i += blockDim.x) s.S[i] = fmaf(s.kv[i / dv], s.u[i % dv], s.S[i]);
+  __syncthreads();
+  if (o != nullptr) {
+    for (int c = tid; c < dv; c += blockDim.x) {
+      float acc = 0.f;
+      for (int r = 0; r < dk; ++r) acc = fmaf(s.S[r * dv + c], s.qv[r], acc);
+      o[c] = __float2bfloat16(acc);
+    }
+  }
+  __syncthreads();
+}
+
+// Inputs of token t of row b, head h in a (B, T, H, d) layout.
+struct RecInputs {
+  const bf16 *q, *k, *v;
+  const float *g, *beta;
+  int T, H, dk, dv;
+  bool per_channel;
+  __device__ __forceinline__ int64_t row(int b, int t) const { return ((int64_t)b * T + t) * H; }
+};
+
+__device__ __forceinline__ void rec_token(const RecSmem& s, const RecInputs& in, int b, int t, int h, float qscale,
+                                          bf16* out) {
+  const int64_t r = in.row(b, t) + h;
+  rec_step(s, in.q + r * in.dk, in.k + r * in.dk, in.v + r * in.dv, in.g + (in.per_channel ? r * in.dk : r),
+           in.beta[r], in.dk, in.dv, qscale, in.per_channel, out != nullptr ? out + r * in.dv : nullptr);
+}
+
+// Decode T tokens from `init` (or zeros); outputs and the final state.
+__global__ void __launch_bounds__(NT)
+gdn_recurrent_kernel(RecInputs in, const float* __restrict__ init, bf16* __restrict__ out, float* __restrict__ fin,
+                     float qscale) {
+  extern __shared__ float sm[];
+  const RecSmem s(sm, in.dk, in.dv);
+  const int b = blockIdx.x / in.H, h = blockIdx.x % in.H;
+  const int64_t sz = (int64_t)in.dk * in.dv, base = ((int64_t)b * in.H + h) * sz;
+  for (int i = threadIdx.x; i < sz; i += blockDim.x) s.S[i] = init != nullptr ? init[base + i] : 0.f;
+  for (int t = 0; t < in.T; ++t) rec_token(s, in, b, t, h, qscale, out);
+  for (int i = threadIdx.x; i < sz; i += blockDim.x) fin[base + i] = s.S[i];
+}
+
+// One speculative-decoding window.  `state` holds the committed state of every (row,
+// head); the previous window's inputs wait in `pend` and the first pending[b] of them were
+// accepted.  The CTA folds those into the state and stores it (the new committed state),
+// runs the W tokens of this window from there producing their outputs, and leaves this
+// window's inputs in `pend` for the next call.  State traffic per call: one read and one
+// write, whatever the acceptance.
+__global__ void __launch_bounds__(NT)
+gdn_spec_window_kernel(RecInputs in, RecInputs pend, float* __restrict__ state, const int* __restrict__ pending,
+                       bf16* __restrict__ out, float qscale) {
+  extern __shared__ float sm[];
+  const RecSmem s(sm, in.dk, in.dv);
+  const int b = blockIdx.x / in.H, h = blockIdx.x % in.H;
+  const int64_t sz = (int64_t)in.dk * in.dv, base = ((int64_t)b * in.H + h) * sz;
+  for (int i = threadIdx.x; i < sz; i += blockDim.x) s.S[i] = state[base + i];
+  const int n = min(max(pending[b], 0), pend.T);
+  for (int t = 0; t < n; ++t) rec_token(s, pend, b, t, h, qscale, nullptr);
+  for (int i = threadIdx.x; i < sz; i += blockDim.x) state[base + i] = s.S[i];
+  for (int t = 0; t < in.T; ++t) rec_token(s, in, b, t, h, qscale, out);
+  // this window's inputs become the pending ones (only this CTA reads its (b, h) slice)
+  const int gdim = in.per_channel ? in.dk : 1;
+  for (int t = 0; t < in.T; ++t) {
+    const int64_t r = in.row(b, t) + h;
+    for (int i = threadIdx.x; i < in.dk; i += blockDim.x) {
+      const_cast<bf16*>(pend.q)[r * in.dk + i] = in.q[r * in.dk + i];
+      const_cast<bf16*>(pend.k)[r * in.dk + i] = in.k[r * in.dk + i];
+    }
+    for (int i = threadIdx.x; i < in.dv; i += blockDim.x) const_cast<bf16*>(pend.v)[r * in.dv + i] = in.v[r * in.dv + i];
+    for (int i = threadIdx.x; i < gdim; i += blockDim.x) const_cast<float*>(pend.g)[r * gdim + i] = in.g[r * gdim + i];
+    if (threadIdx.x == 0) const_cast<float*>(pend.beta)[r] = in.beta[r];
+  }
 }
 
 // ---------------------------------------------------------------------- short conv
@@ -1577,10 +1639,32 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
   return {dq, dk, dv, dg, db, dinit};
 }
 
+static gdnk::RecInputs rec_inputs(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                                  const torch::Tensor& g, const torch::Tensor& beta, bool per_channel) {
+  gdnk::RecInputs in;
+  in.q = (const bf16*)q.data_ptr();
+  in.k = (const bf16*)k.data_ptr();
+  in.v = (const bf16*)v.data_ptr();
+  in.g = g.data_ptr<float>();
+  in.beta = beta.data_ptr<float>();
+  in.T = q.size(1);
+  in.H = q.size(2);
+  in.dk = q.size(3);
+  in.dv = v.size(3);
+  in.per_channel = per_channel;
+  return in;
+}
+
+static int rec_smem(int dk, int dv) {
+  const int smem = (dk * dv + 2 * dk + 32 + dv) * 4;
+  TORCH_CHECK(smem <= 227 * 1024, "gated delta rule decode: state too large");
+  return smem;
+}
+
 std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor gg,
                                          torch::Tensor beta, c10::optional<torch::Tensor> init, bool per_channel) {
   c10::cuda::CUDAGuard guard(q.device());
-  const int B = q.size(0), T = q.size(1), H = q.size(2), dk = q.size(3), dv = v.size(3);
+  const int B = q.size(0), H = q.size(2), dk = q.size(3), dv = v.size(3);
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && v.size(2) == H, "gdn_recurrent: bf16, as many value heads as key heads");
   auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
   auto out = torch::empty_like(vc);
@@ -1589,16 +1673,46 @@ std::vector<torch::Tensor> gdn_recurrent(torch::Tensor q, torch::Tensor k, torch
   auto bf = beta.to(at::kFloat).contiguous();
   torch::Tensor init_f;
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
-  const int smem = (dk * dv + 2 * dk + 32 + dv) * 4;
-  TORCH_CHECK(smem <= 227 * 1024, "gdn_recurrent: state too large");
+  const int smem = rec_smem(dk, dv);
   static SmemOptIn a_rec;
   C10_CUDA_CHECK(a_rec.ensure(gdnk::gdn_recurrent_kernel, 227 * 1024));
   gdnk::gdn_recurrent_kernel<<<B * H, gdnk::NT, smem, at::cuda::getCurrentCUDAStream()>>>(
-      (const bf16*)qc.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), gf.data_ptr<float>(),
-      bf.data_ptr<float>(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)out.data_ptr(),
-      fin.data_ptr<float>(), T, H, dk, dv, 1.f / std::sqrt((float)dk), per_channel);
+      rec_inputs(qc, kc, vc, gf, bf, per_channel), init.has_value() ? init_f.data_ptr<float>() : nullptr,
+      (bf16*)out.data_ptr(), fin.data_ptr<float>(), 1.f / std::sqrt((float)dk));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {out, fin};
+}
+
+torch::Tensor gdn_spec_window(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                              torch::Tensor state, torch::Tensor pq, torch::Tensor pk, torch::Tensor pv,
+                              torch::Tensor pg, torch::Tensor pbeta, torch::Tensor pending, bool per_channel) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const int B = q.size(0), W = q.size(1), H = q.size(2), dk = q.size(3), dv = v.size(3);
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+              "gdn_spec_window: bf16 q/k/v");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && g.is_contiguous() && beta.is_contiguous(),
+              "gdn_spec_window: contiguous inputs");
+  TORCH_CHECK(g.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat, "gdn_spec_window: fp32 g / beta");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.size(0) == B && state.size(1) == H &&
+                  state.size(2) == dk && state.size(3) == dv,
+              "gdn_spec_window: state (B, H, dk, dv) fp32");
+  TORCH_CHECK(pq.sizes() == q.sizes() && pk.sizes() == k.sizes() && pv.sizes() == v.sizes() &&
+                  pg.sizes() == g.sizes() && pbeta.sizes() == beta.sizes(),
+              "gdn_spec_window: pending buffers shaped like the window");
+  TORCH_CHECK(pq.is_contiguous() && pk.is_contiguous() && pv.is_contiguous() && pg.is_contiguous() &&
+                  pbeta.is_contiguous() && pq.scalar_type() == at::kBFloat16 && pg.scalar_type() == at::kFloat,
+              "gdn_spec_window: pending buffers contiguous, bf16 q/k/v, fp32 g / beta");
+  TORCH_CHECK(pending.scalar_type() == at::kInt && pending.numel() == B, "gdn_spec_window: pending (B,) int32");
+  TORCH_CHECK(v.size(2) == H && beta.size(1) == W, "gdn_spec_window: shapes");
+  auto out = torch::empty_like(v);
+  const int smem = rec_smem(dk, dv);
+  static SmemOptIn a_spec;
+  C10_CUDA_CHECK(a_spec.ensure(gdnk::gdn_spec_window_kernel, 227 * 1024));
+  gdnk::gdn_spec_window_kernel<<<B * H, gdnk::NT, smem, at::cuda::getCurrentCUDAStream()>>>(
+      rec_inputs(q, k, v, g, beta, per_channel), rec_inputs(pq, pk, pv, pg, pbeta, per_channel),
+      state.data_ptr<float>(), pending.data_ptr<int>(), (bf16*)out.data_ptr(), 1.f / std::sqrt((float)dk));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
 }
 
 }  // namespace mykb

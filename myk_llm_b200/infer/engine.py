@@ -17,6 +17,12 @@ accepts or rejects drafts.  This module is that loop:
    gives draft ``d_k`` of the next round.  Finally ``seqlens += a + 1``.  Keys/values written
    for rejected positions lie beyond ``seqlens`` and are overwritten later.
 
+DeltaNet layers keep a ``SpecDeltaState``: the committed conv/recurrent state plus the last
+window's inputs, of which the first ``a_b + 1`` are folded in at the start of the next
+window (one state read and one write per layer and round).  Looped models get one cache
+entry per core iteration; n-gram models carry the last ``context`` committed tokens per row
+as the embedding's left context.
+
 Verification is greedy, so the emitted sequence equals plain greedy decoding of the main
 model.  A round has static shapes and no host synchronisation, so on CUDA it is captured
 once in a CUDA graph and replayed; the host looks at the output only every few rounds.
@@ -29,8 +35,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from ..models.config import DELTANET
-from ..models.mixers import Attention, CrossAttention, StaticKV
+from ..models.mixers import DeltaNet, SpecDeltaState, StaticKV
 from ..models.transformer import MykLLM
 
 
@@ -60,9 +65,6 @@ class StaticDecoder:
     def __init__(self, model: MykLLM, batch_size: int, max_len: int, draft_depth: int | None = None,
                  use_cuda_graph: bool = True) -> None:
         cfg = model.config
-        if DELTANET in cfg.layer_types or cfg.loop.core:
-            raise NotImplementedError("static-cache decoding covers attention / YOCO models; use generate() for "
-                                      "DeltaNet or looped models")
         self.model = model.eval()
         self.cfg = cfg
         self.B, self.cap = batch_size, max_len
@@ -72,6 +74,7 @@ class StaticDecoder:
         dt = torch.bfloat16 if dev.type == "cuda" else next(model.parameters()).dtype
         a = cfg.attention
         self.seqlens = torch.zeros(batch_size, dtype=torch.int32, device=dev)
+        self.pending = torch.zeros(batch_size, dtype=torch.int32, device=dev)  # tokens the last round accepted
         cap = max_len + self.K + 2
 
         def kv():
@@ -79,24 +82,26 @@ class StaticDecoder:
                             torch.zeros(batch_size, cap, a.num_kv_heads, a.head_dim, dtype=dt, device=dev),
                             self.seqlens)
 
-        self.cache: list = []
-        for i, blk in enumerate(model.layers):
-            if isinstance(blk.mixer, CrossAttention):
-                continue
-            self.cache.append(kv())
-        if model.shared_kv is not None:
-            self.cache.append(kv())
-        if model.cross_kv_layer is not None:
-            pass  # the shared KV is the source layer's own StaticKV
-        self.cache += [None] * sum(isinstance(b.mixer, CrossAttention) for b in model.layers)
-        self.mtp_cache = [kv() for _ in range(self.K)]
+        def state_for(block):
+            if isinstance(block.mixer, DeltaNet):
+                return SpecDeltaState(block.mixer.inner, batch_size, self.K + 1, self.pending, dt, dev)
+            return kv()
+
+        self.cache: list = [None if e is None else kv() if e == "shared_kv" else state_for(e)
+                            for e in model.cache_blocks()]
+        self.mtp_cache = [state_for(m.block) for m in list(model.mtp)[:self.K]]
+        self.delta_states = [c for c in self.cache + self.mtp_cache if isinstance(c, SpecDeltaState)]
+        ngram = model.embed.ngram
+        self.context = ngram.context if ngram is not None else 0
+        self.history = torch.zeros(batch_size, self.context, dtype=torch.long, device=dev)  # n-gram left context
+        self._ctx_ar = torch.arange(self.context, device=dev)
         self.use_graph = use_cuda_graph and dev.type == "cuda"
         self.graph = None
         self.out_tokens = None
 
     # ---------------------------------------------------------------------------------
-    def _main(self, ids, pos):
-        return self.model(ids, position_ids=pos, cache=self.cache, use_cache=True)
+    def _main(self, ids, pos, prefix=None):
+        return self.model(ids, position_ids=pos, cache=self.cache, use_cache=True, prefix_ids=prefix)
 
     def _head_argmax(self, h):
         return self.model.logits(h).float().argmax(-1)
@@ -114,6 +119,10 @@ class StaticDecoder:
         B, P = prompts.shape
         assert B == self.B
         self.seqlens.zero_()
+        self.pending.zero_()
+        for st in self.delta_states:
+            st.reset()
+            st.prefill = True
         pos = torch.arange(P, device=self.device).expand(B, -1)
         out = self._main(prompts, pos)
         y_last = self._head_argmax(out.hidden[:, -1:])[:, 0]
@@ -127,6 +136,10 @@ class StaticDecoder:
             nxt = seq[:, k + 1:k + 1 + P]
             hidden, hn = self._mtp(k, hidden, nxt, pos)
             drafts.append(self._head_argmax(hn[:, -1:])[:, 0])
+        for st in self.delta_states:
+            st.prefill = False
+        if self.context:
+            self.history.copy_(self.model.embed.ngram.padded_tokens(prompts, None)[:, -self.context:])
         self.seqlens += P
         self.bonus = y_last.clone()
         self.drafts = torch.stack(drafts, 1) if drafts else torch.zeros(B, 0, dtype=torch.long, device=self.device)
@@ -136,7 +149,7 @@ class StaticDecoder:
         K, B = self.K, self.B
         w = torch.cat([self.bonus[:, None], self.drafts], 1)  # (B, K+1)
         pos = self.seqlens.long()[:, None] + self._ar[None, :K + 1]
-        out = self._main(w, pos)
+        out = self._main(w, pos, self.history if self.context else None)
         y = self._head_argmax(out.hidden)  # (B, K+1)
         if K:
             match = (w[:, 1:] == y[:, :-1]).int()
@@ -178,6 +191,11 @@ class StaticDecoder:
         self.bonus.copy_(bonus)
         if K:
             self.drafts.copy_(torch.stack(fresh, 1))
+        if self.context:  # the accepted window tokens w[0..a] extend the n-gram context
+            span = torch.cat([self.history, w], 1)
+            idx = (a + 1)[:, None] + self._ctx_ar[None]
+            self.history.copy_(span.gather(1, idx))
+        self.pending.copy_((a + 1).int())
         self.seqlens += (a + 1).int()
 
     @torch.no_grad()
@@ -223,17 +241,25 @@ class StaticDecoder:
         toks = torch.cat([prompts, self.out_tokens[:, :max_new_tokens]], 1)
         return toks, st
 
+    def _live_tensors(self) -> list[torch.Tensor]:
+        """Decoder state a round mutates besides the attention caches (whose writes land
+        beyond ``seqlens`` and are harmless to repeat)."""
+        out = [self.seqlens, self.pending, self.history, self.bonus, self.drafts, self.out_tokens, self.out_len,
+               self.acc_sum, self.acc_depth]
+        for st in self.delta_states:
+            out += [st.recurrent, *st.inputs] + ([st.conv, st.window_x] if st.conv is not None else [])
+        return out
+
     def _graph_step(self):
         # warm up on a side stream, then capture one round
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
-        snap = [t.clone() for t in (self.seqlens, self.bonus, self.drafts, self.out_tokens, self.out_len, self.acc_sum,
-                                    self.acc_depth)]
+        live = self._live_tensors()
+        snap = [t.clone() for t in live]
         with torch.cuda.stream(s):
             self._round()
         torch.cuda.current_stream().wait_stream(s)
-        for t, v in zip((self.seqlens, self.bonus, self.drafts, self.out_tokens, self.out_len, self.acc_sum,
-                         self.acc_depth), snap):
+        for t, v in zip(live, snap):
             t.copy_(v)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):

@@ -4,8 +4,8 @@ attention, and Gated DeltaNet / Kimi Delta Attention.
 Every mixer is called as ``mixer(x, position_ids, varlen, state, use_cache) ->
 (out, new_state)`` (reference: ``src/myk_llm/model/mixers.py:1-12``).  ``varlen`` holds
 packed-document boundaries for document-masked training; ``state`` is the mixer's own
-decode cache (``KVCache`` for attention, ``DeltaState`` for DeltaNet).  Cross-decoder
-mixers receive the shared KV as ``state``.
+decode cache (``KVCache`` / ``StaticKV`` for attention, ``DeltaState`` /
+``SpecDeltaState`` for DeltaNet).  Cross-decoder mixers receive the shared KV as ``state``.
 
 The parameter names are the reference's (which for DeltaNet are flash-linear-attention's
 ``GatedDeltaNet`` / ``KimiDeltaAttention`` names under ``mixer.inner``), so DCP
@@ -297,6 +297,51 @@ class DeltaState:
     recurrent: torch.Tensor  # (batch, heads, head_k_dim, head_v_dim) fp32
 
 
+class SpecDeltaState:
+    """Static decode cache of a DeltaNet layer for speculative decoding.
+
+    Holds the committed conv inputs (batch, channels, K-1) and recurrent state (batch,
+    heads, dk, dv) fp32, plus the previous window's inputs, of which row b accepted the
+    first ``pending[b]`` tokens (``pending`` int32 is shared by all layers and set by the
+    decoder after verification).  A window call commits that accepted prefix first, then
+    runs the new window without committing it, so rejected drafts never reach the state.
+    ``prefill`` switches a call to a plain pass from the committed state (which it then
+    replaces); the decoder sets it around the prompt pass.  All buffers are static, so a
+    round can be captured in a CUDA graph.
+    """
+
+    def __init__(self, inner: "DeltaNetInner", batch: int, window: int, pending: torch.Tensor,
+                 dtype: torch.dtype, device: torch.device) -> None:
+        h, dk, dv = inner.num_heads, inner.head_k_dim, inner.head_v_dim
+        channels = 2 * inner.key_dim + inner.value_dim
+        self.window, self.pending, self.prefill = window, pending, False
+        self.conv = (torch.zeros(batch, channels, inner.conv_size - 1, dtype=dtype, device=device)
+                     if inner.use_short_conv else None)
+        self.window_x = torch.zeros(batch, window, channels, dtype=dtype, device=device) if inner.use_short_conv else None
+        self.recurrent = torch.zeros(batch, h, dk, dv, dtype=torch.float32, device=device)
+        gdim = (h, dk) if inner.kind == "kda" else (h,)
+        self.inputs = (torch.zeros(batch, window, h, dk, dtype=dtype, device=device),
+                       torch.zeros(batch, window, h, dk, dtype=dtype, device=device),
+                       torch.zeros(batch, window, h, dv, dtype=dtype, device=device),
+                       torch.zeros(batch, window, *gdim, dtype=torch.float32, device=device),
+                       torch.zeros(batch, window, h, dtype=torch.float32, device=device))
+
+    def reset(self) -> None:
+        self.recurrent.zero_()
+        if self.conv is not None:
+            self.conv.zero_()
+
+    def commit_conv(self, raw: torch.Tensor) -> None:
+        """Conv inputs: fold the accepted prefix of the last window into the committed
+        state, then keep this window's raw inputs ``raw`` (batch, W, channels)."""
+        if self.conv is None:
+            return
+        span = torch.cat([self.conv, self.window_x.transpose(1, 2)], 2)  # (B, C, K-1+W)
+        idx = self.pending.long()[:, None] + torch.arange(self.conv.size(2), device=span.device)[None]
+        self.conv.copy_(span.gather(2, idx[:, None, :].expand(-1, span.size(1), -1)))
+        self.window_x.copy_(raw)
+
+
 class DeltaNet(nn.Module):
     def __init__(self, config: ModelConfig) -> None:
         super().__init__()
@@ -331,6 +376,9 @@ class DeltaNet(nn.Module):
                 og = ops.linear(h, inner.g_proj.weight)
         else:
             og = None
+        spec = isinstance(state, SpecDeltaState)
+        if spec and not state.prefill:
+            return self._spec_window(qkv, raw_gate, b, og, state), state
         conv_state = state.conv if state is not None else None
         if inner.use_short_conv:
             qkv, new_conv = ops.causal_conv1d(qkv, inner.conv_weight(), cu_seqlens=cu, initial_state=conv_state,
@@ -355,8 +403,38 @@ class DeltaNet(nn.Module):
         out = ops.linear(o.reshape(b_, t_, inner.value_dim), inner.o_proj.weight)
         if packed:
             out = out.reshape(bsz, seq, hidden)
+        if spec:  # prefill of a speculative decoder: the prompt's final states become committed
+            if new_conv is not None:
+                state.conv.copy_(new_conv)
+            state.recurrent.copy_(final)
+            return out, state
         new_state = DeltaState(new_conv, final) if use_cache else None
         return out, new_state
+
+    def _spec_window(self, qkv, raw_gate, b, og, state: SpecDeltaState):
+        """One speculative window (batch layout, W = state.window tokens)."""
+        inner = self.inner
+        b_, t_ = qkv.shape[:2]
+        if t_ != state.window:
+            raise ValueError(f"speculative window of {t_} tokens, the cache was built for {state.window}")
+        if inner.use_short_conv:
+            state.commit_conv(qkv)
+            qkv, _ = ops.causal_conv1d(qkv, inner.conv_weight(), initial_state=state.conv)
+        else:
+            qkv = ops.silu(qkv)
+        q, k, v = ops.split_cols(qkv, (inner.key_dim, inner.key_dim, inner.value_dim))
+        q = q.reshape(b_, t_, inner.num_heads, inner.head_k_dim)
+        k = k.reshape(b_, t_, inner.num_heads, inner.head_k_dim)
+        v = v.reshape(b_, t_, inner.num_v_heads, inner.head_v_dim)
+        if self.kind == "kda":
+            g = ops.kda_gate(raw_gate.reshape(b_, t_, inner.num_heads, inner.head_k_dim), inner.A_log, inner.dt_bias)
+        else:
+            g = ops.gdn_gate(raw_gate, inner.A_log, inner.dt_bias)
+        beta = torch.sigmoid(b.float())
+        o = ops.delta_spec_window(q, k, v, g, beta, state.recurrent, state.inputs, state.pending,
+                                  per_channel_decay=self.kind == "kda")
+        o = inner.o_norm(o, og.reshape(b_, t_, inner.num_v_heads, inner.head_v_dim) if og is not None else None)
+        return ops.linear(o.reshape(b_, t_, inner.value_dim), inner.o_proj.weight)
 
 
 def build_mixer(config: ModelConfig, layer_type: str, first_global: bool) -> nn.Module:

@@ -435,6 +435,22 @@ class MykLLM(nn.Module):
                 self.core_observer(it, state)
         return materialize(state)
 
+    def cache_blocks(self, iterations: int | None = None) -> list[Any]:
+        """What each entry of the decode cache belongs to, in the order ``forward`` consumes
+        them (the ``_Pass`` layout): the block of every self-decoder call (a looped core's
+        blocks once per iteration), ``"shared_kv"`` for the projected YOCO KV, and None for
+        each cross-decoder block."""
+        n, start, loop = len(self.layers), self.cross_start, self.config.loop
+        order = list(range(start))
+        if loop.core and loop.prelude < start:
+            core = list(range(loop.prelude, loop.prelude + loop.core))
+            order = list(range(loop.prelude)) + core * self.num_iterations(iterations) + \
+                list(range(loop.prelude + loop.core, start))
+        entries: list[Any] = [self.layers[i] for i in order]
+        if self.shared_kv is not None:
+            entries.append("shared_kv")
+        return entries + [None] * (n - start)
+
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return ops.linear(hidden, self.lm_head.weight)
 

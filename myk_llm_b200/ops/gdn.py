@@ -14,7 +14,9 @@ CUDA kernels (``csrc/gdn.cu``):
 * ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64, head dims 128) with the state
   kept in fp32; each CTA owns one (sequence, head, half of the value columns) and walks
   its chunks; the algorithm is stated in :mod:`myk_llm_b200.ops.gdn_chunk`;
-* ``gdn_recurrent``: token-by-token decode over a state cache.
+* ``gdn_recurrent``: token-by-token decode over a state cache;
+* ``gdn_spec_window``: one speculative-decoding window over a committed state plus the
+  previous window's pending inputs (:func:`spec_window`).
 """
 
 from __future__ import annotations
@@ -123,3 +125,32 @@ def gated_delta_rule(q, k, v, g, beta, initial_state=None, cu_seqlens=None, cu_s
     o, fin = _DeltaRule.apply(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
                               beta.float().contiguous(), initial_state, cu)
     return o, (fin if output_final_state else None)
+
+
+def spec_window(q, k, v, g, beta, state, pending_inputs, pending, per_channel_decay=False):
+    """One speculative-decoding window of the gated delta rule.
+
+    ``state`` (B, H, dk, dv) fp32 is the committed state of every row; ``pending_inputs``
+    = (q, k, v, g, beta) of the previous window, of which row b accepted the first
+    ``pending[b]`` tokens.  Folds those into ``state`` in place (the new committed state),
+    runs this window's W tokens from it and returns their outputs (B, W, H, dv); this
+    window's inputs are copied into ``pending_inputs`` for the next call.  So a window can
+    be verified and only the accepted prefix committed, with one state read and one state
+    write per call.
+    """
+    pq, pk, pv, pg, pb = pending_inputs
+    g, beta = g.float().contiguous(), beta.float().contiguous()
+    if q.is_cuda:
+        return ext().gdn_spec_window(q.contiguous(), k.contiguous(), v.contiguous(), g, beta, state, pq, pk, pv, pg, pb,
+                                     pending, bool(per_channel_decay))
+    for b in range(q.size(0)):
+        n = int(pending[b])
+        if n > 0:
+            _, fin = ref.delta_rule_ref(pq[b:b + 1, :n], pk[b:b + 1, :n], pv[b:b + 1, :n], pg[b:b + 1, :n],
+                                        pb[b:b + 1, :n], initial_state=state[b:b + 1],
+                                        per_channel_decay=per_channel_decay)
+            state[b] = fin[0]
+    o, _ = ref.delta_rule_ref(q, k, v, g, beta, initial_state=state, per_channel_decay=per_channel_decay)
+    for dst, src in zip(pending_inputs, (q, k, v, g, beta)):
+        dst.copy_(src)
+    return o.to(v.dtype)

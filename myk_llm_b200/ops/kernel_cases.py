@@ -134,6 +134,34 @@ def build(case: str):
         do = torch.randn_like(o)
         return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), 10 * attn, \
             (q.numel() * 4 + k.numel() * 4) * 2, "FlashAttention bwd B8 L4096 16q/4kv h64 causal (200M layer)"
+    if case in ("fa_fwd_docs_h64", "fa_bwd_docs_h64"):
+        # the 200M training step's attention: 8 rows of 4096 packed with the synthetic
+        # loader's documents (geometric lengths, mean 1024), document-masked varlen
+        import numpy as np
+
+        from ..data.synthetic import packed_row
+        from .attention import flash_attn_varlen_func
+
+        lens = []
+        for i in range(8):
+            lens += packed_row(np.random.default_rng([0, i]), 4096, 65536, 1024, 0)["seqlens"].tolist()
+        cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=dev)
+        q = torch.randn(32768, 16, 64, device=dev).bfloat16().requires_grad_()
+        k = torch.randn(32768, 4, 64, device=dev).bfloat16().requires_grad_()
+        v = torch.randn(32768, 4, 64, device=dev).bfloat16().requires_grad_()
+        attn = 16 * sum(n * n / 2 for n in lens) * 64
+
+        def fwd():
+            return flash_attn_varlen_func(q, k, v, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=4096,
+                                          max_seqlen_k=4096, causal=True)
+
+        what = f"FlashAttention {{}} 200M layer, 8x4096 packed with {len(lens)} synthetic documents, 16q/4kv h64"
+        if case == "fa_fwd_docs_h64":
+            return fwd, 4 * attn, (q.numel() * 2 + k.numel() * 2) * 2, what.format("fwd")
+        o = fwd()
+        do = torch.randn_like(o)
+        return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), 10 * attn, \
+            (q.numel() * 4 + k.numel() * 4) * 2, what.format("bwd")
     if case == "gdn":
         from .gdn import gated_delta_rule
 
@@ -174,7 +202,7 @@ def build(case: str):
     raise ValueError(f"unknown case {case!r}")
 
 
-CASES = ["gemm", "gemm_fwd_200m", "gemm_gather_self_200m", "gemm_gather_prefetch_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
+CASES = ["gemm", "gemm_fwd_200m", "gemm_gather_self_200m", "gemm_gather_prefetch_200m", "gemm_wgrad_200m", "mxgemm", "mxquant", "fp8quant_rows", "fp8quant_tensor", "fp8quant_cols_t", "fa_fwd", "fa_bwd", "fa_fwd_h64", "fa_bwd_h64", "fa_fwd_docs_h64", "fa_bwd_docs_h64", "gdn", "rmsnorm", "ce", "decode_attn", "skinny"]
 
 
 def time_case(case: str, reps: int = 20) -> dict:
