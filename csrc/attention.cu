@@ -28,6 +28,8 @@
 //
 // Semantics follow the reference (src/myk_llm/ops/flash_attn.py): queries end-aligned to
 // the keys, window (left, right) with -1 unbounded, empty rows output 0 with LSE +inf.
+#include <type_traits>
+
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -836,8 +838,7 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
 struct FaBwdParams {
   FaParams f;          // geometry (heads, seqs, window, ...); f.out / f.lse unused
   int k_tiles;         // ceil(max_k / 128)
-  const float* lse;    // natural-log LSE from the forward
-  const float* delta;  // rowsum(dO * O), same layout as lse
+  const float2* ld;    // {base-2 LSE, Delta = rowsum(dO * O)} per (query, head), in the LSE layout
   __nv_bfloat16* dq;   // (tokens, heads, d)
   __nv_bfloat16* dk;   // (tokens_k, kv_heads, d)
   __nv_bfloat16* dv;
@@ -887,9 +888,8 @@ struct DkvSmem {
   static constexpr int kV = kK + kTile;
   static constexpr int kQ0 = kV + kTile;
   static constexpr int kDO0 = kQ0 + kStages * kTile;
-  static constexpr int kLse = kDO0 + kStages * kTile;  // [stages][128] base-2 LSE of the query tile
-  static constexpr int kDelta = kLse + kStages * 512;  // [stages][128] Delta of the query tile
-  static constexpr int kBars = kDelta + kStages * 512;
+  static constexpr int kLd = kDO0 + kStages * kTile;  // [stages][128] {base-2 LSE, Delta} of the query tile
+  static constexpr int kBars = kLd + kStages * 1024;
   static constexpr int kTotal = kBars + 256;
 };
 
@@ -939,7 +939,7 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     mbar_init(kv_full, 1);
     mbar_init(kv_empty, 1);
     for (int i = 0; i < ST; ++i) {
-      mbar_init(&q_full[i], 1);
+      mbar_init(&q_full[i], 1 + 32);  // the TMA transaction plus the producer lanes' cp.async
       mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -958,10 +958,11 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
 
   if (warp == 0) {
-    // Producer warp: lane 0 issues the TMA copies; all lanes stage the query tile's LSE
-    // (pre-scaled to base 2) and Delta into shared memory before lane 0 arrives.
-    float* s_lse = reinterpret_cast<float*>(smem + S::kLse);
-    float* s_delta = reinterpret_cast<float*>(smem + S::kDelta);
+    // Producer warp: lane 0 issues the TMA copies of Q / dO; every lane copies the
+    // {LSE, Delta} pairs of four query rows with cp.async, whose completion the stage's
+    // mbarrier tracks (one no-increment arrival per lane), so no load latency sits on the
+    // producer's path.  Rows past the document are zero-filled (the masks drop them).
+    const uint32_t s_ld = smem_u32(smem + S::kLd);
     const int64_t total_q = p.f.cu_q != nullptr ? (int64_t)p.f.cu_q[p.f.num_seqs] : 0;
     int stage = 0, items = 0;
     uint32_t phase = 0;
@@ -986,16 +987,11 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           for (int i = 0; i < 4; ++i) {
             const int c = lane * 4 + i;
             const int qi = qt * 128 + c;
-            float l2 = INFINITY, dl = 0.f;
-            if (qi < it.g.len_q) {
-              const int64_t li = lse_index(p.f, it.seq, h, it.g.q_start, qi, total_q);
-              l2 = p.lse[li] * kLog2e;
-              dl = p.delta[li];
-            }
-            s_lse[stage * 128 + c] = l2;
-            s_delta[stage * 128 + c] = dl;
+            const bool in = qi < it.g.len_q;
+            const float2* src = in ? p.ld + lse_index(p.f, it.seq, h, it.g.q_start, qi, total_q) : p.ld;
+            cp_async_8(s_ld + (uint32_t)(stage * 128 + c) * 8u, src, in);
           }
-          __syncwarp();
+          cp_async_mbar_arrive_noinc(&q_full[stage]);
           if (lane == 0) {
             mbar_arrive_expect_tx(&q_full[stage], 2 * S::kTile);
             const int row = it.g.q_start + qt * 128;
@@ -1090,8 +1086,7 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int half = (warp - 2) >> 2;  // queries [32 half, 32 half + 32) of each 64-query sub-tile
     const int r = qw * 32 + lane;      // TMEM lane = key row within the tile
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    const float* s_lse = reinterpret_cast<const float*>(smem + S::kLse);
-    const float* s_delta = reinterpret_cast<const float*>(smem + S::kDelta);
+    const float4* s_ld = reinterpret_cast<const float4*>(smem + S::kLd);  // two queries per float4
     uint32_t u = 0;
     int n = 0, items = 0;
     bool ok = true;
@@ -1116,40 +1111,44 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
               const bool edge = (it.k0 + 127 >= it.g.len_k) || (q0 + 63 >= it.g.len_q) ||
                                 (p.f.right >= 0 && it.k0 + 127 > q0 + off + p.f.right) ||
                                 (p.f.left >= 0 && it.k0 < q0 + 63 + off - p.f.left);
-              const float* c_lse = s_lse + st_idx * 128 + 64 * j + 32 * half;
-              const float* c_delta = s_delta + st_idx * 128 + 64 * j + 32 * half;
+              // the queries this key row sees form one range [lo, lo + span) of the 32 columns
+              const int qb = q0 + 32 * half;
+              int lo = 0, hi = min(32, it.g.len_q - qb);
+              if (p.f.right >= 0) lo = max(lo, kp - off - p.f.right - qb);
+              if (p.f.left >= 0) hi = min(hi, kp - off + p.f.left - qb + 1);
+              const int span = kp < it.g.len_k ? max(0, hi - lo) : 0;
+              // the stage's {LSE, Delta} pairs landed with its Q / dO tiles
+              if (j == 0 && !mbar_wait_warp(&q_full[st_idx], (n / ST) & 1, p.f.status, __LINE__)) {
+                ok = false;
+                break;
+              }
+              const float4* c_ld = s_ld + (st_idx * 128 + 64 * j + 32 * half) / 2;
               tmem_wait_ld();
               uint32_t pk[16], dk[16];
               const float2 sc2 = make_float2(p.f.scale_log2, p.f.scale_log2), ps2 = make_float2(p.scale, p.scale);
+              // one straight-line body per case, so the compiler can interleave all 32 columns
+              auto body = [&](auto masked) {
 #pragma unroll
-              for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 l4 = reinterpret_cast<const float4*>(c_lse)[i4];
-                const float4 d4 = reinterpret_cast<const float4*>(c_delta)[i4];
-                const float2 nl[2] = {make_float2(-l4.x, -l4.y), make_float2(-l4.z, -l4.w)};
-                const float2 nd[2] = {make_float2(-d4.x, -d4.y), make_float2(-d4.z, -d4.w)};
-#pragma unroll
-                for (int e = 0; e < 4; e += 2) {
-                  const int i = i4 * 4 + e;
-                  const float2 a = ffma2(make_float2(sv[i], sv[i + 1]), sc2, nl[e >> 1]);
+                for (int i4 = 0; i4 < 16; ++i4) {
+                  const float4 v = c_ld[i4];  // {lse2, delta} of queries 2 i4 and 2 i4 + 1
+                  const int i = 2 * i4;
+                  const float2 a = ffma2(make_float2(sv[i], sv[i + 1]), sc2, make_float2(-v.x, -v.z));
                   float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
-                  if (edge) {
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                      const int qi = q0 + 32 * half + i + u;
-                      const int qpos = qi + off;
-                      bool vis = qi < it.g.len_q && kp < it.g.len_k;
-                      if (p.f.right >= 0) vis = vis && kp <= qpos + p.f.right;
-                      if (p.f.left >= 0) vis = vis && kp >= qpos - p.f.left;
-                      if (!vis) (u == 0 ? pv.x : pv.y) = 0.f;
-                    }
+                  if constexpr (decltype(masked)::value) {
+                    if ((unsigned)(i - lo) >= (unsigned)span) pv.x = 0.f;
+                    if ((unsigned)(i + 1 - lo) >= (unsigned)span) pv.y = 0.f;
                   }
                   sv[i] = pv.x;
                   sv[i + 1] = pv.y;
-                  const float2 d = fmul2(fmul2(pv, ps2), fadd2(make_float2(dp[i], dp[i + 1]), nd[e >> 1]));
+                  const float2 d = fmul2(fmul2(pv, ps2), fadd2(make_float2(dp[i], dp[i + 1]), make_float2(-v.y, -v.w)));
                   dp[i] = d.x;
                   dp[i + 1] = d.y;
                 }
-              }
+              };
+              if (edge)
+                body(std::true_type{});
+              else
+                body(std::false_type{});
 #pragma unroll
               for (int m = 0; m < 16; ++m) {
                 pk[m] = pack_bf16x2(sv[2 * m], sv[2 * m + 1]);
@@ -1391,9 +1390,9 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       const bool qvalid_tile = it.rows == 128;
       float lse2 = INFINITY, dl = 0.f;
       if (qvalid) {
-        const int64_t li = lse_index(f, it.seq, it.head, it.g.q_start, qi, total_q);
-        lse2 = p.lse[li] * kLog2e;
-        dl = p.delta[li];
+        const float2 v = p.ld[lse_index(f, it.seq, it.head, it.g.q_start, qi, total_q)];
+        lse2 = v.x;
+        dl = v.y;
       }
       for (int jt = 0; jt < it.n_kv && ok; ++jt) {
         for (int j = 0; j < 2; ++j, ++u) {
@@ -1474,10 +1473,11 @@ fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
   }
 }
 
-// Delta[row, h] = sum_d dO * O (fp32), written in the LSE layout.
+// ld[row, h] = {LSE * log2(e), Delta = sum_d dO * O} (fp32), in the LSE layout: what the
+// backward kernels read per query, one 8-byte load.
 __global__ void fa_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
-                                float* __restrict__ delta, int64_t rows, int heads, int D, bool packed,
-                                int max_q) {
+                                const float* __restrict__ lse, float2* __restrict__ ld, int64_t rows, int heads,
+                                int D, bool packed, int max_q) {
   // D / 8 consecutive lanes share one (token, head) row: one 16-byte load of each tensor
   // per lane, then a shuffle reduction within the group.
   const int per = D / 8;
@@ -1501,11 +1501,8 @@ __global__ void fa_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __
   if (active && sub == 0) {
     const int64_t tok = gw / heads;
     const int h = (int)(gw % heads);
-    if (packed) delta[(int64_t)h * rows + tok] = s;
-    else {
-      const int64_t b_ = tok / max_q, qi = tok % max_q;
-      delta[(b_ * heads + h) * max_q + qi] = s;
-    }
+    const int64_t li = packed ? (int64_t)h * rows + tok : ((tok / max_q) * heads + h) * max_q + tok % max_q;
+    ld[li] = make_float2(lse[li] * kLog2e, s);
   }
 }
 
@@ -1566,17 +1563,17 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
   auto dq = torch::empty({q_rows, f.heads, D}, q.options());
   auto dk = torch::empty({k_rows, f.kv_heads, D}, q.options());
   auto dv = torch::empty({k_rows, f.kv_heads, D}, q.options());
-  auto delta = torch::empty_like(lse);
+  TORCH_CHECK(lse.is_contiguous() && lse.scalar_type() == at::kFloat, "fa_bwd: contiguous fp32 lse");
+  auto ld = torch::empty({lse.numel(), 2}, lse.options());  // {base-2 LSE, Delta} per (query, head)
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (q_rows > 0) {
     const int64_t threads = q_rows * f.heads * (D / 8);
     fa_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-        (const __nv_bfloat16*)dout_c.data_ptr(), (const __nv_bfloat16*)out.data_ptr(), delta.data_ptr<float>(),
-        q_rows, f.heads, D, packed, (int)max_q);
+        (const __nv_bfloat16*)dout_c.data_ptr(), (const __nv_bfloat16*)out.data_ptr(), lse.data_ptr<float>(),
+        reinterpret_cast<float2*>(ld.data_ptr<float>()), q_rows, f.heads, D, packed, (int)max_q);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  p.lse = lse.data_ptr<float>();
-  p.delta = delta.data_ptr<float>();
+  p.ld = reinterpret_cast<const float2*>(ld.data_ptr<float>());
   p.dq = (__nv_bfloat16*)dq.data_ptr();
   p.dk = (__nv_bfloat16*)dk.data_ptr();
   p.dv = (__nv_bfloat16*)dv.data_ptr();
@@ -1608,16 +1605,16 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
 
 namespace mykb {
 namespace {
-// Working memory of mykb_flash_attn_bwd_noalloc: Delta (one float per query row and head)
-// and the status word its bounded waits write.  Every GPU that loads this library holds
-// these (4 MB + 256 B) until the process exits.
-static __device__ __align__(256) float g_noalloc_delta[MYKB_NOALLOC_MAX_ROWS_X_HEADS];
+// Working memory of mykb_flash_attn_bwd_noalloc: {base-2 LSE, Delta} (two floats per query
+// row and head) and the status word its bounded waits write.  Every GPU that loads this
+// library holds these (8 MB + 256 B) until the process exits.
+static __device__ __align__(256) float2 g_noalloc_ld[MYKB_NOALLOC_MAX_ROWS_X_HEADS];
 static __device__ __align__(256) int g_noalloc_status[64];
 
 thread_local char g_noalloc_err[256] = {0};
 
 struct NoallocScratch {
-  float* delta = nullptr;
+  float2* ld = nullptr;
   int* status = nullptr;
 };
 
@@ -1636,7 +1633,7 @@ NoallocScratch noalloc_scratch(int dev, cudaError_t* err) {
   std::lock_guard<std::mutex> lock(mu);
   if (!ready[dev]) {
     NoallocScratch s;
-    *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.delta), g_noalloc_delta);
+    *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.ld), g_noalloc_ld);
     if (*err != cudaSuccess) return {};
     *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_noalloc_status);
     if (*err != cudaSuccess) return {};
@@ -1707,14 +1704,13 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     f.total_items = f.q_tiles * f.num_seqs * f.heads;
     p.k_tiles = (max_k + 127) / 128;
     p.scale = softmax_scale;
-    p.lse = lse;
-    p.delta = sc.delta;
+    p.ld = sc.ld;
     p.dq = static_cast<__nv_bfloat16*>(dq);
     p.dk = static_cast<__nv_bfloat16*>(dk);
     p.dv = static_cast<__nv_bfloat16*>(dv);
     const int64_t threads = (int64_t)rows_q * heads * (head_dim / 8);
     fa_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), sc.delta, rows_q, heads,
+        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), lse, sc.ld, rows_q, heads,
         head_dim, packed, max_q);
     err = cudaGetLastError();
     if (err != cudaSuccess) return noalloc_fail(7, cudaGetErrorString(err));

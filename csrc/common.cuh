@@ -117,6 +117,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// 8-byte asynchronous global -> shared copy (cp.async); with valid == false nothing is read
+// and the destination is zero-filled.
+__device__ __forceinline__ void cp_async_8(uint32_t dst_smem, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst_smem), "l"(src), "r"(valid ? 8 : 0)
+               : "memory");
+}
+
+// The mbarrier receives one arrival when all of this thread's earlier cp.async copies have
+// landed (no increment of the expected count: the barrier's init count includes it).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -16,7 +16,7 @@
 extern "C" {
 #endif
 
-// Largest rows * heads the built-in scratch holds (one float per query row and head).
+// Largest rows * heads the built-in scratch holds (two floats per query row and head).
 #define MYKB_NOALLOC_MAX_ROWS_X_HEADS (1 << 20)
 
 // FlashAttention backward for packed (cu_seqlens != NULL, num_seqs documents) or batch

@@ -5,6 +5,8 @@
 //   s = x + u;  y = rmsnorm(s)                                   (add + rmsnorm, s returned)
 //   y = rmsnorm(o) * w * act(g),  act = silu (GDN) or sigmoid (KDA)
 //
+// Width-64 rows (per-head norms at head_dim 64) use their own kernels, two elements per lane.
+//
 // Backward accumulates the weight gradient in registers per warp, reduces it across the
 // block in shared memory and adds it to global memory once per block.
 #include <torch/extension.h>
@@ -356,6 +358,74 @@ __global__ void rmsnorm64_bwd_kernel(const __nv_bfloat16* dy, const __nv_bfloat1
   if (threadIdx.x < 64) atomicAdd(&dw[threadIdx.x], sdw[threadIdx.x]);
 }
 
+// Gated RMSNorm over width-64 rows (per-head DeltaNet outputs of head_v_dim 64): one warp
+// per row, two elements per lane.
+__device__ __forceinline__ void gate_act(float g, int act, float& a, float& da) {
+  const float s = sigm(g);
+  if (act == 0) {
+    a = g * s;
+    da = s * (1.f + g * (1.f - s));
+  } else {
+    a = s;
+    da = s * (1.f - s);
+  }
+}
+
+__global__ void gated64_fwd_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g,
+                                   const float* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                                   float* __restrict__ rstd, int rows, float eps, int act) {
+  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const int64_t base = (int64_t)row * 64;
+  const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(o + base)[lane]);
+  const float r = rsqrtf(warp_sum(v.x * v.x + v.y * v.y) / 64 + eps);
+  if (lane == 0) rstd[row] = r;
+  float a0 = 1.f, a1 = 1.f, unused;
+  if (g != nullptr) {
+    const float2 gv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g + base)[lane]);
+    gate_act(gv.x, act, a0, unused);
+    gate_act(gv.y, act, a1, unused);
+  }
+  reinterpret_cast<__nv_bfloat162*>(y + base)[lane] =
+      __floats2bfloat162_rn(v.x * r * w[2 * lane] * a0, v.y * r * w[2 * lane + 1] * a1);
+}
+
+__global__ void gated64_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ o,
+                                   const __nv_bfloat16* __restrict__ g, const float* __restrict__ w,
+                                   const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dO,
+                                   __nv_bfloat16* __restrict__ dg, float* __restrict__ dw, int rows, int act) {
+  __shared__ float sdw[64];
+  if (threadIdx.x < 64) sdw[threadIdx.x] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row < rows) {
+    const int64_t base = (int64_t)row * 64;
+    const float2 ov = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(o + base)[lane]);
+    const float2 dv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(dy + base)[lane]);
+    const float r = rstd[row];
+    const float w0 = w[2 * lane], w1 = w[2 * lane + 1];
+    const float h0 = ov.x * r, h1 = ov.y * r;
+    float a0 = 1.f, a1 = 1.f, da0 = 0.f, da1 = 0.f;
+    if (g != nullptr) {
+      const float2 gv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g + base)[lane]);
+      gate_act(gv.x, act, a0, da0);
+      gate_act(gv.y, act, a1, da1);
+      reinterpret_cast<__nv_bfloat162*>(dg + base)[lane] =
+          __floats2bfloat162_rn(dv.x * h0 * w0 * da0, dv.y * h1 * w1 * da1);
+    }
+    const float dn0 = dv.x * a0, dn1 = dv.y * a1;  // d (normed * w)
+    const float g0 = dn0 * w0, g1 = dn1 * w1;
+    const float dot = warp_sum(g0 * h0 + g1 * h1) / 64;
+    reinterpret_cast<__nv_bfloat162*>(dO + base)[lane] = __floats2bfloat162_rn(r * (g0 - h0 * dot), r * (g1 - h1 * dot));
+    atomicAdd(&sdw[2 * lane], dn0 * h0);
+    atomicAdd(&sdw[2 * lane + 1], dn1 * h1);
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) atomicAdd(&dw[threadIdx.x], sdw[threadIdx.x]);
+}
+
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<std::vector<torch::Tensor>> add,
                                        double eps, c10::ScalarType out_dtype) {
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 2, "rmsnorm_fwd: contiguous 2-D CUDA x");
@@ -462,6 +532,13 @@ std::vector<torch::Tensor> gated_rmsnorm_fwd(torch::Tensor o, c10::optional<torc
   const __nv_bfloat16* gp = g.has_value() ? (const __nv_bfloat16*)g->data_ptr() : nullptr;
   const int grid = norm_grid(rows);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (H == 64) {
+    gated64_fwd_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>((const __nv_bfloat16*)o.data_ptr(), gp,
+                                                               wf.data_ptr<float>(), (__nv_bfloat16*)y.data_ptr(),
+                                                               rstd.data_ptr<float>(), rows, (float)eps, (int)act);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {y, rstd};
+  }
   MYKB_NC_SWITCH(H, gated_fwd_kernel<NC><<<grid, 32 * kNormWarps, 0, st>>>(
                         (const __nv_bfloat16*)o.data_ptr(), gp, wf.data_ptr<float>(), (__nv_bfloat16*)y.data_ptr(),
                         rstd.data_ptr<float>(), rows, (float)eps, (int)act));
@@ -481,6 +558,14 @@ std::vector<torch::Tensor> gated_rmsnorm_bwd(torch::Tensor dy, torch::Tensor o, 
   const __nv_bfloat16* gp = g.has_value() ? (const __nv_bfloat16*)g->data_ptr() : nullptr;
   const int grid = norm_grid(rows);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (H == 64) {
+    gated64_bwd_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)o.data_ptr(), gp, wf.data_ptr<float>(),
+        rstd.data_ptr<float>(), (__nv_bfloat16*)dO.data_ptr(), g.has_value() ? (__nv_bfloat16*)dg.data_ptr() : nullptr,
+        dw.data_ptr<float>(), rows, (int)act);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {dO, dg, dw.to(w.scalar_type())};
+  }
   MYKB_NC_SWITCH(H, gated_bwd_kernel<NC><<<grid, 32 * kNormWarps, 0, st>>>(
                         (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)o.data_ptr(), gp,
                         wf.data_ptr<float>(), rstd.data_ptr<float>(), (__nv_bfloat16*)dO.data_ptr(),

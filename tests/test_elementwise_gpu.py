@@ -60,14 +60,15 @@ def test_add_rmsnorm():
 
 
 @pytest.mark.parametrize("act", ["swish", "sigmoid"])
-def test_gated_rmsnorm(act):
+@pytest.mark.parametrize("width", [64, 128])
+def test_gated_rmsnorm(act, width):
     from myk_llm_b200 import ops
     from myk_llm_b200.ops import reference as ref
 
     torch.manual_seed(2)
-    o = torch.randn(64, 3, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    g = torch.randn(64, 3, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    w = torch.randn(128, device="cuda", requires_grad=True)
+    o = torch.randn(64, 3, width, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    g = torch.randn(64, 3, width, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(width, device="cuda", requires_grad=True)
     y = ops.gated_rms_norm(o, g, w, 1e-5, act)
     gy = torch.randn_like(y)
     (y.float() * gy.float()).sum().backward()

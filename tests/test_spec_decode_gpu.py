@@ -64,7 +64,7 @@ def test_delta_spec_window_matches_recurrence(per_channel):
     state = state0.clone()
     o1 = ops.delta_spec_window(*first, state, pend, pending, per_channel_decay=per_channel)
     want1, _ = ref.delta_rule_ref(*first, initial_state=state0, per_channel_decay=per_channel)
-    torch.testing.assert_close(o1.float(), want1, atol=3e-2, rtol=3e-2)
+    torch.testing.assert_close(o1.float(), want1.float(), atol=3e-2, rtol=3e-2)
     accepted = torch.tensor([0, 1, 2, 3, 2], dtype=torch.int32, device=dev)
     pending.copy_(accepted)
     o2 = ops.delta_spec_window(*second, state, pend, pending, per_channel_decay=per_channel)
@@ -76,7 +76,7 @@ def test_delta_spec_window_matches_recurrence(per_channel):
             _, s = ref.delta_rule_ref(*(t[sl, :n] for t in first), initial_state=s, per_channel_decay=per_channel)
         torch.testing.assert_close(state[sl], s, atol=1e-3, rtol=1e-3)
         want2, _ = ref.delta_rule_ref(*(t[sl] for t in second), initial_state=s, per_channel_decay=per_channel)
-        torch.testing.assert_close(o2[sl].float(), want2, atol=3e-2, rtol=3e-2)
+        torch.testing.assert_close(o2[sl].float(), want2.float(), atol=3e-2, rtol=3e-2)
     for p, t in zip(pend, second):
         assert torch.equal(p, t.to(p.dtype))
     from myk_llm_b200.ops import ext
