@@ -27,11 +27,14 @@
 // reduction stay in fp32.  A 64-row chunk maps onto 16-row MMA fragments without the
 // 128-row minimum of a TMEM accumulator tile, and the sequential kernel keeps its state
 // slice in registers between chunks.
+#include <cstdlib>
+
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "gdn_geo.cuh"
 
 namespace mykb {
 namespace gdnk {
@@ -47,41 +50,6 @@ constexpr int LDF = 65;    // row stride of 64-wide fp32 tiles
 constexpr int PARTS = 4;   // value-column slices of the sequential kernels
 constexpr int PW = DV / PARTS;  // 32 columns per slice
 constexpr int NT = 256;    // threads of every chunk kernel (8 warps)
-
-struct Geo {
-  const int* cu;         // packed document offsets or nullptr (batch layout)
-  const int* chunk_off;  // first global chunk of every sequence; [num_seqs] = total
-  const int* order;      // sequences by decreasing length (sequential kernels start long ones first)
-  int num_seqs, heads, seq_len;
-  int64_t rows;          // token rows (batch x time); per-token scalars are head-major [heads][rows]
-  int64_t row_q, row_v;  // elements between consecutive token rows of q/k and of v
-};
-
-__device__ __forceinline__ void seq_span(const Geo& g, int s, int& t0, int& len) {
-  if (g.cu != nullptr) {
-    t0 = g.cu[s];
-    len = g.cu[s + 1] - t0;
-  } else {
-    t0 = s * g.seq_len;
-    len = g.seq_len;
-  }
-}
-
-// Global chunk -> (first token row, valid rows).  False for chunk indices past the end.
-__device__ __forceinline__ bool locate(const Geo& g, int chunk, int& row0, int& n) {
-  if (chunk >= g.chunk_off[g.num_seqs]) return false;
-  int lo = 0, hi = g.num_seqs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (g.chunk_off[mid] <= chunk) lo = mid; else hi = mid - 1;
-  }
-  int t0, len;
-  seq_span(g, lo, t0, len);
-  const int a = (chunk - g.chunk_off[lo]) * C;
-  row0 = t0 + a;
-  n = min(C, len - a);
-  return n > 0;
-}
 
 // ---------------------------------------------------------------- warp MMA helpers
 __device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const bf16* p) {
@@ -289,7 +257,7 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(Geo g, const bf16* __restr
                                                       const float* __restrict__ bb, float* __restrict__ gcum,
                                                       float* __restrict__ kinv, float* __restrict__ qinv,
                                                       bf16* __restrict__ w_out, bf16* __restrict__ u_out,
-                                                      float qscale) {
+                                                      bf16* __restrict__ t_out, float qscale) {
   extern __shared__ __align__(16) unsigned char smraw[];
   PrepSm& s = *reinterpret_cast<PrepSm*>(smraw);
   const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
@@ -372,6 +340,11 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(Geo g, const bf16* __restr
   }
   __syncthreads();
   const int64_t cbase = ((int64_t)chunk * g.heads + h) * C * DK;
+  for (int i = tid; i < C * C / 8; i += NT) {  // T for the backward (64 x 64 bf16 per chunk and head)
+    const int r = i >> 3, c = (i & 7) * 8;
+    *reinterpret_cast<uint4*>(t_out + ((int64_t)chunk * g.heads + h) * C * C + r * C + c) =
+        *reinterpret_cast<const uint4*>(s.tb + r * LDS + c);
+  }
   const int nb = (warp >> 2) * 64;
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
@@ -1535,7 +1508,14 @@ static void gdn_check(const torch::Tensor& q, const torch::Tensor& k, const torc
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), who, ": contiguous q/k/v");
 }
 
-// Returns (o, final state, saved...) with saved = [states, u, p, w, gcum, kinv, qinv].
+void gdn_grad_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                        const torch::Tensor& v, const torch::Tensor& beta_f, const torch::Tensor& gcum,
+                        const torch::Tensor& kinv, const torch::Tensor& qinv, const torch::Tensor& u,
+                        const torch::Tensor& states, const torch::Tensor& dstates, const torch::Tensor& tmat,
+                        const torch::Tensor& dout, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv,
+                        torch::Tensor& dg, torch::Tensor& db, float qscale, int* status, cudaStream_t stream);
+
+// Returns (o, final state, saved...) with saved = [states, u, p, w, gcum, kinv, qinv, t].
 std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor gg,
                                                torch::Tensor beta, c10::optional<torch::Tensor> init,
                                                c10::optional<torch::Tensor> cu, bool per_channel) {
@@ -1554,6 +1534,7 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
   auto w = torch::empty({nb, H, gdnk::C, gdnk::DK}, q.options());
   auto u = torch::empty({nb, H, gdnk::C, gdnk::DV}, q.options());
   auto p = torch::empty({nb, H, gdnk::C, gdnk::C}, q.options());
+  auto tmat = torch::empty({nb, H, gdnk::C, gdnk::C}, q.options());  // T = (I + A)^-1 per chunk and head
   auto gcum = torch::empty({H, rows}, f32);  // head-major per-token scalars
   auto kinv = torch::empty({H, rows}, f32);
   auto qinv = torch::empty({H, rows}, f32);
@@ -1572,7 +1553,7 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
     gdnk::gdn_prep_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::PrepSm), st>>>(
         g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), gf.data_ptr<float>(),
         bf.data_ptr<float>(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(),
-        (bf16*)w.data_ptr(), (bf16*)u.data_ptr(), qscale);
+        (bf16*)w.data_ptr(), (bf16*)u.data_ptr(), (bf16*)tmat.data_ptr(), qscale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     gdnk::gdn_state_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::StateSm), st>>>(
         g, (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), (const bf16*)w.data_ptr(),
@@ -1587,7 +1568,7 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
   } else {
     fin.zero_();
   }
-  return {out, fin, states, u, p, w, gcum, kinv, qinv};
+  return {out, fin, states, u, p, w, gcum, kinv, qinv, tmat};
 }
 
 // Returns (dq, dk, dv, dg, dbeta, dinit).
@@ -1597,14 +1578,14 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
                                          c10::optional<torch::Tensor> dfinal, bool per_channel) {
   c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(!per_channel, "gdn_chunk_bwd: per-channel decay is not handled by the chunk kernels");
-  TORCH_CHECK(saved.size() == 7, "gdn_chunk_bwd: expects the 7 saved tensors of gdn_chunk_fwd");
+  TORCH_CHECK(saved.size() == 8, "gdn_chunk_bwd: expects the 8 saved tensors of gdn_chunk_fwd");
   gdn_check(q, k, v, "gdn_chunk_bwd");
   torch::Tensor chunk_off, order;
   int bound = 0;
   gdnk::Geo g = make_geo(q, v, cu, chunk_off, order, bound);
   const int H = g.heads;
   auto &states = saved[0], &u = saved[1], &p = saved[2], &w = saved[3], &gcum = saved[4], &kinv = saved[5],
-       &qinv = saved[6];
+       &qinv = saved[6], &tmat = saved[7];
   auto bf = beta.to(at::kFloat).contiguous();
   auto doc = dout.to(at::kBFloat16).contiguous();
   auto f32 = q.options().dtype(at::kFloat);
@@ -1627,12 +1608,18 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
         qinv.data_ptr<float>(), (const bf16*)w.data_ptr(), (const bf16*)p.data_ptr(), (const bf16*)doc.data_ptr(),
         dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, (bf16*)dstates.data_ptr(), dinit.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    static const bool mma_sync_grad = std::getenv("MYKB_GDN_GRAD_MMA_SYNC") != nullptr;
+    if (!mma_sync_grad) {
+      gdn_grad_tc_launch(g, bound, q, k, v, bf, gcum, kinv, qinv, u, states, dstates, tmat, doc, dq, dk, dv, dg, db,
+                         qscale, device_status(), st);
+    } else {
     gdnk::gdn_grad_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::GradSm), st>>>(
         g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), bf.data_ptr<float>(),
         gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(), (const bf16*)u.data_ptr(),
         (const bf16*)states.data_ptr(), (const bf16*)dstates.data_ptr(), (const bf16*)doc.data_ptr(), (bf16*)dq.data_ptr(),
         (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(), dg.data_ptr<float>(), db.data_ptr<float>(), qscale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
   } else {
     dinit.zero_();
   }

@@ -1,0 +1,593 @@
+// Gated DeltaNet chunk gradient on the tcgen05 tensor cores (sm_100a).
+//
+// One CTA per (64-token chunk, head).  Inputs arrive by TMA in 128-byte-swizzled tiles
+// (K^, Q^ rows of the chunk, dO, U, the state S0 entering the chunk, dS at its end, and
+// T = (I + A)^-1 stored by the forward), every chunk product is a 64-row tcgen05 MMA
+// issued by one thread with its fp32 accumulator in TMEM, and eight warps run the
+// element-wise steps between the products on accumulator rows read with tcgen05.ld.
+// The algebra is the one of the mma.sync kernel in gdn.cu (gdn_grad_kernel) and of the
+// PyTorch statement in myk_llm_b200/ops/gdn_chunk.py:
+//
+//   P   = lower_incl(E * Q^K^T)                      dP  = dO U^T
+//   dU  = P^T dO + F (K^ dS)                         dY  = T^T dU,  dV = beta dY
+//   dA  = -(dY U^T) (strictly lower, times E)        dKK = beta dA,  dPE = dP * E
+//   dQ^ = dPE K^ + e^gamma (dO S0^T)
+//   dK^ = -e^gamma beta (dY S0^T) + dKK K^ + dKK^T K^ + dPE^T Q^ + F (U dS^T)
+//
+// followed by the l2-norm backward of q and k and the reverse cumulative sum of dgamma.
+// Reference: the chunked gated delta rule of flash-linear-attention, which the reference
+// framework calls from src/myk_llm/model/mixers.py (GatedDeltaNet).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "gdn_geo.cuh"
+#include "gdn_tc.cuh"
+#include "tma_host.h"
+
+namespace mykb {
+namespace gtc {
+
+constexpr int C = 64;
+constexpr int NT = 256;
+
+// Shared memory (bytes from a 1024-aligned base).
+struct GradTcSm {
+  static constexpr int kKH = 0;          // K^   64 x 128
+  static constexpr int kQH = 16384;      // Q^   64 x 128
+  static constexpr int kDO = 32768;      // dO   64 x 128
+  static constexpr int kU = 49152;       // U    64 x 128
+  static constexpr int kS0 = 65536;      // S0  128 x 128 (rows dk, columns dv)
+  static constexpr int kDS = 98304;      // dS  128 x 128
+  static constexpr int kT = 131072;      // T    64 x 64, then dKK
+  static constexpr int kP = 139264;      // P    64 x 64, then dPE
+  static constexpr int kDU = 147456;     // dU   64 x 128
+  static constexpr int kDY = 163840;     // dY   64 x 128
+  static constexpr int kScal = 180224;   // 10 x 64 floats
+  static constexpr int kBars = kScal + 2560;
+  static constexpr int kTotal = kBars + 128;
+  static constexpr uint32_t kLoadBytes = 4 * 16384 + 2 * 32768 + 8192;  // KH QH DO U, S0 DS, T
+};
+
+// TMEM columns of the accumulators (64-row products, halves of NH columns at lane
+// offsets 0 / 16).  Regions are reused once their readers have finished.
+struct GradTcCols {
+  static constexpr uint32_t kKK = 0;      // K^K^T        NH 32
+  static constexpr uint32_t kQK = 32;     // Q^K^T        NH 32
+  static constexpr uint32_t kKS = 64;     // K^ S0        NH 64, later dQ accumulator
+  static constexpr uint32_t kKdS = 128;   // K^ dS        NH 64, later dY, later dK accumulator
+  static constexpr uint32_t kDP = 192;    // dO U^T       NH 32
+  static constexpr uint32_t kQS = 224;    // Q^ S0        NH 64
+  static constexpr uint32_t kDOS = 288;   // dO S0^T      NH 64
+  static constexpr uint32_t kUdS = 352;   // U dS^T       NH 64
+  static constexpr uint32_t kPdO = 416;   // P^T dO       NH 64, later dA (NH 32)
+  static constexpr uint32_t kDYS = 448;   // dY S0^T      NH 64 (issued after dA)
+  static constexpr uint32_t kDY = kKdS;
+  static constexpr uint32_t kDA = kPdO;
+  static constexpr uint32_t kDQ = kKS;
+  static constexpr uint32_t kDK = kKdS;
+};
+
+struct GradTcArgs {
+  gdnk::Geo g;
+  const bf16* q;
+  const bf16* k;
+  const bf16* v;
+  const float* beta;   // (rows, heads)
+  const float* gcum;   // head-major (heads, rows)
+  const float* kinv;
+  const float* qinv;
+  bf16* dq;
+  bf16* dk;
+  bf16* dv;
+  float* dg;
+  float* db;
+  float qscale;
+  int* status;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int N>
+__device__ __forceinline__ void to_f(const uint32_t (&r)[N], float (&f)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) f[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(NT, 1)
+gdn_grad_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmU,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmDS,
+                   const __grid_constant__ CUtensorMap tmT, const GradTcArgs a) {
+  using S = GradTcSm;
+  using TC = GradTcCols;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const gdnk::Geo& g = a.g;
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!gdnk::locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* gam = reinterpret_cast<float*>(sm + S::kScal);
+  float* eg = gam + 64;
+  float* bet = gam + 128;
+  float* ki = gam + 192;
+  float* qi = gam + 256;
+  float* fF = gam + 320;
+  float* dgam = gam + 384;
+  float* dbet = gam + 448;
+  float* dotq = gam + 512;
+  float* dotk = gam + 576;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBars);  // load, A1, A2, B, C, D, E
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBars + 8 * 8);
+  const int64_t cbase = (int64_t)chunk * g.heads + h;
+  const int64_t hb = (int64_t)h * g.rows + row0;
+
+  if (tid == 0) {
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
+  if (tid < C) {
+    gam[tid] = tid < n ? a.gcum[hb + tid] : 0.f;
+    ki[tid] = tid < n ? a.kinv[hb + tid] : 0.f;
+    qi[tid] = tid < n ? a.qinv[hb + tid] : 0.f;
+    bet[tid] = tid < n ? a.beta[(int64_t)(row0 + tid) * g.heads + h] : 0.f;
+    dgam[tid] = 0.f;
+    dbet[tid] = 0.f;
+    dotq[tid] = 0.f;
+    dotk[tid] = 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sb = smem_u32(sm);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], S::kLoadBytes);
+    for (int cb = 0; cb < 2; ++cb) {
+      tma_load_3d(sm + S::kKH + cb * 8192, &tmK, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kQH + cb * 8192, &tmQ, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kDO + cb * 8192, &tmDO, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kU + cb * 8192, &tmU, &bars[0], cb * 64, (int)(cbase * 64), 0);
+      tma_load_3d(sm + S::kS0 + cb * 16384, &tmS, &bars[0], cb * 64, (int)(cbase * 128), 0);
+      tma_load_3d(sm + S::kDS + cb * 16384, &tmDS, &bars[0], cb * 64, (int)(cbase * 128), 0);
+    }
+    tma_load_3d(sm + S::kT, &tmT, &bars[0], 0, (int)(cbase * 64), 0);
+  }
+  bool ok = mbar_wait_warp(&bars[0], 0, a.status, __LINE__);
+  ok = __syncthreads_and(ok);
+  if (ok) {
+    // gamma past the chunk's end repeats gamma_{n-1}; e^gamma; F_t = e^{gamma_C - gamma_t}
+    const float glast = gam[n - 1];
+    if (tid < C) {
+      const float gv = tid < n ? gam[tid] : glast;
+      eg[tid] = __expf(gv);
+      fF[tid] = tid < n ? __expf(glast - gv) : 0.f;
+    }
+    __syncthreads();
+    if (tid < C && tid >= n) gam[tid] = glast;
+    // K^ = k / |k|, Q^ = c q / |q| (rows past n zero); dO rows past n zero
+    for (int i = tid; i < 3 * 2 * 64 * 8; i += NT) {
+      const int t = i / (2 * 64 * 8), rem = i % (2 * 64 * 8);
+      const int r = (rem >> 3) & 63;
+      uint4* p = reinterpret_cast<uint4*>(sm + (t == 0 ? S::kKH : t == 1 ? S::kQH : S::kDO) + rem * 16);
+      if (r >= n) {
+        *p = make_uint4(0, 0, 0, 0);
+      } else if (t < 2) {
+        const float sc = t == 0 ? ki[r] : qi[r];
+        uint4 w = *p;
+        uint32_t* u = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u[e]));
+          u[e] = pack_bf16x2(f.x * sc, f.y * sc);
+        }
+        *p = w;
+      }
+    }
+    {  // dgamma_C += e^{gamma_C} <S0, dS>  (same swizzle in both tiles: compare bytes in place)
+      float dot = 0.f;
+      for (int i = tid; i < 32768 / 16; i += NT) {
+        const uint4 x = reinterpret_cast<const uint4*>(sm + S::kS0)[i];
+        const uint4 y = reinterpret_cast<const uint4*>(sm + S::kDS)[i];
+        const uint32_t xa[4] = {x.x, x.y, x.z, x.w}, ya[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xa[e]));
+          const float2 yf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ya[e]));
+          dot += xf.x * yf.x + xf.y * yf.y;
+        }
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) atomicAdd(&dgam[C - 1], __expf(glast) * dot);
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+
+  const uint32_t aKH = sb + S::kKH, aQH = sb + S::kQH, aDO = sb + S::kDO, aU = sb + S::kU, aS0 = sb + S::kS0,
+                 aDS = sb + S::kDS, aT = sb + S::kT, aP = sb + S::kP, aDU = sb + S::kDU, aDY = sb + S::kDY;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    // A1: K^K^T, Q^K^T, K^ dS
+    mma64<32, 8, false, false>(tmem, TC::kKK, [&](int kk) { return desc_k(aKH, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aKH, 64, 32 * hf, kk); }, false);
+    mma64<32, 8, false, false>(tmem, TC::kQK, [&](int kk) { return desc_k(aQH, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aKH, 64, 32 * hf, kk); }, false);
+    mma64<64, 8, false, true>(tmem, TC::kKdS, [&](int kk) { return desc_k(aKH, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aDS, 128, 64 * hf, kk); }, false);
+    umma_commit(&bars[1]);
+    // A2: K^ S0, dO U^T, Q^ S0, dO S0^T, U dS^T
+    mma64<64, 8, false, true>(tmem, TC::kKS, [&](int kk) { return desc_k(aKH, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aS0, 128, 64 * hf, kk); }, false);
+    mma64<32, 8, false, false>(tmem, TC::kDP, [&](int kk) { return desc_k(aDO, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aU, 64, 32 * hf, kk); }, false);
+    mma64<64, 8, false, true>(tmem, TC::kQS, [&](int kk) { return desc_k(aQH, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aS0, 128, 64 * hf, kk); }, false);
+    mma64<64, 8, false, false>(tmem, TC::kDOS, [&](int kk) { return desc_k(aDO, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aS0, 128, 64 * hf, kk); }, false);
+    mma64<64, 8, false, false>(tmem, TC::kUdS, [&](int kk) { return desc_k(aU, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aDS, 128, 64 * hf, kk); }, false);
+    umma_commit(&bars[2]);
+  }
+
+  const int r = acc_row();
+  // ---- epilogue A: P = lower_incl(E * Q^K^T)
+  if (ok) {
+    ok = mbar_wait_warp(&bars[1], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(32);
+      uint32_t raw[16];
+      tmem_ld16_raw(acc_addr(tmem, TC::kQK, 32), raw);
+      tmem_wait_ld();
+      float p[16];
+      const float gr = gam[r];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        p[j] = c <= r ? __expf(gr - gam[c]) * __uint_as_float(raw[j]) : 0.f;
+      }
+      st8(sm + S::kP, 64, r, c0, p);
+      st8(sm + S::kP, 64, r, c0 + 8, p + 8);
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    // B: P^T dO
+    mma64<64, 4, true, true>(tmem, TC::kPdO, [&](int kk) { return desc_mn(aP, 64, 0, kk); },
+                             [&](int hf, int kk) { return desc_mn(aDO, 64, 64 * hf, kk); }, false);
+    umma_commit(&bars[3]);
+  }
+  // ---- epilogue B: dU = P^T dO + F (K^ dS); dF
+  if (ok) {
+    ok = mbar_wait_warp(&bars[3], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(64);
+      uint32_t r1[32], r2[32];
+      tmem_ld32_raw(acc_addr(tmem, TC::kPdO, 64), r1);
+      tmem_ld32_raw(acc_addr(tmem, TC::kKdS, 64), r2);
+      tmem_wait_ld();
+      float u[32], du[32];
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) ld8(sm + S::kU, 64, r, c0 + 8 * q8, u + 8 * q8);
+      const float fr = fF[r];
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float kd = __uint_as_float(r2[j]);
+        du[j] = __uint_as_float(r1[j]) + fr * kd;
+        d += kd * u[j];
+      }
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) st8(sm + S::kDU, 64, r, c0 + 8 * q8, du + 8 * q8);
+      d *= fr;
+      atomicAdd(&dgam[r], -d);
+      d = warp_sum(d);
+      if (lane == 0) atomicAdd(&dgam[C - 1], d);
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    // C: dY = T^T dU
+    mma64<64, 4, true, true>(tmem, TC::kDY, [&](int kk) { return desc_mn(aT, 64, 0, kk); },
+                             [&](int hf, int kk) { return desc_mn(aDU, 64, 64 * hf, kk); }, false);
+    umma_commit(&bars[4]);
+  }
+  // ---- epilogue C: dY, dV = beta dY, dbeta, dgamma
+  if (ok) {
+    ok = mbar_wait_warp(&bars[4], 0, a.status, __LINE__) && mbar_wait_warp(&bars[2], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(64);
+      uint32_t r1[32], r2[32];
+      tmem_ld32_raw(acc_addr(tmem, TC::kDY, 64), r1);
+      tmem_ld32_raw(acc_addr(tmem, TC::kKS, 64), r2);
+      tmem_wait_ld();
+      float dy[32], vv[32];
+      to_f(r1, dy);
+      const bool valid = r < n;
+      const bf16* vrow = a.v + (int64_t)(row0 + r) * g.row_v + (int64_t)h * 128 + c0;
+      bf16* dvrow = a.dv + (int64_t)(row0 + r) * g.row_v + (int64_t)h * 128 + c0;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        uint4 w = valid ? *reinterpret_cast<const uint4*>(vrow + 8 * q8) : make_uint4(0, 0, 0, 0);
+        const uint32_t wa[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wa[e]));
+          vv[8 * q8 + 2 * e] = f.x;
+          vv[8 * q8 + 2 * e + 1] = f.y;
+        }
+      }
+      const float br = bet[r], er = eg[r];
+      float dbp = 0.f, dkp = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float ks = __uint_as_float(r2[j]);
+        dbp += dy[j] * (vv[j] - er * ks);
+        dkp += ks * dy[j];
+      }
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        st8(sm + S::kDY, 64, r, c0 + 8 * q8, dy + 8 * q8);
+        if (valid) {
+          uint4 w;
+          w.x = pack_bf16x2(br * dy[8 * q8 + 0], br * dy[8 * q8 + 1]);
+          w.y = pack_bf16x2(br * dy[8 * q8 + 2], br * dy[8 * q8 + 3]);
+          w.z = pack_bf16x2(br * dy[8 * q8 + 4], br * dy[8 * q8 + 5]);
+          w.w = pack_bf16x2(br * dy[8 * q8 + 6], br * dy[8 * q8 + 7]);
+          *reinterpret_cast<uint4*>(dvrow + 8 * q8) = w;
+        }
+      }
+      atomicAdd(&dbet[r], dbp);
+      atomicAdd(&dgam[r], -er * br * dkp);
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    // D: dA = dY U^T; then dY S0^T (read in epilogue E)
+    mma64<32, 8, false, false>(tmem, TC::kDA, [&](int kk) { return desc_k(aDY, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aU, 64, 32 * hf, kk); }, false);
+    umma_commit(&bars[5]);
+    mma64<64, 8, false, false>(tmem, TC::kDYS, [&](int kk) { return desc_k(aDY, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aS0, 128, 64 * hf, kk); }, false);
+  }
+  // ---- epilogue D: dKK (into T's tile), dPE (into P's tile), dbeta, dgamma rows and columns
+  if (ok) {
+    ok = mbar_wait_warp(&bars[5], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(32);
+      uint32_t rA[16], rP[16], rK[16], rQ[16];
+      tmem_ld16_raw(acc_addr(tmem, TC::kDA, 32), rA);
+      tmem_ld16_raw(acc_addr(tmem, TC::kDP, 32), rP);
+      tmem_ld16_raw(acc_addr(tmem, TC::kKK, 32), rK);
+      tmem_ld16_raw(acc_addr(tmem, TC::kQK, 32), rQ);
+      tmem_wait_ld();
+      const int t = r;
+      const float gt = gam[t], bt = bet[t];
+      float dkk[16], dpe[16], colg[16];
+      float rowb = 0.f, rowg = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        const float ex = c <= t ? __expf(gt - gam[c]) : 0.f;
+        const float kk = __uint_as_float(rK[j]);
+        float gs = 0.f;
+        dkk[j] = 0.f;
+        if (c < t) {
+          const float dae = -__uint_as_float(rA[j]) * ex;
+          rowb += dae * kk;
+          dkk[j] = dae * bt;
+          gs += dkk[j] * kk;
+        }
+        dpe[j] = __uint_as_float(rP[j]) * ex;
+        gs += dpe[j] * __uint_as_float(rQ[j]);
+        rowg += gs;
+        colg[j] = -gs;
+      }
+      st8(sm + S::kT, 64, t, c0, dkk);
+      st8(sm + S::kT, 64, t, c0 + 8, dkk + 8);
+      st8(sm + S::kP, 64, t, c0, dpe);
+      st8(sm + S::kP, 64, t, c0 + 8, dpe + 8);
+      atomicAdd(&dbet[t], rowb);
+      atomicAdd(&dgam[t], rowg);
+      // column sums over the 16 rows of this lane's half (lanes sharing lane / 16)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v = colg[j];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        colg[j] = v;
+      }
+      if ((lane & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) atomicAdd(&dgam[c0 + j], colg[j]);
+      }
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    // E: dQ acc = dPE K^;  dK acc = dKK K^ + dKK^T K^ + dPE^T Q^
+    mma64<64, 4, false, true>(tmem, TC::kDQ, [&](int kk) { return desc_k(aP, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aKH, 64, 64 * hf, kk); }, false);
+    mma64<64, 4, false, true>(tmem, TC::kDK, [&](int kk) { return desc_k(aT, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aKH, 64, 64 * hf, kk); }, false);
+    mma64<64, 4, true, true>(tmem, TC::kDK, [&](int kk) { return desc_mn(aT, 64, 0, kk); },
+                             [&](int hf, int kk) { return desc_mn(aKH, 64, 64 * hf, kk); }, true);
+    mma64<64, 4, true, true>(tmem, TC::kDK, [&](int kk) { return desc_mn(aP, 64, 0, kk); },
+                             [&](int hf, int kk) { return desc_mn(aQH, 64, 64 * hf, kk); }, true);
+    umma_commit(&bars[6]);
+  }
+  // ---- epilogue E: dQ^, dK^, their l2-norm backward, dgamma of the inter-chunk term
+  if (ok) {
+    ok = mbar_wait_warp(&bars[6], 0, a.status, __LINE__);
+  }
+  float dqv[32], dkv[32];
+  const int c0 = acc_col0(64);
+  if (ok) {
+    tc_fence_after();
+    const float er = eg[r], br = bet[r], fr = fF[r];
+    uint32_t r1[32], r2[32];
+    float x[32];
+    tmem_ld32_raw(acc_addr(tmem, TC::kDQ, 64), r1);
+    tmem_ld32_raw(acc_addr(tmem, TC::kDOS, 64), r2);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dqv[j] = __uint_as_float(r1[j]) + er * __uint_as_float(r2[j]);
+    tmem_ld32_raw(acc_addr(tmem, TC::kQS, 64), r1);
+    tmem_wait_ld();
+    float gq = 0.f, qd = 0.f;
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) ld8(sm + S::kDO, 64, r, c0 + 8 * q8, x + 8 * q8);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) gq += __uint_as_float(r1[j]) * x[j];
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) ld8(sm + S::kQH, 64, r, c0 + 8 * q8, x + 8 * q8);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) qd += x[j] * dqv[j];
+    atomicAdd(&dgam[r], er * gq);
+    atomicAdd(&dotq[r], qd);
+    tmem_ld32_raw(acc_addr(tmem, TC::kDK, 64), r1);
+    tmem_ld32_raw(acc_addr(tmem, TC::kDYS, 64), r2);
+    tmem_wait_ld();
+    const float sy = -er * br;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dkv[j] = __uint_as_float(r1[j]) + sy * __uint_as_float(r2[j]);
+    tmem_ld32_raw(acc_addr(tmem, TC::kUdS, 64), r1);
+    tmem_wait_ld();
+    float kd = 0.f;
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) ld8(sm + S::kKH, 64, r, c0 + 8 * q8, x + 8 * q8);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      dkv[j] += fr * __uint_as_float(r1[j]);
+      kd += x[j] * dkv[j];
+    }
+    atomicAdd(&dotk[r], kd);
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok) {
+    // l2-norm backward: q^ = c q / |q| (qi = c / |q|): dq = qi (dq^ - q^ (q^.dq^) / c^2);
+    // k^ = k / |k| (ki = 1 / |k|): dk = ki (dk^ - k^ (k^.dk^))
+    if (r < n) {
+      const float qr = qi[r], kr = ki[r], tq = dotq[r] / (a.qscale * a.qscale), tk = dotk[r];
+      const int64_t ob = (int64_t)(row0 + r) * g.row_q + (int64_t)h * 128 + c0;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const uint4 qw = *reinterpret_cast<const uint4*>(a.q + ob + 8 * q8);
+        const uint4 kw = *reinterpret_cast<const uint4*>(a.k + ob + 8 * q8);
+        const uint32_t qa[4] = {qw.x, qw.y, qw.z, qw.w}, ka[4] = {kw.x, kw.y, kw.z, kw.w};
+        uint32_t oq[4], ok4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qa[e]));
+          const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ka[e]));
+          const int j = 8 * q8 + 2 * e;
+          oq[e] = pack_bf16x2(qr * (dqv[j] - qf.x * qr * tq), qr * (dqv[j + 1] - qf.y * qr * tq));
+          ok4[e] = pack_bf16x2(kr * (dkv[j] - kf.x * kr * tk), kr * (dkv[j + 1] - kf.y * kr * tk));
+        }
+        *reinterpret_cast<uint4*>(a.dq + ob + 8 * q8) = make_uint4(oq[0], oq[1], oq[2], oq[3]);
+        *reinterpret_cast<uint4*>(a.dk + ob + 8 * q8) = make_uint4(ok4[0], ok4[1], ok4[2], ok4[3]);
+      }
+    }
+    if (warp == 0) {  // dg = reverse cumulative sum of dgamma over the chunk; dbeta
+      const int i0 = 2 * lane, i1 = 2 * lane + 1;
+      const float x0 = dgam[i0], x1 = dgam[i1];
+      float c = x0 + x1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, c, o);
+        if (lane + o < 32) c += y;
+      }
+      if (i0 < n) {
+        a.dg[(int64_t)(row0 + i0) * g.heads + h] = c;
+        a.db[(int64_t)(row0 + i0) * g.heads + h] = dbet[i0];
+      }
+      if (i1 < n) {
+        a.dg[(int64_t)(row0 + i1) * g.heads + h] = c - x0;
+        a.db[(int64_t)(row0 + i1) * g.heads + h] = dbet[i1];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace gtc
+
+// Host launcher, called by gdn_chunk_bwd (gdn.cu) after the dS recurrence: one CTA per
+// (chunk, head) over `bound` chunks (CTAs past the real chunk count exit at once).
+void gdn_grad_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                        const torch::Tensor& v, const torch::Tensor& beta_f, const torch::Tensor& gcum,
+                        const torch::Tensor& kinv, const torch::Tensor& qinv, const torch::Tensor& u,
+                        const torch::Tensor& states, const torch::Tensor& dstates, const torch::Tensor& tmat,
+                        const torch::Tensor& dout, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv,
+                        torch::Tensor& dg, torch::Tensor& db, float qscale, int* status, cudaStream_t stream) {
+  using S = gtc::GradTcSm;
+  const int H = g.heads;
+  const int64_t rows = g.rows;
+  const int64_t nbh = (int64_t)std::max(bound, 1) * H;
+  TORCH_CHECK(nbh * 128 < (int64_t)INT32_MAX, "gdn_grad_tc: too many chunks for 32-bit TMA coordinates");
+  auto bfmap = [&](const torch::Tensor& t, int64_t dim0, int64_t dim1, int64_t stride1, int box1) {
+    return make_tmap_3d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dim0, dim1, 1, stride1, 0, 64, box1);
+  };
+  const CUtensorMap tmK = bfmap(k, g.row_q, rows, g.row_q, 64);
+  const CUtensorMap tmQ = bfmap(q, g.row_q, rows, g.row_q, 64);
+  const CUtensorMap tmDO = bfmap(dout, g.row_v, rows, g.row_v, 64);
+  const CUtensorMap tmU = bfmap(u, 128, nbh * 64, 128, 64);
+  const CUtensorMap tmS = bfmap(states, 128, nbh * 128, 128, 128);
+  const CUtensorMap tmDS = bfmap(dstates, 128, nbh * 128, 128, 128);
+  const CUtensorMap tmT = bfmap(tmat, 64, nbh * 64, 64, 64);
+  gtc::GradTcArgs a;
+  a.g = g;
+  a.q = (const gtc::bf16*)q.data_ptr();
+  a.k = (const gtc::bf16*)k.data_ptr();
+  a.v = (const gtc::bf16*)v.data_ptr();
+  a.beta = beta_f.data_ptr<float>();
+  a.gcum = gcum.data_ptr<float>();
+  a.kinv = kinv.data_ptr<float>();
+  a.qinv = qinv.data_ptr<float>();
+  a.dq = (gtc::bf16*)dq.data_ptr();
+  a.dk = (gtc::bf16*)dk.data_ptr();
+  a.dv = (gtc::bf16*)dv.data_ptr();
+  a.dg = dg.data_ptr<float>();
+  a.db = db.data_ptr<float>();
+  a.qscale = qscale;
+  a.status = status;
+  static SmemOptIn opt;
+  const int smem = S::kTotal + 1024;
+  C10_CUDA_CHECK(opt.ensure(gtc::gdn_grad_tc_kernel, smem));
+  gtc::gdn_grad_tc_kernel<<<(unsigned)(bound * H), gtc::NT, smem, stream>>>(tmK, tmQ, tmDO, tmU, tmS, tmDS, tmT, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb
