@@ -13,22 +13,20 @@
 //   S1 = e^{gamma_C} S0 + (F * K^)^T U,             F_s = exp(gamma_C - gamma_s)
 //
 // Everything except the S0 -> S1 recurrence is independent per chunk, so the work is
-// split into chunk-parallel kernels (one CTA per (chunk, head)) around a thin sequential
-// kernel (one CTA per (sequence, head, 32 value columns)) that carries the state:
+// split into chunk-parallel kernels (one CTA per (chunk, head), on the tcgen05 tensor
+// cores, in gdn_tc.cu) around a thin sequential kernel (one CTA per (sequence, head, 32
+// value columns), here) that carries the state:
 //
-//   forward:  gdn_prep   (K^K^T, blocked triangular inverse, W, U~)
-//             gdn_state  (U = U~ - W S0, S1 = ...; saves S0 per chunk, U)
-//             gdn_out    (P = lower(E * Q^K^T), O)
-//   backward: gdn_dstate (dS at every chunk end, reverse recurrence)
-//             gdn_grad   (dq, dk, dv, dg, dbeta of every chunk, l2-norm backward)
+//   forward:  gdn_prep_tc (K^K^T, blocked triangular inverse, W, U~, T)
+//             gdn_state   (U = U~ - W S0, S1 = ...; saves S0 per chunk, U)
+//             gdn_out_tc  (P = lower(E * Q^K^T), O)
+//   backward: gdn_dstate  (dS at every chunk end, reverse recurrence)
+//             gdn_grad_tc (dq, dk, dv, dg, dbeta of every chunk, l2-norm backward)
 //
-// All chunk products run on the tensor cores through warp-level bf16 MMAs (fp32
-// accumulate) fed by ldmatrix from padded shared-memory tiles; the state and every
-// reduction stay in fp32.  A 64-row chunk maps onto 16-row MMA fragments without the
-// 128-row minimum of a TMEM accumulator tile, and the sequential kernel keeps its state
-// slice in registers between chunks.
-#include <cstdlib>
-
+// The sequential kernels keep their 128 x 32 state slice in the fragments of warp-level
+// bf16 MMAs (fp32 accumulate) between chunks, fed by ldmatrix from padded shared-memory
+// tiles, with the next chunk's operands streaming in by cp.async; the state and every
+// reduction stay in fp32.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -46,7 +44,6 @@ constexpr int DV = 128;    // head_v_dim
 constexpr int LD = 136;    // padded row stride (elements) of 128-wide bf16 tiles
 constexpr int LDS = 72;    // padded row stride of 64-wide bf16 tiles
 constexpr int LDP = 40;    // padded row stride of 32-wide bf16 tiles
-constexpr int LDF = 65;    // row stride of 64-wide fp32 tiles
 constexpr int PARTS = 4;   // value-column slices of the sequential kernels
 constexpr int PW = DV / PARTS;  // 32 columns per slice
 constexpr int NT = 256;    // threads of every chunk kernel (8 warps)
@@ -112,60 +109,6 @@ __device__ __forceinline__ float2 ld2(const bf16* p) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
 
-// T = (I + A)^-1 for the strictly lower A(i, k) = beta_i exp(gamma_i - gamma_k) KK[i][k],
-// by 16 x 16 blocks: diagonal blocks by forward substitution (one thread per column),
-// then T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj level by level.  Tf: fp32 [64][LDF];
-// X: fp32 scratch of 768 floats.  Ends synchronised.
-__device__ void invert_unit_lower(const float* KK, const float* gam, const float* bet, float* Tf, float* X) {
-  auto Aik = [&](int i, int k) -> float { return k < i ? bet[i] * __expf(gam[i] - gam[k]) * KK[i * LDF + k] : 0.f; };
-  const int tid = threadIdx.x;
-  for (int i = tid; i < C * LDF; i += NT) Tf[i] = 0.f;
-  __syncthreads();
-  if (tid < C) {
-    const int b = tid >> 4, j = tid & 15, base = b * 16;
-    Tf[(base + j) * LDF + base + j] = 1.f;
-    for (int i = j + 1; i < 16; ++i) {
-      float s = 0.f;
-      for (int k = j; k < i; ++k) s = fmaf(Aik(base + i, base + k), Tf[(base + k) * LDF + base + j], s);
-      Tf[(base + i) * LDF + base + j] = -s;
-    }
-  }
-  __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;
-    for (int e = tid; e < nb * 256; e += NT) {
-      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
-      float s = 0.f;
-      for (int kb = bj; kb < bi; ++kb)
-        for (int kk = 0; kk < 16; ++kk)
-          s = fmaf(Aik(bi * 16 + i, kb * 16 + kk), Tf[(kb * 16 + kk) * LDF + bj * 16 + j], s);
-      X[e] = s;
-    }
-    __syncthreads();
-    for (int e = tid; e < nb * 256; e += NT) {
-      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
-      float s = 0.f;
-      for (int kk = 0; kk < 16; ++kk) s = fmaf(Tf[(bi * 16 + i) * LDF + bi * 16 + kk], X[(bj << 8) + kk * 16 + j], s);
-      Tf[(bi * 16 + i) * LDF + bj * 16 + j] = -s;
-    }
-    __syncthreads();
-  }
-}
-
-// Sum over the 4 lanes of a quad (the lanes sharing a fragment row).
-__device__ __forceinline__ float quad_sum(float v) {
-  v += __shfl_xor_sync(0xffffffff, v, 1);
-  v += __shfl_xor_sync(0xffffffff, v, 2);
-  return v;
-}
-// Sum over the 8 lanes sharing lane % 4 (a fragment column).
-__device__ __forceinline__ float col_sum(float v) {
-  v += __shfl_xor_sync(0xffffffff, v, 4);
-  v += __shfl_xor_sync(0xffffffff, v, 8);
-  v += __shfl_xor_sync(0xffffffff, v, 16);
-  return v;
-}
-
 // ---------------------------------------------------------------- async copies
 __device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
   // zero-fills the 16 bytes when !valid (no bytes are read)
@@ -214,153 +157,6 @@ __device__ __forceinline__ void tile64_async(bf16* dst, const bf16* src) {
 __device__ __forceinline__ void scal_async(float* dst, const float* src, int n) {
   if (threadIdx.x < C) cp4(dst + threadIdx.x, src + (threadIdx.x < n ? threadIdx.x : 0), threadIdx.x < n);
 }
-// rows of a padded 128-wide tile times scale[r], in place
-__device__ __forceinline__ void scale_rows128(bf16* t, const float* scale) {
-  for (int i = threadIdx.x; i < C * 16; i += NT) {
-    const int r = i >> 4, c = (i & 15) * 8;
-    uint4 v = *reinterpret_cast<uint4*>(t + r * LD + c);
-    const float s = scale[r];
-    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
-      w[e] = pack2(f.x * s, f.y * s);
-    }
-    *reinterpret_cast<uint4*>(t + r * LD + c) = v;
-  }
-}
-
-// gamma of a chunk (its cumulative log decay) from the head-major scalars: entries past
-// n repeat gamma_{n-1}; e^gamma.
-__device__ __forceinline__ void pad_gamma(float* gam, float* eg, int n) {
-  if (threadIdx.x < C) {
-    const float gv = gam[min((int)threadIdx.x, n - 1)];
-    eg[threadIdx.x] = __expf(gv);
-  }
-}
-
-// ------------------------------------------------------------------------ forward
-// gdn_prep: norms, gamma, W = T diag(beta e^gamma) K^, U~ = T diag(beta) V.
-struct PrepSm {
-  bf16 kh[C * LD];    // K raw -> K^
-  bf16 kb[C * LD];    // beta e^gamma K^
-  bf16 vb[C * LD];    // V raw -> beta V
-  bf16 tb[C * LDS];   // T
-  float kk[C * LDF];  // K^ K^T
-  float tf[C * LDF];  // T (fp32)
-  float x[768];
-  float gam[C], eg[C], bet[C];
-};
-
-__global__ void __launch_bounds__(NT) gdn_prep_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                      const bf16* __restrict__ v, const float* __restrict__ gg,
-                                                      const float* __restrict__ bb, float* __restrict__ gcum,
-                                                      float* __restrict__ kinv, float* __restrict__ qinv,
-                                                      bf16* __restrict__ w_out, bf16* __restrict__ u_out,
-                                                      bf16* __restrict__ t_out, float qscale) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  PrepSm& s = *reinterpret_cast<PrepSm*>(smraw);
-  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
-  int row0, n;
-  if (!locate(g, chunk, row0, n)) return;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-  rows128_async(s.vb, v + (int64_t)row0 * g.row_v + (int64_t)h * DV, g.row_v, n);
-  cp_commit();
-  const int64_t hb = (int64_t)h * g.rows + row0;  // head-major scalar index of row0
-  if (warp == 0) {  // gamma = inclusive cumsum of g over the chunk; beta
-    const int i0 = 2 * lane, i1 = 2 * lane + 1;
-    const float x0 = i0 < n ? gg[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
-    const float x1 = i1 < n ? gg[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
-    float c = x0 + x1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffff, c, o);
-      if (lane >= o) c += y;
-    }
-    const float c0 = c - x1;
-    s.gam[i0] = c0;
-    s.gam[i1] = c;
-    s.eg[i0] = __expf(c0);
-    s.eg[i1] = __expf(c);
-    s.bet[i0] = i0 < n ? bb[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
-    s.bet[i1] = i1 < n ? bb[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
-    if (i0 < n) gcum[hb + i0] = c0;
-    if (i1 < n) gcum[hb + i1] = c;
-  } else {  // q norms (rows 0..63 over warps 1..7), straight from global memory
-    for (int r = warp - 1; r < n; r += NT / 32 - 1) {
-      const float2 a = ld2(q + (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK + lane * 4);
-      const float2 b = ld2(q + (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK + lane * 4 + 2);
-      float sq = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffff, sq, o);
-      if (lane == 0) qinv[hb + r] = qscale / fmaxf(sqrtf(sq), 1e-6f);
-    }
-  }
-  cp_wait<0>();
-  __syncthreads();
-  for (int r = warp; r < C; r += NT / 32) {  // k^, beta e^gamma k^, beta v (in place)
-    bf16* kh = s.kh + r * LD + lane * 4;
-    bf16* vb = s.vb + r * LD + lane * 4;
-    const float2 a = ld2(kh), b = ld2(kh + 2), va = ld2(vb), vc = ld2(vb + 2);
-    float sk = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sk += __shfl_xor_sync(0xffffffff, sk, o);
-    const float ik = r < n ? 1.f / fmaxf(sqrtf(sk), 1e-6f) : 0.f;
-    if (lane == 0 && r < n) kinv[hb + r] = ik;
-    const float kbs = s.bet[r] * s.eg[r] * ik, bv = s.bet[r];
-    st2(kh, a.x * ik, a.y * ik);
-    st2(kh + 2, b.x * ik, b.y * ik);
-    st2(s.kb + r * LD + lane * 4, a.x * kbs, a.y * kbs);
-    st2(s.kb + r * LD + lane * 4 + 2, b.x * kbs, b.y * kbs);
-    st2(vb, va.x * bv, va.y * bv);
-    st2(vb + 2, vc.x * bv, vc.y * bv);
-  }
-  __syncthreads();
-  const int mt = warp & 3, gq = lane >> 2, cq = (lane & 3) * 2;
-  {  // KK = K^ K^T
-    float acc[4][4];
-    zero(acc);
-    const int nb = (warp >> 2) * 32;
-    warp_mma<4, false, false>(acc, s.kh, LD, mt * 16, s.kh, LD, nb, DK);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
-      s.kk[r * LDF + c] = acc[j][0];
-      s.kk[r * LDF + c + 1] = acc[j][1];
-      s.kk[(r + 8) * LDF + c] = acc[j][2];
-      s.kk[(r + 8) * LDF + c + 1] = acc[j][3];
-    }
-  }
-  __syncthreads();
-  invert_unit_lower(s.kk, s.gam, s.bet, s.tf, s.x);
-  for (int i = tid; i < C * C / 2; i += NT) {
-    const int r = i >> 5, c = (i & 31) * 2;
-    st2(s.tb + r * LDS + c, s.tf[r * LDF + c], s.tf[r * LDF + c + 1]);
-  }
-  __syncthreads();
-  const int64_t cbase = ((int64_t)chunk * g.heads + h) * C * DK;
-  for (int i = tid; i < C * C / 8; i += NT) {  // T for the backward (64 x 64 bf16 per chunk and head)
-    const int r = i >> 3, c = (i & 7) * 8;
-    *reinterpret_cast<uint4*>(t_out + ((int64_t)chunk * g.heads + h) * C * C + r * C + c) =
-        *reinterpret_cast<const uint4*>(s.tb + r * LDS + c);
-  }
-  const int nb = (warp >> 2) * 64;
-#pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    float acc[8][4];
-    zero(acc);
-    warp_mma<8, false, true>(acc, s.tb, LDS, mt * 16, which ? s.vb : s.kb, LD, nb, C);
-    bf16* out = (which ? u_out : w_out) + cbase;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
-      st2(out + r * DK + c, acc[j][0], acc[j][1]);
-      st2(out + (r + 8) * DK + c, acc[j][2], acc[j][3]);
-    }
-  }
-}
-
 // gdn_state: one CTA per (sequence, head, 32 value columns); the state slice (128 x 32,
 // fp32) lives in the MMA accumulators of the 8 warps (warp w: key rows 16w..16w+15).
 // The next chunk's operands stream in (cp.async, double buffered) while this one runs;
@@ -477,85 +273,6 @@ __global__ void __launch_bounds__(NT) gdn_state_kernel(Geo g, const bf16* __rest
       const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
       *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(S[j][0], S[j][1]);
       *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(S[j][2], S[j][3]);
-    }
-  }
-}
-
-// gdn_out: P = lower_incl(E * Q^ K^T) (saved for the backward), O = e^gamma Q^ S0 + P U.
-struct OutSm {
-  bf16 qh[C * LD];
-  bf16 kh[C * LD];
-  bf16 u[C * LD];
-  bf16 sb[DK * LD];
-  bf16 p[C * LDS];
-  float gam[C], eg[C], ki[C], qi[C];
-};
-
-__global__ void __launch_bounds__(NT) gdn_out_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                     const float* __restrict__ gcum, const float* __restrict__ kinv,
-                                                     const float* __restrict__ qinv, const bf16* __restrict__ u_in,
-                                                     const bf16* __restrict__ states, bf16* __restrict__ p_out,
-                                                     bf16* __restrict__ out) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  OutSm& s = *reinterpret_cast<OutSm*>(smraw);
-  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
-  int row0, n;
-  if (!locate(g, chunk, row0, n)) return;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, cq = (lane & 3) * 2, mt = warp & 3;
-  const int64_t cbase = (int64_t)chunk * g.heads + h;
-  const int64_t hb = (int64_t)h * g.rows + row0;
-  rows128_async(s.qh, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-  tile128_async(s.u, u_in + cbase * C * DV, C);
-  tile128_async(s.sb, states + cbase * DK * DV, DK);
-  scal_async(s.gam, gcum + hb, n);
-  scal_async(s.ki, kinv + hb, n);
-  scal_async(s.qi, qinv + hb, n);
-  cp_commit();
-  cp_wait<0>();
-  __syncthreads();
-  pad_gamma(s.gam, s.eg, n);
-  scale_rows128(s.qh, s.qi);
-  scale_rows128(s.kh, s.ki);
-  __syncthreads();
-  if (tid < C && tid >= n) s.gam[tid] = s.gam[n - 1];
-  __syncthreads();
-  {
-    float acc[4][4];
-    zero(acc);
-    const int nb = (warp >> 2) * 32;
-    warp_mma<4, false, false>(acc, s.qh, LD, mt * 16, s.kh, LD, nb, DK);
-    bf16* pg = p_out + cbase * C * C;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int t = mt * 16 + gq + hf * 8, c = nb + j * 8 + cq;
-        const float p0 = c <= t ? __expf(s.gam[t] - s.gam[c]) * acc[j][2 * hf] : 0.f;
-        const float p1 = c + 1 <= t ? __expf(s.gam[t] - s.gam[c + 1]) * acc[j][2 * hf + 1] : 0.f;
-        st2(s.p + t * LDS + c, p0, p1);
-        st2(pg + t * C + c, p0, p1);
-      }
-    }
-  }
-  __syncthreads();
-  {
-    float acc[8][4];
-    zero(acc);
-    const int nb = (warp >> 2) * 64;
-    warp_mma<8, false, true>(acc, s.qh, LD, mt * 16, s.sb, LD, nb, DK);
-    const float e0 = s.eg[mt * 16 + gq], e1 = s.eg[mt * 16 + gq + 8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[j][0] *= e0, acc[j][1] *= e0, acc[j][2] *= e1, acc[j][3] *= e1;
-    }
-    warp_mma<8, false, true>(acc, s.p, LDS, mt * 16, s.u, LD, nb, C);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
-      if (r < n) st2(out + (int64_t)(row0 + r) * g.row_v + (int64_t)h * DV + c, acc[j][0], acc[j][1]);
-      if (r + 8 < n) st2(out + (int64_t)(row0 + r + 8) * g.row_v + (int64_t)h * DV + c, acc[j][2], acc[j][3]);
     }
   }
 }
@@ -696,356 +413,6 @@ __global__ void __launch_bounds__(NT) gdn_dstate_kernel(Geo g, const bf16* __res
       const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
       *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(dS[j][0], dS[j][1]);
       *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(dS[j][2], dS[j][3]);
-    }
-  }
-}
-
-// gdn_grad: every gradient of one chunk from S0, dS_C and U (one CTA per (chunk, head)).
-struct GradSm {
-  bf16 kh[C * LD];
-  bf16 qh[C * LD];
-  bf16 dob[C * LD];
-  bf16 u[C * LD];
-  bf16 dy[C * LD];    // the inversion scratch, then dU, then dY
-  bf16 sb[DK * LD];   // S0
-  bf16 dsb[DK * LD];  // dS_C
-  bf16 pb[C * LDS];   // P, then dPE
-  bf16 tb[C * LDS];   // T, then dKK
-  float kk[C * LDF];  // K^ K^T
-  float qk[C * LDF];  // T (fp32) during the inversion, then Q^ K^T
-  float gam[C], eg[C], bet[C], ki[C], qi[C], f[C];
-  float dgam[C], dbet[C], dotq[C], dotk[C];
-};
-
-__global__ void __launch_bounds__(NT) gdn_grad_kernel(
-    Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
-    const float* __restrict__ bb, const float* __restrict__ gcum, const float* __restrict__ kinv,
-    const float* __restrict__ qinv, const bf16* __restrict__ u_in, const bf16* __restrict__ states,
-    const bf16* __restrict__ dstates, const bf16* __restrict__ dout, bf16* __restrict__ dq, bf16* __restrict__ dk,
-    bf16* __restrict__ dv, float* __restrict__ dg, float* __restrict__ db, float qscale) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  GradSm& s = *reinterpret_cast<GradSm*>(smraw);
-  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
-  int row0, n;
-  if (!locate(g, chunk, row0, n)) return;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, cq = (lane & 3) * 2, mt = warp & 3;
-  const int64_t cbase = (int64_t)chunk * g.heads + h;
-  const int64_t hb = (int64_t)h * g.rows + row0;
-  rows128_async(s.kh, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-  rows128_async(s.qh, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-  rows128_async(s.dob, dout + (int64_t)row0 * g.row_v + (int64_t)h * DV, g.row_v, n);
-  tile128_async(s.u, u_in + cbase * C * DV, C);
-  tile128_async(s.sb, states + cbase * DK * DV, DK);
-  tile128_async(s.dsb, dstates + cbase * DK * DV, DK);
-  scal_async(s.gam, gcum + hb, n);
-  scal_async(s.ki, kinv + hb, n);
-  scal_async(s.qi, qinv + hb, n);
-  cp_commit();
-  if (tid < C) {
-    s.bet[tid] = tid < n ? bb[(int64_t)(row0 + tid) * g.heads + h] : 0.f;
-    s.dgam[tid] = 0.f;
-    s.dbet[tid] = 0.f;
-    s.dotq[tid] = 0.f;
-    s.dotk[tid] = 0.f;
-  }
-  cp_wait<0>();
-  __syncthreads();
-  pad_gamma(s.gam, s.eg, n);
-  if (tid < C) s.f[tid] = tid < n ? __expf(s.gam[n - 1] - s.gam[tid]) : 0.f;
-  scale_rows128(s.kh, s.ki);
-  scale_rows128(s.qh, s.qi);
-  {  // dgamma_C += e^{gamma_C} <S0, dS_C>
-    float dot = 0.f;
-    for (int i = tid; i < DK * DV / 8; i += NT) {
-      const int r = i >> 4, c = (i & 15) * 8;
-      const uint4 a = *reinterpret_cast<const uint4*>(s.sb + r * LD + c);
-      const uint4 b = *reinterpret_cast<const uint4*>(s.dsb + r * LD + c);
-      const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
-      const uint32_t* bw = reinterpret_cast<const uint32_t*>(&b);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[e]));
-        const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[e]));
-        dot += x.x * y.x + x.y * y.y;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffff, dot, o);
-    if (lane == 0) atomicAdd(&s.dgam[C - 1], __expf(s.gam[n - 1]) * dot);
-  }
-  __syncthreads();
-  if (tid < C && tid >= n) s.gam[tid] = s.gam[n - 1];
-  __syncthreads();
-  {  // KK
-    float acc[4][4];
-    zero(acc);
-    const int nb = (warp >> 2) * 32;
-    warp_mma<4, false, false>(acc, s.kh, LD, mt * 16, s.kh, LD, nb, DK);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = mt * 16 + gq, c = nb + j * 8 + cq;
-      s.kk[r * LDF + c] = acc[j][0];
-      s.kk[r * LDF + c + 1] = acc[j][1];
-      s.kk[(r + 8) * LDF + c] = acc[j][2];
-      s.kk[(r + 8) * LDF + c + 1] = acc[j][3];
-    }
-  }
-  __syncthreads();
-  invert_unit_lower(s.kk, s.gam, s.bet, s.qk, reinterpret_cast<float*>(s.dy));
-  for (int i = tid; i < C * C / 2; i += NT) {
-    const int r = i >> 5, c = (i & 31) * 2;
-    st2(s.tb + r * LDS + c, s.qk[r * LDF + c], s.qk[r * LDF + c + 1]);
-  }
-  __syncthreads();
-  {  // QK (fp32) and P (bf16)
-    float acc[4][4];
-    zero(acc);
-    const int nb = (warp >> 2) * 32;
-    warp_mma<4, false, false>(acc, s.qh, LD, mt * 16, s.kh, LD, nb, DK);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int t = mt * 16 + gq + hf * 8, c = nb + j * 8 + cq;
-        s.qk[t * LDF + c] = acc[j][2 * hf];
-        s.qk[t * LDF + c + 1] = acc[j][2 * hf + 1];
-        const float p0 = c <= t ? __expf(s.gam[t] - s.gam[c]) * acc[j][2 * hf] : 0.f;
-        const float p1 = c + 1 <= t ? __expf(s.gam[t] - s.gam[c + 1]) * acc[j][2 * hf + 1] : 0.f;
-        st2(s.pb + t * LDS + c, p0, p1);
-      }
-  }
-  __syncthreads();
-  const int nb = (warp >> 2) * 64;
-  const int r0 = mt * 16 + gq, r1 = r0 + 8;
-  {  // dU = P^T dO + F (K^ dS_C); dF_s = sum_v (K^ dS_C)_sv U_sv
-    float acc[8][4], kd[8][4];
-    zero(acc);
-    zero(kd);
-    warp_mma<8, true, true>(acc, s.pb, LDS, mt * 16, s.dob, LD, nb, C);
-    warp_mma<8, false, true>(kd, s.kh, LD, mt * 16, s.dsb, LD, nb, DK);
-    const float f0 = s.f[r0], f1 = s.f[r1];
-    float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = nb + j * 8 + cq;
-      const float2 u0 = ld2(s.u + r0 * LD + c), u1 = ld2(s.u + r1 * LD + c);
-      d0 += kd[j][0] * u0.x + kd[j][1] * u0.y;
-      d1 += kd[j][2] * u1.x + kd[j][3] * u1.y;
-      acc[j][0] += f0 * kd[j][0];
-      acc[j][1] += f0 * kd[j][1];
-      acc[j][2] += f1 * kd[j][2];
-      acc[j][3] += f1 * kd[j][3];
-    }
-    d0 = quad_sum(d0) * f0;
-    d1 = quad_sum(d1) * f1;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = nb + j * 8 + cq;
-      st2(s.dy + r0 * LD + c, acc[j][0], acc[j][1]);
-      st2(s.dy + r1 * LD + c, acc[j][2], acc[j][3]);
-    }
-    if ((lane & 3) == 0) {
-      atomicAdd(&s.dgam[r0], -d0);
-      atomicAdd(&s.dgam[r1], -d1);
-      atomicAdd(&s.dgam[C - 1], d0 + d1);
-    }
-  }
-  __syncthreads();
-  {  // dY = T^T dU; dV = beta dY; R = V - e^gamma K^ S0; dbeta += dY . R; dgamma -= e^gamma beta KS . dY
-    float acc[8][4], ks[8][4];
-    zero(acc);
-    zero(ks);
-    warp_mma<8, true, true>(acc, s.tb, LDS, mt * 16, s.dy, LD, nb, C);
-    warp_mma<8, false, true>(ks, s.kh, LD, mt * 16, s.sb, LD, nb, DK);
-    __syncthreads();  // every warp has read dU
-    const float b0 = s.bet[r0], b1 = s.bet[r1], e0 = s.eg[r0], e1 = s.eg[r1];
-    float db0 = 0.f, db1 = 0.f, dk0 = 0.f, dk1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = nb + j * 8 + cq;
-      st2(s.dy + r0 * LD + c, acc[j][0], acc[j][1]);
-      st2(s.dy + r1 * LD + c, acc[j][2], acc[j][3]);
-      float2 v0 = make_float2(0.f, 0.f), v1 = v0;
-      if (r0 < n) {
-        v0 = ld2(v + (int64_t)(row0 + r0) * g.row_v + (int64_t)h * DV + c);
-        st2(dv + (int64_t)(row0 + r0) * g.row_v + (int64_t)h * DV + c, b0 * acc[j][0], b0 * acc[j][1]);
-      }
-      if (r1 < n) {
-        v1 = ld2(v + (int64_t)(row0 + r1) * g.row_v + (int64_t)h * DV + c);
-        st2(dv + (int64_t)(row0 + r1) * g.row_v + (int64_t)h * DV + c, b1 * acc[j][2], b1 * acc[j][3]);
-      }
-      db0 += acc[j][0] * (v0.x - e0 * ks[j][0]) + acc[j][1] * (v0.y - e0 * ks[j][1]);
-      db1 += acc[j][2] * (v1.x - e1 * ks[j][2]) + acc[j][3] * (v1.y - e1 * ks[j][3]);
-      dk0 += ks[j][0] * acc[j][0] + ks[j][1] * acc[j][1];
-      dk1 += ks[j][2] * acc[j][2] + ks[j][3] * acc[j][3];
-    }
-    db0 = quad_sum(db0), db1 = quad_sum(db1), dk0 = quad_sum(dk0), dk1 = quad_sum(dk1);
-    if ((lane & 3) == 0) {
-      atomicAdd(&s.dbet[r0], db0);
-      atomicAdd(&s.dbet[r1], db1);
-      atomicAdd(&s.dgam[r0], -e0 * b0 * dk0);
-      atomicAdd(&s.dgam[r1], -e1 * b1 * dk1);
-    }
-  }
-  __syncthreads();
-  {  // dA = -dY U^T (s < t), dP = dO U^T (s <= t) -> dKK (into tb), dPE (into pb), dbeta, dgamma
-    float da[4][4], dp[4][4];
-    zero(da);
-    zero(dp);
-    const int nc = (warp >> 2) * 32;
-    warp_mma<4, false, false>(da, s.dy, LD, mt * 16, s.u, LD, nc, DV);
-    warp_mma<4, false, false>(dp, s.dob, LD, mt * 16, s.u, LD, nc, DV);
-    __syncthreads();  // T and P are no longer read
-    float rowb[2] = {0.f, 0.f}, rowg[2] = {0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float colg[2] = {0.f, 0.f};
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int t = r0 + hf * 8;
-        float dkk[2], dpe[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = nc + j * 8 + cq + e;
-          const float ex = c <= t ? __expf(s.gam[t] - s.gam[c]) : 0.f;
-          float gsum = 0.f;
-          dkk[e] = 0.f;
-          if (c < t) {
-            const float dae = -da[j][2 * hf + e] * ex;
-            const float kkv = s.kk[t * LDF + c];
-            rowb[hf] += dae * kkv;
-            dkk[e] = dae * s.bet[t];
-            gsum += dkk[e] * kkv;
-          }
-          dpe[e] = dp[j][2 * hf + e] * ex;
-          gsum += dpe[e] * s.qk[t * LDF + c];  // dP * P, P = E * QK
-          rowg[hf] += gsum;
-          colg[e] -= gsum;
-        }
-        st2(s.tb + t * LDS + nc + j * 8 + cq, dkk[0], dkk[1]);
-        st2(s.pb + t * LDS + nc + j * 8 + cq, dpe[0], dpe[1]);
-      }
-      colg[0] = col_sum(colg[0]);
-      colg[1] = col_sum(colg[1]);
-      if (gq == 0) {
-        atomicAdd(&s.dgam[nc + j * 8 + cq], colg[0]);
-        atomicAdd(&s.dgam[nc + j * 8 + cq + 1], colg[1]);
-      }
-    }
-    rowb[0] = quad_sum(rowb[0]), rowb[1] = quad_sum(rowb[1]);
-    rowg[0] = quad_sum(rowg[0]), rowg[1] = quad_sum(rowg[1]);
-    if ((lane & 3) == 0) {
-      atomicAdd(&s.dbet[r0], rowb[0]);
-      atomicAdd(&s.dbet[r1], rowb[1]);
-      atomicAdd(&s.dgam[r0], rowg[0]);
-      atomicAdd(&s.dgam[r1], rowg[1]);
-    }
-  }
-  __syncthreads();
-  float dqa[8][4];
-  {  // dQ^ = dPE K^ + e^gamma dO S0^T ; dgamma += e^gamma (Q^ S0) . dO
-    float t2[8][4];
-    zero(dqa);
-    zero(t2);
-    warp_mma<8, false, true>(dqa, s.pb, LDS, mt * 16, s.kh, LD, nb, C);
-    warp_mma<8, false, false>(t2, s.dob, LD, mt * 16, s.sb, LD, nb, DV);
-    const float e0 = s.eg[r0], e1 = s.eg[r1];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      dqa[j][0] += e0 * t2[j][0], dqa[j][1] += e0 * t2[j][1];
-      dqa[j][2] += e1 * t2[j][2], dqa[j][3] += e1 * t2[j][3];
-    }
-    zero(t2);
-    warp_mma<8, false, true>(t2, s.qh, LD, mt * 16, s.sb, LD, nb, DK);
-    float g0 = 0.f, g1 = 0.f, q0 = 0.f, q1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = nb + j * 8 + cq;
-      const float2 o0 = ld2(s.dob + r0 * LD + c), o1 = ld2(s.dob + r1 * LD + c);
-      g0 += t2[j][0] * o0.x + t2[j][1] * o0.y;
-      g1 += t2[j][2] * o1.x + t2[j][3] * o1.y;
-      const float2 x0 = ld2(s.qh + r0 * LD + c), x1 = ld2(s.qh + r1 * LD + c);
-      q0 += x0.x * dqa[j][0] + x0.y * dqa[j][1];
-      q1 += x1.x * dqa[j][2] + x1.y * dqa[j][3];
-    }
-    g0 = quad_sum(g0), g1 = quad_sum(g1), q0 = quad_sum(q0), q1 = quad_sum(q1);
-    if ((lane & 3) == 0) {
-      atomicAdd(&s.dgam[r0], e0 * g0);
-      atomicAdd(&s.dgam[r1], e1 * g1);
-      atomicAdd(&s.dotq[r0], q0);
-      atomicAdd(&s.dotq[r1], q1);
-    }
-  }
-  float dka[8][4];
-  {  // dK^ = -e^gamma beta (dY S0^T) + dKK K^ + dKK^T K^ + dPE^T Q^ + F (U dS_C^T)
-    float t2[8][4];
-    zero(dka);
-    warp_mma<8, false, false>(dka, s.dy, LD, mt * 16, s.sb, LD, nb, DV);
-    const float a0 = -s.eg[r0] * s.bet[r0], a1 = -s.eg[r1] * s.bet[r1];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      dka[j][0] *= a0, dka[j][1] *= a0, dka[j][2] *= a1, dka[j][3] *= a1;
-    }
-    warp_mma<8, false, true>(dka, s.tb, LDS, mt * 16, s.kh, LD, nb, C);
-    warp_mma<8, true, true>(dka, s.tb, LDS, mt * 16, s.kh, LD, nb, C);
-    warp_mma<8, true, true>(dka, s.pb, LDS, mt * 16, s.qh, LD, nb, C);
-    zero(t2);
-    warp_mma<8, false, false>(t2, s.u, LD, mt * 16, s.dsb, LD, nb, DV);
-    const float f0 = s.f[r0], f1 = s.f[r1];
-    float k0 = 0.f, k1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = nb + j * 8 + cq;
-      dka[j][0] += f0 * t2[j][0], dka[j][1] += f0 * t2[j][1];
-      dka[j][2] += f1 * t2[j][2], dka[j][3] += f1 * t2[j][3];
-      const float2 x0 = ld2(s.kh + r0 * LD + c), x1 = ld2(s.kh + r1 * LD + c);
-      k0 += x0.x * dka[j][0] + x0.y * dka[j][1];
-      k1 += x1.x * dka[j][2] + x1.y * dka[j][3];
-    }
-    k0 = quad_sum(k0), k1 = quad_sum(k1);
-    if ((lane & 3) == 0) {
-      atomicAdd(&s.dotk[r0], k0);
-      atomicAdd(&s.dotk[r1], k1);
-    }
-  }
-  __syncthreads();
-  // l2-norm backward: q^ = c q / |q| (c = qscale): dq = (c/|q|) (dq^ - q^ (q^.dq^) / c^2);
-  // k^ = k / |k|: dk = (1/|k|) (dk^ - k^ (k^.dk^)).  qi = c/|q|, ki = 1/|k|.
-  {
-    const float ic2 = 1.f / (qscale * qscale);
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int r = hf ? r1 : r0;
-      if (r >= n) continue;
-      const float qi = s.qi[r], ki = s.ki[r], tq = s.dotq[r] * ic2, tk = s.dotk[r];
-      const int64_t ob = (int64_t)(row0 + r) * g.row_q + (int64_t)h * DK;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = nb + j * 8 + cq;
-        const float2 qr = ld2(q + ob + c), kr = ld2(k + ob + c);
-        const float qh0 = qr.x * qi, qh1 = qr.y * qi, kh0 = kr.x * ki, kh1 = kr.y * ki;
-        st2(dq + ob + c, qi * (dqa[j][2 * hf] - qh0 * tq), qi * (dqa[j][2 * hf + 1] - qh1 * tq));
-        st2(dk + ob + c, ki * (dka[j][2 * hf] - kh0 * tk), ki * (dka[j][2 * hf + 1] - kh1 * tk));
-      }
-    }
-  }
-  if (warp == 0) {  // dg = reverse cumulative sum of dgamma over the chunk; dbeta
-    const int i0 = 2 * lane, i1 = 2 * lane + 1;
-    const float x0 = s.dgam[i0], x1 = s.dgam[i1];
-    float c = x0 + x1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_down_sync(0xffffffff, c, o);
-      if (lane + o < 32) c += y;
-    }
-    if (i0 < n) {
-      dg[(int64_t)(row0 + i0) * g.heads + h] = c;
-      db[(int64_t)(row0 + i0) * g.heads + h] = s.dbet[i0];
-    }
-    if (i1 < n) {
-      dg[(int64_t)(row0 + i1) * g.heads + h] = c - x0;
-      db[(int64_t)(row0 + i1) * g.heads + h] = s.dbet[i1];
     }
   }
 }
@@ -1515,6 +882,15 @@ void gdn_grad_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, c
                         const torch::Tensor& dout, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv,
                         torch::Tensor& dg, torch::Tensor& db, float qscale, int* status, cudaStream_t stream);
 
+void gdn_prep_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                        const torch::Tensor& v, const torch::Tensor& gg_f, const torch::Tensor& beta_f,
+                        torch::Tensor& gcum, torch::Tensor& kinv, torch::Tensor& qinv, torch::Tensor& w,
+                        torch::Tensor& u, torch::Tensor& tmat, float qscale, int* status, cudaStream_t stream);
+void gdn_out_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                       const torch::Tensor& gcum, const torch::Tensor& kinv, const torch::Tensor& qinv,
+                       const torch::Tensor& u, const torch::Tensor& states, torch::Tensor& p, torch::Tensor& out,
+                       int* status, cudaStream_t stream);
+
 // Returns (o, final state, saved...) with saved = [states, u, p, w, gcum, kinv, qinv, t].
 std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor gg,
                                                torch::Tensor beta, c10::optional<torch::Tensor> init,
@@ -1543,28 +919,18 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
   auto bf = beta.to(at::kFloat).contiguous();
   torch::Tensor init_f;
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
-  static SmemOptIn a_prep, a_state, a_out;
-  C10_CUDA_CHECK(a_prep.ensure(gdnk::gdn_prep_kernel, (int)sizeof(gdnk::PrepSm)));
+  static SmemOptIn a_state;
   C10_CUDA_CHECK(a_state.ensure(gdnk::gdn_state_kernel, (int)sizeof(gdnk::StateSm)));
-  C10_CUDA_CHECK(a_out.ensure(gdnk::gdn_out_kernel, (int)sizeof(gdnk::OutSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (rows > 0 && g.num_seqs > 0) {
-    gdnk::gdn_prep_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::PrepSm), st>>>(
-        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), gf.data_ptr<float>(),
-        bf.data_ptr<float>(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(),
-        (bf16*)w.data_ptr(), (bf16*)u.data_ptr(), (bf16*)tmat.data_ptr(), qscale);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdn_prep_tc_launch(g, bound, q, k, v, gf, bf, gcum, kinv, qinv, w, u, tmat, qscale, device_status(), st);
     gdnk::gdn_state_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::StateSm), st>>>(
         g, (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), (const bf16*)w.data_ptr(),
         (bf16*)u.data_ptr(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)states.data_ptr(),
         fin.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    gdnk::gdn_out_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::OutSm), st>>>(
-        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(),
-        qinv.data_ptr<float>(), (const bf16*)u.data_ptr(), (const bf16*)states.data_ptr(), (bf16*)p.data_ptr(),
-        (bf16*)out.data_ptr());
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdn_out_tc_launch(g, bound, q, k, gcum, kinv, qinv, u, states, p, out, device_status(), st);
   } else {
     fin.zero_();
   }
@@ -1596,9 +962,8 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
   auto dinit = torch::empty({g.num_seqs, H, gdnk::DK, gdnk::DV}, f32);
   torch::Tensor dfin_f;
   if (dfinal.has_value()) dfin_f = dfinal->to(at::kFloat).contiguous();
-  static SmemOptIn a_dstate, a_grad;
+  static SmemOptIn a_dstate;
   C10_CUDA_CHECK(a_dstate.ensure(gdnk::gdn_dstate_kernel, (int)sizeof(gdnk::DStateSm)));
-  C10_CUDA_CHECK(a_grad.ensure(gdnk::gdn_grad_kernel, (int)sizeof(gdnk::GradSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int64_t rows = (int64_t)q.size(0) * q.size(1);
@@ -1608,18 +973,8 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
         qinv.data_ptr<float>(), (const bf16*)w.data_ptr(), (const bf16*)p.data_ptr(), (const bf16*)doc.data_ptr(),
         dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, (bf16*)dstates.data_ptr(), dinit.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    static const bool mma_sync_grad = std::getenv("MYKB_GDN_GRAD_MMA_SYNC") != nullptr;
-    if (!mma_sync_grad) {
-      gdn_grad_tc_launch(g, bound, q, k, v, bf, gcum, kinv, qinv, u, states, dstates, tmat, doc, dq, dk, dv, dg, db,
-                         qscale, device_status(), st);
-    } else {
-    gdnk::gdn_grad_kernel<<<bound * H, gdnk::NT, sizeof(gdnk::GradSm), st>>>(
-        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(), bf.data_ptr<float>(),
-        gcum.data_ptr<float>(), kinv.data_ptr<float>(), qinv.data_ptr<float>(), (const bf16*)u.data_ptr(),
-        (const bf16*)states.data_ptr(), (const bf16*)dstates.data_ptr(), (const bf16*)doc.data_ptr(), (bf16*)dq.data_ptr(),
-        (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(), dg.data_ptr<float>(), db.data_ptr<float>(), qscale);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    }
+    gdn_grad_tc_launch(g, bound, q, k, v, bf, gcum, kinv, qinv, u, states, dstates, tmat, doc, dq, dk, dv, dg, db,
+                       qscale, device_status(), st);
   } else {
     dinit.zero_();
   }

@@ -542,6 +542,420 @@ gdn_grad_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   }
 }
 
+// ------------------------------------------------------------------------ forward
+// gdn_prep_tc: per (chunk, head): gamma = cumsum(g), the key / query norms, A =
+// strictly_lower(beta E * K^K^T), T = (I + A)^-1 (fp32 blocked forward substitution on
+// the CUDA cores), W = T diag(beta e^gamma) K^ and U~ = T diag(beta) V (tcgen05).
+struct PrepTcSm {
+  static constexpr int kKH = 0;        // K -> K^            64 x 128
+  static constexpr int kKB = 16384;    // beta e^gamma K^    64 x 128
+  static constexpr int kVB = 32768;    // V -> beta V        64 x 128
+  static constexpr int kT = 49152;     // T (bf16)           64 x 64
+  static constexpr int kA = 57344;     // A (fp32, row stride 65)
+  static constexpr int kTf = kA + 64 * 65 * 4;
+  static constexpr int kX = kTf + 64 * 65 * 4;  // 768 floats of inversion scratch
+  static constexpr int kScal = kX + 768 * 4;    // gam, eg, bet
+  static constexpr int kBars = kScal + 3 * 256;
+  static constexpr int kTotal = kBars + 64;
+};
+constexpr int LDA = 65;
+
+struct PrepTcArgs {
+  gdnk::Geo g;
+  const bf16* q;
+  const float* gg;    // (rows, heads) log decay
+  const float* bb;    // (rows, heads) beta
+  float* gcum;        // head-major outputs
+  float* kinv;
+  float* qinv;
+  bf16* w_out;        // (chunks, heads, 64, 128)
+  bf16* u_out;
+  bf16* t_out;        // (chunks, heads, 64, 64)
+  float qscale;
+  int* status;
+};
+
+// T = (I + A)^-1 for the strictly lower A (fp32, row stride LDA) by 16 x 16 blocks:
+// diagonal blocks by forward substitution (one thread per block column), then
+// T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj level by level.  Ends synchronised.
+__device__ void invert_lower_from_a(const float* A, float* Tf, float* X) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < C * LDA; i += NT) Tf[i] = 0.f;
+  __syncthreads();
+  if (tid < C) {
+    const int base = (tid >> 4) * 16, j = tid & 15;
+    Tf[(base + j) * LDA + base + j] = 1.f;
+    for (int i = j + 1; i < 16; ++i) {
+      float s = 0.f;
+      for (int k = j; k < i; ++k) s = fmaf(A[(base + i) * LDA + base + k], Tf[(base + k) * LDA + base + j], s);
+      Tf[(base + i) * LDA + base + j] = -s;
+    }
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    for (int e = tid; e < nb * 256; e += NT) {
+      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
+      const float* arow = A + (bi * 16 + i) * LDA;
+      float s = 0.f;
+      for (int k = bj * 16; k < bi * 16; ++k) s = fmaf(arow[k], Tf[k * LDA + bj * 16 + j], s);
+      X[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 256; e += NT) {
+      const int bj = e >> 8, bi = bj + d, i = (e >> 4) & 15, j = e & 15;
+      float s = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) s = fmaf(Tf[(bi * 16 + i) * LDA + bi * 16 + kk], X[(bj << 8) + kk * 16 + j], s);
+      Tf[(bi * 16 + i) * LDA + bj * 16 + j] = -s;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(NT, 2)
+gdn_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const PrepTcArgs a) {
+  using S = PrepTcSm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const gdnk::Geo& g = a.g;
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!gdnk::locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* gam = reinterpret_cast<float*>(sm + S::kScal);
+  float* eg = gam + 64;
+  float* bet = gam + 128;
+  float* Af = reinterpret_cast<float*>(sm + S::kA);
+  float* Tf = reinterpret_cast<float*>(sm + S::kTf);
+  float* X = reinterpret_cast<float*>(sm + S::kX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBars);  // load, KK, W/U
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBars + 32);
+  const int64_t cbase = (int64_t)chunk * g.heads + h;
+  const int64_t hb = (int64_t)h * g.rows + row0;
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], 2 * 16384);
+    for (int cb = 0; cb < 2; ++cb) {
+      tma_load_3d(sm + S::kKH + cb * 8192, &tmK, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kVB + cb * 8192, &tmV, &bars[0], h * 128 + cb * 64, row0, 0);
+    }
+  }
+  if (warp == 0) {  // gamma = inclusive cumsum of g over the chunk; beta
+    const int i0 = 2 * lane, i1 = 2 * lane + 1;
+    const float x0 = i0 < n ? a.gg[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
+    const float x1 = i1 < n ? a.gg[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
+    float c = x0 + x1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) c += y;
+    }
+    const float c0 = c - x1;
+    gam[i0] = c0;
+    gam[i1] = c;
+    eg[i0] = __expf(c0);
+    eg[i1] = __expf(c);
+    bet[i0] = i0 < n ? a.bb[(int64_t)(row0 + i0) * g.heads + h] : 0.f;
+    bet[i1] = i1 < n ? a.bb[(int64_t)(row0 + i1) * g.heads + h] : 0.f;
+    if (i0 < n) a.gcum[hb + i0] = c0;
+    if (i1 < n) a.gcum[hb + i1] = c;
+  } else {  // query norms (rows over warps 1..7), straight from global memory
+    for (int r = warp - 1; r < n; r += NT / 32 - 1) {
+      const uint2 w = *reinterpret_cast<const uint2*>(a.q + (int64_t)(row0 + r) * g.row_q + (int64_t)h * 128 + lane * 4);
+      const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+      const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+      const float sq = warp_sum(x.x * x.x + x.y * x.y + y.x * y.x + y.y * y.y);
+      if (lane == 0) a.qinv[hb + r] = a.qscale / fmaxf(sqrtf(sq), 1e-6f);
+    }
+  }
+  bool ok = mbar_wait_warp(&bars[0], 0, a.status, __LINE__);
+  ok = __syncthreads_and(ok);
+  if (ok) {  // K^ = k / |k|, beta e^gamma K^, beta V; rows past n zero
+    for (int r = warp; r < C; r += NT / 32) {
+      const uint32_t off = sw_off(64, r, lane * 4);
+      uint2* kp = reinterpret_cast<uint2*>(sm + S::kKH + off);
+      uint2* vp = reinterpret_cast<uint2*>(sm + S::kVB + off);
+      const uint2 kw = *kp, vw = *vp;
+      const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.x));
+      const float2 k1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.y));
+      const float2 v0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw.x));
+      const float2 v1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw.y));
+      const float sk = warp_sum(k0.x * k0.x + k0.y * k0.y + k1.x * k1.x + k1.y * k1.y);
+      const bool valid = r < n;
+      const float ik = valid ? 1.f / fmaxf(sqrtf(sk), 1e-6f) : 0.f;
+      if (lane == 0 && valid) a.kinv[hb + r] = ik;
+      const float kbs = valid ? bet[r] * eg[r] * ik : 0.f, bv = valid ? bet[r] : 0.f;
+      *kp = valid ? make_uint2(pack_bf16x2(k0.x * ik, k0.y * ik), pack_bf16x2(k1.x * ik, k1.y * ik)) : make_uint2(0, 0);
+      *reinterpret_cast<uint2*>(sm + S::kKB + off) =
+          valid ? make_uint2(pack_bf16x2(k0.x * kbs, k0.y * kbs), pack_bf16x2(k1.x * kbs, k1.y * kbs)) : make_uint2(0, 0);
+      *vp = valid ? make_uint2(pack_bf16x2(v0.x * bv, v0.y * bv), pack_bf16x2(v1.x * bv, v1.y * bv)) : make_uint2(0, 0);
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  const uint32_t sb = smem_u32(sm);
+  const uint32_t aKH = sb + S::kKH, aKB = sb + S::kKB, aVB = sb + S::kVB, aT = sb + S::kT;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    mma64<32, 8, false, false>(tmem, 0, [&](int kk) { return desc_k(aKH, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aKH, 64, 32 * hf, kk); }, false);
+    umma_commit(&bars[1]);
+  }
+  const int r = acc_row();
+  if (ok) {  // A = strictly_lower(beta_r e^{gamma_r - gamma_c} K^K^T)
+    ok = mbar_wait_warp(&bars[1], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(32);
+      uint32_t raw[16];
+      tmem_ld16_raw(acc_addr(tmem, 0, 32), raw);
+      tmem_wait_ld();
+      const float br = bet[r], gr = gam[r];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        Af[r * LDA + c] = c < r ? br * __expf(gr - gam[c]) * __uint_as_float(raw[j]) : 0.f;
+      }
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok) {
+    invert_lower_from_a(Af, Tf, X);
+    for (int i = tid; i < C * 8; i += NT) {  // T -> bf16 operand tile and global memory
+      const int rr = i >> 3, c = (i & 7) * 8;
+      float v8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v8[e] = Tf[rr * LDA + c + e];
+      st8(sm + S::kT, 64, rr, c, v8);
+      *reinterpret_cast<uint4*>(a.t_out + cbase * C * C + rr * C + c) =
+          *reinterpret_cast<const uint4*>(sm + S::kT + sw_off(64, rr, c));
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ok && tid == 0) {
+    tc_fence_after();
+    mma64<64, 4, false, true>(tmem, 32, [&](int kk) { return desc_k(aT, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aKB, 64, 64 * hf, kk); }, false);
+    mma64<64, 4, false, true>(tmem, 96, [&](int kk) { return desc_k(aT, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aVB, 64, 64 * hf, kk); }, false);
+    umma_commit(&bars[2]);
+  }
+  if (ok) {  // W, U~ rows to global memory
+    ok = mbar_wait_warp(&bars[2], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(64);
+      uint32_t rw[32], ru[32];
+      tmem_ld32_raw(acc_addr(tmem, 32, 64), rw);
+      tmem_ld32_raw(acc_addr(tmem, 96, 64), ru);
+      tmem_wait_ld();
+      bf16* wo = a.w_out + cbase * C * 128 + r * 128 + c0;
+      bf16* uo = a.u_out + cbase * C * 128 + r * 128 + c0;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int j = 8 * q8;
+        *reinterpret_cast<uint4*>(wo + j) =
+            make_uint4(pack_bf16x2(__uint_as_float(rw[j]), __uint_as_float(rw[j + 1])),
+                       pack_bf16x2(__uint_as_float(rw[j + 2]), __uint_as_float(rw[j + 3])),
+                       pack_bf16x2(__uint_as_float(rw[j + 4]), __uint_as_float(rw[j + 5])),
+                       pack_bf16x2(__uint_as_float(rw[j + 6]), __uint_as_float(rw[j + 7])));
+        *reinterpret_cast<uint4*>(uo + j) =
+            make_uint4(pack_bf16x2(__uint_as_float(ru[j]), __uint_as_float(ru[j + 1])),
+                       pack_bf16x2(__uint_as_float(ru[j + 2]), __uint_as_float(ru[j + 3])),
+                       pack_bf16x2(__uint_as_float(ru[j + 4]), __uint_as_float(ru[j + 5])),
+                       pack_bf16x2(__uint_as_float(ru[j + 6]), __uint_as_float(ru[j + 7])));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// gdn_out_tc: P = lower_incl(E * Q^K^T) (also stored for the backward's dS recurrence),
+// O = diag(e^gamma) Q^ S0 + P U.
+struct OutTcSm {
+  static constexpr int kQH = 0;        // Q^   64 x 128
+  static constexpr int kKH = 16384;    // K^   64 x 128
+  static constexpr int kU = 32768;     // U    64 x 128
+  static constexpr int kS0 = 49152;    // S0  128 x 128
+  static constexpr int kP = 81920;     // P    64 x 64
+  static constexpr int kScal = 90112;  // gam, eg, ki, qi
+  static constexpr int kBars = kScal + 4 * 256;
+  static constexpr int kTotal = kBars + 64;
+};
+
+struct OutTcArgs {
+  gdnk::Geo g;
+  const float* gcum;
+  const float* kinv;
+  const float* qinv;
+  bf16* p_out;   // (chunks, heads, 64, 64)
+  bf16* out;     // (rows, heads, 128)
+  int* status;
+};
+
+__global__ void __launch_bounds__(NT, 2)
+gdn_out_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmS,
+                  const OutTcArgs a) {
+  using S = OutTcSm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const gdnk::Geo& g = a.g;
+  const int chunk = blockIdx.x / g.heads, h = blockIdx.x % g.heads;
+  int row0, n;
+  if (!gdnk::locate(g, chunk, row0, n)) return;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  float* gam = reinterpret_cast<float*>(sm + S::kScal);
+  float* eg = gam + 64;
+  float* ki = gam + 128;
+  float* qi = gam + 192;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBars);  // load, QK/QS, PU
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBars + 32);
+  const int64_t cbase = (int64_t)chunk * g.heads + h;
+  const int64_t hb = (int64_t)h * g.rows + row0;
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  if (tid < C) {
+    gam[tid] = tid < n ? a.gcum[hb + tid] : 0.f;
+    ki[tid] = tid < n ? a.kinv[hb + tid] : 0.f;
+    qi[tid] = tid < n ? a.qinv[hb + tid] : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], 3 * 16384 + 32768);
+    for (int cb = 0; cb < 2; ++cb) {
+      tma_load_3d(sm + S::kQH + cb * 8192, &tmQ, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kKH + cb * 8192, &tmK, &bars[0], h * 128 + cb * 64, row0, 0);
+      tma_load_3d(sm + S::kU + cb * 8192, &tmU, &bars[0], cb * 64, (int)(cbase * 64), 0);
+      tma_load_3d(sm + S::kS0 + cb * 16384, &tmS, &bars[0], cb * 64, (int)(cbase * 128), 0);
+    }
+  }
+  const float glast = gam[n - 1];
+  if (tid < C) eg[tid] = __expf(tid < n ? gam[tid] : glast);
+  bool ok = mbar_wait_warp(&bars[0], 0, a.status, __LINE__);
+  ok = __syncthreads_and(ok);
+  if (tid < C && tid >= n) gam[tid] = glast;
+  if (ok) {  // Q^ = qi q, K^ = ki k; rows past n zero
+    for (int i = tid; i < 2 * 2 * 64 * 8; i += NT) {
+      const int t = i / (2 * 64 * 8), rem = i % (2 * 64 * 8);
+      const int rr = (rem >> 3) & 63;
+      uint4* p = reinterpret_cast<uint4*>(sm + (t == 0 ? S::kQH : S::kKH) + rem * 16);
+      if (rr >= n) {
+        *p = make_uint4(0, 0, 0, 0);
+      } else {
+        const float sc = t == 0 ? qi[rr] : ki[rr];
+        uint4 w = *p;
+        uint32_t* u = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u[e]));
+          u[e] = pack_bf16x2(f.x * sc, f.y * sc);
+        }
+        *p = w;
+      }
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  const uint32_t sb = smem_u32(sm);
+  const uint32_t aQH = sb + S::kQH, aKH = sb + S::kKH, aU = sb + S::kU, aS0 = sb + S::kS0, aP = sb + S::kP;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    mma64<32, 8, false, false>(tmem, 0, [&](int kk) { return desc_k(aQH, 64, 0, kk); },
+                               [&](int hf, int kk) { return desc_k(aKH, 64, 32 * hf, kk); }, false);
+    umma_commit(&bars[1]);
+    mma64<64, 8, false, true>(tmem, 32, [&](int kk) { return desc_k(aQH, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aS0, 128, 64 * hf, kk); }, false);
+  }
+  const int r = acc_row();
+  if (ok) {
+    ok = mbar_wait_warp(&bars[1], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(32);
+      uint32_t raw[16];
+      tmem_ld16_raw(acc_addr(tmem, 0, 32), raw);
+      tmem_wait_ld();
+      float p[16];
+      const float gr = gam[r];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        p[j] = c <= r ? __expf(gr - gam[c]) * __uint_as_float(raw[j]) : 0.f;
+      }
+      st8(sm + S::kP, 64, r, c0, p);
+      st8(sm + S::kP, 64, r, c0 + 8, p + 8);
+      bf16* pg = a.p_out + cbase * C * C + r * C + c0;
+      *reinterpret_cast<uint4*>(pg) = *reinterpret_cast<const uint4*>(sm + S::kP + sw_off(64, r, c0));
+      *reinterpret_cast<uint4*>(pg + 8) = *reinterpret_cast<const uint4*>(sm + S::kP + sw_off(64, r, c0 + 8));
+      fence_proxy_async_smem();
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    mma64<64, 4, false, true>(tmem, 96, [&](int kk) { return desc_k(aP, 64, 0, kk); },
+                              [&](int hf, int kk) { return desc_mn(aU, 64, 64 * hf, kk); }, false);
+    umma_commit(&bars[2]);
+  }
+  if (ok) {  // O = e^gamma (Q^ S0) + P U
+    ok = mbar_wait_warp(&bars[2], 0, a.status, __LINE__);
+    if (ok) {
+      tc_fence_after();
+      const int c0 = acc_col0(64);
+      uint32_t rs[32], ru[32];
+      tmem_ld32_raw(acc_addr(tmem, 32, 64), rs);
+      tmem_ld32_raw(acc_addr(tmem, 96, 64), ru);
+      tmem_wait_ld();
+      if (r < n) {
+        const float er = eg[r];
+        bf16* o = a.out + (int64_t)(row0 + r) * g.row_v + (int64_t)h * 128 + c0;
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float v8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v8[e] = er * __uint_as_float(rs[8 * q8 + e]) + __uint_as_float(ru[8 * q8 + e]);
+          *reinterpret_cast<uint4*>(o + 8 * q8) = make_uint4(pack_bf16x2(v8[0], v8[1]), pack_bf16x2(v8[2], v8[3]),
+                                                             pack_bf16x2(v8[4], v8[5]), pack_bf16x2(v8[6], v8[7]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace gtc
 
 // Host launcher, called by gdn_chunk_bwd (gdn.cu) after the dS recurrence: one CTA per
@@ -587,6 +1001,63 @@ void gdn_grad_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, c
   const int smem = S::kTotal + 1024;
   C10_CUDA_CHECK(opt.ensure(gtc::gdn_grad_tc_kernel, smem));
   gtc::gdn_grad_tc_kernel<<<(unsigned)(bound * H), gtc::NT, smem, stream>>>(tmK, tmQ, tmDO, tmU, tmS, tmDS, tmT, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb
+
+namespace mykb {
+
+void gdn_prep_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                        const torch::Tensor& v, const torch::Tensor& gg_f, const torch::Tensor& beta_f,
+                        torch::Tensor& gcum, torch::Tensor& kinv, torch::Tensor& qinv, torch::Tensor& w,
+                        torch::Tensor& u, torch::Tensor& tmat, float qscale, int* status, cudaStream_t stream) {
+  const int64_t rows = g.rows;
+  const CUtensorMap tmK = make_tmap_3d(k.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.row_q, rows, 1, g.row_q, 0, 64, 64);
+  const CUtensorMap tmV = make_tmap_3d(v.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.row_v, rows, 1, g.row_v, 0, 64, 64);
+  gtc::PrepTcArgs a;
+  a.g = g;
+  a.q = (const gtc::bf16*)q.data_ptr();
+  a.gg = gg_f.data_ptr<float>();
+  a.bb = beta_f.data_ptr<float>();
+  a.gcum = gcum.data_ptr<float>();
+  a.kinv = kinv.data_ptr<float>();
+  a.qinv = qinv.data_ptr<float>();
+  a.w_out = (gtc::bf16*)w.data_ptr();
+  a.u_out = (gtc::bf16*)u.data_ptr();
+  a.t_out = (gtc::bf16*)tmat.data_ptr();
+  a.qscale = qscale;
+  a.status = status;
+  static SmemOptIn opt;
+  const int smem = gtc::PrepTcSm::kTotal + 1024;
+  C10_CUDA_CHECK(opt.ensure(gtc::gdn_prep_tc_kernel, smem));
+  gtc::gdn_prep_tc_kernel<<<(unsigned)(bound * g.heads), gtc::NT, smem, stream>>>(tmK, tmV, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_out_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                       const torch::Tensor& gcum, const torch::Tensor& kinv, const torch::Tensor& qinv,
+                       const torch::Tensor& u, const torch::Tensor& states, torch::Tensor& p, torch::Tensor& out,
+                       int* status, cudaStream_t stream) {
+  const int64_t rows = g.rows;
+  const int64_t nbh = (int64_t)std::max(bound, 1) * g.heads;
+  TORCH_CHECK(nbh * 128 < (int64_t)INT32_MAX, "gdn_out_tc: too many chunks for 32-bit TMA coordinates");
+  const CUtensorMap tmQ = make_tmap_3d(q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.row_q, rows, 1, g.row_q, 0, 64, 64);
+  const CUtensorMap tmK = make_tmap_3d(k.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.row_q, rows, 1, g.row_q, 0, 64, 64);
+  const CUtensorMap tmU = make_tmap_3d(u.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, nbh * 64, 1, 128, 0, 64, 64);
+  const CUtensorMap tmS = make_tmap_3d(states.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, nbh * 128, 1, 128, 0, 64, 128);
+  gtc::OutTcArgs a;
+  a.g = g;
+  a.gcum = gcum.data_ptr<float>();
+  a.kinv = kinv.data_ptr<float>();
+  a.qinv = qinv.data_ptr<float>();
+  a.p_out = (gtc::bf16*)p.data_ptr();
+  a.out = (gtc::bf16*)out.data_ptr();
+  a.status = status;
+  static SmemOptIn opt;
+  const int smem = gtc::OutTcSm::kTotal + 1024;
+  C10_CUDA_CHECK(opt.ensure(gtc::gdn_out_tc_kernel, smem));
+  gtc::gdn_out_tc_kernel<<<(unsigned)(bound * g.heads), gtc::NT, smem, stream>>>(tmQ, tmK, tmU, tmS, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
