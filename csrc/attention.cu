@@ -617,21 +617,27 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int kmin = (p.left >= 0 ? max(0, qpos - p.left) : 0) - k0;
         const int kspan = max(0, min(it.g.len_k, p.right >= 0 ? qpos + p.right + 1 : it.g.len_k) - k0 - kmin);
         float mx = -INFINITY;
+        // two 32-column TMEM loads in flight per wait
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t cr[32];
-          tmem_ld32_raw(tmem + lane_base + s_col + c * 32, cr);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t cr[2][32];
+          tmem_ld32_raw(tmem + lane_base + s_col + c2 * 64, cr[0]);
+          tmem_ld32_raw(tmem + lane_base + s_col + c2 * 64 + 32, cr[1]);
           tmem_wait_ld();
-          if (edge) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              float sc = __uint_as_float(cr[i]);
-              if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
-              mx = fmaxf(mx, sc);
+          for (int h = 0; h < 2; ++h) {
+            const int c = 2 * c2 + h;
+            if (edge) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                float sc = __uint_as_float(cr[h][i]);
+                if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) sc = -INFINITY;
+                mx = fmaxf(mx, sc);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(cr[h][i]), __uint_as_float(cr[h][i + 1]));
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(cr[i]), __uint_as_float(cr[i + 1]));
           }
         }
         const float m_tile = mx * p.scale_log2;
@@ -657,25 +663,30 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const float2 scale2 = make_float2(p.scale_log2, p.scale_log2), neg2 = make_float2(neg, neg);
         float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t cr[32];
-          tmem_ld32_raw(tmem + lane_base + s_col + c * 32, cr);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t cr[2][32];
+          tmem_ld32_raw(tmem + lane_base + s_col + c2 * 64, cr[0]);
+          tmem_ld32_raw(tmem + lane_base + s_col + c2 * 64 + 32, cr[1]);
           tmem_wait_ld();
-          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float s0 = __uint_as_float(cr[i]), s1 = __uint_as_float(cr[i + 1]);
-            if (edge) {
-              if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) s0 = -INFINITY;
-              if ((unsigned)(c * 32 + i + 1 - kmin) >= (unsigned)kspan) s1 = -INFINITY;
+          for (int h = 0; h < 2; ++h) {
+            const int c = 2 * c2 + h;
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              float s0 = __uint_as_float(cr[h][i]), s1 = __uint_as_float(cr[h][i + 1]);
+              if (edge) {
+                if ((unsigned)(c * 32 + i - kmin) >= (unsigned)kspan) s0 = -INFINITY;
+                if ((unsigned)(c * 32 + i + 1 - kmin) >= (unsigned)kspan) s1 = -INFINITY;
+              }
+              const float2 a = ffma2(make_float2(s0, s1), scale2, neg2);  // both exponents in one FMA
+              const float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
+              rs2 = fadd2(rs2, pv);
+              pk[i >> 1] = pack_bf16x2(pv.x, pv.y);
             }
-            const float2 a = ffma2(make_float2(s0, s1), scale2, neg2);  // both exponents in one FMA
-            const float2 pv = make_float2(exp2f(a.x), exp2f(a.y));
-            rs2 = fadd2(rs2, pv);
-            pk[i >> 1] = pack_bf16x2(pv.x, pv.y);
+            // P columns [16 c, 16 c + 16) lie in S columns this thread has already read
+            tmem_st16_raw(tmem + lane_base + s_col + c * 16, pk);
           }
-          // P columns [16 c, 16 c + 16) lie in S columns this thread has already read
-          tmem_st16_raw(tmem + lane_base + s_col + c * 16, pk);
         }
         l += rs2.x + rs2.y;
         tmem_wait_st();

@@ -313,6 +313,54 @@ static int comm_grid(int64_t work) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sms * 4));
 }
 
+// fp8 all-gather of one MXFP8 weight whose rows are sharded over the ranks.  Every rank
+// holds, in symmetric memory, the MXFP8 copies of its R rows of W (N x K): q0 (R x K) with
+// its row-blocked scale atoms s0, and q1 = (W rows)^T (K x R) blocked along R with atoms
+// s1.  The full operands are assembled locally from every rank's copies with 16-byte peer
+// loads: q0 / s0 are one contiguous run per rank, q1 a column slab (one run of rows_r bytes
+// per K row) and s1 one run of atoms per 128-row block of K.  grid.y = rank, grid.z =
+// part (q0, s0, q1, s1).
+struct MxGatherArgs {
+  int64_t base[kMaxWorld];  // each rank's copies: q0 at +0, s0 at +R K, q1 at +R K (1 + 1/32), s1 after it
+  uint8_t* q0;              // full (N x K)
+  uint8_t* s0;
+  uint8_t* q1;              // full (K x N)
+  uint8_t* s1;
+  int64_t R, K, N;
+};
+
+__global__ void __launch_bounds__(256) mx_shard_gather_kernel(MxGatherArgs a) {
+  const int r = blockIdx.y, part = blockIdx.z;
+  const int64_t row0 = (int64_t)r * a.R;
+  const int64_t rows = max((int64_t)0, min(a.R, a.N - row0));  // this rank's valid rows (multiple of 128)
+  if (rows == 0) return;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(a.base[r]);
+  const int64_t rk = a.R * a.K;
+  int64_t units;
+  if (part == 0 || part == 2) units = rows * a.K / 16;
+  else units = rows * a.K / 32 / 16;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const uint4* from;
+    uint4* to;
+    if (part == 0) {
+      from = reinterpret_cast<const uint4*>(src) + u;
+      to = reinterpret_cast<uint4*>(a.q0 + row0 * a.K) + u;
+    } else if (part == 1) {
+      from = reinterpret_cast<const uint4*>(src + rk) + u;
+      to = reinterpret_cast<uint4*>(a.s0 + row0 * a.K / 32) + u;
+    } else if (part == 2) {
+      const int64_t per = rows / 16, k = u / per, c = u - k * per;
+      from = reinterpret_cast<const uint4*>(src + rk + rk / 32 + k * a.R) + c;
+      to = reinterpret_cast<uint4*>(a.q1 + k * a.N + row0) + c;
+    } else {
+      const int64_t per = rows / 4, kb = u / per, c = u - kb * per;  // rows / 128 atoms of 512 bytes per K block
+      from = reinterpret_cast<const uint4*>(src + 2 * rk + rk / 32 + kb * (a.R / 128) * 512) + c;
+      to = reinterpret_cast<uint4*>(a.s1 + kb * (a.N / 128) * 512 + (row0 / 128) * 512) + c;
+    }
+    *to = *from;
+  }
+}
+
 void peer_barrier(torch::Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch) {
   TORCH_CHECK(world <= kMaxWorld, "peer_barrier: world > 8");
   peer_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(flag_ptrs.data_ptr<int64_t>(), (int)rank,
@@ -401,6 +449,32 @@ void cast_ranges_bf16(torch::Tensor src, torch::Tensor dst, torch::Tensor src_of
   TORCH_CHECK(src.scalar_type() == at::kFloat && dst.scalar_type() == at::kBFloat16, "cast_ranges_bf16: dtypes");
   cast_ranges_bf16_kernel<<<comm_grid(total / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       src.data_ptr<float>(), (__nv_bfloat16*)dst.data_ptr(), tab, dst_offsets.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mx_shard_gather(torch::Tensor bases, int64_t R, int64_t K, int64_t N, torch::Tensor q0, torch::Tensor s0,
+                     torch::Tensor q1, torch::Tensor s1) {
+  auto b = bases.to(at::kCPU);
+  const int world = (int)b.numel();
+  TORCH_CHECK(b.scalar_type() == at::kLong && world >= 1 && world <= kMaxWorld, "mx_shard_gather: rank bases");
+  TORCH_CHECK(R % 128 == 0 && K % 128 == 0 && N % 128 == 0 && R * world >= N, "mx_shard_gather: 128-multiples");
+  TORCH_CHECK(q0.numel() == N * K && q1.numel() == N * K && s0.numel() == N * K / 32 && s1.numel() == N * K / 32,
+              "mx_shard_gather: output sizes");
+  MxGatherArgs a{};
+  for (int r = 0; r < world; ++r) {
+    a.base[r] = b.data_ptr<int64_t>()[r];
+    TORCH_CHECK(a.base[r] % 16 == 0, "mx_shard_gather: 16-byte aligned copies");
+  }
+  a.q0 = q0.data_ptr<uint8_t>();
+  a.s0 = s0.data_ptr<uint8_t>();
+  a.q1 = q1.data_ptr<uint8_t>();
+  a.s1 = s1.data_ptr<uint8_t>();
+  a.R = R;
+  a.K = K;
+  a.N = N;
+  const int64_t units = R * K / 16;
+  dim3 grid((unsigned)std::min<int64_t>((units + 255) / 256, 148 * 2), world, 4);
+  mx_shard_gather_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

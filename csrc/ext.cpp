@@ -96,6 +96,18 @@ void gemm_skinny(torch::Tensor a, torch::Tensor w, torch::Tensor d);
 std::vector<torch::Tensor> ngram_embed_fwd(torch::Tensor tokens, std::vector<torch::Tensor> tables,
                                            std::vector<int64_t> orders, int64_t context);
 void ngram_embed_bwd(torch::Tensor rows, torch::Tensor dout, std::vector<torch::Tensor> grads);
+std::vector<torch::Tensor> ngram_embed_fwd_shard(torch::Tensor tokens, torch::Tensor bases, int64_t order_stride,
+                                                 int64_t rows_per_rank, int64_t buckets, int64_t dim,
+                                                 std::vector<int64_t> orders, int64_t context);
+void ngram_embed_bwd_shard(torch::Tensor rows, torch::Tensor dout, torch::Tensor bases, int64_t order_stride,
+                           int64_t rows_per_rank, int64_t buckets);
+void shard_sumsq(torch::Tensor g, torch::Tensor partial);
+void mx_quantize_into(torch::Tensor x, bool e5m2, torch::Tensor q0, torch::Tensor s0, torch::Tensor q1,
+                      torch::Tensor s1);
+void mx_shard_gather(torch::Tensor bases, int64_t R, int64_t K, int64_t N, torch::Tensor q0, torch::Tensor s0,
+                     torch::Tensor q1, torch::Tensor s1);
+void shard_adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double wd, double b1,
+                 double b2, double eps, int64_t step, torch::Tensor partial_ptrs, int64_t world, double max_norm);
 // ngram.cu
 torch::Tensor ngram_stage(torch::Tensor ids, torch::Tensor W, torch::Tensor M, torch::Tensor V, torch::Tensor last,
                           int64_t step, double lr, double wd, double b1, double b2, double eps, bool rowwise,
@@ -155,6 +167,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_spec_window", &mykb::gdn_spec_window);
   m.def("ngram_stage", &mykb::ngram_stage);
   m.def("ngram_embed_fwd", &mykb::ngram_embed_fwd, "hashed n-gram embedding: hash, gather and sum in one kernel");
+  m.def("ngram_embed_fwd_shard", &mykb::ngram_embed_fwd_shard,
+        "hashed n-gram embedding over row-sharded tables (peer loads from the owners' shards)");
+  m.def("ngram_embed_bwd_shard", &mykb::ngram_embed_bwd_shard,
+        "hashed n-gram embedding gradient added into the owners' gradient shards (peer reductions)");
+  m.def("shard_sumsq", &mykb::shard_sumsq, "squared norm of an fp32 buffer added into a partial norm");
+  m.def("mx_quantize_into", &mykb::mx_quantize_into, "MXFP8 quantisation (both copies) into given buffers");
+  m.def("mx_shard_gather", &mykb::mx_shard_gather,
+        "fp8 all-gather of a row-sharded MXFP8 weight from every rank's quantised shard (peer loads)");
+  m.def("shard_adamw", &mykb::shard_adamw, "AdamW over a local shard with the global clip coefficient; zeroes the gradient");
   m.def("ngram_embed_bwd", &mykb::ngram_embed_bwd, "hashed n-gram embedding backward: scatter-add per order");
   m.def("gemm_skinny", &mykb::gemm_skinny);
   m.def("mx_quantize", &mykb::mx_quantize);

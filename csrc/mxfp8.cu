@@ -418,6 +418,37 @@ std::vector<torch::Tensor> mx_quantize(torch::Tensor x, bool e5m2, bool dim0, bo
   return out;
 }
 
+// mx_quantize into caller-given buffers (both copies): q0 (R, C) and q1 (C, R) uint8,
+// s0 / s1 their scale atoms.  Used for the row shards of fp8-gathered weights, whose
+// quantized copies live in symmetric memory that peers read.
+void mx_quantize_into(torch::Tensor x, bool e5m2, torch::Tensor q0, torch::Tensor s0, torch::Tensor q1,
+                      torch::Tensor s1) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kBFloat16 && x.is_contiguous(),
+              "mx_quantize_into: contiguous 2-D bf16 CUDA matrix");
+  const int R = x.size(0), C = x.size(1);
+  TORCH_CHECK(C % 128 == 0 && R % 128 == 0, "mx_quantize_into: rows and columns must be multiples of 128");
+  for (const auto& t : {q0, s0, q1, s1})
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kByte && t.is_contiguous() &&
+                    ((uintptr_t)t.data_ptr() % 16) == 0,
+                "mx_quantize_into: 16-byte aligned contiguous uint8 outputs");
+  TORCH_CHECK(q0.numel() == (int64_t)R * C && q1.numel() == (int64_t)R * C &&
+                  s0.numel() == (int64_t)R * C / 32 && s1.numel() == (int64_t)R * C / 32,
+              "mx_quantize_into: output sizes");
+  c10::cuda::CUDAGuard guard(x.device());
+  if (R == 0) return;
+  dim3 grid(C / mx::QT_COLS, (R + mx::QT_ROWS - 1) / mx::QT_ROWS);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (e5m2)
+    mx::mx_quantize_kernel<true><<<grid, mx::QT_THREADS, 0, st>>>((const mx::bf16*)x.data_ptr(), R, C, C,
+                                                                   q0.data_ptr<uint8_t>(), s0.data_ptr<uint8_t>(),
+                                                                   q1.data_ptr<uint8_t>(), s1.data_ptr<uint8_t>(), R);
+  else
+    mx::mx_quantize_kernel<false><<<grid, mx::QT_THREADS, 0, st>>>((const mx::bf16*)x.data_ptr(), R, C, C,
+                                                                    q0.data_ptr<uint8_t>(), s0.data_ptr<uint8_t>(),
+                                                                    q1.data_ptr<uint8_t>(), s1.data_ptr<uint8_t>(), R);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 template <bool AE, bool BE, bool F32, bool ACC>
 static void mx_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const mx::GemmArgs& p,
                       int grid, cudaStream_t st) {

@@ -15,6 +15,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "ngram_hash.cuh"
+
 namespace mykb {
 
 struct NgramHyper {
@@ -181,9 +183,6 @@ void ngram_adam(torch::Tensor ids, torch::Tensor grad, torch::Tensor W, torch::T
 // the row ids (for the backward and for lazy tables); the backward scatter-adds the output
 // gradient into every order's gradient rows.
 // ------------------------------------------------------------------------------------
-__constant__ uint64_t kNgramMul[4] = {0x1F3D5B79A2C4E681ull, 0x0DDC0FFEEBADF00Dull, 0x1B873593CC9E2D51ull,
-                                      0x0000000100000001B3ull};
-
 constexpr int kNgramMaxOrders = 8;
 
 struct NgramTables {
@@ -192,17 +191,6 @@ struct NgramTables {
   int order[kNgramMaxOrders];
   int k;
 };
-
-__device__ __forceinline__ int64_t ngram_row(const int64_t* tok, int order, int64_t buckets) {
-  int64_t h = order;
-  for (int o = 0; o < order; ++o) {
-    const uint64_t u = (uint64_t)h * kNgramMul[o & 3] + (uint64_t)tok[-o] + 1ull;
-    h = (int64_t)u;
-    h ^= h >> 29;
-  }
-  int64_t r = h % buckets;
-  return r < 0 ? r + buckets : r;
-}
 
 // One warp per position: lane 0..k-1 hash one order each, then the warp sums the rows with
 // 16-byte loads.  tokens: (batch, context + seq) with `context` columns of left context.
@@ -217,7 +205,7 @@ ngram_embed_fwd_kernel(const int64_t* __restrict__ tokens, int64_t batch, int64_
     const int64_t* tok = tokens + b * (seq + context) + context + s;
     int64_t my = 0;
     if (lane < t.k) {
-      my = ngram_row(tok, t.order[lane], buckets);
+      my = ngram_bucket(tok, t.order[lane], buckets);
       rows[(int64_t)lane * n + pos] = my + lane * buckets;
     }
     const float4* src[kNgramMaxOrders];

@@ -45,15 +45,23 @@ class _NgramEmbed(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, tokens, context: int, orders: tuple[int, ...], *tables):
-        out, rows = ops.ext().ngram_embed_fwd(tokens.contiguous(), list(tables), list(orders), context)
+        shards = getattr(tables[0], "_mykb_table", None)  # row-sharded over the ranks (parallel/sharded.py)
+        if shards is not None:
+            out, rows = shards.forward(tokens.contiguous(), context)
+        else:
+            out, rows = ops.ext().ngram_embed_fwd(tokens.contiguous(), list(tables), list(orders), context)
         ctx.save_for_backward(rows)
         ctx.tables = tables
+        ctx.shards = shards
         ctx.lead = tokens.shape[0], tokens.shape[1] - context
         return out.view(*ctx.lead, out.shape[-1])
 
     @staticmethod
     def backward(ctx, dout):
         (rows,) = ctx.saved_tensors
+        if ctx.shards is not None:  # added into the owners' gradient rows
+            ctx.shards.backward(rows, dout.reshape(-1, dout.shape[-1]).float().contiguous())
+            return (None, None, None, *(None for _ in ctx.tables))
         grads, fresh = [], []
         for t in ctx.tables:
             main = getattr(t, "main_grad", None)

@@ -87,6 +87,9 @@ def _weight_operands(w: torch.Tensor) -> list[torch.Tensor]:
     """[W q0, s0, W^T q1, s1] (E4M3), re-quantized when the weight changed."""
     from .linear import _WEIGHT_EPOCH, bf16_weight
 
+    shard = getattr(w, "_mykb_shard", None)
+    if shard is not None:  # row-sharded by the parameter-sharded runtime: gathered in fp8
+        return shard.mx_operands()
     key = (w._version, _WEIGHT_EPOCH[0], w.data_ptr())
     cache = getattr(w, "_mykb_mx", None)
     if cache is not None and cache[0] == key:

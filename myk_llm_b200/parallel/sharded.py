@@ -78,6 +78,8 @@ class Slot:
     rows_per_rank: int = 0
     boff: int = 0        # offset of the bf16 shard in the flat bf16 buffer
     weight: "ShardedWeight | None" = field(default=None, repr=False)
+    mx: bool = False     # MXFP8 linear: its rows' fp8 copies are what the ranks gather
+    moff: int = 0        # offset of those copies in the flat fp8 buffer (bytes)
 
     @property
     def shard_numel(self) -> int:
@@ -126,6 +128,25 @@ class ShardedWeight:
         self.buf = buf
         self.rows, self.cols = slot.rows, slot.cols
         self._cpu_full: tuple[int, torch.Tensor] | None = None
+        self._mx: list[torch.Tensor] | None = None
+        self._mx_version = -1
+
+    def mx_operands(self) -> list[torch.Tensor]:
+        """[W q0, s0, W^T q1, s1] (E4M3) of an MXFP8 weight, gathered once per optimizer step
+        from every rank's fp8 copies of its rows (``mx_shard_gather``: 16-byte peer loads of
+        fp8 values and E8M0 scale atoms, about half the bytes of a bf16 gather)."""
+        rt, s = self.rt, self.slot
+        if self._mx is None:
+            dev = rt.info.device
+            n, k = s.rows, s.cols
+            u8 = dict(dtype=torch.uint8, device=dev)
+            self._mx = [torch.empty(n, k, **u8), torch.empty(n * k // 32, **u8), torch.empty(k, n, **u8),
+                        torch.empty(n * k // 32, **u8)]
+            self._mx_bases = rt.mx_bases + s.moff
+        if self._mx_version != rt.version:
+            ops.ext().mx_shard_gather(self._mx_bases, s.rows_per_rank, s.cols, s.rows, *self._mx)
+            self._mx_version = rt.version
+        return self._mx
 
     # -- CUDA --------------------------------------------------------------------------
     def _key(self) -> tuple[int, int]:
@@ -191,6 +212,10 @@ class ShardedWeight:
         """y = x W^T through this handle (``ops.linear`` calls it for sharded parameters)."""
         if not x.is_cuda:
             return _ShardedLinearCPU.apply(x, weight, self)
+        if self.slot.mx and x.numel() // x.shape[-1] > SKINNY_MAX_ROWS:
+            from ..ops.mxfp8 import mx_linear  # fp8-gathered operands (``mx_operands``)
+
+            return mx_linear(x, weight, weight._mykb_mxfp8)
         return _ShardedLinear.apply(x, weight, self)
 
     def full_cpu(self) -> torch.Tensor:
@@ -263,6 +288,109 @@ class _ShardedLinearCPU(torch.autograd.Function):
         return dx, None, None
 
 
+class TableShards:
+    """Row-sharded hashed n-gram tables (GPU, two or more ranks).
+
+    Rank ``r`` owns rows ``[r*R, (r+1)*R)`` (``R = ceil(buckets / world)``) of every order's
+    table: the fp32 master and the gradient rows live in symmetric memory (peers read the
+    master rows and add into the gradient rows), the AdamW moments are local.  The
+    embedding forward (``ngram_embed_fwd_shard``) hashes each position and reads its rows
+    from their owners; the backward (``ngram_embed_bwd_shard``) adds the position's
+    gradient into the owners' rows.  At the optimizer step each rank adds its gradient
+    shard's squared norm to the global clipping norm and runs AdamW on its rows, zeroing
+    the gradient rows for the next step (here, between the step's barriers: a peer may add
+    into them as soon as the step is over).  Only the rows a step's tokens touch cross
+    NVLink, where a replicated table would reduce and gather the whole table.  The tables
+    keep their parameters' full shapes and optimizer-state keys in checkpoints.
+    """
+
+    def __init__(self, rt: "ShardedDataParallel", params: list[nn.Parameter], orders: list[int]) -> None:
+        import torch.distributed._symmetric_memory as symm
+
+        self.rt = rt
+        self.params = params
+        self.orders = list(orders)
+        self.buckets, self.dim = params[0].shape
+        if any(tuple(p.shape) != (self.buckets, self.dim) for p in params) or self.dim % 4:
+            raise ValueError("row-sharded n-gram tables need one shape and a width that is a multiple of 4")
+        world, rank = rt.world, rt.rank
+        self.rows_per_rank = -(-self.buckets // world)
+        self.stride = _align(self.rows_per_rank * self.dim)  # elements between orders in a rank's buffer
+        total = self.stride * len(params)
+        dev = rt.info.device
+        self.param = symm.empty(total, dtype=torch.float32, device=dev)
+        self.grad = symm.empty(total, dtype=torch.float32, device=dev)
+        self.param.zero_()
+        self.grad.zero_()
+        self.m = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.v = torch.zeros(total, dtype=torch.float32, device=dev)
+        group = dist.group.WORLD
+        self._handles = [symm.rendezvous(t, group) for t in (self.param, self.grad)]
+        # base addresses stay on the host: the launch reads them without a device sync
+        self.param_bases = torch.tensor(list(self._handles[0].buffer_ptrs), dtype=torch.int64)
+        self.grad_bases = torch.tensor(list(self._handles[1].buffer_ptrs), dtype=torch.int64)
+        self.lo = rank * self.rows_per_rank
+        self.hi = min(self.buckets, self.lo + self.rows_per_rank)
+        with torch.no_grad():
+            for j, p in enumerate(params):
+                full = p.detach().float().contiguous()
+                dist.broadcast(full, src=0)
+                if self.hi > self.lo:
+                    self.shard(self.param, j)[:self.hi - self.lo].copy_(full[self.lo:self.hi])
+                p.data = torch.zeros(1, dtype=torch.float32, device=dev).expand(self.buckets, self.dim)
+                p._mykb_table = self
+                p.main_grad = None
+                p.grad = None
+        self.group: dict | None = None
+
+    def shard(self, buf: torch.Tensor, j: int) -> torch.Tensor:
+        return buf[j * self.stride:j * self.stride + self.rows_per_rank * self.dim].view(self.rows_per_rank, self.dim)
+
+    # -- embedding kernels -----------------------------------------------------------------
+    def forward(self, tokens: torch.Tensor, context: int):
+        return ops.ext().ngram_embed_fwd_shard(tokens, self.param_bases, self.stride * 4, self.rows_per_rank,
+                                               self.buckets, self.dim, self.orders, context)
+
+    def backward(self, rows: torch.Tensor, dout: torch.Tensor) -> None:
+        ops.ext().ngram_embed_bwd_shard(rows, dout, self.grad_bases, self.stride * 4, self.rows_per_rank,
+                                        self.buckets)
+
+    # -- optimizer step (between the runtime's barriers) -------------------------------------
+    def add_sumsq(self, partial: torch.Tensor) -> None:
+        ops.ext().shard_sumsq(self.grad, partial)
+
+    def adamw(self, step: int, b1: float, b2: float, eps: float, clip: float) -> None:
+        g = self.group or {"lr": 0.0, "weight_decay": 0.0}
+        ops.ext().shard_adamw(self.param, self.grad, self.m, self.v, g["lr"], g["weight_decay"], b1, b2, eps, step,
+                              self.rt.partial_ptrs, self.rt.world, clip)
+
+    # -- checkpoints ---------------------------------------------------------------------
+    def gather(self, buf: torch.Tensor, j: int) -> torch.Tensor:
+        mine = self.shard(buf, j).contiguous()
+        parts = [torch.empty_like(mine) for _ in range(self.rt.world)]
+        dist.all_gather(parts, mine)
+        return torch.cat(parts, 0)[:self.buckets]
+
+    def scatter(self, buf: torch.Tensor, j: int, full: torch.Tensor) -> None:
+        dst = self.shard(buf, j)
+        dst.zero_()
+        if self.hi > self.lo:
+            dst[:self.hi - self.lo].copy_(full[self.lo:self.hi].to(dst.dtype))
+
+    def materialise(self) -> None:
+        with torch.no_grad():
+            for j, p in enumerate(self.params):
+                p.data = self.gather(self.param, j).contiguous()
+
+    def dematerialise(self) -> None:
+        dev = self.rt.info.device
+        for p in self.params:
+            p.data = torch.zeros(1, dtype=torch.float32, device=dev).expand(self.buckets, self.dim)
+
+    def memory_bytes(self) -> int:
+        return 4 * (self.param.numel() + self.grad.numel() + self.m.numel() + self.v.numel())
+
+
 class ShardedDataParallel(nn.Module):
     """Wraps a model; see module docstring.  ``owns_gradients`` tells the trainer that this
     runtime provides the gradient buffers and the whole optimizer step."""
@@ -287,6 +415,8 @@ class ShardedDataParallel(nn.Module):
         self._linear_weights = {id(m.weight) for m in model.modules() if type(m) is nn.Linear}
         self.trace = UseTrace()
         self.grad_mc = 0  # NVSwitch multicast address of the gradient buffer (0: peer loads)
+        self.tables: TableShards | None = None  # row-sharded n-gram tables
+        self.table_ids: set[int] = set()
 
     # -- module plumbing ----------------------------------------------------------------
     def forward(self, *args, **kwargs):
@@ -317,9 +447,12 @@ class ShardedDataParallel(nn.Module):
     def _shardable(self, p: nn.Parameter) -> bool:
         if not self.shard_params or self.world < 2 or p.dim() != 2 or id(p) not in self._linear_weights:
             return False
-        if getattr(p, "_mykb_mxfp8", None) is not None or getattr(p, "_mykb_fp8", None) is not None:
-            return False  # float8 linears quantise their own (replicated) master copy
         rows, cols = p.shape
+        if getattr(p, "_mykb_mxfp8", None) is not None:
+            # MXFP8 linears: row shards of 128-row multiples, gathered as fp8 + E8M0 scales
+            return self.cuda and rows % 128 == 0 and cols % 128 == 0
+        if getattr(p, "_mykb_fp8", None) is not None:
+            return False  # per-tensor / per-row float8 linears quantise their own replicated master
         return rows % 8 == 0 and cols % 8 == 0 and rows >= self.world
 
     def attach_optimizers(self, optimizers: list[torch.optim.Optimizer]) -> None:
@@ -340,7 +473,9 @@ class ShardedDataParallel(nn.Module):
             if p.requires_grad and id(p) not in seen:
                 seen.add(id(p))
                 ordered.append(p)
-        rep = [p for p in ordered if not (id(p) in muon_ids and self._shardable(p))]
+        table_params, table_orders = self._ngram_tables(muon_ids)
+        self.table_ids = {id(p) for p in table_params}
+        rep = [p for p in ordered if id(p) not in self.table_ids and not (id(p) in muon_ids and self._shardable(p))]
         shd = [p for p in ordered if id(p) in muon_ids and self._shardable(p)]
         # replicated slots: the same offset in the gradient and parameter buffers
         off = 0
@@ -348,19 +483,61 @@ class ShardedDataParallel(nn.Module):
             self.slots.append(Slot(p, names.get(id(p), "?"), off, off, p.numel()))
             off += _align(p.numel())
         self.rep_total = off
-        goff, poff, boff = off, off, 0
+        goff, poff, boff, moff = off, off, 0, 0
         for p in shd:
             rows, cols = p.shape
             r = -(-rows // self.world)
-            s = Slot(p, names.get(id(p), "?"), goff, poff, p.numel(), True, rows, cols, r, boff)
+            mx = getattr(p, "_mykb_mxfp8", None) is not None
+            if mx:
+                r = -(-r // 128) * 128
+            s = Slot(p, names.get(id(p), "?"), goff, poff, p.numel(), True, rows, cols, r, boff, mx=mx, moff=moff)
             self.slots.append(s)
             goff += _align(p.numel())
             poff += _align(r * cols)
             boff += _align(r * cols)
+            if mx:
+                moff += -(-(2 * r * cols + r * cols // 16) // 512) * 512
         self.grad_total, self.param_total, self.bf16_total = _align(goff), _align(poff), _align(max(boff, ALIGN))
+        self.mx_total = moff
         self._allocate()
         self._load_params_into_buffers()
+        self.tables = TableShards(self, table_params, table_orders) if table_params else None
         self._build_ownership(optimizers, Muon, lr_ratio)
+        self._quantize_mx_shards(sync=True)
+
+    def _quantize_mx_shards(self, sync: bool = False) -> None:
+        """MXFP8 copies (both blockings, E4M3) of this rank's rows of every MXFP8 weight, into
+        symmetric memory where the other ranks' gathers read them; then a barrier."""
+        mx = [s for s in self.slots if s.mx]
+        if not mx or not self.cuda:
+            return
+        ext = ops.ext()
+        for s in mx:
+            r, k = s.rows_per_rank, s.cols
+            rk = r * k
+            base = self.flat_mx[s.moff:s.moff + 2 * rk + rk // 16]
+            ext.mx_quantize_into(self.flat_bf16[s.boff:s.boff + rk].view(r, k), False, base[:rk],
+                                 base[rk:rk + rk // 32], base[rk + rk // 32:2 * rk + rk // 32],
+                                 base[2 * rk + rk // 32:])
+        if sync:
+            torch.cuda.synchronize(self.info.device)
+            dist.barrier()
+        else:
+            self._barrier()
+
+    def _ngram_tables(self, muon_ids: set[int]) -> tuple[list[nn.Parameter], list[int]]:
+        """The hashed n-gram tables to row-shard: GPU, two or more ranks, parameter sharding
+        on, dense (not lazily updated) tables trained by AdamW."""
+        from ..models.embeddings import NgramEmbedding
+
+        if not (self.cuda and self.shard_params and self.world >= 2):
+            return [], []
+        for m in self.module.modules():
+            if isinstance(m, NgramEmbedding) and m.row_source is None:
+                params = [t.weight for t in m.tables]
+                if params and all(p.requires_grad and id(p) not in muon_ids for p in params):
+                    return params, list(m.orders)
+        return [], []
 
     def _allocate(self) -> None:
         dev = self.info.device
@@ -372,9 +549,12 @@ class ShardedDataParallel(nn.Module):
             self.flat_grad = symm.empty(self.grad_total, dtype=torch.float32, device=dev)
             self.flat_bf16 = symm.empty(self.bf16_total, dtype=torch.bfloat16, device=dev)
             self.ctrl = symm.empty(64, dtype=torch.int32, device=dev)  # [0, world): barrier flags; [32]: norm partial
+            self.flat_mx = symm.empty(max(self.mx_total, 512), dtype=torch.uint8, device=dev)
             self.flat_grad.zero_()
             self.ctrl.zero_()
             handles = [symm.rendezvous(t, group) for t in (self.flat_param, self.flat_grad, self.flat_bf16, self.ctrl)]
+            self._mx_handle = symm.rendezvous(self.flat_mx, group)
+            self.mx_bases = torch.tensor(list(self._mx_handle.buffer_ptrs), dtype=torch.int64)  # host side
             ptrs = [torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=dev) for h in handles]
             self.param_ptrs, self.grad_ptrs, self.bf16_ptrs, self.flag_ptrs = ptrs
             self.partial_ptrs = self.flag_ptrs + 32 * 4
@@ -460,9 +640,12 @@ class ShardedDataParallel(nn.Module):
         for opt in optimizers:
             for group in opt.param_groups:
                 for p in group["params"]:
+                    if id(p) in self.table_ids:
+                        self.tables.group = group
+                        continue
                     s = by_param[id(p)]
                     if isinstance(opt, Muon):
-                        key = (tuple(p.shape), s.sharded)
+                        key = (tuple(p.shape), s.sharded, s.rows_per_rank)  # one shard layout per bucket
                         b = self.muon_buckets.setdefault(key, {"slots": [], "group": group,
                                                                "ratio": lr_ratio(p.shape, group["adjust_lr"])})
                         b["slots"].append(s)
@@ -573,6 +756,8 @@ class ShardedDataParallel(nn.Module):
         else:
             ext.dp_reduce_sumsq(self.grad_ptrs, self.rank, self.world, self.red_offsets, self.red_prefix,
                                 self.partial, self.red_total)
+        if self.tables is not None:
+            self.tables.add_sumsq(self.partial)
         self._barrier()
         b1, b2, eps = self._adam_hparams()
         dev = self.info.device
@@ -582,10 +767,12 @@ class ShardedDataParallel(nn.Module):
         ext.dp_adamw_allgather(self.param_ptrs, self.grad_ptrs, self.rank, self.world, self.adam_offsets,
                                self.adam_prefix, wd, lr, self.adam_m, self.adam_v, b1, b2, eps, self.step_count,
                                self.partial_ptrs, 0.0, clip, norm, self.adam_total)
+        if self.tables is not None:
+            self.tables.adamw(self.step_count, b1, b2, eps, clip)
         for key, sl in self.owned_muon.items():
             if not sl:
                 continue
-            shape, sharded = key
+            shape, sharded = key[:2]
             b = self.muon_buckets[key]
             g = b["group"]
             packed = torch.empty(len(sl), *shape, dtype=torch.bfloat16, device=dev)
@@ -600,6 +787,7 @@ class ShardedDataParallel(nn.Module):
                 ext.dp_muon_apply_allgather(self.param_ptrs, self.rank, self.world, self.muon_poffs[key],
                                             math.prod(shape), decay, scale, orth)
         self._barrier()
+        self._quantize_mx_shards()  # the new rows' fp8 copies (own barrier)
         # A peer wait that gave up leaves its code in the device status word; the trainer
         # reads it at its next host sync (Trainer.check_health).
         self.last_norm = norm[0]
@@ -653,7 +841,7 @@ class ShardedDataParallel(nn.Module):
             pos += n
         shard_updates: dict[int, torch.Tensor] = {}
         for key, b in self.muon_buckets.items():
-            shape, sharded = key
+            shape, sharded = key[:2]
             g = b["group"]
             mine = self.owned_muon[key]
             ups = []
@@ -716,9 +904,16 @@ class ShardedDataParallel(nn.Module):
             for t in (full_m, full_v, full_mom):
                 dist.all_reduce(t)
         slot_of = {id(s.param): s for s in self.slots}
+        table_index = {id(p): j for j, p in enumerate(self.tables.params)} if self.tables is not None else {}
         for opt in self.optimizers:
             for group in opt.param_groups:
                 for p in group["params"]:
+                    if id(p) in table_index:  # row-sharded table: gather its moments (collective)
+                        j, st = table_index[id(p)], opt.state[p]
+                        st["step"] = torch.tensor(float(self.step_count))
+                        st["exp_avg"] = self.tables.gather(self.tables.m, j)
+                        st["exp_avg_sq"] = self.tables.gather(self.tables.v, j)
+                        continue
                     s = slot_of[id(p)]
                     st = opt.state[p]
                     sl = slice(s.goff, s.goff + s.numel)
@@ -735,12 +930,16 @@ class ShardedDataParallel(nn.Module):
             for s in self.slots:
                 if s.sharded:
                     s.param.data = self.gather_full_fp32(s).contiguous()
+        if self.tables is not None:
+            self.tables.materialise()
 
     def _dematerialise_sharded(self) -> None:
         dev = self.info.device
         for s in self.slots:
             if s.sharded:
                 s.param.data = torch.zeros(1, dtype=torch.float32, device=dev).expand(s.rows, s.cols)
+        if self.tables is not None:
+            self.tables.dematerialise()
 
     def after_checkpoint_save(self) -> None:
         self._dematerialise_sharded()
@@ -760,6 +959,10 @@ class ShardedDataParallel(nn.Module):
             for s in self.slots:
                 if s.sharded and s.param.data.stride() != (0, 0):
                     self._set_full_fp32(s, s.param.data)
+            if self.tables is not None:
+                for j, p in enumerate(self.tables.params):
+                    if p.data.stride() != (0, 0):
+                        self.tables.scatter(self.tables.param, j, p.data)
             self._dematerialise_sharded()
         slot_of = {id(s.param): s for s in self.slots}
         dev = self.info.device
@@ -767,9 +970,18 @@ class ShardedDataParallel(nn.Module):
         flat_v = torch.zeros_like(flat_m)
         flat_mom = torch.zeros_like(flat_m)
         step = None
+        table_index = {id(p): j for j, p in enumerate(self.tables.params)} if self.tables is not None else {}
         for opt in self.optimizers:
             for group in opt.param_groups:
                 for p in group["params"]:
+                    if id(p) in table_index:
+                        st = opt.state.get(p, {})
+                        if "exp_avg" in st:
+                            j = table_index[id(p)]
+                            self.tables.scatter(self.tables.m, j, st["exp_avg"].float())
+                            self.tables.scatter(self.tables.v, j, st["exp_avg_sq"].float())
+                            step = int(float(st["step"]))
+                        continue
                     s = slot_of[id(p)]
                     st = opt.state.get(p, {})
                     sl = slice(s.goff, s.goff + s.numel)
@@ -793,14 +1005,19 @@ class ShardedDataParallel(nn.Module):
         if self.cuda:
             torch.cuda.synchronize(dev)
             dist.barrier()
+            self._quantize_mx_shards(sync=True)
 
     def full_named_parameters(self) -> dict[str, torch.Tensor]:
         """Every trainable parameter as a full fp32 tensor (row-sharded weights gathered: a
         collective, so every rank calls it)."""
         out = {}
+        table_index = {id(p): j for j, p in enumerate(self.tables.params)} if self.tables is not None else {}
         for n, p in self.module.named_parameters():
             s = getattr(p, "_mykb_shard", None)
-            out[n] = self.gather_full_fp32(s.slot).clone() if s is not None else p.detach().clone()
+            if id(p) in table_index:
+                out[n] = self.tables.gather(self.tables.param, table_index[id(p)])
+            else:
+                out[n] = self.gather_full_fp32(s.slot).clone() if s is not None else p.detach().clone()
         return out
 
     # -- memory report ------------------------------------------------------------------
@@ -814,6 +1031,7 @@ class ShardedDataParallel(nn.Module):
             "optimizer_state": (self.adam_m.numel() + self.adam_v.numel()
                                 + sum(t.numel() for t in self.muon_mom.values())) * 4,
             "gather_buffers": sum(b.w.numel() * 2 for b in bufs.values()),
+            "ngram_table_shards": self.tables.memory_bytes() if self.tables is not None else 0,
         }
 
 
