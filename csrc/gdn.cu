@@ -12,21 +12,18 @@
 //   O  = diag(e^gamma) Q^ S0 + lower_incl(E * Q^ K^T) U
 //   S1 = e^{gamma_C} S0 + (F * K^)^T U,             F_s = exp(gamma_C - gamma_s)
 //
-// Everything except the S0 -> S1 recurrence is independent per chunk, so the work is
-// split into chunk-parallel kernels (one CTA per (chunk, head), on the tcgen05 tensor
-// cores, in gdn_tc.cu) around a thin sequential kernel (one CTA per (sequence, head, 32
-// value columns), here) that carries the state:
+// Everything except the S0 -> S1 recurrence is independent per chunk; all five kernels
+// are tcgen05 kernels in gdn_tc.cu:
 //
-//   forward:  gdn_prep_tc (K^K^T, blocked triangular inverse, W, U~, T)
-//             gdn_state   (U = U~ - W S0, S1 = ...; saves S0 per chunk, U)
-//             gdn_out_tc  (P = lower(E * Q^K^T), O)
-//   backward: gdn_dstate  (dS at every chunk end, reverse recurrence)
-//             gdn_grad_tc (dq, dk, dv, dg, dbeta of every chunk, l2-norm backward)
+//   forward:  gdn_prep_tc   (K^K^T, blocked triangular inverse, W, U~, T), one CTA per (chunk, head)
+//             gdn_state_tc  (U = U~ - W S0, S1 = ...; saves S0 per chunk, U), one CTA per
+//                           (sequence, head, 64 value columns), state in TMEM
+//             gdn_out_tc    (P = lower(E * Q^K^T), O)
+//   backward: gdn_dstate_tc (dS at every chunk end, reverse recurrence, dS in TMEM)
+//             gdn_grad_tc   (dq, dk, dv, dg, dbeta of every chunk, l2-norm backward)
 //
-// The sequential kernels keep their 128 x 32 state slice in the fragments of warp-level
-// bf16 MMAs (fp32 accumulate) between chunks, fed by ldmatrix from padded shared-memory
-// tiles, with the next chunk's operands streaming in by cp.async; the state and every
-// reduction stay in fp32.
+// This file holds the host entry points, the token recurrence for decoding and the
+// speculative-decoding window, and the short causal convolution.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -41,64 +38,7 @@ typedef __nv_bfloat16 bf16;
 constexpr int C = 64;      // chunk length
 constexpr int DK = 128;    // head_k_dim
 constexpr int DV = 128;    // head_v_dim
-constexpr int LD = 136;    // padded row stride (elements) of 128-wide bf16 tiles
-constexpr int LDS = 72;    // padded row stride of 64-wide bf16 tiles
-constexpr int LDP = 40;    // padded row stride of 32-wide bf16 tiles
-constexpr int PARTS = 4;   // value-column slices of the sequential kernels
-constexpr int PW = DV / PARTS;  // 32 columns per slice
-constexpr int NT = 256;    // threads of every chunk kernel (8 warps)
-
-// ---------------------------------------------------------------- warp MMA helpers
-__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const bf16* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], const bf16* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// acc[j] (16 x 8 tile j) += A(m0.., 0..K) * B(0..K, n0 + 8j ..)
-//   A_T == false: A(m, k) at A[m * lda + k];  true: at A[k * lda + m]
-//   B_T == false: B(k, n) at B[n * ldb + k];  true: at B[k * ldb + n]
-// Fragment element e of acc[j] sits at row m0 + lane/4 + 8 (e >= 2), column
-// n0 + 8j + 2 (lane % 4) + (e & 1).
-template <int NT8, bool A_T, bool B_T>
-__device__ __forceinline__ void warp_mma(float (&acc)[NT8][4], const bf16* A, int lda, int m0, const bf16* B, int ldb,
-                                         int n0, int K) {
-  static_assert(NT8 % 2 == 0, "pairs of n8 tiles");
-  const int lane = threadIdx.x & 31;
-  const int r = lane & 7, mat = lane >> 3;
-#pragma unroll 2
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    uint32_t a[4];
-    if (!A_T) ldsm4(a, A + (m0 + (lane & 15)) * lda + k0 + (lane >> 4) * 8);
-    else ldsm4t(a, A + (k0 + r + (mat >> 1) * 8) * lda + m0 + (mat & 1) * 8);
-#pragma unroll
-    for (int j = 0; j < NT8; j += 2) {
-      uint32_t b[4];
-      if (!B_T) ldsm4(b, B + (n0 + j * 8 + r + (mat >> 1) * 8) * ldb + k0 + (mat & 1) * 8);
-      else ldsm4t(b, B + (k0 + (mat & 1) * 8 + r) * ldb + n0 + j * 8 + (mat >> 1) * 8);
-      mma(acc[j], a, b[0], b[1]);
-      mma(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-template <int NT8>
-__device__ __forceinline__ void zero(float (&acc)[NT8][4]) {
-#pragma unroll
-  for (int j = 0; j < NT8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-}
+constexpr int NT = 256;    // threads of the recurrent decoding kernels
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -107,314 +47,6 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 __device__ __forceinline__ void st2(bf16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack2(a, b); }
 __device__ __forceinline__ float2 ld2(const bf16* p) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
-}
-
-// ---------------------------------------------------------------- async copies
-__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
-  // zero-fills the 16 bytes when !valid (no bytes are read)
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp4(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// 64 token rows (stride `stride` elements) x 128 columns -> padded tile; rows >= n zero.
-__device__ __forceinline__ void rows128_async(bf16* dst, const bf16* src, int64_t stride, int n) {
-  for (int i = threadIdx.x; i < C * 16; i += NT) {
-    const int r = i >> 4, c = (i & 15) * 8;
-    cp16(dst + r * LD + c, src + (r < n ? r : 0) * stride + c, r < n);
-  }
-}
-// 64 token rows x 32 columns (a value slice) -> padded tile; rows >= n zero.
-__device__ __forceinline__ void rows32_async(bf16* dst, const bf16* src, int64_t stride, int n) {
-  if (threadIdx.x < C * 4) {
-    const int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 8;
-    cp16(dst + r * LDP + c, src + (r < n ? r : 0) * stride + c, r < n);
-  }
-}
-// contiguous (rows x 128) bf16 block -> padded tile
-__device__ __forceinline__ void tile128_async(bf16* dst, const bf16* src, int rows) {
-  for (int i = threadIdx.x; i < rows * 16; i += NT) {
-    const int r = i >> 4, c = (i & 15) * 8;
-    cp16(dst + r * LD + c, src + r * 128 + c, true);
-  }
-}
-// contiguous (64 x 64) bf16 block -> padded tile
-__device__ __forceinline__ void tile64_async(bf16* dst, const bf16* src) {
-  for (int i = threadIdx.x; i < C * 8; i += NT) {
-    const int r = i >> 3, c = (i & 7) * 8;
-    cp16(dst + r * LDS + c, src + r * C + c, true);
-  }
-}
-// 64 per-token floats of head-major scalars (rows >= n zero) -> shared
-__device__ __forceinline__ void scal_async(float* dst, const float* src, int n) {
-  if (threadIdx.x < C) cp4(dst + threadIdx.x, src + (threadIdx.x < n ? threadIdx.x : 0), threadIdx.x < n);
-}
-// gdn_state: one CTA per (sequence, head, 32 value columns); the state slice (128 x 32,
-// fp32) lives in the MMA accumulators of the 8 warps (warp w: key rows 16w..16w+15).
-// The next chunk's operands stream in (cp.async, double buffered) while this one runs;
-// S += K^T diag(F kinv) U uses the raw keys with the scaling folded into U's rows.
-struct StateBuf {
-  bf16 w[C * LD];   // W
-  bf16 k[C * LD];   // raw keys
-  bf16 u[C * LDP];  // U~ slice
-  float gam[C], ki[C];
-};
-struct StateSm {
-  StateBuf buf[2];
-  bf16 uf[C * LDP];   // diag(F kinv) U (operand)
-  bf16 sb[DK * LDP];  // S0 slice (operand)
-};
-
-__global__ void __launch_bounds__(NT) gdn_state_kernel(Geo g, const bf16* __restrict__ k, const float* __restrict__ gcum,
-                                                       const float* __restrict__ kinv, const bf16* __restrict__ w_in,
-                                                       bf16* __restrict__ u_io, const float* __restrict__ init,
-                                                       bf16* __restrict__ states, float* __restrict__ fin) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  StateSm& s = *reinterpret_cast<StateSm*>(smraw);
-  const int part = blockIdx.x % PARTS;
-  const int h = (blockIdx.x / PARTS) % g.heads;
-  const int seq = g.order[blockIdx.x / (PARTS * g.heads)];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, cq = (lane & 3) * 2;
-  const int col0 = part * PW;
-  int t0, len;
-  seq_span(g, seq, t0, len);
-  float S[4][4];
-  {
-    const float* src = init != nullptr ? init + ((int64_t)seq * g.heads + h) * DK * DV : nullptr;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
-      S[j][0] = src ? src[r * DV + c] : 0.f;
-      S[j][1] = src ? src[r * DV + c + 1] : 0.f;
-      S[j][2] = src ? src[(r + 8) * DV + c] : 0.f;
-      S[j][3] = src ? src[(r + 8) * DV + c + 1] : 0.f;
-    }
-  }
-  const int nch = (len + C - 1) / C;
-  auto prefetch = [&](int ci) {
-    StateBuf& b = s.buf[ci & 1];
-    const int chunk = g.chunk_off[seq] + ci;
-    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
-    const int64_t cbase = (int64_t)chunk * g.heads + h;
-    tile128_async(b.w, w_in + cbase * C * DK, C);
-    rows128_async(b.k, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-    rows32_async(b.u, u_io + cbase * C * DV + col0, DV, C);
-    scal_async(b.gam, gcum + (int64_t)h * g.rows + row0, n);
-    scal_async(b.ki, kinv + (int64_t)h * g.rows + row0, n);
-    cp_commit();
-  };
-  if (nch > 0) prefetch(0);
-  for (int ci = 0; ci < nch; ++ci) {
-    if (ci + 1 < nch) {
-      prefetch(ci + 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    StateBuf& b = s.buf[ci & 1];
-    const int chunk = g.chunk_off[seq] + ci;
-    const int n = min(C, len - ci * C);
-    const int64_t cbase = (int64_t)chunk * g.heads + h;
-    bf16* st = states + cbase * DK * DV + col0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {  // S0 of this chunk: to global and to the operand tile
-      const int r = warp * 16 + gq, c = j * 8 + cq;
-      st2(st + r * DV + c, S[j][0], S[j][1]);
-      st2(st + (r + 8) * DV + c, S[j][2], S[j][3]);
-      st2(s.sb + r * LDP + c, S[j][0], S[j][1]);
-      st2(s.sb + (r + 8) * LDP + c, S[j][2], S[j][3]);
-    }
-    __syncthreads();
-    const float gl = b.gam[n - 1];
-    {  // U = U~ - W S0  (64 x 32): warp -> rows 16 (w % 4), columns 16 (w / 4)
-      float acc[2][4];
-      zero(acc);
-      const int mt = warp & 3, nb = (warp >> 2) * 16;
-      warp_mma<2, false, true>(acc, b.w, LD, mt * 16, s.sb, LDP, nb, DK);
-      bf16* ug = u_io + cbase * C * DV + col0;
-      const int r = mt * 16 + gq;
-      const float f0 = r < n ? __expf(gl - b.gam[r]) * b.ki[r] : 0.f;
-      const float f1 = r + 8 < n ? __expf(gl - b.gam[r + 8]) * b.ki[r + 8] : 0.f;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = nb + j * 8 + cq;
-        const float2 u0 = ld2(b.u + r * LDP + c), u1 = ld2(b.u + (r + 8) * LDP + c);
-        const float a0 = u0.x - acc[j][0], a1 = u0.y - acc[j][1], a2 = u1.x - acc[j][2], a3 = u1.y - acc[j][3];
-        st2(ug + r * DV + c, a0, a1);
-        st2(ug + (r + 8) * DV + c, a2, a3);
-        st2(s.uf + r * LDP + c, f0 * a0, f0 * a1);
-        st2(s.uf + (r + 8) * LDP + c, f1 * a2, f1 * a3);
-      }
-    }
-    __syncthreads();
-    {  // S <- e^{gamma_C} S + K_raw^T (diag(F kinv) U)
-      const float egl = __expf(gl);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) S[j][e] *= egl;
-      warp_mma<4, true, true>(S, b.k, LD, warp * 16, s.uf, LDP, 0, C);
-    }
-    __syncthreads();
-  }
-  if (fin != nullptr) {
-    float* dst = fin + ((int64_t)seq * g.heads + h) * DK * DV;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
-      *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(S[j][0], S[j][1]);
-      *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(S[j][2], S[j][3]);
-    }
-  }
-}
-
-// ----------------------------------------------------------------------- backward
-// gdn_dstate: dS at every chunk end (dS_C), in reverse:
-//   dU  = P^T dO + diag(F kinv) (K_raw dS_C)
-//   dS0 = e^{gamma_C} dS_C + Q_raw^T diag(e^gamma qinv) dO - W^T dU
-// with the next (earlier) chunk's operands streaming in while this one runs.
-struct DStateBuf {
-  bf16 q[C * LD];     // raw queries
-  bf16 w[C * LD];
-  bf16 k[C * LD];     // raw keys
-  bf16 p[C * LDS];
-  bf16 dob[C * LDP];  // dO slice
-  float gam[C], ki[C], qi[C];
-};
-struct DStateSm {
-  DStateBuf buf[2];
-  bf16 doq[C * LDP];  // diag(e^gamma qinv) dO slice
-  bf16 du[C * LDP];   // -dU slice
-  bf16 dsb[DK * LDP];
-};
-
-__global__ void __launch_bounds__(NT) gdn_dstate_kernel(Geo g, const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                        const float* __restrict__ gcum, const float* __restrict__ kinv,
-                                                        const float* __restrict__ qinv, const bf16* __restrict__ w_in,
-                                                        const bf16* __restrict__ p_in, const bf16* __restrict__ dout,
-                                                        const float* __restrict__ dfinal, bf16* __restrict__ dstates,
-                                                        float* __restrict__ dinit) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  DStateSm& s = *reinterpret_cast<DStateSm*>(smraw);
-  const int part = blockIdx.x % PARTS;
-  const int h = (blockIdx.x / PARTS) % g.heads;
-  const int seq = g.order[blockIdx.x / (PARTS * g.heads)];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, cq = (lane & 3) * 2;
-  const int col0 = part * PW;
-  int t0, len;
-  seq_span(g, seq, t0, len);
-  float dS[4][4];
-  {
-    const float* src = dfinal != nullptr ? dfinal + ((int64_t)seq * g.heads + h) * DK * DV : nullptr;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
-      dS[j][0] = src ? src[r * DV + c] : 0.f;
-      dS[j][1] = src ? src[r * DV + c + 1] : 0.f;
-      dS[j][2] = src ? src[(r + 8) * DV + c] : 0.f;
-      dS[j][3] = src ? src[(r + 8) * DV + c + 1] : 0.f;
-    }
-  }
-  const int nch = (len + C - 1) / C;
-  auto prefetch = [&](int ci) {
-    DStateBuf& b = s.buf[ci & 1];
-    const int chunk = g.chunk_off[seq] + ci;
-    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
-    const int64_t cbase = (int64_t)chunk * g.heads + h;
-    const int64_t hb = (int64_t)h * g.rows + row0;
-    rows128_async(b.q, q + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-    tile128_async(b.w, w_in + cbase * C * DK, C);
-    rows128_async(b.k, k + (int64_t)row0 * g.row_q + (int64_t)h * DK, g.row_q, n);
-    tile64_async(b.p, p_in + cbase * C * C);
-    rows32_async(b.dob, dout + (int64_t)row0 * g.row_v + (int64_t)h * DV + col0, g.row_v, n);
-    scal_async(b.gam, gcum + hb, n);
-    scal_async(b.ki, kinv + hb, n);
-    scal_async(b.qi, qinv + hb, n);
-    cp_commit();
-  };
-  if (nch > 0) prefetch(nch - 1);
-  for (int ci = nch - 1; ci >= 0; --ci) {
-    if (ci > 0) {
-      prefetch(ci - 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    DStateBuf& b = s.buf[ci & 1];
-    const int chunk = g.chunk_off[seq] + ci;
-    const int n = min(C, len - ci * C);
-    const int64_t cbase = (int64_t)chunk * g.heads + h;
-    bf16* dst = dstates + cbase * DK * DV + col0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * 16 + gq, c = j * 8 + cq;
-      st2(dst + r * DV + c, dS[j][0], dS[j][1]);
-      st2(dst + (r + 8) * DV + c, dS[j][2], dS[j][3]);
-      st2(s.dsb + r * LDP + c, dS[j][0], dS[j][1]);
-      st2(s.dsb + (r + 8) * LDP + c, dS[j][2], dS[j][3]);
-    }
-    __syncthreads();  // this chunk's buffer and dsb are visible
-    const float gl = b.gam[n - 1];
-    if (tid < C * 4) {  // diag(e^gamma qinv) dO
-      const int r = tid >> 2, c = (tid & 3) * 8;
-      const float sc = r < n ? __expf(b.gam[r]) * b.qi[r] : 0.f;
-      uint4 v = *reinterpret_cast<const uint4*>(b.dob + r * LDP + c);
-      uint32_t* wv = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wv[e]));
-        wv[e] = pack2(f.x * sc, f.y * sc);
-      }
-      *reinterpret_cast<uint4*>(s.doq + r * LDP + c) = v;
-    }
-    {  // -dU = -(P^T dO + diag(F kinv) (K_raw dS_C))
-      float acc[2][4], kd[2][4];
-      zero(acc);
-      zero(kd);
-      const int mt = warp & 3, nb = (warp >> 2) * 16;
-      warp_mma<2, true, true>(acc, b.p, LDS, mt * 16, b.dob, LDP, nb, C);
-      warp_mma<2, false, true>(kd, b.k, LD, mt * 16, s.dsb, LDP, nb, DK);
-      const int r = mt * 16 + gq;
-      const float f0 = r < n ? __expf(gl - b.gam[r]) * b.ki[r] : 0.f;
-      const float f1 = r + 8 < n ? __expf(gl - b.gam[r + 8]) * b.ki[r + 8] : 0.f;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = nb + j * 8 + cq;
-        st2(s.du + r * LDP + c, -(acc[j][0] + f0 * kd[j][0]), -(acc[j][1] + f0 * kd[j][1]));
-        st2(s.du + (r + 8) * LDP + c, -(acc[j][2] + f1 * kd[j][2]), -(acc[j][3] + f1 * kd[j][3]));
-      }
-    }
-    __syncthreads();
-    {
-      const float egl = __expf(gl);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) dS[j][e] *= egl;
-      warp_mma<4, true, true>(dS, b.q, LD, warp * 16, s.doq, LDP, 0, C);
-      warp_mma<4, true, true>(dS, b.w, LD, warp * 16, s.du, LDP, 0, C);
-    }
-    __syncthreads();
-  }
-  if (dinit != nullptr) {
-    float* dst = dinit + ((int64_t)seq * g.heads + h) * DK * DV;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * 16 + gq, c = col0 + j * 8 + cq;
-      *reinterpret_cast<float2*>(dst + r * DV + c) = make_float2(dS[j][0], dS[j][1]);
-      *reinterpret_cast<float2*>(dst + (r + 8) * DV + c) = make_float2(dS[j][2], dS[j][3]);
-    }
-  }
 }
 
 // ---------------------------------------------------------------------- recurrence
@@ -886,6 +518,14 @@ void gdn_prep_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, c
                         const torch::Tensor& v, const torch::Tensor& gg_f, const torch::Tensor& beta_f,
                         torch::Tensor& gcum, torch::Tensor& kinv, torch::Tensor& qinv, torch::Tensor& w,
                         torch::Tensor& u, torch::Tensor& tmat, float qscale, int* status, cudaStream_t stream);
+void gdn_state_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& k, const torch::Tensor& gcum,
+                         const torch::Tensor& kinv, const torch::Tensor& w, torch::Tensor& u, const float* init,
+                         torch::Tensor& states, torch::Tensor& fin, int* status, cudaStream_t stream);
+void gdn_dstate_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                          const torch::Tensor& gcum, const torch::Tensor& kinv, const torch::Tensor& qinv,
+                          const torch::Tensor& w, const torch::Tensor& p, const torch::Tensor& dout,
+                          const float* dfinal, torch::Tensor& dstates, torch::Tensor& dinit, int* status,
+                          cudaStream_t stream);
 void gdn_out_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
                        const torch::Tensor& gcum, const torch::Tensor& kinv, const torch::Tensor& qinv,
                        const torch::Tensor& u, const torch::Tensor& states, torch::Tensor& p, torch::Tensor& out,
@@ -919,17 +559,12 @@ std::vector<torch::Tensor> gdn_chunk_fwd_entry(torch::Tensor q, torch::Tensor k,
   auto bf = beta.to(at::kFloat).contiguous();
   torch::Tensor init_f;
   if (init.has_value()) init_f = init->to(at::kFloat).contiguous();
-  static SmemOptIn a_state;
-  C10_CUDA_CHECK(a_state.ensure(gdnk::gdn_state_kernel, (int)sizeof(gdnk::StateSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (rows > 0 && g.num_seqs > 0) {
     gdn_prep_tc_launch(g, bound, q, k, v, gf, bf, gcum, kinv, qinv, w, u, tmat, qscale, device_status(), st);
-    gdnk::gdn_state_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::StateSm), st>>>(
-        g, (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(), (const bf16*)w.data_ptr(),
-        (bf16*)u.data_ptr(), init.has_value() ? init_f.data_ptr<float>() : nullptr, (bf16*)states.data_ptr(),
-        fin.data_ptr<float>());
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdn_state_tc_launch(g, bound, k, gcum, kinv, w, u, init.has_value() ? init_f.data_ptr<float>() : nullptr, states,
+                        fin, device_status(), st);
     gdn_out_tc_launch(g, bound, q, k, gcum, kinv, qinv, u, states, p, out, device_status(), st);
   } else {
     fin.zero_();
@@ -962,17 +597,12 @@ std::vector<torch::Tensor> gdn_chunk_bwd(torch::Tensor dout, torch::Tensor q, to
   auto dinit = torch::empty({g.num_seqs, H, gdnk::DK, gdnk::DV}, f32);
   torch::Tensor dfin_f;
   if (dfinal.has_value()) dfin_f = dfinal->to(at::kFloat).contiguous();
-  static SmemOptIn a_dstate;
-  C10_CUDA_CHECK(a_dstate.ensure(gdnk::gdn_dstate_kernel, (int)sizeof(gdnk::DStateSm)));
   const float qscale = 1.f / std::sqrt((float)gdnk::DK);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int64_t rows = (int64_t)q.size(0) * q.size(1);
   if (rows > 0 && g.num_seqs > 0) {
-    gdnk::gdn_dstate_kernel<<<g.num_seqs * H * gdnk::PARTS, gdnk::NT, sizeof(gdnk::DStateSm), st>>>(
-        g, (const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), gcum.data_ptr<float>(), kinv.data_ptr<float>(),
-        qinv.data_ptr<float>(), (const bf16*)w.data_ptr(), (const bf16*)p.data_ptr(), (const bf16*)doc.data_ptr(),
-        dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, (bf16*)dstates.data_ptr(), dinit.data_ptr<float>());
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    gdn_dstate_tc_launch(g, bound, q, k, gcum, kinv, qinv, w, p, doc,
+                         dfinal.has_value() ? dfin_f.data_ptr<float>() : nullptr, dstates, dinit, device_status(), st);
     gdn_grad_tc_launch(g, bound, q, k, v, bf, gcum, kinv, qinv, u, states, dstates, tmat, doc, dq, dk, dv, dg, db,
                        qscale, device_status(), st);
   } else {

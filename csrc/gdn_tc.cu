@@ -956,6 +956,429 @@ gdn_out_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
   }
 }
 
+// gdn_state_tc: the forward state recurrence.  One CTA (four warps) per (sequence, head,
+// 64 value columns); the state slice S (128 x 64, fp32) stays in TMEM as the accumulator
+// of its own update.  Per chunk: S0 -> bf16 operand tile and the saved states; S <-
+// e^{gamma_C} S (tcgen05.ld / st); U = U~ - W S0 (64-row MMA, written back over U~); then
+// S += K^T diag(F kinv) U (128-row MMA on the raw keys).  The next chunk's W, K, U~ and
+// per-token scalars are loaded (TMA and cp.async on one mbarrier) while this one runs.
+struct StateTcSm {
+  static constexpr int kW = 0;          // W        2 x (64 x 128)
+  static constexpr int kK = 32768;      // raw K    2 x (64 x 128)
+  static constexpr int kU = 65536;      // U~ slice 2 x (64 x 64)
+  static constexpr int kS0 = 81920;     // S0 (bf16) 128 x 64
+  static constexpr int kFU = 98304;     // diag(F kinv) U  64 x 64
+  static constexpr int kScal = 106496;  // 2 x {gamma[64], kinv[64]}
+  static constexpr int kBars = kScal + 1024;
+  static constexpr int kTotal = kBars + 64;
+};
+
+struct StateTcArgs {
+  gdnk::Geo g;
+  const float* gcum;
+  const float* kinv;
+  bf16* u_io;          // (chunks, heads, 64, 128): U~ in, U out
+  const float* init;   // (seqs, heads, 128, 128) or nullptr
+  bf16* states;        // (chunks, heads, 128, 128): S at every chunk start
+  float* fin;          // (seqs, heads, 128, 128) or nullptr
+  int* status;
+};
+
+__global__ void __launch_bounds__(128, 2)
+gdn_state_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmU, const StateTcArgs a) {
+  using S = StateTcSm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const gdnk::Geo& g = a.g;
+  const int part = blockIdx.x & 1;
+  const int h = (blockIdx.x >> 1) % g.heads;
+  const int seq = g.order[(blockIdx.x >> 1) / g.heads];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col0 = part * 64;
+  int t0, len;
+  gdnk::seq_span(g, seq, t0, len);
+  const int nch = (len + C - 1) / C;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBars);  // load[2], U, S
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBars + 32);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1 + C);  // TMA arrival + one cp.async arrival per scalar lane
+    mbar_init(&bars[1], 1 + C);
+    mbar_init(&bars[2], 1);
+    mbar_init(&bars[3], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tU = tmem + 64;
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  const int64_t sh = (int64_t)seq * g.heads + h;
+  {  // initial state slice: row d = tid
+    uint32_t v[2][32];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) {
+      const float x = a.init != nullptr ? a.init[(sh * 128 + tid) * 128 + col0 + c] : 0.f;
+      v[c >> 5][c & 31] = __float_as_uint(x);
+    }
+    tmem_st32(tS + lane_base, v[0]);
+    tmem_st32(tS + lane_base + 32, v[1]);
+  }
+  auto prefetch = [&](int ci) {
+    const int b = ci & 1;
+    const int chunk = g.chunk_off[seq] + ci;
+    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    float* sc = reinterpret_cast<float*>(sm + S::kScal + b * 512);
+    if (tid < C) {
+      const int64_t src = (int64_t)h * g.rows + row0 + (tid < n ? tid : 0);
+      cp_async_4(smem_u32(sc + tid), a.gcum + src, tid < n);
+      cp_async_4(smem_u32(sc + 64 + tid), a.kinv + src, tid < n);
+      cp_async_mbar_arrive_noinc(&bars[b]);
+    }
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bars[b], 2 * 16384 + 8192);
+      for (int cb = 0; cb < 2; ++cb) {
+        tma_load_3d(sm + S::kW + b * 16384 + cb * 8192, &tmW, &bars[b], cb * 64, (int)(cbase * 64), 0);
+        tma_load_3d(sm + S::kK + b * 16384 + cb * 8192, &tmK, &bars[b], h * 128 + cb * 64, row0, 0);
+      }
+      tma_load_3d(sm + S::kU + b * 8192, &tmU, &bars[b], col0, (int)(cbase * 64), 0);
+    }
+  };
+  const uint32_t sb = smem_u32(sm);
+  bool ok = true;
+  if (nch > 0) prefetch(0);
+  tc_fence_before();
+  __syncthreads();
+  for (int ci = 0; ci < nch && ok; ++ci) {
+    const int b = ci & 1;
+    const int chunk = g.chunk_off[seq] + ci;
+    const int n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    if (ci > 0) ok = mbar_wait_warp(&bars[3], (ci - 1) & 1, a.status, __LINE__);  // previous S update done
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    if (ci + 1 < nch) prefetch(ci + 1);  // into the buffer the previous chunk released
+    ok = mbar_wait_warp(&bars[b], (ci >> 1) & 1, a.status, __LINE__);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    tc_fence_after();
+    const float* sc = reinterpret_cast<const float*>(sm + S::kScal + b * 512);
+    const float gl = sc[n - 1];
+    {  // S0 -> operand tile and saved states; S <- e^{gamma_C} S
+      uint32_t v[2][32];
+      tmem_ld32_raw(tS + lane_base, v[0]);
+      tmem_ld32_raw(tS + lane_base + 32, v[1]);
+      tmem_wait_ld();
+      const int d = tid;
+      bf16* dst = a.states + (cbase * 128 + d) * 128 + col0;
+      const float eg = __expf(gl);
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[c8 >> 2][(c8 & 3) * 8 + e]);
+        st8(sm + S::kS0, 128, d, c8 * 8, f);
+        *reinterpret_cast<uint4*>(dst + c8 * 8) = *reinterpret_cast<const uint4*>(sm + S::kS0 + sw_off(128, d, c8 * 8));
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[hh][i] = __float_as_uint(__uint_as_float(v[hh][i]) * eg);
+      tmem_st32(tS + lane_base, v[0]);
+      tmem_st32(tS + lane_base + 32, v[1]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // U (accumulator) = W S0
+      tc_fence_after();
+      constexpr uint32_t idesc = make_idesc_bf16(64, 64, false, true);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16_ss(tU, desc_k(sb + S::kW + b * 16384, 64, 0, kk), desc_mn(sb + S::kS0, 128, 0, kk), idesc,
+                     kk > 0 ? 1u : 0u);
+      umma_commit(&bars[2]);
+    }
+    ok = mbar_wait_warp(&bars[2], ci & 1, a.status, __LINE__);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    tc_fence_after();
+    {  // U = U~ - W S0 (back to global); diag(F kinv) U -> operand tile
+      uint32_t v[2][32];
+      tmem_ld32_raw(tU + lane_base, v[0]);
+      tmem_ld32_raw(tU + lane_base + 32, v[1]);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const int t = 16 * warp + lane;
+        const float f = t < n ? __expf(gl - sc[t]) * sc[64 + t] : 0.f;
+        bf16* ug = a.u_io + (cbase * C + t) * 128 + col0;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float ut[8], fu[8];
+          ld8(sm + S::kU + b * 8192, 64, t, c8 * 8, ut);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            ut[e] -= __uint_as_float(v[c8 >> 2][(c8 & 3) * 8 + e]);
+            fu[e] = f * ut[e];
+          }
+          *reinterpret_cast<uint4*>(ug + c8 * 8) = make_uint4(pack_bf16x2(ut[0], ut[1]), pack_bf16x2(ut[2], ut[3]),
+                                                              pack_bf16x2(ut[4], ut[5]), pack_bf16x2(ut[6], ut[7]));
+          st8(sm + S::kFU, 64, t, c8 * 8, fu);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // S += K^T (diag(F kinv) U)
+      tc_fence_after();
+      constexpr uint32_t idesc = make_idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tS, desc_mn(sb + S::kK + b * 16384, 64, 0, kk), desc_mn(sb + S::kFU, 64, 0, kk), idesc, 1u);
+      umma_commit(&bars[3]);
+    }
+  }
+  if (ok && nch > 0) ok = mbar_wait_warp(&bars[3], (nch - 1) & 1, a.status, __LINE__);
+  ok = __syncthreads_and(ok);
+  if (ok && a.fin != nullptr) {
+    tc_fence_after();
+    uint32_t v[2][32];
+    tmem_ld32_raw(tS + lane_base, v[0]);
+    tmem_ld32_raw(tS + lane_base + 32, v[1]);
+    tmem_wait_ld();
+    float* dst = a.fin + (sh * 128 + tid) * 128 + col0;
+#pragma unroll
+    for (int c4 = 0; c4 < 16; ++c4)
+      *reinterpret_cast<float4*>(dst + c4 * 4) =
+          make_float4(__uint_as_float(v[c4 >> 3][(c4 & 7) * 4]), __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 1]),
+                      __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 2]), __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 3]));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// gdn_dstate_tc: the reverse state-gradient recurrence.  One CTA (four warps) per
+// (sequence, head, 64 value columns); dS (128 x 64, fp32) stays in TMEM.  Per chunk, last
+// to first: dS_C -> bf16 operand tile and the saved dstates; dS <- e^{gamma_C} dS;
+//   dU  = P^T dO + diag(F kinv) (K_raw dS_C)            (two 64-row MMAs)
+//   dS += Q_raw^T diag(e^gamma qinv) dO - W^T dU        (two 128-row MMAs)
+struct DStateTcSm {
+  static constexpr int kQ = 0;          // raw Q     64 x 128
+  static constexpr int kW = 16384;      // W         64 x 128
+  static constexpr int kK = 32768;      // raw K     64 x 128
+  static constexpr int kP = 49152;      // P         64 x 64
+  static constexpr int kDO = 57344;     // dO slice  64 x 64, scaled in place to diag(e^gamma qinv) dO
+  static constexpr int kDS = 65536;     // dS_C (bf16) 128 x 64
+  static constexpr int kDU = 81920;     // -dU       64 x 64
+  static constexpr int kScal = 90112;   // gamma, kinv, qinv (64 each)
+  static constexpr int kBars = kScal + 768;
+  static constexpr int kTotal = kBars + 64;
+};
+
+struct DStateTcArgs {
+  gdnk::Geo g;
+  const float* gcum;
+  const float* kinv;
+  const float* qinv;
+  const float* dfinal;  // (seqs, heads, 128, 128) or nullptr
+  bf16* dstates;        // (chunks, heads, 128, 128): dS at every chunk end
+  float* dinit;         // (seqs, heads, 128, 128)
+  int* status;
+};
+
+__global__ void __launch_bounds__(128, 2)
+gdn_dstate_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmP,
+                     const __grid_constant__ CUtensorMap tmDO, const DStateTcArgs a) {
+  using S = DStateTcSm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const gdnk::Geo& g = a.g;
+  const int part = blockIdx.x & 1;
+  const int h = (blockIdx.x >> 1) % g.heads;
+  const int seq = g.order[(blockIdx.x >> 1) / g.heads];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col0 = part * 64;
+  int t0, len;
+  gdnk::seq_span(g, seq, t0, len);
+  const int nch = (len + C - 1) / C;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBars);  // load, dU products, dS update
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBars + 32);
+  float* gam = reinterpret_cast<float*>(sm + S::kScal);
+  float* ki = gam + 64;
+  float* qi = gam + 128;
+  if (tid == 0) {
+    mbar_init(&bars[0], 1 + C);
+    mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tA = tmem + 64, tB = tmem + 128;  // dS, P^T dO, K_raw dS_C
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  const int64_t sh = (int64_t)seq * g.heads + h;
+  {
+    uint32_t v[2][32];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) {
+      const float x = a.dfinal != nullptr ? a.dfinal[(sh * 128 + tid) * 128 + col0 + c] : 0.f;
+      v[c >> 5][c & 31] = __float_as_uint(x);
+    }
+    tmem_st32(tS + lane_base, v[0]);
+    tmem_st32(tS + lane_base + 32, v[1]);
+  }
+  const uint32_t sb = smem_u32(sm);
+  bool ok = true;
+  tc_fence_before();
+  __syncthreads();
+  for (int it = 0; it < nch && ok; ++it) {
+    const int ci = nch - 1 - it;
+    const int chunk = g.chunk_off[seq] + ci;
+    const int row0 = t0 + ci * C, n = min(C, len - ci * C);
+    const int64_t cbase = (int64_t)chunk * g.heads + h;
+    if (it > 0) ok = mbar_wait_warp(&bars[2], (it - 1) & 1, a.status, __LINE__);  // previous dS update done
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    if (tid < C) {
+      const int64_t src = (int64_t)h * g.rows + row0 + (tid < n ? tid : 0);
+      cp_async_4(smem_u32(gam + tid), a.gcum + src, tid < n);
+      cp_async_4(smem_u32(ki + tid), a.kinv + src, tid < n);
+      cp_async_4(smem_u32(qi + tid), a.qinv + src, tid < n);
+      cp_async_mbar_arrive_noinc(&bars[0]);
+    }
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bars[0], 3 * 16384 + 2 * 8192);
+      for (int cb = 0; cb < 2; ++cb) {
+        tma_load_3d(sm + S::kQ + cb * 8192, &tmQ, &bars[0], h * 128 + cb * 64, row0, 0);
+        tma_load_3d(sm + S::kW + cb * 8192, &tmW, &bars[0], cb * 64, (int)(cbase * 64), 0);
+        tma_load_3d(sm + S::kK + cb * 8192, &tmK, &bars[0], h * 128 + cb * 64, row0, 0);
+      }
+      tma_load_3d(sm + S::kP, &tmP, &bars[0], 0, (int)(cbase * 64), 0);
+      tma_load_3d(sm + S::kDO, &tmDO, &bars[0], h * 128 + col0, row0, 0);
+    }
+    tc_fence_after();
+    {  // dS_C -> operand tile and saved dstates; dS <- e^{gamma_C} dS (after the scalars land)
+      uint32_t v[2][32];
+      tmem_ld32_raw(tS + lane_base, v[0]);
+      tmem_ld32_raw(tS + lane_base + 32, v[1]);
+      tmem_wait_ld();
+      const int d = tid;
+      bf16* dst = a.dstates + (cbase * 128 + d) * 128 + col0;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[c8 >> 2][(c8 & 3) * 8 + e]);
+        st8(sm + S::kDS, 128, d, c8 * 8, f);
+        *reinterpret_cast<uint4*>(dst + c8 * 8) = *reinterpret_cast<const uint4*>(sm + S::kDS + sw_off(128, d, c8 * 8));
+      }
+      ok = mbar_wait_warp(&bars[0], it & 1, a.status, __LINE__);
+      ok = __syncthreads_and(ok);
+      if (!ok) break;
+      const float eg = __expf(gam[n - 1]);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[hh][i] = __float_as_uint(__uint_as_float(v[hh][i]) * eg);
+      tmem_st32(tS + lane_base, v[0]);
+      tmem_st32(tS + lane_base + 32, v[1]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // P^T dO and K_raw dS_C
+      tc_fence_after();
+      constexpr uint32_t id64 = make_idesc_bf16(64, 64, true, true);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tA, desc_mn(sb + S::kP, 64, 0, kk), desc_mn(sb + S::kDO, 64, 0, kk), id64, kk > 0 ? 1u : 0u);
+      constexpr uint32_t idk = make_idesc_bf16(64, 64, false, true);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16_ss(tB, desc_k(sb + S::kK, 64, 0, kk), desc_mn(sb + S::kDS, 128, 0, kk), idk, kk > 0 ? 1u : 0u);
+      umma_commit(&bars[1]);
+    }
+    ok = mbar_wait_warp(&bars[1], it & 1, a.status, __LINE__);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    tc_fence_after();
+    {  // -dU -> operand tile; dO rows scaled by e^gamma qinv in place (P^T dO has read them)
+      uint32_t va[2][32], vb[2][32];
+      tmem_ld32_raw(tA + lane_base, va[0]);
+      tmem_ld32_raw(tA + lane_base + 32, va[1]);
+      tmem_ld32_raw(tB + lane_base, vb[0]);
+      tmem_ld32_raw(tB + lane_base + 32, vb[1]);
+      tmem_wait_ld();
+      const float gl = gam[n - 1];
+      if (lane < 16) {
+        const int t = 16 * warp + lane;
+        const float f = t < n ? __expf(gl - gam[t]) * ki[t] : 0.f;
+        const float sq = t < n ? __expf(gam[t]) * qi[t] : 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float du[8], dq[8];
+          ld8(sm + S::kDO, 64, t, c8 * 8, dq);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = (c8 & 3) * 8 + e;
+            du[e] = -(__uint_as_float(va[c8 >> 2][j]) + f * __uint_as_float(vb[c8 >> 2][j]));
+            dq[e] *= sq;
+          }
+          st8(sm + S::kDU, 64, t, c8 * 8, du);
+          st8(sm + S::kDO, 64, t, c8 * 8, dq);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // dS += Q_raw^T (diag(e^gamma qinv) dO) + W^T (-dU)
+      tc_fence_after();
+      constexpr uint32_t id128 = make_idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tS, desc_mn(sb + S::kQ, 64, 0, kk), desc_mn(sb + S::kDO, 64, 0, kk), id128, 1u);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(tS, desc_mn(sb + S::kW, 64, 0, kk), desc_mn(sb + S::kDU, 64, 0, kk), id128, 1u);
+      umma_commit(&bars[2]);
+    }
+  }
+  if (ok && nch > 0) ok = mbar_wait_warp(&bars[2], (nch - 1) & 1, a.status, __LINE__);
+  ok = __syncthreads_and(ok);
+  if (ok) {
+    tc_fence_after();
+    uint32_t v[2][32];
+    tmem_ld32_raw(tS + lane_base, v[0]);
+    tmem_ld32_raw(tS + lane_base + 32, v[1]);
+    tmem_wait_ld();
+    float* dst = a.dinit + (sh * 128 + tid) * 128 + col0;
+#pragma unroll
+    for (int c4 = 0; c4 < 16; ++c4)
+      *reinterpret_cast<float4*>(dst + c4 * 4) =
+          make_float4(__uint_as_float(v[c4 >> 3][(c4 & 7) * 4]), __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 1]),
+                      __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 2]), __uint_as_float(v[c4 >> 3][(c4 & 7) * 4 + 3]));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace gtc
 
 // Host launcher, called by gdn_chunk_bwd (gdn.cu) after the dS recurrence: one CTA per
@@ -1058,6 +1481,69 @@ void gdn_out_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, co
   const int smem = gtc::OutTcSm::kTotal + 1024;
   C10_CUDA_CHECK(opt.ensure(gtc::gdn_out_tc_kernel, smem));
   gtc::gdn_out_tc_kernel<<<(unsigned)(bound * g.heads), gtc::NT, smem, stream>>>(tmQ, tmK, tmU, tmS, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb
+
+namespace mykb {
+
+void gdn_state_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& k, const torch::Tensor& gcum,
+                         const torch::Tensor& kinv, const torch::Tensor& w, torch::Tensor& u, const float* init,
+                         torch::Tensor& states, torch::Tensor& fin, int* status, cudaStream_t stream) {
+  const int64_t nbh = (int64_t)std::max(bound, 1) * g.heads;
+  TORCH_CHECK(nbh * 128 < (int64_t)INT32_MAX, "gdn_state_tc: too many chunks for 32-bit TMA coordinates");
+  const CUtensorMap tmW = make_tmap_3d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, nbh * 64, 1, 128, 0, 64, 64);
+  const CUtensorMap tmK = make_tmap_3d(k.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.row_q, g.rows, 1, g.row_q, 0, 64, 64);
+  const CUtensorMap tmU = make_tmap_3d(u.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 128, nbh * 64, 1, 128, 0, 64, 64);
+  gtc::StateTcArgs a;
+  a.g = g;
+  a.gcum = gcum.data_ptr<float>();
+  a.kinv = kinv.data_ptr<float>();
+  a.u_io = (gtc::bf16*)u.data_ptr();
+  a.init = init;
+  a.states = (gtc::bf16*)states.data_ptr();
+  a.fin = fin.data_ptr<float>();
+  a.status = status;
+  static SmemOptIn opt;
+  const int smem = gtc::StateTcSm::kTotal + 1024;
+  C10_CUDA_CHECK(opt.ensure(gtc::gdn_state_tc_kernel, smem));
+  gtc::gdn_state_tc_kernel<<<(unsigned)(g.num_seqs * g.heads * 2), 128, smem, stream>>>(tmW, tmK, tmU, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mykb
+
+namespace mykb {
+
+void gdn_dstate_tc_launch(const gdnk::Geo& g, int bound, const torch::Tensor& q, const torch::Tensor& k,
+                          const torch::Tensor& gcum, const torch::Tensor& kinv, const torch::Tensor& qinv,
+                          const torch::Tensor& w, const torch::Tensor& p, const torch::Tensor& dout,
+                          const float* dfinal, torch::Tensor& dstates, torch::Tensor& dinit, int* status,
+                          cudaStream_t stream) {
+  const int64_t nbh = (int64_t)std::max(bound, 1) * g.heads;
+  TORCH_CHECK(nbh * 128 < (int64_t)INT32_MAX, "gdn_dstate_tc: too many chunks for 32-bit TMA coordinates");
+  auto bfmap = [&](const torch::Tensor& t, int64_t dim0, int64_t dim1) {
+    return make_tmap_3d(t.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dim0, dim1, 1, dim0, 0, 64, 64);
+  };
+  const CUtensorMap tmQ = bfmap(q, g.row_q, g.rows);
+  const CUtensorMap tmW = bfmap(w, 128, nbh * 64);
+  const CUtensorMap tmK = bfmap(k, g.row_q, g.rows);
+  const CUtensorMap tmP = bfmap(p, 64, nbh * 64);
+  const CUtensorMap tmDO = bfmap(dout, g.row_v, g.rows);
+  gtc::DStateTcArgs a;
+  a.g = g;
+  a.gcum = gcum.data_ptr<float>();
+  a.kinv = kinv.data_ptr<float>();
+  a.qinv = qinv.data_ptr<float>();
+  a.dfinal = dfinal;
+  a.dstates = (gtc::bf16*)dstates.data_ptr();
+  a.dinit = dinit.data_ptr<float>();
+  a.status = status;
+  static SmemOptIn opt;
+  const int smem = gtc::DStateTcSm::kTotal + 1024;
+  C10_CUDA_CHECK(opt.ensure(gtc::gdn_dstate_tc_kernel, smem));
+  gtc::gdn_dstate_tc_kernel<<<(unsigned)(g.num_seqs * g.heads * 2), 128, smem, stream>>>(tmQ, tmW, tmK, tmP, tmDO, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

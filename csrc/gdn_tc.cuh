@@ -62,6 +62,12 @@ __device__ __forceinline__ void ld8(const uint8_t* tile, int R, int r, int c, fl
   }
 }
 
+// 4-byte asynchronous global -> shared copy (cp.async); zero-filled when !valid.
+__device__ __forceinline__ void cp_async_4(uint32_t dst_smem, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst_smem), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+
 // 16 consecutive fp32 columns of this thread's TMEM lane (warp-collective, no wait).
 __device__ __forceinline__ void tmem_ld16_raw(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
