@@ -170,8 +170,11 @@ def synthetic_batches(n: int, step0: int, rank: int, world: int, batch_cls, seq_
     from myk_llm_b200.data.config import DataConfig, SyntheticDataConfig
     from myk_llm_b200.data.synthetic import SyntheticLoader
 
+    # with several ranks, the global batch's rows go to ranks balanced by attention work
+    # (the same global batch for both arms; only the row-to-rank mapping changes)
     cfg = DataConfig(kind="synthetic", seq_len=seq_len, micro_batch_size=micro, seed=seed,
-                     synthetic=SyntheticDataConfig(vocab_size=65536, mean_doc_len=1024, eos_id=0))
+                     synthetic=SyntheticDataConfig(vocab_size=65536, mean_doc_len=1024, eos_id=0,
+                                                   balance_ranks=world > 1))
     ld = SyntheticLoader(cfg, rank, world)
     out = []
     for s in range(step0, step0 + n):
@@ -449,6 +452,8 @@ def main():
                        "parallelism": f"dp{world}" + _parallel_desc(trainer, world),
                        "optimizer": "Muon(ns=5)+AdamW", "z_loss": 1e-4,
                        "l2": "working set >> 126 MB L2 (no flush inserted)",
+                       **({"row_assignment": "global batch rows balanced over ranks by attention work"}
+                          if world > 1 else {}),
                        "layers": a.layers if a.layers is not None else _model_layers(a.model),
                        **({"overrides": a.set} if a.set else {})},
             "clocks": clk,

@@ -40,6 +40,10 @@ class SyntheticDataConfig:
     vocab_size: int = 65536
     mean_doc_len: int = 1024
     eos_id: int = 0
+    # Assign the rows of each global batch to ranks so that every rank gets about the same
+    # attention work (sum of squared document lengths) instead of a fixed slice; the global
+    # batch, and so the data-parallel gradient, is unchanged.
+    balance_ranks: bool = False
 
 
 @dataclass

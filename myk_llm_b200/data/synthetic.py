@@ -53,14 +53,39 @@ class SyntheticLoader:
         self.config, self.rank, self.world_size = config, rank, world_size
         self.step = 0
 
-    def batch_at(self, step: int) -> Batch:
+    def _row(self, global_row: int) -> dict[str, np.ndarray]:
         c, s = self.config, self.config.synthetic
-        rows = []
-        for i in range(c.micro_batch_size):
-            global_row = (step * self.world_size + self.rank) * c.micro_batch_size + i
-            rng = np.random.default_rng([c.seed, global_row])
-            rows.append(packed_row(rng, c.seq_len, s.vocab_size, s.mean_doc_len, s.eos_id, c.document_masking))
-        return collate(rows)
+        rng = np.random.default_rng([c.seed, global_row])
+        return packed_row(rng, c.seq_len, s.vocab_size, s.mean_doc_len, s.eos_id, c.document_masking)
+
+    def rows_of(self, step: int) -> list[int]:
+        """Global row indices of this rank's micro-batch at ``step``: a fixed slice of the
+        global batch, or, with ``synthetic.balance_ranks``, the rows that a longest-first
+        assignment gives this rank so that every rank's attention work (sum over its rows of
+        the squared document lengths) is about equal.  Every rank computes the same
+        assignment from the same global batch."""
+        c = self.config
+        micro, world = c.micro_batch_size, self.world_size
+        first = step * world * micro
+        if not c.synthetic.balance_ranks or world == 1 or not c.document_masking:
+            return [first + self.rank * micro + i for i in range(micro)]
+        cost = []
+        for g in range(first, first + world * micro):
+            lens = self._row(g)["seqlens"].astype(np.float64)
+            cost.append(float((lens * lens).sum()))
+        order = sorted(range(world * micro), key=lambda i: (-cost[i], i))
+        load, count = [0.0] * world, [0] * world
+        mine = []
+        for i in order:
+            r = min((r for r in range(world) if count[r] < micro), key=lambda r: (load[r], r))
+            load[r] += cost[i]
+            count[r] += 1
+            if r == self.rank:
+                mine.append(first + i)
+        return sorted(mine)
+
+    def batch_at(self, step: int) -> Batch:
+        return collate([self._row(g) for g in self.rows_of(step)])
 
     def next_batch(self) -> Batch:
         b = self.batch_at(self.step)

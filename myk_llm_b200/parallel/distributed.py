@@ -60,6 +60,7 @@ def init_distributed(device_type: str | None = None, timeout_s: float | None = N
         device = torch.device("cuda", local)
         if not dist.is_initialized():
             dist.init_process_group("nccl", timeout=timeout, device_id=device)
+            _host_group(timeout)
     else:
         device = torch.device("cpu")
         if not dist.is_initialized():
@@ -72,12 +73,30 @@ def shutdown() -> None:
         dist.destroy_process_group()
 
 
-def all_reduce_sum(value: float | int, device: torch.device) -> float:
+_HOST_GROUP: list = []
+
+
+def _host_group(timeout: timedelta | None = None):
+    """A gloo group over the same ranks for host-side scalars (created once, by every rank
+    at the same point, right after the NCCL group); the default group when it is gloo."""
+    if not _HOST_GROUP:
+        if dist.get_backend() == "gloo":
+            _HOST_GROUP.append(dist.group.WORLD)
+        else:
+            kw = {"timeout": timeout} if timeout is not None else {}
+            _HOST_GROUP.append(dist.new_group(backend="gloo", **kw))
+    return _HOST_GROUP[0]
+
+
+def all_reduce_sum(value: float | int, device: torch.device) -> float:  # noqa: ARG001
+    """Sum of a host value over the ranks, on the host (gloo).  A per-step scalar such as the
+    global target count then costs no GPU work and no device synchronisation, so each
+    rank's host keeps queueing the next step's kernels while its GPU still runs this one."""
     if not dist.is_initialized():
         return float(value)
-    t = torch.tensor(float(value), device=device, dtype=torch.float64)
-    dist.all_reduce(t)
-    return float(t)
+    t = torch.tensor([float(value)], dtype=torch.float64)
+    dist.all_reduce(t, group=_host_group())
+    return float(t[0])
 
 
 def barrier() -> None:
