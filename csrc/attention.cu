@@ -91,13 +91,33 @@ struct Item {
   int n_kv;      // number of 128-key tiles
 };
 
+// Work items: CTA c takes items c, c + grid, c + 2 grid, ...  The tiles of every (sequence,
+// head) column are cut into bands of kBand tiles, heaviest band first (so every CTA starts
+// on heavy tiles and the tail is light); inside a band the items run column by column, and
+// band b is rotated by b * kBand items.  So the tiles of one long document go to different
+// CTAs whatever the number of columns: numbering by tile first sends every tile of a
+// column to the same CTA whenever the column count is a multiple of the grid, and one long
+// packed document then serialises there.
+constexpr int kBand = 4;
+__host__ __device__ __forceinline__ int fa_item_count(int tiles, int cols) {
+  return (tiles + kBand - 1) / kBand * kBand * cols;
+}
+// (band-ordered tile index from the heavy end, column) of item w
+__device__ __forceinline__ void fa_item_coords(int w, int cols, int& t, int& col) {
+  const int band = kBand * cols;
+  const int b = w / band;
+  const int r = (w % band + b * kBand) % band;
+  col = r / kBand;
+  t = b * kBand + r % kBand;
+}
+
 __device__ __forceinline__ bool decode_item(const FaParams& p, int w, Item& it) {
-  // heavier (later) query tiles first
-  const int per_tile = p.num_seqs * p.heads;
-  it.qt = p.q_tiles - 1 - w / per_tile;
-  const int rem = w % per_tile;
-  it.seq = rem / p.heads;
-  it.head = rem % p.heads;
+  int t, col;
+  fa_item_coords(w, p.num_seqs * p.heads, t, col);
+  if (t >= p.q_tiles) return false;
+  it.qt = p.q_tiles - 1 - t;  // heaviest (last) query tiles first
+  it.seq = col / p.heads;
+  it.head = col % p.heads;
   it.g = seq_geom(p, it.seq);
   it.q0 = it.qt * 128;
   if (it.q0 >= it.g.len_q) return false;
@@ -438,10 +458,12 @@ struct PairItem {
 };
 
 __device__ __forceinline__ bool decode_pair(const FaParams& p, int w, PairItem& it) {
+  // banded, rotated order of decode_item; heaviest query tiles first
   const int pairs = p.group / 2;
-  const int per_tile = p.num_seqs * p.kv_heads * pairs;
-  it.qt = p.q_tiles - 1 - w / per_tile;  // heavier (later) query tiles first
-  int rem = w % per_tile;
+  int t, rem;
+  fa_item_coords(w, p.num_seqs * p.kv_heads * pairs, t, rem);
+  if (t >= p.q_tiles) return false;
+  it.qt = p.q_tiles - 1 - t;
   it.seq = rem / (p.kv_heads * pairs);
   rem %= p.kv_heads * pairs;
   it.kvh = rem / pairs;
@@ -484,7 +506,7 @@ fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 10);
   constexpr int kCols = 512;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int total = p.q_tiles * p.num_seqs * p.kv_heads * (p.group / 2);
+  const int total = fa_item_count(p.q_tiles, p.num_seqs * p.kv_heads * (p.group / 2));
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
@@ -784,7 +806,7 @@ static void launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
     auto pk = fa_fwd_pair_kernel<D>;
     static SmemOptIn pair_configured;
     C10_CUDA_CHECK(pair_configured.ensure(pk, SP::kTotal));
-    const int items = p.q_tiles * p.num_seqs * p.kv_heads * (p.group / 2);
+    const int items = fa_item_count(p.q_tiles, p.num_seqs * p.kv_heads * (p.group / 2));
     pk<<<std::max(1, std::min(items, sm_count())), kFaPairThreads, SP::kTotal, st>>>(tq, tk, tv, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
@@ -830,7 +852,7 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
     p.seqused_k = seqused_k->data_ptr<int>();
   }
   p.q_tiles = (int)((max_q + 127) / 128);
-  p.total_items = p.q_tiles * p.num_seqs * p.heads;
+  p.total_items = fa_item_count(p.q_tiles, p.num_seqs * p.heads);
   p.out = (__nv_bfloat16*)out.data_ptr();
   p.out_row_stride = (int64_t)p.heads * D;
   p.lse = lse.data_ptr<float>();
@@ -869,11 +891,14 @@ struct BwdItem {
 };
 
 __device__ __forceinline__ bool decode_bwd(const FaBwdParams& p, int w, BwdItem& it) {
-  const int per = p.f.num_seqs * p.f.kv_heads;
-  it.kt = w / per;  // early key tiles (most work under a causal mask) first
-  const int rem = w % per;
-  it.seq = rem / p.f.kv_heads;
-  it.kvh = rem % p.f.kv_heads;
+  // banded, rotated order of decode_item; early key tiles (most work under a causal
+  // mask) first
+  int t, col;
+  fa_item_coords(w, p.f.num_seqs * p.f.kv_heads, t, col);
+  if (t >= p.k_tiles) return false;
+  it.kt = t;
+  it.seq = col / p.f.kv_heads;
+  it.kvh = col % p.f.kv_heads;
   it.g = seq_geom(p.f, it.seq);
   it.k0 = it.kt * 128;
   if (it.k0 >= it.g.len_k || it.g.len_q == 0) return false;
@@ -966,7 +991,7 @@ fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
+  const int total = fa_item_count(p.k_tiles, p.f.num_seqs * p.f.kv_heads);
 
   if (warp == 0) {
     // Producer warp: lane 0 issues the TMA copies of Q / dO; every lane copies the
@@ -1525,7 +1550,7 @@ static void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
     auto kern = fa_bwd_dkdv_kernel<D>;
     static SmemOptIn configured;
     C10_CUDA_CHECK(configured.ensure(kern, S::kTotal));
-    const int total = p.k_tiles * p.f.num_seqs * p.f.kv_heads;
+    const int total = fa_item_count(p.k_tiles, p.f.num_seqs * p.f.kv_heads);
     kern<<<std::max(1, std::min(total, sm_count())), kFaBwdThreads, S::kTotal, st>>>(tq, tk, tv, tdo, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
@@ -1565,7 +1590,7 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
     f.num_seqs = q.size(0);
   }
   f.q_tiles = (int)((max_q + 127) / 128);
-  f.total_items = f.q_tiles * f.num_seqs * f.heads;
+  f.total_items = fa_item_count(f.q_tiles, f.num_seqs * f.heads);
   p.k_tiles = (int)((max_k + 127) / 128);
   p.scale = (float)scale;
   auto dout_c = dout.contiguous();
@@ -1712,7 +1737,7 @@ extern "C" int mykb_flash_attn_bwd_noalloc(const void* dout, const void* q, cons
     f.cu_q = cu_seqlens;
     f.cu_k = cu_seqlens;
     f.q_tiles = (max_q + 127) / 128;
-    f.total_items = f.q_tiles * f.num_seqs * f.heads;
+    f.total_items = fa_item_count(f.q_tiles, f.num_seqs * f.heads);
     p.k_tiles = (max_k + 127) / 128;
     p.scale = softmax_scale;
     p.ld = sc.ld;
