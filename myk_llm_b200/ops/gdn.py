@@ -7,13 +7,16 @@ scale is ``head_k_dim ** -0.5``, the decay is ``g = -exp(A_log) * softplus(a + d
 log space (per head for GDN, per key channel for KDA), beta arrives already passed
 through a sigmoid.
 
-CUDA kernels (``csrc/gdn.cu``):
+CUDA kernels (``csrc/gdn.cu``, ``csrc/gdn_tc.cu``):
 
 * ``conv1d_fwd/bwd``: depthwise causal conv + SiLU over the packed q/k/v, resetting at
   document boundaries;
-* ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64, head dims 128) with the state
-  kept in fp32; each CTA owns one (sequence, head, half of the value columns) and walks
-  its chunks; the algorithm is stated in :mod:`myk_llm_b200.ops.gdn_chunk`;
+* ``gdn_chunk_fwd/bwd``: the chunked delta rule (chunk 64, head dims 128) on the tcgen05
+  tensor cores: chunk-parallel prep / output / gradient kernels (one CTA per chunk and
+  head) around the two state recurrences (one CTA per sequence, head and 64 value
+  columns, the fp32 state slice kept in TMEM); the algorithm is stated in
+  :mod:`myk_llm_b200.ops.gdn_chunk`.  Per-channel (KDA) decay runs that statement in
+  PyTorch on the GPU;
 * ``gdn_recurrent``: token-by-token decode over a state cache;
 * ``gdn_spec_window``: one speculative-decoding window over a committed state plus the
   previous window's pending inputs (:func:`spec_window`).
