@@ -131,25 +131,28 @@ rmsnorm_bwd_kernel(const TY* __restrict__ dy, const TX* __restrict__ x, const fl
   for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[c][i] = 0.f;
-  float wv[NC][4];
-#pragma unroll
-  for (int c = 0; c < NC; ++c) load4<float>(w + (c * 32 + lane) * 4, wv[c]);
 
   for (int row = blockIdx.x * kNormWarps + warp; row < rows; row += gridDim.x * kNormWarps) {
     const int64_t base = (int64_t)row * H;
     const float r = rstd[row];
-    float xh[NC][4], g[NC][4];
+    float xh[NC][4], g[NC][4], t[NC][4];
     float dot = 0.f;
+    // rows up to 1024 wide issue every load of the row (x, dy and the residual gradient)
+    // before the row reduction, so they are in flight together (wider rows would spill);
+    // the weights come from L1 each row
+    constexpr bool kEarly = NC <= 8;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int idx = (c * 32 + lane) * 4;
-      float xv[4], dv[4];
+      float xv[4], dv[4], wv[4];
       load4<TX>(x + base + idx, xv);
       load4<TY>(dy + base + idx, dv);
+      if (kEarly && dres != nullptr) load4<TX>(dres + base + idx, t[c]);
+      load4<float>(w + idx, wv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         xh[c][i] = xv[i] * r;
-        g[c][i] = dv[i] * wv[c][i];
+        g[c][i] = dv[i] * wv[i];
         dot += g[c][i] * xh[c][i];
         acc[c][i] += dv[i] * xh[c][i];
       }
@@ -162,10 +165,9 @@ rmsnorm_bwd_kernel(const TY* __restrict__ dy, const TX* __restrict__ x, const fl
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[i] = r * (g[c][i] - xh[c][i] * dot);
       if (dres != nullptr) {
-        float t[4];
-        load4<TX>(dres + base + idx, t);
+        if (!kEarly) load4<TX>(dres + base + idx, t[c]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] += t[i];
+        for (int i = 0; i < 4; ++i) o[i] += t[c][i];
       }
       store4<TX>(dx + base + idx, o);
       if (dx_bf != nullptr) store4<__nv_bfloat16>(dx_bf + base + idx, o);  // bf16 copy for a bf16 residual branch
