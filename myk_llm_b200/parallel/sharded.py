@@ -567,16 +567,21 @@ class ShardedDataParallel(nn.Module):
             self.flat_bf16 = torch.zeros(self.bf16_total, dtype=torch.bfloat16, device=dev)
 
     def _multicast_address(self, handle, tensor: torch.Tensor) -> int:
-        """NVSwitch multicast address of a symmetric buffer when every rank's GPU supports
-        NVLS (and ``MYKB_NVLS`` is not ``0``), else 0: the gradient reduce-scatter then reads
-        through the switch (``multimem.ld_reduce``) instead of from every peer."""
+        """NVSwitch multicast address of a symmetric buffer, or 0: with an address the gradient
+        reduce-scatter reads through the switch (``multimem.ld_reduce``) instead of from
+        every peer.  ``MYKB_NVLS``: ``0`` never, ``1`` whenever every rank's GPU supports
+        NVLS, unset: only from 8 ranks.  A multicast read also carries the reading GPU's own
+        copy over NVLink, N / (N - 1) times the bytes of the peer loads: measured on the
+        200M gradient buffer at 2 ranks the peer loads took 1.25 ms and the multicast read
+        2.42 ms (``python -m myk_llm_b200.parallel.benchmark_collectives``)."""
         import os
 
         from torch._C._autograd import DeviceType
         from torch._C._distributed_c10d import _SymmetricMemory
 
-        ok = os.environ.get("MYKB_NVLS", "1") != "0" and \
-            _SymmetricMemory.has_multicast_support(DeviceType.CUDA, tensor.device.index)
+        mode = os.environ.get("MYKB_NVLS", "auto")
+        want = mode == "1" or (mode != "0" and self.world >= 8)
+        ok = want and _SymmetricMemory.has_multicast_support(DeviceType.CUDA, tensor.device.index)
         mc = int(handle.multicast_ptr) if ok else 0
         flag = torch.tensor([1 if mc else 0], dtype=torch.int32, device=tensor.device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)  # all ranks take the same path
