@@ -572,8 +572,9 @@ class ShardedDataParallel(nn.Module):
         every peer.  ``MYKB_NVLS``: ``0`` never, ``1`` whenever every rank's GPU supports
         NVLS, unset: only from 8 ranks.  A multicast read also carries the reading GPU's own
         copy over NVLink, N / (N - 1) times the bytes of the peer loads: measured on the
-        200M gradient buffer at 2 ranks the peer loads took 1.25 ms and the multicast read
-        2.42 ms (``python -m myk_llm_b200.parallel.benchmark_collectives``)."""
+        200M gradient buffer the peer loads took 1.25 ms and the multicast read 2.42 ms at
+        2 ranks, 2.52 ms and 2.27 ms at 8 ranks
+        (``python -m myk_llm_b200.parallel.benchmark_collectives``)."""
         import os
 
         from torch._C._autograd import DeviceType
