@@ -82,31 +82,41 @@ class _DeltaRule(torch.autograd.Function):
 
 
 def _chunked_torch(q, k, v, g, beta, initial_state, cu_seqlens, per_channel):
-    """Differentiable chunked statement (``gdn_chunk.chunk_fwd``) per sequence and head;
-    the path for per-channel (KDA) decay on the GPU."""
-    from .gdn_chunk import chunk_fwd
+    """Differentiable chunked statement (``gdn_chunk.chunk_fwd_batched``) over every
+    sequence and head at once; the path for per-channel (KDA) decay and for head dims other
+    than 128 on the GPU.  Packed documents are gathered into rows padded at the end to the
+    longest document (padding leaves the state unchanged) and scattered back."""
+    from .gdn_chunk import chunk_fwd_batched
 
     bsz, t_len, heads, dk = q.shape
+    dv = v.shape[-1]
     qf = F.normalize(q.float(), dim=-1, eps=1e-6) * dk ** -0.5
     kf = F.normalize(k.float(), dim=-1, eps=1e-6)
-    spans = ([(0, a, b) for a, b in zip(cu_seqlens.tolist()[:-1], cu_seqlens.tolist()[1:])] if cu_seqlens is not None
-             else [(b, 0, t_len) for b in range(bsz)])
-    rows, finals = [], []
-    for i, (b, a, e) in enumerate(spans):
-        outs, fins = [], []
-        for h in range(heads):
-            s0 = initial_state[i, h] if initial_state is not None else None
-            o, s, _ = chunk_fwd(qf[b, a:e, h], kf[b, a:e, h], v[b, a:e, h], g[b, a:e, h], beta[b, a:e, h], s0,
-                                per_channel=per_channel)
-            outs.append(o)
-            fins.append(s)
-        rows.append(torch.stack(outs, 1))
-        finals.append(torch.stack(fins))
+    gf, bf, vf = g.float(), beta.float(), v.float()
     if cu_seqlens is not None:
-        o = torch.cat(rows, 0)[None]
+        cu = cu_seqlens.to(device="cpu", dtype=torch.long)
+        lens = cu[1:] - cu[:-1]
+        n, width = lens.numel(), max(1, int(lens.max())) if lens.numel() else 1
+        pos = torch.arange(width)
+        valid = pos[None, :] < lens[:, None]  # (n, width)
+        idx = (cu[:-1, None] + pos[None, :]).clamp(max=max(0, t_len - 1))
+        valid_d, idx_d = valid.to(q.device), idx.to(q.device)
+
+        def rows(x):  # (1, T, ...) -> (n, width, ...) with zeros past each document
+            y = x[0][idx_d]
+            return y * valid_d.view(n, width, *([1] * (y.dim() - 2))).to(y.dtype)
+        qf, kf, vf, gf, bf = (rows(t) for t in (qf, kf, vf, gf, bf))
     else:
-        o = torch.stack(rows)
-    return o.to(v.dtype), torch.stack(finals)
+        n, width = bsz, t_len
+    # (n, width, heads, d) -> (n * heads, width, d)
+    def flat(x):
+        return x.transpose(1, 2).reshape(n * heads, width, *x.shape[3:])
+    s0 = initial_state.reshape(n * heads, dk, dv) if initial_state is not None else None
+    o, fin = chunk_fwd_batched(flat(qf), flat(kf), flat(vf), flat(gf), flat(bf), s0, per_channel=per_channel)
+    o = o.reshape(n, heads, width, dv).transpose(1, 2)
+    if cu_seqlens is not None:
+        o = o[valid_d][None]
+    return o.to(v.dtype), fin.reshape(n, heads, dk, dv)
 
 
 def gated_delta_rule(q, k, v, g, beta, initial_state=None, cu_seqlens=None, cu_seqlens_cpu=None,

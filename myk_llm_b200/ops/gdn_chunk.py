@@ -68,6 +68,45 @@ def chunk_fwd(q, k, v, g, beta, s0=None, chunk: int = 64, per_channel: bool = Fa
     return out, s, states
 
 
+def chunk_fwd_batched(q, k, v, g, beta, s0=None, chunk: int = 64, per_channel: bool = False):
+    """``chunk_fwd`` over a batch of independent (sequence, head) rows at once: q/k (N, T, dk)
+    (already normalised / scaled), v (N, T, dv), g (N, T) or (N, T, dk), beta (N, T), s0
+    (N, dk, dv) or None.  Rows shorter than T are padded at the end with zeros (zero k, v,
+    beta and g leave the state unchanged).  Returns (o (N, T, dv), final states (N, dk, dv));
+    differentiable, so autograd gives the backward.  Only the walk over chunks is a Python
+    loop: every product is one batched matmul / triangular solve over the N rows."""
+    n, t_len, dk = k.shape
+    dv = v.shape[-1]
+    dt = torch.promote_types(q.dtype, torch.float32)
+    s = torch.zeros(n, dk, dv, dtype=dt, device=q.device) if s0 is None else s0.to(dt)
+    outs = []
+    for a, b in _chunks(t_len, chunk):
+        Q, K, V, B = q[:, a:b].to(dt), k[:, a:b].to(dt), v[:, a:b].to(dt), beta[:, a:b].to(dt)
+        gam = torch.cumsum(g[:, a:b].to(dt), 1)  # (n, c) or (n, c, dk)
+        eye = torch.eye(b - a, device=q.device, dtype=dt)
+        if per_channel:
+            up, down = torch.exp(gam), torch.exp(-gam)
+            Kd, Kinv, Qd = K * up, K * down, Q * up
+            A = torch.tril(B[..., None] * (Kd @ Kinv.transpose(1, 2)), -1)
+            W = V - Kd @ s
+            P = torch.tril(Qd @ Kinv.transpose(1, 2))
+            U = torch.linalg.solve_triangular(eye + A, B[..., None] * W, upper=False, unitriangular=True)
+            outs.append(Qd @ s + P @ U)
+            gl = gam[:, -1]  # (n, dk)
+            s = torch.exp(gl)[..., None] * s + (K * torch.exp(gl[:, None, :] - gam)).transpose(1, 2) @ U
+        else:
+            E = torch.exp(gam[:, :, None] - gam[:, None, :])
+            eg = torch.exp(gam)[..., None]
+            A = torch.tril(B[..., None] * E * (K @ K.transpose(1, 2)), -1)
+            W = V - eg * (K @ s)
+            P = torch.tril(E * (Q @ K.transpose(1, 2)))
+            U = torch.linalg.solve_triangular(eye + A, B[..., None] * W, upper=False, unitriangular=True)
+            outs.append(eg * (Q @ s) + P @ U)
+            gl = gam[:, -1]  # (n,)
+            s = torch.exp(gl)[:, None, None] * s + (K * torch.exp(gl[:, None] - gam)[..., None]).transpose(1, 2) @ U
+    return torch.cat(outs, 1), s
+
+
 def chunk_bwd(q, k, v, g, beta, states, do, ds_final=None, chunk: int = 64):
     """Gradients (dq, dk, dv, dg, dbeta, ds0) of chunk_fwd (scalar decay per head)."""
     t_len, dk = k.shape

@@ -150,3 +150,35 @@ def test_causal_conv1d_kernels_match_reference(layout):
     (y_ref.float() * dy).sum().backward()
     assert _rel(xl.grad, xr.grad) < 1e-2
     assert _rel(wl.grad, wr.grad) < 1e-2
+
+
+@pytest.mark.parametrize("per_channel", [False, True])
+@pytest.mark.parametrize("packed", [False, True])
+def test_batched_chunked_statement_matches_recurrence_and_its_gradients(per_channel, packed):
+    """The chunked statement run over every sequence and head at once (the GPU path for
+    per-channel decay and for head dims other than 128) against the token recurrence:
+    outputs, final states and the gradients of every input, for packed documents of
+    unequal lengths (one of a single token) and for a batch of rows."""
+    from myk_llm_b200.ops.gdn import _chunked_torch
+
+    torch.manual_seed(3)
+    H, dk, dv = 2, 16, 8
+    if packed:
+        B, T, cu = 1, 100, torch.tensor([0, 37, 38, 100], dtype=torch.int32)
+    else:
+        B, T, cu = 2, 70, None
+    seqs = 3 if packed else B
+    leaves = [torch.randn(B, T, H, dk), torch.randn(B, T, H, dk), torch.randn(B, T, H, dv),
+              -torch.rand(B, T, H, *((dk,) if per_channel else ())) * 0.3, torch.rand(B, T, H),
+              torch.randn(seqs, H, dk, dv) * 0.1]
+    a = [t.clone().requires_grad_() for t in leaves]
+    b = [t.clone().requires_grad_() for t in leaves]
+    o, fin = _chunked_torch(*a[:5], a[5], cu, per_channel)
+    o_ref, fin_ref = ref.delta_rule_ref(*b[:5], initial_state=b[5], cu_seqlens=cu, per_channel_decay=per_channel)
+    torch.testing.assert_close(o, o_ref, atol=2e-5, rtol=2e-5)
+    torch.testing.assert_close(fin, fin_ref, atol=2e-5, rtol=2e-5)
+    wo, wf = torch.randn_like(o), torch.randn_like(fin)
+    ((o * wo).sum() + (fin * wf).sum()).backward()
+    ((o_ref * wo).sum() + (fin_ref * wf).sum()).backward()
+    for x, y in zip(a, b):
+        torch.testing.assert_close(x.grad, y.grad, atol=1e-4, rtol=1e-4)
