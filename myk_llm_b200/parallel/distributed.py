@@ -151,9 +151,12 @@ def parallelize(model, config, info: DistInfo):
         for block in model.blocks:
             fully_shard(block, mp_policy=policy, reshard_after_forward=config.reshard_after_forward)
         fully_shard(model, mp_policy=policy, reshard_after_forward=config.reshard_after_forward)
+        gloo = dist.get_backend() == "gloo"
         for m in model.modules():
             if isinstance(m, FSDPModule):
                 m.set_gradient_divide_factor(1.0)
+                if gloo:  # gloo has no PREMUL_SUM: plain SUM (the factor is 1 anyway)
+                    m.set_force_sum_reduction_for_comms(True)
         return model
     if uses_sharded(config, info) and info.enabled:
         from .sharded import shard_model

@@ -74,8 +74,7 @@ def _single(tmp):
 
 
 @pytest.mark.parametrize("strategy,reshard", [("sharded", True), ("sharded", False), ("replicated", False),
-                                              pytest.param("fsdp", False, marks=pytest.mark.skip(
-    reason="torch FSDP2's sum reduction uses ReduceOp.PREMUL_SUM, which gloo does not implement"))])
+                                              ("fsdp", False)])
 def test_world2_matches_single_process(strategy, reshard, tmp_path):
     out = str(tmp_path / "p.pt")
     mp.spawn(_worker, args=(2, _port(), out, strategy, reshard), nprocs=2, join=True)
