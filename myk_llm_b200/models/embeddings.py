@@ -118,6 +118,9 @@ class NgramEmbedding(nn.Module):
             return _NgramEmbed.apply(self.padded_tokens(input_ids, prefix_ids), self.context, tuple(self.orders),
                                      *weights)
         ids = self.row_ids(input_ids, prefix_ids)
+        shards = getattr(self.tables[0].weight, "_mykb_table", None)  # row-sharded (parallel/sharded.py)
+        if shards is not None:
+            return shards.lookup_cpu(ids)
         return sum(t(ids[k] - k * self.num_buckets) for k, t in enumerate(self.tables))
 
     def forward(self, input_ids: torch.Tensor, prefix_ids: torch.Tensor | None) -> dict[int, torch.Tensor]:

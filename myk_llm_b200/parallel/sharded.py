@@ -305,8 +305,6 @@ class TableShards:
     """
 
     def __init__(self, rt: "ShardedDataParallel", params: list[nn.Parameter], orders: list[int]) -> None:
-        import torch.distributed._symmetric_memory as symm
-
         self.rt = rt
         self.params = params
         self.orders = list(orders)
@@ -318,17 +316,22 @@ class TableShards:
         self.stride = _align(self.rows_per_rank * self.dim)  # elements between orders in a rank's buffer
         total = self.stride * len(params)
         dev = rt.info.device
-        self.param = symm.empty(total, dtype=torch.float32, device=dev)
-        self.grad = symm.empty(total, dtype=torch.float32, device=dev)
-        self.param.zero_()
-        self.grad.zero_()
+        if rt.cuda:
+            import torch.distributed._symmetric_memory as symm
+
+            self.param = symm.empty(total, dtype=torch.float32, device=dev)
+            self.grad = symm.empty(total, dtype=torch.float32, device=dev)
+            self.param.zero_()
+            self.grad.zero_()
+            self._handles = [symm.rendezvous(t, dist.group.WORLD) for t in (self.param, self.grad)]
+            # base addresses stay on the host: the launch reads them without a device sync
+            self.param_bases = torch.tensor(list(self._handles[0].buffer_ptrs), dtype=torch.int64)
+            self.grad_bases = torch.tensor(list(self._handles[1].buffer_ptrs), dtype=torch.int64)
+        else:  # gloo: the same ownership with collectives instead of peer memory
+            self.param = torch.zeros(total, dtype=torch.float32, device=dev)
+            self.grad = torch.zeros(total, dtype=torch.float32, device=dev)
         self.m = torch.zeros(total, dtype=torch.float32, device=dev)
         self.v = torch.zeros(total, dtype=torch.float32, device=dev)
-        group = dist.group.WORLD
-        self._handles = [symm.rendezvous(t, group) for t in (self.param, self.grad)]
-        # base addresses stay on the host: the launch reads them without a device sync
-        self.param_bases = torch.tensor(list(self._handles[0].buffer_ptrs), dtype=torch.int64)
-        self.grad_bases = torch.tensor(list(self._handles[1].buffer_ptrs), dtype=torch.int64)
         self.lo = rank * self.rows_per_rank
         self.hi = min(self.buckets, self.lo + self.rows_per_rank)
         with torch.no_grad():
@@ -354,6 +357,13 @@ class TableShards:
     def backward(self, rows: torch.Tensor, dout: torch.Tensor) -> None:
         ops.ext().ngram_embed_bwd_shard(rows, dout, self.grad_bases, self.stride * 4, self.rows_per_rank,
                                         self.buckets)
+
+    # -- CPU (gloo) path -----------------------------------------------------------------
+    def lookup_cpu(self, ids: torch.Tensor) -> torch.Tensor:
+        """Sum over the orders of the rows ``ids`` (orders, ...) addresses in the stacked
+        tables; forward from the all-gathered tables, backward adds the rank-summed gradient
+        of this rank's rows into its shard."""
+        return _TableLookupCPU.apply(ids, self, *self.params)  # the parameters make autograd call backward
 
     # -- optimizer step (between the runtime's barriers) -------------------------------------
     def add_sumsq(self, partial: torch.Tensor) -> None:
@@ -389,6 +399,43 @@ class TableShards:
 
     def memory_bytes(self) -> int:
         return 4 * (self.param.numel() + self.grad.numel() + self.m.numel() + self.v.numel())
+
+    def step_cpu(self, step: int, b1: float, b2: float, eps: float, coef: float) -> None:
+        """AdamW on this rank's rows (the same rule as ``shard_adamw``), gradient rows zeroed."""
+        g = self.group or {"lr": 0.0, "weight_decay": 0.0}
+        lr, wd = g["lr"], g["weight_decay"]
+        gr = self.grad * coef
+        self.m.lerp_(gr, 1 - b1)
+        self.v.mul_(b2).addcmul_(gr, gr, value=1 - b2)
+        bc1, bc2 = 1 - b1 ** step, math.sqrt(1 - b2 ** step)
+        self.param.mul_(1 - lr * wd).sub_((lr / bc1) * self.m / (self.v.sqrt() / bc2 + eps))
+        self.grad.zero_()
+
+
+class _TableLookupCPU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids: torch.Tensor, shards: "TableShards", *params):
+        ctx.shards = shards
+        ctx.save_for_backward(ids)
+        out = None
+        for j in range(len(shards.params)):
+            full = shards.gather(shards.param, j)
+            rows = full[ids[j] - j * shards.buckets]
+            out = rows if out is None else out + rows
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: torch.Tensor):
+        (ids,) = ctx.saved_tensors
+        t = ctx.shards
+        d = dout.reshape(-1, dout.shape[-1]).float()
+        for j in range(len(t.params)):
+            dense = torch.zeros(t.buckets, t.dim, dtype=torch.float32)
+            dense.index_add_(0, (ids[j] - j * t.buckets).reshape(-1), d)
+            dist.all_reduce(dense)
+            if t.hi > t.lo:
+                t.shard(t.grad, j)[:t.hi - t.lo].add_(dense[t.lo:t.hi])
+        return (None, None, *(None for _ in t.params))
 
 
 class ShardedDataParallel(nn.Module):
@@ -530,7 +577,7 @@ class ShardedDataParallel(nn.Module):
         on, dense (not lazily updated) tables trained by AdamW."""
         from ..models.embeddings import NgramEmbedding
 
-        if not (self.cuda and self.shard_params and self.world >= 2):
+        if not (self.shard_params and self.world >= 2):
             return [], []
         for m in self.module.modules():
             if isinstance(m, NgramEmbedding) and m.row_source is None:
@@ -826,11 +873,15 @@ class ShardedDataParallel(nn.Module):
         sizes = (self.red_prefix[1:] - self.red_prefix[:-1]).tolist()
         for o, n in zip(self.red_offsets.tolist(), sizes):
             sq += self.flat_grad[o:o + n].double().square().sum()
+        if self.tables is not None:  # this rank's table rows (each row is owned by one rank)
+            sq += self.tables.grad.double().square().sum()
         if dist.is_initialized():
             dist.all_reduce(sq)
         norm = sq.sqrt().float()
         coef = min(1.0, grad_clip / (float(norm) + 1e-6)) if grad_clip and grad_clip > 0 else 1.0
         b1, b2, eps = self._adam_hparams()
+        if self.tables is not None:
+            self.tables.step_cpu(self.step_count, b1, b2, eps, coef)
         bc1 = 1 - b1 ** self.step_count
         bc2 = math.sqrt(1 - b2 ** self.step_count)
         new = torch.zeros(self.rep_total)

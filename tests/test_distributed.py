@@ -180,3 +180,57 @@ def test_killed_rank_fails_fast_and_the_job_resumes_bit_exactly(tmp_path):
     resumed, clean = torch.load(tmp_path / "resumed.pt"), torch.load(tmp_path / "clean.pt")
     for name, p in clean.items():
         assert torch.equal(resumed[name], p), name
+
+
+NGRAM = ["model.ngram.orders=[2,3]", "model.ngram.num_buckets=1031", "model.ngram.dim=256"]
+
+
+def _ngram_worker(rank, world, port, out_path, ckpt):
+    """World-2 training with row-sharded n-gram tables over gloo, a checkpoint after step 2,
+    step 3, then the checkpoint loaded back and step 3 repeated."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), MYKB_PG_TIMEOUT_S="60")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from myk_llm_b200.data.synthetic import SyntheticLoader
+    from myk_llm_b200.train.checkpoint import load_checkpoint, save_checkpoint
+    from myk_llm_b200.train.trainer import Trainer
+
+    info = DistInfo(rank, world, rank, torch.device("cpu"))
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OVERRIDES + NGRAM + ["parallel.strategy=sharded"])
+    tr = Trainer(cfg, info, build_data=False)
+    assert tr.model.tables is not None and tr.model.tables.rows_per_rank == 516
+    ld = SyntheticLoader(tr.config.data, rank, world)
+
+    def step(s):
+        tr.train_step([ld.batch_at((s - 1) * tr.grad_accum + i) for i in range(tr.grad_accum)], s)
+
+    step(1)
+    step(2)
+    save_checkpoint(ckpt, tr.model, tr.optimizers, {"step": 2}, None, info, export_weights=False)
+    step(3)
+    first = {n: p.clone() for n, p in tr.model.full_named_parameters().items()}
+    load_checkpoint(ckpt, tr.model, tr.optimizers, info)
+    step(3)
+    again = tr.model.full_named_parameters()
+    if rank == 0:
+        torch.save({"first": first, "again": again}, out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_world2_row_sharded_ngram_tables_match_single_process_and_resume(tmp_path):
+    """The hashed n-gram tables row-sharded over two gloo ranks (each rank holds about half
+    of every table and its AdamW moments, and updates only its rows) train like one process
+    holding the whole tables, and a DCP checkpoint of the sharded tables resumes exactly."""
+    out = str(tmp_path / "p.pt")
+    mp.spawn(_ngram_worker, args=(2, _port(), out, str(tmp_path / "ckpt")), nprocs=2, join=True)
+    got = torch.load(out)
+    from myk_llm_b200.train.trainer import Trainer
+
+    cfg = load_config(TrainConfig, "configs/baseline/tiny_cpu.yaml", OVERRIDES + NGRAM)
+    ref = _run_steps(Trainer(cfg, DistInfo(0, 1, 0, torch.device("cpu")), build_data=False), 1, 0)
+    assert any("ngram" in n for n in ref)
+    for n, p in ref.items():
+        tol = 5e-4 if p.ndim == 2 and n.startswith("layers") else 1e-4  # bf16 Newton-Schulz noise
+        assert torch.allclose(got["first"][n], p, atol=tol, rtol=1e-4), (n, (got["first"][n] - p).abs().max())
+        assert torch.equal(got["again"][n], got["first"][n]), n
